@@ -1,0 +1,426 @@
+"""Benchmark of the titan.rs operator hot path on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--op gemm|softmax|sdpa|conv2d] [--impl ours|reference]
+
+Prints ONE JSON line (rank 0). Workloads are the BASELINE.json configurations:
+  gemm    C3  bf16 A[8192,8192] row-major x B column-major, fp32 accumulate, bf16 C (TFLOP/s);
+              N>1: B is N-sharded and C re-assembled with an all-gather (strong scaling).
+  softmax C2  fp32 [32768, 4096] row softmax, N(0, 2^2), seed 1 (GB/s; replicas at N>1).
+  sdpa    C4  causal bf16 B8 H32 S4096 D128 (TFLOP/s, causal-halved FLOPs); B*H-sharded at N>1.
+  conv2d  C5  bf16 NHWC 64x56x56x256 -> 256, 3x3 s1 p1 (TFLOP/s); batch-sharded at N>1.
+Inputs are seeded synthetic data (no dataset exists for this path).
+
+`value` is the device-timed whole-job throughput with inputs resident in HBM;
+`e2e` is the same metric through the C ABI with pinned-host inputs copied in and
+the result copied out inside every timed step. `--impl reference` times the CPU
+restatement of the reference's scalar operator (oracle/) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PEAK_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:
+            pass
+    return dict(PEAK_FALLBACK), "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi during the timed region (SM clock, max clock, throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- workloads
+class Workload:
+    """One hot-path op at one configuration, on one rank."""
+    name = ""
+    metric = ""
+    unit = ""
+    dtype = ""
+    scaling = "weak"
+    bound = "hbm"
+    flush_l2 = False
+
+    def __init__(self, tb, session, stream, rank: int, world: int, comm=None, small: bool = False):
+        self.tb, self.s, self.st, self.rank, self.world, self.comm = tb, session, stream, rank, world, comm
+        self.small = small
+
+    # work per step on this rank, in the metric's unit base (bytes or FLOPs)
+    def units_per_step(self) -> float:
+        raise NotImplementedError
+
+    def job_units_per_step(self) -> float:
+        return self.units_per_step() * self.world
+
+    def step(self):
+        raise NotImplementedError
+
+    def e2e_step(self):
+        raise NotImplementedError
+
+    def h2d_bytes(self) -> int:
+        raise NotImplementedError
+
+    def d2h_bytes(self) -> int:
+        raise NotImplementedError
+
+    def config(self) -> dict:
+        raise NotImplementedError
+
+    def cpu_sample(self, budget_s: float) -> dict:
+        raise NotImplementedError
+
+
+def _tensor(tb, buf, dtype, shape):
+    from titan_rs_b200.runtime import c_tensor, contiguous_strides
+    return c_tensor(buf, dtype, shape, contiguous_strides(shape))
+
+
+class SoftmaxWorkload(Workload):
+    name = "softmax"
+    metric = "row softmax fp32 [32768,4096] HBM throughput per B200"
+    unit = "GB/s"
+    dtype = "f32"
+    scaling = "weak"
+    bound = "hbm"
+    rows, cols = 32768, 4096
+
+    def __init__(self, *a, **k):
+        super().__init__(*a, **k)
+        import ctypes
+        from titan_rs_b200 import _native as N
+        from titan_rs_b200.kernel_abi import DType
+        self.N, self.ctypes, self.DType = N, ctypes, DType
+        if self.small:
+            self.rows = 16384  # 256 MiB input: still larger than L2, for ncu captures
+        n = self.rows * self.cols
+        self.nbytes = n * 4
+        self.host_in = self.s.host_alloc(self.nbytes)
+        self.host_out = self.s.host_alloc(self.nbytes)
+        x = self.host_in.array(np.float32, (self.rows, self.cols))
+        x[:] = self.tb.fill_normal(n, seed=1, mean=0.0, std=2.0).reshape(self.rows, self.cols)
+        self.x_host = x
+        self.din = self.s.allocate(self.nbytes)
+        self.dout = self.s.allocate(self.nbytes)
+        self.s.upload_pinned(self.st, self.din, self.host_in)
+        self.s.synchronize(self.st)
+        self.tin = _tensor(self.tb, self.din, DType.F32, (self.rows, self.cols))
+        self.tout = _tensor(self.tb, self.dout, DType.F32, (self.rows, self.cols))
+        self.kernel = "softmax_f32_warp32"
+
+    def units_per_step(self):
+        return 2.0 * self.nbytes  # read x once, write y once
+
+    def step(self):
+        rc = self.N.lib().tb_op_softmax(self.s.ptr, self.st.ptr, self.ctypes.byref(self.tin),
+                                        self.ctypes.byref(self.tout), None, 0, None)
+        if rc:
+            raise RuntimeError(self.N.last_error())
+
+    def e2e_step(self):
+        self.s.upload_pinned(self.st, self.din, self.host_in)
+        self.step()
+        self.s.download_pinned(self.st, self.dout, self.host_out)
+
+    def h2d_bytes(self):
+        return self.nbytes
+
+    def d2h_bytes(self):
+        return self.nbytes
+
+    def config(self):
+        return {"workload": "C2 row softmax fp32 [32768,4096], x~N(0,2^2) seed 1", "rows": self.rows,
+                "cols": self.cols, "parallelism": f"replicas{self.world}", "l2": "inputs 512 MiB > 126 MB L2"}
+
+    def cpu_sample(self, budget_s):
+        import oracle
+        threads = oracle.num_threads()
+        rows = 256
+        t0 = time.perf_counter()
+        done = 0
+        while True:
+            r0 = (done * rows) % self.rows
+            oracle.softmax_rows_mt(self.x_host[r0:r0 + rows], threads)
+            done += 1
+            if time.perf_counter() - t0 > budget_s:
+                break
+        dt = time.perf_counter() - t0
+        gbs = done * rows * self.cols * 8 / dt / 1e9
+        return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+                "sample": f"{done * rows} rows of the [32768,4096] tensor ({done} x {rows}-row chunks), "
+                          f"{dt:.1f} s on {threads} threads"}
+
+
+WORKLOADS = {"softmax": SoftmaxWorkload}
+DEFAULT_OP = "softmax"
+
+
+# ----------------------------------------------------------------------------- driver
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return world, rank, local
+
+
+def init_dist(world, local):
+    if world <= 1:
+        return None
+    import datetime
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    return dist
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def reduce_max(dist, value: float) -> float:
+    if dist is None:
+        return value
+    import torch
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_reference_arm(args, world, rank):
+    """CPU restatement of the reference's scalar operator, all host threads, bounded samples."""
+    if rank != 0:
+        return 0
+    sys.path.insert(0, str(ROOT))
+    import titan_rs_b200 as tb
+    import oracle
+    wl_cls = WORKLOADS[args.op]
+    sampler = REFERENCE_SAMPLERS[args.op]
+    times = []
+    info = None
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        info = sampler(tb, oracle, budget_s=args.ref_step_seconds)
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    line = {"impl": "reference", "metric": wl_cls.metric, "value": info["value"], "unit": info["unit"],
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * statistics.mean(times), "higher_is_better": True, "scaling": wl_cls.scaling,
+            "vs_baseline": None, "dtype": wl_cls.dtype, "data": "synthetic",
+            "config": info["config"],
+            "cpu_baseline": {"value": info["value"], "unit": info["unit"], "cores": info["cores"], "kind": "port",
+                             "sample": info["sample"]},
+            "e2e": {"value": info["value"], "unit": info["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def _ref_softmax(tb, oracle, budget_s):
+    rows, cols = SoftmaxWorkload.rows, SoftmaxWorkload.cols
+    chunk = 512
+    x = tb.fill_normal(chunk * cols, seed=1, std=2.0).reshape(chunk, cols)  # the first rows of the C2 tensor
+    threads = oracle.num_threads()
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < budget_s or n == 0:
+        oracle.softmax_rows_mt(x, threads)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": n * chunk * cols * 8 / dt / 1e9, "unit": "GB/s", "cores": threads,
+            "sample": f"{n * chunk} of {rows} rows of C2 in {dt:.1f} s",
+            "config": {"workload": "C2 row softmax fp32 [32768,4096], x~N(0,2^2) seed 1", "rows": rows, "cols": cols}}
+
+
+REFERENCE_SAMPLERS = {"softmax": _ref_softmax}
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--op", default=DEFAULT_OP, choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU baseline sample budget (rank 0, N=1)")
+    ap.add_argument("--ref-step-seconds", type=float, default=4.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--small", action="store_true",
+                    help="reduced problem (still larger than L2) for profiler captures; not a bench line")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        return run_reference_arm(args, world, rank)
+
+    import titan_rs_b200 as tb
+    from titan_rs_b200 import _native as N
+    dist = init_dist(world, local)
+    session = tb.Session(local)
+    stream = session.create_stream()
+    wl = WORKLOADS[args.op](tb, session, stream, rank, world, small=args.small)
+    peaks, peak_src = load_peaks()
+
+    for _ in range(args.warmup):
+        wl.step()
+    session.synchronize(stream)
+
+    # Device-timed steps: one event pair per step on the launching stream.
+    clocks = ClockSampler(local)
+    barrier(dist)
+    session.synchronize(stream)
+    clocks.start()
+    launches0 = int(N.lib().tb_launch_count())
+    evs = []
+    for _ in range(args.steps):
+        e0 = session.record(stream)
+        wl.step()
+        e1 = session.record(stream)
+        evs.append((e0, e1))
+    session.synchronize(stream)
+    launches = int(N.lib().tb_launch_count()) - launches0
+    barrier(dist)
+    clock_info = clocks.stop()
+    per_step = [session.elapsed_ms(a, b) for a, b in evs]
+    total_ms = reduce_max(dist, sum(per_step))
+    ms_step = total_ms / args.steps
+    units_step = wl.job_units_per_step()
+    scale = 1e9 if wl.unit == "GB/s" else 1e12
+    value = units_step / (ms_step / 1e3) / scale
+
+    # Roofline of the dominant kernel: algorithmic units of one launch / its average duration.
+    per_launch_ms = statistics.mean(per_step)
+    achieved = wl.units_per_step() / (per_launch_ms / 1e3) / scale
+    if wl.bound == "hbm":
+        peak = float(peaks.get("hbm_gbs", PEAK_FALLBACK["hbm_gbs"]))
+        r_unit = "GB/s"
+    else:
+        peak = float(peaks.get("bf16_tflops", PEAK_FALLBACK["bf16_tflops"]))
+        r_unit = "TFLOP/s"
+    traffic = TRAFFIC_PER_LAUNCH.get(args.op)
+
+    # End to end through the C ABI with pinned host buffers.
+    for _ in range(2):
+        wl.e2e_step()
+    session.synchronize(stream)
+    barrier(dist)
+    session.synchronize(stream)
+    e0 = session.record(stream)
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(e2e_steps):
+        wl.e2e_step()
+    e1 = session.record(stream)
+    session.synchronize(stream)
+    e2e_ms = reduce_max(dist, session.elapsed_ms(e0, e1)) / e2e_steps
+    e2e_value = units_step / (e2e_ms / 1e3) / scale
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = wl.cpu_sample(args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": wl.scaling,
+            "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded, BASELINE.json shapes)",
+            "config": wl.config(), "op": wl.name,
+            "roofline": {"bound": wl.bound, "kernel": wl.kernel, "achieved": achieved, "peak": peak, "unit": r_unit,
+                         "frac": achieved / peak, "peak_source": f"{peak_src} (MEASURED_PEAKS.json)"
+                         if peak_src == "measured" else "fallback", "traffic": traffic},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d_bytes(),
+                    "d2h_bytes_per_step": wl.d2h_bytes(), "ms_per_step": e2e_ms},
+            "gpu_launches": launches,
+            "clocks": clock_info,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+# DRAM bytes per launch from one ncu capture (profiles/), or None when not yet captured.
+TRAFFIC_PER_LAUNCH: dict = {}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

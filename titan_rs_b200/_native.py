@@ -1,0 +1,175 @@
+"""ctypes binding of libtitan_b200.so (the C ABI in include/titan_b200.h).
+
+The library is built in-tree by titan_rs_b200.build. Loading fails loudly when
+it is missing: there is no CPU or Python fallback for any operator.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+
+_PKG = pathlib.Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libtitan_b200.so"
+
+TB_OK = 0
+TB_ERR_DRIVER_UNAVAILABLE = 1
+TB_ERR_INVALID = 2
+TB_ERR_FOREIGN = 3
+TB_ERR_CUDA = 4
+TB_ERR_UNSUPPORTED = 5
+TB_ERR_TIMEOUT = 6
+TB_ERR_NCCL = 7
+TB_ERR_OUT_OF_MEMORY = 8
+
+TB_F32, TB_F16, TB_BF16, TB_I32, TB_I64 = 0, 1, 2, 3, 4
+TB_ARG_BUFFER, TB_ARG_SCALAR, TB_ARG_SHAPE = 0, 1, 2
+TB_MAX_RANK = 6
+TB_COMM_ID_BYTES = 128
+
+
+class Fingerprint(ctypes.Structure):
+    _fields_ = [("ordinal", ctypes.c_uint32), ("model", ctypes.c_char * 128), ("driver", ctypes.c_char * 32),
+                ("capability_revision", ctypes.c_char * 16), ("sm_count", ctypes.c_uint32),
+                ("total_memory", ctypes.c_uint64)]
+
+
+class LaunchArg(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_uint32), ("width", ctypes.c_uint32)]
+
+
+class LaunchMetadata(ctypes.Structure):
+    _fields_ = [("version", ctypes.c_uint32), ("entry", ctypes.c_char_p), ("arguments", ctypes.POINTER(LaunchArg)),
+                ("num_arguments", ctypes.c_uint32), ("block", ctypes.c_uint32 * 3), ("shared_bytes", ctypes.c_uint32)]
+
+
+class Binding(ctypes.Structure):
+    _fields_ = [("slot", ctypes.c_uint32), ("buffer", ctypes.c_void_p), ("owner", ctypes.c_void_p)]
+
+
+class EncodedArgs(ctypes.Structure):
+    _fields_ = [("payload", ctypes.POINTER(ctypes.c_uint8)), ("payload_len", ctypes.c_size_t),
+                ("bindings", ctypes.POINTER(Binding)), ("num_bindings", ctypes.c_uint32),
+                ("canonical_abi", ctypes.POINTER(ctypes.c_uint8)), ("canonical_abi_len", ctypes.c_size_t)]
+
+
+class LaunchGeometry(ctypes.Structure):
+    _fields_ = [("grid", ctypes.c_uint32 * 3), ("block", ctypes.c_uint32 * 3), ("shared_bytes", ctypes.c_uint32)]
+
+
+class Tensor(ctypes.Structure):
+    _fields_ = [("buffer", ctypes.c_void_p), ("dtype", ctypes.c_uint32), ("rank", ctypes.c_uint32),
+                ("shape", ctypes.c_uint64 * TB_MAX_RANK), ("strides", ctypes.c_int64 * TB_MAX_RANK)]
+
+
+class Attr(ctypes.Structure):
+    _fields_ = [("key", ctypes.c_char_p), ("value", ctypes.c_int64), ("str", ctypes.c_char_p)]
+
+
+_P = ctypes.c_void_p
+_PP = ctypes.POINTER(ctypes.c_void_p)
+_S = ctypes.c_int
+_SZ = ctypes.c_size_t
+_U32 = ctypes.c_uint32
+_U64 = ctypes.c_uint64
+
+# name -> (restype, argtypes)
+_SIGNATURES = {
+    "tb_last_error_operation": (ctypes.c_char_p, []),
+    "tb_last_error_detail": (ctypes.c_char_p, []),
+    "tb_version": (ctypes.c_char_p, []),
+    "tb_last_candidate": (ctypes.c_char_p, []),
+    "tb_launch_count": (_U64, []),
+    "tb_driver_open": (_S, []),
+    "tb_driver_enumerate": (_S, [ctypes.POINTER(Fingerprint), _U32, ctypes.POINTER(_U32)]),
+    "tb_session_open": (_S, [_U32, _PP]),
+    "tb_session_retain": (None, [_P]),
+    "tb_session_release": (None, [_P]),
+    "tb_session_fingerprint": (_S, [_P, ctypes.POINTER(Fingerprint)]),
+    "tb_allocate": (_S, [_P, _SZ, _SZ, _PP]),
+    "tb_buffer_wrap": (_S, [_P, _U64, _SZ, _PP]),
+    "tb_buffer_retain": (None, [_P]),
+    "tb_buffer_release": (None, [_P]),
+    "tb_buffer_byte_len": (_SZ, [_P]),
+    "tb_buffer_identity": (_U64, [_P]),
+    "tb_buffer_device_ptr": (_U64, [_P]),
+    "tb_create_stream": (_S, [_P, _PP]),
+    "tb_stream_release": (None, [_P]),
+    "tb_create_event": (_S, [_P, _PP]),
+    "tb_event_release": (None, [_P]),
+    "tb_upload": (_S, [_P, _P, _P, _P, _SZ, _PP]),
+    "tb_download": (_S, [_P, _P, _P, _P, _SZ, _PP]),
+    "tb_copy": (_S, [_P, _P, _P, _P, _SZ, _PP]),
+    "tb_load": (_S, [_P, _P, _SZ, ctypes.c_char_p, ctypes.POINTER(LaunchMetadata), _PP]),
+    "tb_kernel_release": (None, [_P]),
+    "tb_builtin_cubin": (_S, [ctypes.c_char_p, _PP, ctypes.POINTER(_SZ)]),
+    "tb_launch": (_S, [_P, _P, _P, ctypes.POINTER(EncodedArgs), ctypes.POINTER(LaunchGeometry), _PP]),
+    "tb_poll": (_S, [_P, _P, ctypes.POINTER(ctypes.c_int)]),
+    "tb_wait": (_S, [_P, _P]),
+    "tb_wait_event": (_S, [_P, _P, _P]),
+    "tb_record": (_S, [_P, _P, _PP]),
+    "tb_event_elapsed_ms": (_S, [_P, _P, _P, ctypes.POINTER(ctypes.c_float)]),
+    "tb_stream_synchronize": (_S, [_P, _P]),
+    "tb_stream_handle": (_U64, [_P]),
+    "tb_host_alloc": (_S, [_P, _SZ, _PP]),
+    "tb_host_free": (_S, [_P, _P]),
+    "tb_upload_pinned": (_S, [_P, _P, _P, _SZ, _P, _SZ, _PP]),
+    "tb_download_pinned": (_S, [_P, _P, _P, _SZ, _P, _SZ, _PP]),
+    "tb_op_softmax": (_S, [_P, _P, ctypes.POINTER(Tensor), ctypes.POINTER(Tensor), ctypes.POINTER(Attr), _U32, _PP]),
+    "tb_op_gemm": (_S, [_P, _P, ctypes.POINTER(Tensor), ctypes.POINTER(Tensor), ctypes.POINTER(Tensor),
+                        ctypes.POINTER(Attr), _U32, _PP]),
+    "tb_op_sdpa": (_S, [_P, _P, ctypes.POINTER(Tensor), ctypes.POINTER(Tensor), ctypes.POINTER(Tensor),
+                        ctypes.POINTER(Tensor), ctypes.POINTER(Attr), _U32, _PP]),
+    "tb_op_conv2d": (_S, [_P, _P, ctypes.POINTER(Tensor), ctypes.POINTER(Tensor), ctypes.POINTER(Tensor),
+                          ctypes.POINTER(Tensor), ctypes.POINTER(Attr), _U32, _PP]),
+    "tb_comm_unique_id": (_S, [ctypes.POINTER(ctypes.c_uint8)]),
+    "tb_comm_init": (_S, [_P, ctypes.POINTER(ctypes.c_uint8), _S, _S, _U32, _PP]),
+    "tb_comm_release": (None, [_P]),
+    "tb_comm_rank": (_S, [_P]),
+    "tb_comm_size": (_S, [_P]),
+    "tb_comm_all_gather": (_S, [_P, _P, _P, _P, _SZ, _PP]),
+    "tb_comm_barrier": (_S, [_P, _P]),
+    "tb_op_gemm_sharded": (_S, [_P, _P, ctypes.POINTER(Tensor), ctypes.POINTER(Tensor), ctypes.POINTER(Tensor), _P,
+                                _PP]),
+    "tb_fill_normal": (_S, [_P, _U32, _SZ, _U64, ctypes.c_double, ctypes.c_double, _S]),
+    "tb_fill_uniform": (_S, [_P, _U32, _SZ, _U64, ctypes.c_double, ctypes.c_double, _S]),
+}
+
+EXPORTED = tuple(_SIGNATURES)
+
+_lib = None
+
+
+class NativeLibraryMissing(RuntimeError):
+    pass
+
+
+def lib():
+    """Loads libtitan_b200.so once; raises NativeLibraryMissing when it is not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise NativeLibraryMissing(
+            f"{LIB_PATH} is not built: run `python -m titan_rs_b200.build` (there is no fallback path)")
+    L = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in _SIGNATURES.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def builtin_cubin(module: str) -> bytes:
+    """Bytes of an embedded sm_100a cubin (tb_builtin_cubin)."""
+    L = lib()
+    data = ctypes.c_void_p(0)
+    n = ctypes.c_size_t(0)
+    if L.tb_builtin_cubin(module.encode(), ctypes.byref(data), ctypes.byref(n)) != TB_OK:
+        raise KeyError(module)
+    return ctypes.string_at(data.value, n.value)
+
+
+def last_error() -> tuple[str, str]:
+    L = lib()
+    return L.tb_last_error_operation().decode(), L.tb_last_error_detail().decode()
