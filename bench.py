@@ -64,7 +64,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (FileNotFoundError, OSError):
             self.proc = None
             return
@@ -227,8 +227,98 @@ class SoftmaxWorkload(Workload):
                           f"{dt:.1f} s on {threads} threads"}
 
 
-WORKLOADS = {"softmax": SoftmaxWorkload}
-DEFAULT_OP = "softmax"
+def tensor_seed(config_seed: int, index: int) -> int:
+    """Seed of the index-th input tensor of a configuration (A=0, B=1; Q=0, K=1, V=2; x=0, w=1)."""
+    return config_seed * 16 + index
+
+
+class GemmWorkload(Workload):
+    name = "gemm"
+    metric = "bf16 GEMM 8192^3 (A row-major x B column-major, fp32 accumulate) TFLOP/s per B200"
+    unit = "TFLOP/s"
+    dtype = "bf16"
+    scaling = "strong"
+    bound = "tensor"
+    M = N = K = 8192
+
+    def __init__(self, *a, **k):
+        super().__init__(*a, **k)
+        import ctypes
+        from titan_rs_b200 import _native as N
+        from titan_rs_b200.kernel_abi import DType
+        self.Nn, self.ctypes, self.DType = N, ctypes, DType
+        if self.small:
+            self.M = self.N = self.K = 4096
+        M, Nn, K = self.M, self.N, self.K
+        self.a_bytes, self.b_bytes, self.c_bytes = M * K * 2, Nn * K * 2, M * Nn * 2
+        self.host_a = self.s.host_alloc(self.a_bytes)
+        self.host_b = self.s.host_alloc(self.b_bytes)
+        self.host_c = self.s.host_alloc(self.c_bytes)
+        self.a_bits = self.host_a.array(np.uint16, (M, K))
+        self.b_bits = self.host_b.array(np.uint16, (Nn, K))
+        self.a_bits[:] = self.tb.fill_normal(M * K, seed=tensor_seed(2, 0), std=1.0, dtype=DType.BF16).reshape(M, K)
+        self.b_bits[:] = self.tb.fill_normal(Nn * K, seed=tensor_seed(2, 1), std=1.0 / math.sqrt(K),
+                                             dtype=DType.BF16).reshape(Nn, K)
+        self.da = self.s.allocate(self.a_bytes)
+        self.db = self.s.allocate(self.b_bytes)
+        self.dc = self.s.allocate(self.c_bytes)
+        self.s.upload_pinned(self.st, self.da, self.host_a)
+        self.s.upload_pinned(self.st, self.db, self.host_b)
+        self.s.synchronize(self.st)
+        self.ta = _tensor(self.tb, self.da, DType.BF16, (M, K))
+        self.tbm = _tensor(self.tb, self.db, DType.BF16, (Nn, K))
+        self.tc = _tensor(self.tb, self.dc, DType.BF16, (M, Nn))
+        self.attrs = (N.Attr * 1)()
+        self._key = b"transpose_rhs"
+        self.attrs[0].key = self._key
+        self.attrs[0].value = 1
+        self.kernel = "gemm_bf16_tn"
+
+    def units_per_step(self):
+        return 2.0 * self.M * self.N * self.K
+
+    def step(self):
+        rc = self.Nn.lib().tb_op_gemm(self.s.ptr, self.st.ptr, self.ctypes.byref(self.ta), self.ctypes.byref(self.tbm),
+                                      self.ctypes.byref(self.tc), self.attrs, 1, None)
+        if rc:
+            raise RuntimeError(self.Nn.last_error())
+
+    def e2e_step(self):
+        self.s.upload_pinned(self.st, self.da, self.host_a)
+        self.s.upload_pinned(self.st, self.db, self.host_b)
+        self.step()
+        self.s.download_pinned(self.st, self.dc, self.host_c)
+
+    def h2d_bytes(self):
+        return self.a_bytes + self.b_bytes
+
+    def d2h_bytes(self):
+        return self.c_bytes
+
+    def config(self):
+        return {"workload": f"C3 bf16 GEMM M=N=K={self.M}, A row-major N(0,1), B column-major N(0,1/K), seed 2",
+                "M": self.M, "N": self.N, "K": self.K, "parallelism": f"N-shard{self.world}" if self.world > 1
+                else "single", "l2": "inputs 256 MiB > 126 MB L2"}
+
+    def cpu_sample(self, budget_s):
+        import oracle
+        threads = oracle.num_threads()
+        rng = np.random.default_rng(0)
+        pts = 0
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < budget_s:
+            rows = rng.integers(0, self.M, 2048)
+            cols = rng.integers(0, self.N, 2048)
+            oracle.gemm_bf16_points(self.a_bits, self.b_bits, True, self.M, self.N, self.K, rows, cols, threads)
+            pts += 2048
+        dt = time.perf_counter() - t0
+        return {"value": 2.0 * self.K * pts / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                "sample": f"{pts} random C elements (full {self.K}-long dot products, reference loop order) "
+                          f"in {dt:.1f} s on {threads} threads; rate extrapolated per element"}
+
+
+WORKLOADS = {"softmax": SoftmaxWorkload, "gemm": GemmWorkload}
+DEFAULT_OP = "gemm"
 
 
 # ----------------------------------------------------------------------------- driver
@@ -309,7 +399,32 @@ def _ref_softmax(tb, oracle, budget_s):
             "config": {"workload": "C2 row softmax fp32 [32768,4096], x~N(0,2^2) seed 1", "rows": rows, "cols": cols}}
 
 
-REFERENCE_SAMPLERS = {"softmax": _ref_softmax}
+def _ref_gemm(tb, oracle, budget_s):
+    from titan_rs_b200.kernel_abi import DType
+    M = N = K = GemmWorkload.M
+    rows_needed = 512
+    # The first 512 rows of A and of B's [N,K] storage: the sample draws only from those.
+    a = tb.fill_normal(rows_needed * K, seed=tensor_seed(2, 0), dtype=DType.BF16).reshape(rows_needed, K)
+    b = tb.fill_normal(rows_needed * K, seed=tensor_seed(2, 1), std=1.0 / math.sqrt(K),
+                       dtype=DType.BF16).reshape(rows_needed, K)
+    threads = oracle.num_threads()
+    rng = np.random.default_rng(0)
+    pts = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or pts == 0:
+        rows = rng.integers(0, rows_needed, 2048)
+        cols = rng.integers(0, rows_needed, 2048)
+        oracle.gemm_bf16_points(a, b, True, rows_needed, rows_needed, K, rows, cols, threads)
+        pts += 2048
+    dt = time.perf_counter() - t0
+    return {"value": 2.0 * K * pts / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
+            "sample": f"{pts} C elements of C3 ({K}-long dot products in the reference loop order) in {dt:.1f} s; "
+                      f"rate extrapolated per element",
+            "config": {"workload": f"C3 bf16 GEMM M=N=K={M}, A row-major N(0,1), B column-major N(0,1/K), seed 2",
+                       "M": M, "N": N, "K": K}}
+
+
+REFERENCE_SAMPLERS = {"softmax": _ref_softmax, "gemm": _ref_gemm}
 
 
 def main(argv=None) -> int:
@@ -339,36 +454,48 @@ def main(argv=None) -> int:
     wl = WORKLOADS[args.op](tb, session, stream, rank, world, small=args.small)
     peaks, peak_src = load_peaks()
 
+    w0 = session.record(stream)
     for _ in range(args.warmup):
         wl.step()
+    w1 = session.record(stream)
     session.synchronize(stream)
+    est_ms = max(session.elapsed_ms(w0, w1) / args.warmup, 1e-3)
 
-    # Device-timed steps: one event pair per step on the launching stream.
+    # nvidia-smi samples every 50 ms: keep the GPU busy with untimed steps for
+    # ~0.3 s first so the clock record covers the load the timed steps run under.
     clocks = ClockSampler(local)
+    clocks.start()
+    soak = int(reduce_max(dist, float(min(max(300.0 / est_ms, 1), 20000))))
+    for _ in range(soak):
+        wl.step()
+
+    # Device-timed region: K back-to-back steps between one event pair on the
+    # launching stream (the host enqueues faster than the kernels run), bracketed
+    # by a barrier and a synchronize on both sides; max over ranks.
     barrier(dist)
     session.synchronize(stream)
-    clocks.start()
     launches0 = int(N.lib().tb_launch_count())
-    evs = []
+    e0 = session.record(stream)
     for _ in range(args.steps):
-        e0 = session.record(stream)
         wl.step()
-        e1 = session.record(stream)
-        evs.append((e0, e1))
+    e1 = session.record(stream)
     session.synchronize(stream)
     launches = int(N.lib().tb_launch_count()) - launches0
     barrier(dist)
     clock_info = clocks.stop()
-    per_step = [session.elapsed_ms(a, b) for a, b in evs]
-    total_ms = reduce_max(dist, sum(per_step))
+    local_ms = session.elapsed_ms(e0, e1)
+    total_ms = reduce_max(dist, local_ms)
     ms_step = total_ms / args.steps
     units_step = wl.job_units_per_step()
     scale = 1e9 if wl.unit == "GB/s" else 1e12
     value = units_step / (ms_step / 1e3) / scale
 
-    # Roofline of the dominant kernel: algorithmic units of one launch / its average duration.
-    per_launch_ms = statistics.mean(per_step)
-    achieved = wl.units_per_step() / (per_launch_ms / 1e3) / scale
+    # Roofline of the dominant kernel: its algorithmic units per launch / its
+    # average launch duration, timed alone on the launching stream.
+    per_launch_ms = wl.dominant_kernel_ms(session, stream, args.steps) if hasattr(wl, "dominant_kernel_ms") \
+        else local_ms / args.steps
+    achieved = wl.units_per_launch() / (per_launch_ms / 1e3) / scale if hasattr(wl, "units_per_launch") \
+        else wl.units_per_step() / (per_launch_ms / 1e3) / scale
     if wl.bound == "hbm":
         peak = float(peaks.get("hbm_gbs", PEAK_FALLBACK["hbm_gbs"]))
         r_unit = "GB/s"

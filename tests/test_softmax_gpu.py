@@ -57,7 +57,14 @@ def test_softmax_matches_oracle_on_ragged_shapes(session, rt, shape):
     h = run_op(rt, "softmax", [upload(session, rt.stream, x)], DType.F32, shape)
     y = h.outputs[0].to_numpy()
     ref = oracle.softmax(x, axis=-1)
-    assert elementwise_rel_err(y, ref) <= REL_TOL
+    # The oracle sums exp() sequentially in f32 like the reference, so on long rows
+    # its own error grows ~sqrt(cols)*eps; the bound is 1e-5 plus that error,
+    # and the kernel must also be within 1e-5 of the float64 truth.
+    x64 = x.astype(np.float64)
+    e = np.exp(x64 - x64.max(axis=-1, keepdims=True))
+    truth = e / e.sum(axis=-1, keepdims=True)
+    assert elementwise_rel_err(y, truth) <= REL_TOL
+    assert elementwise_rel_err(y, ref) <= REL_TOL + elementwise_rel_err(ref, truth)
     # Size-independent property: every row sums to 1.
     assert np.all(np.abs(y.reshape(-1, shape[-1]).sum(axis=-1, dtype=np.float64) - 1.0) <= 1e-5)
 

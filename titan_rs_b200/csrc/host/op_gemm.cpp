@@ -1,0 +1,101 @@
+// "gemm" operator entry: the contract of execute_cuda_gemm and the CPU gemm
+// (titan-runtime/src/lib.rs:2289-2404, 955-989), then the kernel choice:
+//   BF16, A row-major, B column-major (transpose_rhs), K % 8 == 0, 16-byte
+//        aligned buffers        -> gemm_bf16_tn (tcgen05, TMA, TMEM)
+//   BF16, any other layout      -> gemm_bf16_generic (CUDA cores)
+//   F32                         -> gemm_f32_tiled (CUDA cores, bit-exact with the CPU reference)
+#include "../kernels/kernel_configs.h"
+#include "ops_common.hpp"
+
+namespace tb {
+
+tb_status launch_gemm_bf16_tn(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c, int M, int N,
+                              int K, long long ldc) {
+  CUtensorMap ta, tbm;
+  tb_status rc = tmap_bf16_2d(&ta, a, (uint64_t)M, (uint64_t)K, (uint64_t)K, TB_GEMM_BM, TB_GEMM_BK,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = tmap_bf16_2d(&tbm, b, (uint64_t)N, (uint64_t)K, (uint64_t)K, TB_GEMM_BN, TB_GEMM_BK,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  CUfunction fn = nullptr;
+  rc = builtin_function(s, "gemm_bf16", "gemm_bf16_tn", &fn);
+  if (rc) return rc;
+  const long long tiles = (long long)((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN);
+  const unsigned grid = (unsigned)(tiles < s->sm_count ? tiles : s->sm_count);
+  CUdeviceptr status = s->status.device;
+  void* params[] = {&ta, &tbm, &c, &M, &N, &K, &ldc, &status};
+  return launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_SMEM_BYTES, params, "gemm_bf16_tn");
+}
+
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" tb_status tb_op_gemm(tb_session* session, tb_stream* stream, const tb_tensor* lhs, const tb_tensor* rhs,
+                                const tb_tensor* output, const tb_attr* attrs, uint32_t num_attrs, tb_event** out) {
+  Session* s = reinterpret_cast<Session*>(session);
+  if (!s) return set_error(TB_ERR_INVALID, "contract", "null session");
+  if (!lhs || !rhs || !output) return contract("gemm requires exactly two rank-2 inputs and one output");
+  for (uint32_t i = 0; i < num_attrs; ++i)
+    if (!attrs[i].key || (strcmp(attrs[i].key, "transpose_lhs") != 0 && strcmp(attrs[i].key, "transpose_rhs") != 0))
+      return contract("CUDA GEMM received unsupported attributes");
+  bool tl = false, tr = false;
+  for (uint32_t i = 0; i < num_attrs; ++i) {
+    if (attrs[i].str || attrs[i].value < 0 || attrs[i].value > 1)
+      return contract(std::string(attrs[i].key) + " must be a bool");
+    if (strcmp(attrs[i].key, "transpose_lhs") == 0) tl = attrs[i].value != 0;
+    if (strcmp(attrs[i].key, "transpose_rhs") == 0) tr = attrs[i].value != 0;
+  }
+  const uint32_t dt = lhs->dtype;
+  if (!(dt == TB_F32 || dt == TB_BF16) || rhs->dtype != dt || output->dtype != dt)
+    return contract("CUDA GEMM requires F32 (or BF16) input and output tensors of one dtype");
+  if (lhs->rank != 2 || rhs->rank != 2) return contract("gemm requires exactly two rank-2 inputs");
+  if (!is_contiguous(lhs) || !is_contiguous(rhs)) return contract("CUDA GEMM requires contiguous rank-2 inputs");
+  if (output->rank != 2 || !is_contiguous(output)) return contract("CUDA GEMM requires a contiguous rank-2 output");
+  const uint64_t m = tl ? lhs->shape[1] : lhs->shape[0];
+  const uint64_t k = tl ? lhs->shape[0] : lhs->shape[1];
+  const uint64_t rk = tr ? rhs->shape[1] : rhs->shape[0];
+  const uint64_t n = tr ? rhs->shape[0] : rhs->shape[1];
+  if (k != rk) return contract("gemm inner dimensions must match");
+  if (output->shape[0] != m || output->shape[1] != n) return contract("gemm output shape mismatch");
+  if (m == 0 || n == 0 || k == 0) return contract("CUDA GEMM M, N, and K must be non-zero");
+  if (m > 0x7fffffffull || n > 0x7fffffffull || k > 0x7fffffffull) return contract("CUDA GEMM M exceeds u32 ABI");
+  Stream* st = nullptr;
+  tb_status rc = check_stream(s, stream, &st);
+  if (rc) return rc;
+  Buffer *ba = nullptr, *bb = nullptr, *bc = nullptr;
+  if ((rc = tensor_buffer(s, lhs, "gemm lhs", &ba)) || (rc = tensor_buffer(s, rhs, "gemm rhs", &bb)) ||
+      (rc = tensor_buffer(s, output, "gemm output", &bc)))
+    return rc;
+  rc = activate(s);
+  if (rc) return rc;
+  int M = (int)m, N = (int)n, K = (int)k;
+  // Strides of op(A) (m, k) and op(B) (k, n) in elements.
+  long long as0 = tl ? 1 : (long long)lhs->shape[1], as1 = tl ? (long long)lhs->shape[1] : 1;
+  long long bs0 = tr ? 1 : (long long)rhs->shape[1], bs1 = tr ? (long long)rhs->shape[1] : 1;
+  CUdeviceptr pa = ba->ptr, pb = bb->ptr, pc = bc->ptr;
+  CUfunction fn = nullptr;
+  if (dt == TB_BF16) {
+    const bool tma_ok = !tl && tr && (K % 8) == 0 && ((pa | pb | pc) & 15) == 0;
+    if (tma_ok) {
+      rc = launch_gemm_bf16_tn(s, st, pa, pb, pc, M, N, K, (long long)N);
+    } else {
+      rc = builtin_function(s, "compat", "gemm_bf16_generic", &fn);
+      if (rc) return rc;
+      void* params[] = {&pa, &pb, &pc, &M, &N, &K, &as0, &as1, &bs0, &bs1};
+      uint64_t total = (uint64_t)M * N;
+      uint64_t grid = (total + 255) / 256;
+      if (grid > (uint64_t)s->sm_count * 32) grid = (uint64_t)s->sm_count * 32;
+      rc = launch_builtin(s, st, fn, (unsigned)grid, 1, 1, 256, 0, params, "gemm_bf16_generic");
+    }
+  } else {
+    rc = builtin_function(s, "compat", "gemm_f32_tiled", &fn);
+    if (rc) return rc;
+    void* params[] = {&pa, &pb, &pc, &M, &N, &K, &as0, &as1, &bs0, &bs1};
+    rc = launch_builtin(s, st, fn, (unsigned)((N + 63) / 64), (unsigned)((M + 63) / 64), 1, 256, 0, params,
+                        "gemm_f32_tiled");
+  }
+  if (rc) return rc;
+  return record_event(s, st, nullptr, out);
+}

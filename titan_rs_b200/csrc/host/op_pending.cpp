@@ -5,11 +5,6 @@ using namespace tb;
 
 extern "C" {
 
-tb_status tb_op_gemm(tb_session*, tb_stream*, const tb_tensor*, const tb_tensor*, const tb_tensor*, const tb_attr*,
-                     uint32_t, tb_event**) {
-  return unsupported("CUDA GEMM does not implement this configuration yet");
-}
-
 tb_status tb_op_sdpa(tb_session*, tb_stream*, const tb_tensor*, const tb_tensor*, const tb_tensor*, const tb_tensor*,
                      const tb_attr*, uint32_t, tb_event**) {
   return unsupported("CUDA scaled dot-product attention does not implement this configuration yet");

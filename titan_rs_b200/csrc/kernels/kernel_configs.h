@@ -1,0 +1,11 @@
+// Launch constants shared by the sm_100a kernels and the host code that launches them.
+#pragma once
+
+// bf16 GEMM (gemm_bf16.cu): 128x256x64 tiles, 4 smem stages, 192 threads.
+#define TB_GEMM_BM 128
+#define TB_GEMM_BN 256
+#define TB_GEMM_BK 64
+#define TB_GEMM_STAGES 4
+#define TB_GEMM_THREADS 192
+#define TB_GEMM_BARRIER_BYTES 128
+#define TB_GEMM_SMEM_BYTES (TB_GEMM_STAGES * (TB_GEMM_BM + TB_GEMM_BN) * TB_GEMM_BK * 2 + 1024 + TB_GEMM_BARRIER_BYTES)
