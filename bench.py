@@ -317,7 +317,103 @@ class GemmWorkload(Workload):
                           f"in {dt:.1f} s on {threads} threads; rate extrapolated per element"}
 
 
-WORKLOADS = {"softmax": SoftmaxWorkload, "gemm": GemmWorkload}
+class SdpaWorkload(Workload):
+    name = "sdpa"
+    metric = "causal SDPA fwd bf16 B8 H32 S4096 D128 TFLOP/s per B200 (causal-halved FLOPs)"
+    unit = "TFLOP/s"
+    dtype = "bf16"
+    scaling = "strong"
+    bound = "tensor"
+    B, H, S, D = 8, 32, 4096, 128
+
+    def __init__(self, *a, **k):
+        super().__init__(*a, **k)
+        import ctypes
+        from titan_rs_b200 import _native as N
+        from titan_rs_b200.kernel_abi import DType
+        self.Nn, self.ctypes = N, ctypes
+        if self.small:
+            self.B = 2
+        total_bh = self.B * self.H
+        if total_bh % self.world:
+            raise SystemExit(f"B*H={total_bh} does not split over {self.world} GPUs")
+        self.bh_local = total_bh // self.world  # batch*heads shard of this rank: no communication
+        S, D = self.S, self.D
+        n = self.bh_local * S * D
+        self.nbytes = n * 2
+        self.hosts = [self.s.host_alloc(self.nbytes) for _ in range(3)]
+        self.host_o = self.s.host_alloc(self.nbytes)
+        self.bits = []
+        for i, host in enumerate(self.hosts):
+            arr = host.array(np.uint16, (self.bh_local, S, D))
+            full_offset = self.rank * n  # this rank's slice of the seeded tensor (counter-based generator)
+            arr[:] = self.tb.fill_normal(full_offset + n, seed=tensor_seed(3, i),
+                                         dtype=DType.BF16)[full_offset:].reshape(self.bh_local, S, D)
+            self.bits.append(arr)
+        self.dev = [self.s.allocate(self.nbytes) for _ in range(3)]
+        self.do = self.s.allocate(self.nbytes)
+        for h, d in zip(self.hosts, self.dev):
+            self.s.upload_pinned(self.st, d, h)
+        self.s.synchronize(self.st)
+        shape = (1, self.bh_local, S, D)
+        self.tq, self.tk, self.tv = (_tensor(self.tb, d, DType.BF16, shape) for d in self.dev)
+        self.to = _tensor(self.tb, self.do, DType.BF16, shape)
+        self.attrs = (N.Attr * 1)()
+        self._key = b"causal"
+        self.attrs[0].key = self._key
+        self.attrs[0].value = 1
+        self.kernel = "sdpa_fwd_bf16_d128"
+
+    def units_per_step(self):
+        return 4.0 * self.bh_local * self.S * self.S * self.D / 2.0
+
+    def step(self):
+        c = self.ctypes
+        rc = self.Nn.lib().tb_op_sdpa(self.s.ptr, self.st.ptr, c.byref(self.tq), c.byref(self.tk), c.byref(self.tv),
+                                      c.byref(self.to), self.attrs, 1, None)
+        if rc:
+            raise RuntimeError(self.Nn.last_error())
+
+    def e2e_step(self):
+        for h, d in zip(self.hosts, self.dev):
+            self.s.upload_pinned(self.st, d, h)
+        self.step()
+        self.s.download_pinned(self.st, self.do, self.host_o)
+
+    def h2d_bytes(self):
+        return 3 * self.nbytes
+
+    def d2h_bytes(self):
+        return self.nbytes
+
+    def config(self):
+        return {"workload": f"C4 causal SDPA fwd bf16 B{self.B} H{self.H} S{self.S} D{self.D}, N(0,1) seed 3, "
+                            "scale 1/sqrt(128), FLOPs = 4*B*H*S^2*D/2",
+                "B": self.B, "H": self.H, "S": self.S, "D": self.D,
+                "parallelism": f"bh-shard{self.world}" if self.world > 1 else "single",
+                "l2": "inputs 768 MiB > 126 MB L2"}
+
+    def cpu_sample(self, budget_s):
+        import oracle
+        threads = oracle.num_threads()
+        S, D = self.S, self.D
+        rng = np.random.default_rng(0)
+        macs = 0.0
+        rows_done = 0
+        t0 = time.perf_counter()
+        q, k, v = (b.reshape(-1) for b in self.bits)
+        while time.perf_counter() - t0 < budget_s:
+            ids = np.sort(rng.integers(0, self.bh_local * S, 256))
+            oracle.sdpa_bf16_rows(q, k, v, 1, self.bh_local, S, S, D, True, ids, threads=threads)
+            macs += float(np.sum((ids % S) + 1)) * 2 * D  # QK^T and PV per visible key
+            rows_done += ids.size
+        dt = time.perf_counter() - t0
+        return {"value": 2.0 * macs / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                "sample": f"{rows_done} random causal query rows (reference loop order) in {dt:.1f} s on "
+                          f"{threads} threads; FLOP/s of the rows computed"}
+
+
+WORKLOADS = {"softmax": SoftmaxWorkload, "gemm": GemmWorkload, "sdpa": SdpaWorkload}
 DEFAULT_OP = "gemm"
 
 
@@ -424,7 +520,29 @@ def _ref_gemm(tb, oracle, budget_s):
                        "M": M, "N": N, "K": K}}
 
 
-REFERENCE_SAMPLERS = {"softmax": _ref_softmax, "gemm": _ref_gemm}
+def _ref_sdpa(tb, oracle, budget_s):
+    from titan_rs_b200.kernel_abi import DType
+    B, H, S, D = SdpaWorkload.B, SdpaWorkload.H, SdpaWorkload.S, SdpaWorkload.D
+    heads = 2  # the first two (b, h) pairs of C4
+    n = heads * S * D
+    q, k, v = (tb.fill_normal(n, seed=tensor_seed(3, i), dtype=DType.BF16) for i in range(3))
+    threads = oracle.num_threads()
+    rng = np.random.default_rng(0)
+    macs, rows_done = 0.0, 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or rows_done == 0:
+        ids = np.sort(rng.integers(0, heads * S, 256))
+        oracle.sdpa_bf16_rows(q, k, v, 1, heads, S, S, D, True, ids, threads=threads)
+        macs += float(np.sum((ids % S) + 1)) * 2 * D
+        rows_done += ids.size
+    dt = time.perf_counter() - t0
+    return {"value": 2.0 * macs / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
+            "sample": f"{rows_done} causal query rows of the first 2 heads of C4 in {dt:.1f} s",
+            "config": {"workload": f"C4 causal SDPA fwd bf16 B{B} H{H} S{S} D{D}, N(0,1) seed 3", "B": B, "H": H,
+                       "S": S, "D": D}}
+
+
+REFERENCE_SAMPLERS = {"softmax": _ref_softmax, "gemm": _ref_gemm, "sdpa": _ref_sdpa}
 
 
 def main(argv=None) -> int:

@@ -1,0 +1,150 @@
+"""Scaled-dot-product attention on the B200 against the CPU oracle
+(restated projects/titan-runtime/src/lib.rs:1090-1151, plus the causal extension).
+
+Tolerances: f32 (reference ABI) uses the reference GPU test's 2e-4
+(projects/titan-runtime/tests/cuda_attention.rs:88-91); bf16 uses the north-star
+bound max|err| <= 1e-2 * max|ref| against the f32 oracle on the same bf16 inputs.
+"""
+import json
+import pathlib
+
+import numpy as np
+import pytest
+
+import oracle
+import titan_rs_b200 as tb
+from titan_rs_b200.kernel_abi import DType
+
+from gpu_util import max_rel_err, run_op, upload
+
+pytestmark = pytest.mark.gpu
+
+KATS = json.loads((pathlib.Path(__file__).parent / "golden" / "reference_kats.json").read_text())
+BF16_TOL = 1e-2
+
+
+@pytest.fixture(scope="module")
+def session():
+    s = tb.Session(0)
+    yield s
+    s.close()
+
+
+@pytest.fixture(scope="module")
+def rt(session):
+    return tb.Runtime(session)
+
+
+def qkv_bf16(b, h, tq, tk, d, seed):
+    q = tb.fill_normal(b * h * tq * d, seed=seed * 16, dtype=DType.BF16).reshape(b, h, tq, d)
+    k = tb.fill_normal(b * h * tk * d, seed=seed * 16 + 1, dtype=DType.BF16).reshape(b, h, tk, d)
+    v = tb.fill_normal(b * h * tk * d, seed=seed * 16 + 2, dtype=DType.BF16).reshape(b, h, tk, d)
+    return q, k, v
+
+
+def run_sdpa(session, rt, q, k, v, causal, dtype=DType.BF16):
+    attrs = {"causal": True} if causal else {}
+    ins = [upload(session, rt.stream, t, dtype) for t in (q, k, v)]
+    return run_op(rt, "scaled_dot_product_attention", ins, dtype, q.shape, attrs)
+
+
+@pytest.mark.parametrize("case", [c for c in KATS["cases"] if c["op"] == "sdpa_f32"], ids=lambda c: c["name"])
+def test_sdpa_f32_reference_kats(session, rt, case):
+    q = np.array(case["q"], np.float32).reshape(case["q_shape"])
+    k = np.array(case["k"], np.float32).reshape(case["kv_shape"])
+    v = np.array(case["v"], np.float32).reshape(case["kv_shape"])
+    h = run_sdpa(session, rt, q, k, v, False, DType.F32)
+    assert np.max(np.abs(h.outputs[0].to_numpy().ravel() - np.array(case["expected"]))) <= 2e-4
+
+
+def test_sdpa_f32_matches_oracle(session, rt):
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((2, 3, 17, 40)).astype(np.float32)
+    k = rng.standard_normal((2, 3, 29, 40)).astype(np.float32)
+    v = rng.standard_normal((2, 3, 29, 40)).astype(np.float32)
+    h = run_sdpa(session, rt, q, k, v, False, DType.F32)
+    assert np.max(np.abs(h.outputs[0].to_numpy() - oracle.sdpa(q, k, v))) <= 2e-4
+
+
+def test_sdpa_f32_rejects_mask_and_causal_like_the_reference(session, rt):
+    """projects/titan-runtime/tests/cuda_attention.rs:93-99."""
+    q = upload(session, rt.stream, np.ones((1, 1, 2, 2), np.float32))
+    kv = upload(session, rt.stream, np.ones((1, 1, 3, 2), np.float32))
+    for attr in ("mask", "causal"):
+        with pytest.raises(tb.ExecutionError) as e:
+            rt.execute(tb.OpRequest("scaled_dot_product_attention", [q, kv, kv],
+                                    [tb.TensorSpec(DType.F32, (1, 1, 2, 2))], {attr: True}))
+        assert e.value.phase == "contract" and "does not implement" in e.value.message
+
+
+@pytest.mark.parametrize("b,h,tq,tk,causal", [(1, 1, 128, 128, False), (1, 1, 128, 128, True), (1, 2, 256, 256, True),
+                                              (2, 1, 384, 384, True), (1, 1, 200, 200, True), (1, 2, 130, 130, False),
+                                              (1, 1, 256, 384, False), (1, 1, 256, 384, True),
+                                              (1, 1, 384, 256, True), (2, 2, 1024, 1024, True)])
+def test_sdpa_bf16_tcgen05_matches_oracle(session, rt, b, h, tq, tk, causal):
+    d = 128
+    q, k, v = qkv_bf16(b, h, tq, tk, d, seed=b * 1000 + h * 100 + tq + tk + causal)
+    res = run_sdpa(session, rt, q, k, v, causal)
+    assert res.candidate == "sdpa_fwd_bf16_d128"
+    got = res.outputs[0].to_f32()
+    ids = np.arange(b * h * tq)
+    ref = oracle.sdpa_bf16_rows(q, k, v, b, h, tq, tk, d, causal, ids).reshape(b, h, tq, d)
+    assert np.isfinite(got).all()
+    assert max_rel_err(got, ref) <= BF16_TOL, max_rel_err(got, ref)
+
+
+def test_sdpa_bf16_generic_head_dim(session, rt):
+    b, h, t, d = 1, 2, 100, 64
+    q, k, v = qkv_bf16(b, h, t, t, d, seed=77)
+    res = run_sdpa(session, rt, q, k, v, True)
+    assert res.candidate == "sdpa_bf16_generic"
+    ref = oracle.sdpa_bf16_rows(q, k, v, b, h, t, t, d, True, np.arange(b * h * t)).reshape(b, h, t, d)
+    assert max_rel_err(res.outputs[0].to_f32(), ref) <= BF16_TOL
+
+
+def test_sdpa_bf16_full_c4_config(session, rt):
+    """C4: causal B8 H32 S4096 D128, seed 3. Sampled full rows against the oracle, and
+    the size-independent property that causal row 0 of every head equals V[..., 0, :]."""
+    b, h, s, d = 8, 32, 4096, 128
+    q, k, v = qkv_bf16(b, h, s, s, d, seed=3)
+    res = run_sdpa(session, rt, q, k, v, True)
+    got = res.outputs[0].to_numpy()
+    rng = np.random.default_rng(3)
+    bh = rng.integers(0, b * h, 48)
+    rows = rng.integers(0, s, 48)
+    rows[:8] = [0, 1, 127, 128, 129, 2047, 4094, 4095]
+    ids = np.sort(bh * s + rows)
+    ref = oracle.sdpa_bf16_rows(q, k, v, b, h, s, s, d, True, ids)
+    got_rows = tb.bf16_bits_to_f32(got.reshape(-1, d)[ids]).reshape(-1, d)
+    assert max_rel_err(got_rows, ref) <= BF16_TOL, max_rel_err(got_rows, ref)
+    np.testing.assert_array_equal(got[:, :, 0, :], v[:, :, 0, :])
+    assert np.isfinite(tb.bf16_bits_to_f32(got)).all()
+
+
+def test_sdpa_bf16_is_bit_reproducible(session, rt):
+    q, k, v = qkv_bf16(1, 4, 512, 512, 128, seed=8)
+    a = run_sdpa(session, rt, q, k, v, True).outputs[0].to_numpy()
+    b = run_sdpa(session, rt, q, k, v, True).outputs[0].to_numpy()
+    np.testing.assert_array_equal(a, b)
+
+
+def test_sdpa_contract_rejections(session, rt):
+    """projects/titan-runtime/tests/cpu_reference_ops.rs:231-310 keywords."""
+    q = upload(session, rt.stream, np.ones((1, 1, 2, 2), np.float32))
+    k = upload(session, rt.stream, np.ones((1, 1, 3, 2), np.float32))
+    v = upload(session, rt.stream, np.ones((1, 1, 3, 2), np.float32))
+    v2 = upload(session, rt.stream, np.ones((1, 1, 2, 2), np.float32))
+    r3 = upload(session, rt.stream, np.ones((1, 2, 2), np.float32))
+
+    def err(inputs, shape, dtype=DType.F32, layout="Contiguous"):
+        with pytest.raises(tb.ExecutionError) as e:
+            rt.execute(tb.OpRequest("scaled_dot_product_attention", inputs,
+                                    [tb.TensorSpec(dtype, shape, layout=layout)]))
+        return e.value.message
+
+    assert "exactly three" in err([q, k], (1, 1, 2, 2))
+    assert "rank-4" in err([r3, k, v], (1, 1, 2, 2))
+    assert "K/V sequence" in err([q, k, v2], (1, 1, 2, 2))
+    assert "output shape" in err([q, k, v], (1, 1, 3, 2))
+    assert "F32" in err([q, k, v], (1, 1, 2, 2), dtype=DType.I32)
+    assert "contiguous" in err([q, k, v], (1, 1, 2, 2), layout="Strided")

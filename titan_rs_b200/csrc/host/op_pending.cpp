@@ -5,11 +5,6 @@ using namespace tb;
 
 extern "C" {
 
-tb_status tb_op_sdpa(tb_session*, tb_stream*, const tb_tensor*, const tb_tensor*, const tb_tensor*, const tb_tensor*,
-                     const tb_attr*, uint32_t, tb_event**) {
-  return unsupported("CUDA scaled dot-product attention does not implement this configuration yet");
-}
-
 tb_status tb_op_conv2d(tb_session*, tb_stream*, const tb_tensor*, const tb_tensor*, const tb_tensor*,
                        const tb_tensor*, const tb_attr*, uint32_t, tb_event**) {
   return unsupported("CUDA Conv2D does not implement this configuration yet");

@@ -1,0 +1,124 @@
+// "scaled_dot_product_attention" operator entry: the contract of
+// execute_cuda_attention and the CPU reference (titan-runtime/src/lib.rs:2575-2705,
+// 1090-1151), then the kernel choice:
+//   BF16, D == 128, 16-byte aligned  -> sdpa_fwd_bf16_d128 (tcgen05, TMA, TMEM); causal optional
+//   BF16, other head dims            -> sdpa_bf16_generic (CUDA cores)
+//   F32                              -> scaled_dot_product_attention_f32 (reference ABI kernel);
+//                                       mask/causal rejected as the reference does
+#include <cmath>
+
+#include "../kernels/kernel_configs.h"
+#include "ops_common.hpp"
+
+namespace tb {
+
+tb_status tmap_bhtd(CUtensorMap* map, CUdeviceptr base, uint64_t bh, uint64_t t, uint64_t d) {
+  cuuint64_t dims[3] = {d, t, bh};
+  cuuint64_t strides[2] = {d * 2, t * d * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t elem[3] = {1, 1, 1};
+  TB_CU("cuTensorMapEncodeTiled",
+        driver()->cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, reinterpret_cast<void*>(base), dims,
+                                         strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE));
+  return TB_OK;
+}
+
+tb_status launch_sdpa_bf16_d128(Session* s, Stream* st, CUdeviceptr q, CUdeviceptr k, CUdeviceptr v, CUdeviceptr o,
+                                int bh, int tq, int tk, int causal) {
+  CUtensorMap mq, mk, mv;
+  tb_status rc;
+  if ((rc = tmap_bhtd(&mq, q, bh, tq, TB_SDPA_HD)) || (rc = tmap_bhtd(&mk, k, bh, tk, TB_SDPA_HD)) ||
+      (rc = tmap_bhtd(&mv, v, bh, tk, TB_SDPA_HD)))
+    return rc;
+  CUfunction fn = nullptr;
+  rc = builtin_function(s, "sdpa_bf16", "sdpa_fwd_bf16_d128", &fn);
+  if (rc) return rc;
+  float scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)TB_SDPA_HD));
+  CUdeviceptr status = s->status.device;
+  void* params[] = {&mq, &mk, &mv, &o, &tq, &tk, &causal, &scale_log2, &status};
+  const unsigned qtiles = (unsigned)((tq + TB_SDPA_BM - 1) / TB_SDPA_BM);
+  return launch_builtin(s, st, fn, (unsigned)bh, qtiles, 1, TB_SDPA_THREADS, TB_SDPA_SMEM_BYTES, params,
+                        "sdpa_fwd_bf16_d128");
+}
+
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" tb_status tb_op_sdpa(tb_session* session, tb_stream* stream, const tb_tensor* q, const tb_tensor* k,
+                                const tb_tensor* v, const tb_tensor* output, const tb_attr* attrs, uint32_t num_attrs,
+                                tb_event** out) {
+  Session* s = reinterpret_cast<Session*>(session);
+  if (!s) return set_error(TB_ERR_INVALID, "contract", "null session");
+  if (!q || !k || !v || !output)
+    return contract("scaled dot-product attention requires exactly three rank-4 BHTD inputs");
+  const uint32_t dt = q->dtype;
+  bool causal = false;
+  if (dt == TB_F32) {
+    if (num_attrs)
+      return unsupported("CUDA scaled dot-product attention does not implement mask, causal, or other attributes");
+  } else {
+    for (uint32_t i = 0; i < num_attrs; ++i) {
+      if (attrs[i].key && strcmp(attrs[i].key, "causal") == 0 && !attrs[i].str && attrs[i].value >= 0 &&
+          attrs[i].value <= 1) {
+        causal = attrs[i].value != 0;
+        continue;
+      }
+      return unsupported("CUDA scaled dot-product attention does not implement mask or attributes other than causal");
+    }
+  }
+  if (!(dt == TB_F32 || dt == TB_BF16) || k->dtype != dt || v->dtype != dt || output->dtype != dt)
+    return contract("CUDA scaled dot-product attention requires F32 (or BF16) Q, K, V, and output of one dtype");
+  if (q->rank != 4 || k->rank != 4 || v->rank != 4)
+    return contract("scaled dot-product attention requires exactly three rank-4 BHTD inputs");
+  if (!is_contiguous(q) || !is_contiguous(k) || !is_contiguous(v))
+    return contract("CUDA scaled dot-product attention requires contiguous rank-4 BHTD Q, K, and V");
+  if (output->rank != 4 || !is_contiguous(output))
+    return contract("CUDA scaled dot-product attention requires a contiguous rank-4 output");
+  const uint64_t B = q->shape[0], H = q->shape[1], Tq = q->shape[2], D = q->shape[3];
+  const uint64_t Tk = k->shape[2];
+  if (k->shape[0] != B || v->shape[0] != B || k->shape[1] != H || v->shape[1] != H || k->shape[3] != D ||
+      v->shape[3] != D || v->shape[2] != Tk)
+    return contract("scaled dot-product attention B, H, D, and K/V sequence dimensions must match");
+  if (Tq == 0 || Tk == 0 || D == 0)
+    return contract("scaled dot-product attention requires non-zero Tq, Tk, and D dimensions");
+  if (B == 0 || H == 0) return contract("CUDA attention B, H, Tq, Tk, and D must be non-zero");
+  if (output->shape[0] != B || output->shape[1] != H || output->shape[2] != Tq || output->shape[3] != D)
+    return contract("scaled dot-product attention output shape mismatch");
+  if (B * H > 0x7fffffffull || Tq > 0x7fffffffull || Tk > 0x7fffffffull)
+    return contract("CUDA attention shape exceeds u32 ABI");
+  if (D > 256) return unsupported("CUDA scaled dot-product attention does not implement head dimensions above 256");
+  Stream* st = nullptr;
+  tb_status rc = check_stream(s, stream, &st);
+  if (rc) return rc;
+  Buffer *bq = nullptr, *bk = nullptr, *bv = nullptr, *bo = nullptr;
+  if ((rc = tensor_buffer(s, q, "attention Q", &bq)) || (rc = tensor_buffer(s, k, "attention K", &bk)) ||
+      (rc = tensor_buffer(s, v, "attention V", &bv)) || (rc = tensor_buffer(s, output, "attention output", &bo)))
+    return rc;
+  rc = activate(s);
+  if (rc) return rc;
+  CUdeviceptr pq = bq->ptr, pk = bk->ptr, pv = bv->ptr, po = bo->ptr;
+  int b = (int)B, h = (int)H, tq = (int)Tq, tk = (int)Tk, d = (int)D, c = causal ? 1 : 0;
+  if (dt == TB_BF16 && D == TB_SDPA_HD && ((pq | pk | pv | po) & 15) == 0) {
+    rc = launch_sdpa_bf16_d128(s, st, pq, pk, pv, po, b * h, tq, tk, c);
+  } else {
+    const bool bf = dt == TB_BF16;
+    CUfunction fn = nullptr;
+    rc = builtin_function(s, "compat", bf ? "sdpa_bf16_generic" : "scaled_dot_product_attention_f32", &fn);
+    if (rc) return rc;
+    uint64_t rows = B * H * Tq;
+    uint64_t grid = (rows + 7) / 8;
+    if (grid > (uint64_t)s->sm_count * 64) grid = (uint64_t)s->sm_count * 64;
+    if (bf) {
+      void* params[] = {&pq, &pk, &pv, &po, &b, &h, &tq, &tk, &d, &c};
+      rc = launch_builtin(s, st, fn, (unsigned)grid, 1, 1, 256, 0, params, "sdpa_bf16_generic");
+    } else {
+      void* params[] = {&pq, &pk, &pv, &po, &b, &h, &tq, &tk, &d};
+      rc = launch_builtin(s, st, fn, (unsigned)grid, 1, 1, 256, 0, params, "scaled_dot_product_attention_f32");
+    }
+  }
+  if (rc) return rc;
+  return record_event(s, st, nullptr, out);
+}

@@ -182,3 +182,58 @@ extern "C" __global__ void scaled_dot_product_attention_f32(const float* __restr
     }
   }
 }
+
+// bf16 attention for shapes the tensor-core kernel does not take (D != 128,
+// unaligned buffers): one warp per query row, online softmax in fp32, D <= 256.
+// causal != 0 masks keys j > i (top-left aligned).
+extern "C" __global__ void sdpa_bf16_generic(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                                             const __nv_bfloat16* __restrict__ v, __nv_bfloat16* __restrict__ o,
+                                             int B, int H, int Tq, int Tk, int D, int causal) {
+  const int lane = threadIdx.x & 31;
+  const long long rows = (long long)B * H * Tq;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const float scale = 1.0f / sqrtf((float)D);
+  for (long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += warps) {
+    const long long bh = row / Tq;
+    const int i = (int)(row % Tq);
+    const int visible = causal ? min(Tk, i + 1) : Tk;
+    const __nv_bfloat16* qr = q + row * D;
+    const __nv_bfloat16* kb = k + bh * (long long)Tk * D;
+    const __nv_bfloat16* vb = v + bh * (long long)Tk * D;
+    float qv[8], acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d = lane + 32 * j;
+      qv[j] = d < D ? __bfloat162float(qr[d]) : 0.f;
+      acc[j] = 0.f;
+    }
+    float m = -INFINITY, l = 0.f;
+    for (int t = 0; t < visible; ++t) {
+      float part = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int d = lane + 32 * j;
+        if (d < D) part = fmaf(qv[j], __bfloat162float(kb[(long long)t * D + d]), part);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+      const float s = part * scale;
+      const float mn = fmaxf(m, s);
+      const float corr = expf(m - mn);
+      const float p = expf(s - mn);
+      l = l * corr + p;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int d = lane + 32 * j;
+        if (d < D) acc[j] = fmaf(p, __bfloat162float(vb[(long long)t * D + d]), acc[j] * corr);
+      }
+      m = mn;
+    }
+    const float inv = 1.0f / l;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d = lane + 32 * j;
+      if (d < D) o[row * D + d] = __float2bfloat16_rn(acc[j] * inv);
+    }
+  }
+}

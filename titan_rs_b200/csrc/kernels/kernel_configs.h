@@ -9,3 +9,12 @@
 #define TB_GEMM_THREADS 192
 #define TB_GEMM_BARRIER_BYTES 128
 #define TB_GEMM_SMEM_BYTES (TB_GEMM_STAGES * (TB_GEMM_BM + TB_GEMM_BN) * TB_GEMM_BK * 2 + 1024 + TB_GEMM_BARRIER_BYTES)
+
+// Causal SDPA forward (sdpa_bf16.cu): 128-row query tiles, 128-key tiles, head dim 128.
+// Shared memory: Q 32 KB + K ring 2x32 KB + V ring 2x32 KB + P 2x32 KB + barriers.
+#define TB_SDPA_BM 128
+#define TB_SDPA_BN 128
+#define TB_SDPA_HD 128
+#define TB_SDPA_THREADS 192
+#define TB_SDPA_BARRIER_BYTES 256
+#define TB_SDPA_SMEM_BYTES (7 * 32768 + TB_SDPA_BARRIER_BYTES + 1024)
