@@ -413,7 +413,119 @@ class SdpaWorkload(Workload):
                           f"{threads} threads; FLOP/s of the rows computed"}
 
 
-WORKLOADS = {"softmax": SoftmaxWorkload, "gemm": GemmWorkload, "sdpa": SdpaWorkload}
+class ConvWorkload(Workload):
+    name = "conv2d"
+    metric = "conv2d fwd bf16 NHWC 64x56x56x256->256 3x3 s1 p1 (implicit GEMM) TFLOP/s per B200"
+    unit = "TFLOP/s"
+    dtype = "bf16"
+    scaling = "strong"
+    bound = "tensor"
+    N, H, W, C, K, R, S = 64, 56, 56, 256, 256, 3, 3
+    ROTATE = 3  # input/output pairs cycled so each step reads an input evicted from L2
+
+    def __init__(self, *a, **k):
+        super().__init__(*a, **k)
+        import ctypes
+        from titan_rs_b200 import _native as N
+        from titan_rs_b200.kernel_abi import DType
+        self.Nn, self.ctypes = N, ctypes
+        if self.small:
+            self.N = 16
+        if self.N % self.world:
+            raise SystemExit(f"batch {self.N} does not split over {self.world} GPUs")
+        self.n_local = self.N // self.world  # batch shard of this rank: no communication
+        H, W, C, K = self.H, self.W, self.C, self.K
+        nx = self.n_local * H * W * C
+        self.x_bytes = nx * 2
+        self.w_bytes = K * self.R * self.S * C * 2
+        self.y_bytes = self.n_local * H * W * K * 2
+        self.host_x = self.s.host_alloc(self.x_bytes)
+        self.host_w = self.s.host_alloc(self.w_bytes)
+        self.host_y = self.s.host_alloc(self.y_bytes)
+        off = self.rank * nx
+        self.x_bits = self.host_x.array(np.uint16, (self.n_local, H, W, C))
+        self.x_bits[:] = self.tb.fill_normal(off + nx, seed=tensor_seed(4, 0), dtype=DType.BF16)[off:].reshape(
+            self.x_bits.shape)
+        self.w_bits = self.host_w.array(np.uint16, (K, self.R, self.S, C))
+        self.w_bits[:] = self.tb.fill_normal(K * self.R * self.S * C, seed=tensor_seed(4, 1),
+                                             std=math.sqrt(2.0 / (self.R * self.S * C)),
+                                             dtype=DType.BF16).reshape(self.w_bits.shape)
+        self.dx = [self.s.allocate(self.x_bytes) for _ in range(self.ROTATE)]
+        self.dy = [self.s.allocate(self.y_bytes) for _ in range(self.ROTATE)]
+        self.dw = self.s.allocate(self.w_bytes)
+        for d in self.dx:
+            self.s.upload_pinned(self.st, d, self.host_x)
+        self.s.upload_pinned(self.st, self.dw, self.host_w)
+        self.s.synchronize(self.st)
+        self.tx = [_tensor(self.tb, d, DType.BF16, (self.n_local, H, W, C)) for d in self.dx]
+        self.ty = [_tensor(self.tb, d, DType.BF16, (self.n_local, H, W, K)) for d in self.dy]
+        self.tw = _tensor(self.tb, self.dw, DType.BF16, (K, self.R, self.S, C))
+        names = ["stride_h", "stride_w", "pad_h", "pad_w", "dilation_h", "dilation_w", "groups", "layout"]
+        vals = [1, 1, 1, 1, 1, 1, 1, None]
+        self._keys = [n.encode() for n in names]
+        self._nhwc = b"NHWC"
+        self.attrs = (N.Attr * len(names))()
+        for i, (key, v) in enumerate(zip(self._keys, vals)):
+            self.attrs[i].key = key
+            if v is None:
+                self.attrs[i].str = self._nhwc
+            else:
+                self.attrs[i].value = v
+        self.i = 0
+        self.kernel = "conv2d_fprop_bf16_nhwc"
+
+    def units_per_step(self):
+        return 2.0 * self.n_local * self.H * self.W * self.K * self.C * self.R * self.S
+
+    def step(self):
+        c = self.ctypes
+        j = self.i % self.ROTATE
+        self.i += 1
+        rc = self.Nn.lib().tb_op_conv2d(self.s.ptr, self.st.ptr, c.byref(self.tx[j]), c.byref(self.tw), None,
+                                        c.byref(self.ty[j]), self.attrs, len(self._keys), None)
+        if rc:
+            raise RuntimeError(self.Nn.last_error())
+
+    def e2e_step(self):
+        self.s.upload_pinned(self.st, self.dx[0], self.host_x)
+        self.s.upload_pinned(self.st, self.dw, self.host_w)
+        self.i = 0
+        self.step()
+        self.s.download_pinned(self.st, self.dy[0], self.host_y)
+
+    def h2d_bytes(self):
+        return self.x_bytes + self.w_bytes
+
+    def d2h_bytes(self):
+        return self.y_bytes
+
+    def config(self):
+        return {"workload": f"C5 conv2d fwd bf16 NHWC N{self.N} {self.H}x{self.W} Cin{self.C} Cout{self.K} 3x3 s1 p1, "
+                            "x N(0,1), w N(0,2/2304), seed 4",
+                "N": self.N, "H": self.H, "W": self.W, "Cin": self.C, "Cout": self.K, "R": self.R, "S": self.S,
+                "parallelism": f"batch-shard{self.world}" if self.world > 1 else "single",
+                "l2": f"{self.ROTATE} rotating input/output pairs (588 MB working set > 126 MB L2)"}
+
+    def cpu_sample(self, budget_s):
+        import oracle
+        threads = oracle.num_threads()
+        rng = np.random.default_rng(0)
+        pts = 0
+        t0 = time.perf_counter()
+        total = self.n_local * self.H * self.W * self.K
+        while time.perf_counter() - t0 < budget_s:
+            idx = rng.integers(0, total, 2048)
+            oracle.conv2d_nhwc_bf16_points(self.x_bits, self.w_bits, None, self.n_local, self.H, self.W, self.C,
+                                           self.K, self.R, self.S, (1, 1), (1, 1), (1, 1), self.H, self.W, idx,
+                                           threads)
+            pts += 2048
+        dt = time.perf_counter() - t0
+        return {"value": 2.0 * self.C * self.R * self.S * pts / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
+                "kind": "port", "sample": f"{pts} random output elements (reference loop order) in {dt:.1f} s on "
+                                          f"{threads} threads; rate extrapolated per element (border taps counted)"}
+
+
+WORKLOADS = {"softmax": SoftmaxWorkload, "gemm": GemmWorkload, "sdpa": SdpaWorkload, "conv2d": ConvWorkload}
 DEFAULT_OP = "gemm"
 
 
@@ -542,7 +654,30 @@ def _ref_sdpa(tb, oracle, budget_s):
                        "S": S, "D": D}}
 
 
-REFERENCE_SAMPLERS = {"softmax": _ref_softmax, "gemm": _ref_gemm, "sdpa": _ref_sdpa}
+def _ref_conv2d(tb, oracle, budget_s):
+    from titan_rs_b200.kernel_abi import DType
+    wl = ConvWorkload
+    imgs = 2  # the first two images of C5
+    x = tb.fill_normal(imgs * wl.H * wl.W * wl.C, seed=tensor_seed(4, 0), dtype=DType.BF16)
+    w = tb.fill_normal(wl.K * wl.R * wl.S * wl.C, seed=tensor_seed(4, 1), std=math.sqrt(2.0 / (wl.R * wl.S * wl.C)),
+                       dtype=DType.BF16)
+    threads = oracle.num_threads()
+    rng = np.random.default_rng(0)
+    pts = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or pts == 0:
+        idx = rng.integers(0, imgs * wl.H * wl.W * wl.K, 2048)
+        oracle.conv2d_nhwc_bf16_points(x, w, None, imgs, wl.H, wl.W, wl.C, wl.K, wl.R, wl.S, (1, 1), (1, 1), (1, 1),
+                                       wl.H, wl.W, idx, threads)
+        pts += 2048
+    dt = time.perf_counter() - t0
+    return {"value": 2.0 * wl.C * wl.R * wl.S * pts / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
+            "sample": f"{pts} output elements of the first 2 images of C5 in {dt:.1f} s",
+            "config": {"workload": f"C5 conv2d fwd bf16 NHWC N{wl.N} {wl.H}x{wl.W} Cin{wl.C} Cout{wl.K} 3x3 s1 p1",
+                       "N": wl.N, "H": wl.H, "W": wl.W, "Cin": wl.C, "Cout": wl.K}}
+
+
+REFERENCE_SAMPLERS = {"softmax": _ref_softmax, "gemm": _ref_gemm, "sdpa": _ref_sdpa, "conv2d": _ref_conv2d}
 
 
 def main(argv=None) -> int:

@@ -5,11 +5,6 @@ using namespace tb;
 
 extern "C" {
 
-tb_status tb_op_conv2d(tb_session*, tb_stream*, const tb_tensor*, const tb_tensor*, const tb_tensor*,
-                       const tb_tensor*, const tb_attr*, uint32_t, tb_event**) {
-  return unsupported("CUDA Conv2D does not implement this configuration yet");
-}
-
 tb_status tb_comm_unique_id(uint8_t*) { return unsupported("collective not built"); }
 tb_status tb_comm_init(tb_session*, const uint8_t*, int, int, uint32_t, tb_comm**) {
   return unsupported("collective not built");

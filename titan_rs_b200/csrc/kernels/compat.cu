@@ -183,6 +183,42 @@ extern "C" __global__ void scaled_dot_product_attention_f32(const float* __restr
   }
 }
 
+// bf16 NHWC conv for shapes the implicit-GEMM kernel does not take (groups,
+// channel counts that are not multiples of 8, strides above 1): one thread per
+// output element, fp32 accumulation, optional fp32 bias. x [N,H,W,C],
+// w [Cout,R,S,C/groups], y [N,Ho,Wo,Cout].
+extern "C" __global__ void conv2d_bf16_nhwc_generic(const __nv_bfloat16* __restrict__ x,
+                                                    const __nv_bfloat16* __restrict__ w,
+                                                    const float* __restrict__ bias, __nv_bfloat16* __restrict__ y,
+                                                    int batch, int h, int wd, int cin, int cout, int kh, int kw,
+                                                    int ho, int wo, int sh, int sw, int ph, int pw, int dh, int dw,
+                                                    int groups) {
+  const long long total = (long long)batch * ho * wo * cout;
+  const int cpg = cin / groups, opg = cout / groups;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int oc = (int)(i % cout);
+    const long long pix = i / cout;
+    const int ow = (int)(pix % wo);
+    const int oh = (int)((pix / wo) % ho);
+    const int n = (int)(pix / ((long long)wo * ho));
+    const int g = oc / opg;
+    float sum = bias ? bias[oc] : 0.f;
+    for (int r = 0; r < kh; ++r) {
+      const int ih = oh * sh + r * dh - ph;
+      if (ih < 0 || ih >= h) continue;
+      for (int s = 0; s < kw; ++s) {
+        const int iw = ow * sw + s * dw - pw;
+        if (iw < 0 || iw >= wd) continue;
+        const __nv_bfloat16* xp = x + (((long long)n * h + ih) * wd + iw) * cin + g * cpg;
+        const __nv_bfloat16* wp = w + (((long long)oc * kh + r) * kw + s) * cpg;
+        for (int c = 0; c < cpg; ++c) sum = fmaf(__bfloat162float(xp[c]), __bfloat162float(wp[c]), sum);
+      }
+    }
+    y[i] = __float2bfloat16_rn(sum);
+  }
+}
+
 // bf16 attention for shapes the tensor-core kernel does not take (D != 128,
 // unaligned buffers): one warp per query row, online softmax in fp32, D <= 256.
 // causal != 0 masks keys j > i (top-left aligned).
