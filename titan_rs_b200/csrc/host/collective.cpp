@@ -1,0 +1,341 @@
+// Collective over NVLink/NVSwitch: the titan.rs `Collective` trait's all_gather
+// (projects/titan-distributed/src/lib.rs:95-99, LocalRing :129-134) on device
+// buffers through NCCL, plus the N-sharded GEMM that uses it.
+//
+// NCCL is opened with dlopen like the CUDA driver, so the library still loads
+// where NCCL is absent. Communicators are non-blocking (ncclConfig_t.blocking = 0).
+// A watchdog thread per communicator watches the event recorded after each
+// collective: if it has not completed `timeout_ms` after it was enqueued, or
+// NCCL reports an asynchronous error, the watchdog aborts the communicator, so
+// the stuck collective kernel returns and later calls fail with TB_ERR_NCCL
+// instead of hanging on a peer that died.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <condition_variable>
+#include <thread>
+
+#include "../kernels/kernel_configs.h"
+#include "ops_common.hpp"
+
+namespace tb {
+
+tb_status launch_gemm_bf16_tn(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c, int M, int N,
+                              int K, long long ldc);
+
+namespace {
+
+struct NcclApi {
+  decltype(&::ncclGetUniqueId) GetUniqueId = nullptr;
+  decltype(&::ncclCommInitRankConfig) CommInitRankConfig = nullptr;
+  decltype(&::ncclCommDestroy) CommDestroy = nullptr;
+  decltype(&::ncclCommAbort) CommAbort = nullptr;
+  decltype(&::ncclCommGetAsyncError) CommGetAsyncError = nullptr;
+  decltype(&::ncclAllGather) AllGather = nullptr;
+  decltype(&::ncclAllReduce) AllReduce = nullptr;
+  decltype(&::ncclGetErrorString) GetErrorString = nullptr;
+  bool ok = false;
+  std::string error;
+};
+
+NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      api.error = dlerror() ? dlerror() : "libnccl.so.2 not found";
+      return;
+    }
+#define TB_NCCL(field, sym)                                               \
+  api.field = reinterpret_cast<decltype(api.field)>(dlsym(h, #sym));      \
+  if (!api.field) {                                                       \
+    api.error = "missing NCCL symbol " #sym;                              \
+    return;                                                               \
+  }
+    TB_NCCL(GetUniqueId, ncclGetUniqueId)
+    TB_NCCL(CommInitRankConfig, ncclCommInitRankConfig)
+    TB_NCCL(CommDestroy, ncclCommDestroy)
+    TB_NCCL(CommAbort, ncclCommAbort)
+    TB_NCCL(CommGetAsyncError, ncclCommGetAsyncError)
+    TB_NCCL(AllGather, ncclAllGather)
+    TB_NCCL(AllReduce, ncclAllReduce)
+    TB_NCCL(GetErrorString, ncclGetErrorString)
+#undef TB_NCCL
+    api.ok = true;
+  });
+  return api;
+}
+
+tb_status nccl_error(const char* op, ncclResult_t r) {
+  NcclApi& n = nccl();
+  return set_error(TB_ERR_NCCL, op, std::string("NCCL status ") + std::to_string((int)r) + " (" +
+                                        (n.GetErrorString ? n.GetErrorString(r) : "?") + ")");
+}
+
+}  // namespace
+
+struct Comm {
+  Session* session = nullptr;
+  ncclComm_t comm = nullptr;
+  int rank = 0, size = 0;
+  uint32_t timeout_ms = 0;
+  CUdeviceptr barrier_word = 0;
+  // Watchdog state.
+  std::mutex mu;
+  std::condition_variable cv;
+  std::thread watchdog;
+  bool stop = false;
+  bool aborted = false;
+  std::string abort_reason;
+  std::vector<std::pair<CUevent, std::chrono::steady_clock::time_point>> pending;
+};
+
+namespace {
+
+// Waits for a non-blocking NCCL call to leave ncclInProgress (bounded by the comm timeout).
+tb_status settle(Comm* c, const char* op) {
+  NcclApi& n = nccl();
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(c->timeout_ms);
+  while (true) {
+    ncclResult_t st = ncclSuccess;
+    ncclResult_t r = n.CommGetAsyncError(c->comm, &st);
+    if (r != ncclSuccess) return nccl_error(op, r);
+    if (st == ncclSuccess) return TB_OK;
+    if (st != ncclInProgress) return nccl_error(op, st);
+    if (std::chrono::steady_clock::now() > deadline) {
+      n.CommAbort(c->comm);
+      c->comm = nullptr;
+      return set_error(TB_ERR_NCCL, op, "NCCL operation did not complete before the communicator timeout; aborted");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+void watchdog_loop(Comm* c) {
+  const DriverApi* d = driver();
+  NcclApi& n = nccl();
+  std::unique_lock<std::mutex> lock(c->mu);
+  while (!c->stop) {
+    c->cv.wait_for(lock, std::chrono::milliseconds(10));
+    if (c->stop || c->aborted || !c->comm) continue;
+    d->cuCtxSetCurrent(c->session->context);
+    // Drop completed collectives; abort when the oldest one is overdue.
+    while (!c->pending.empty() && d->cuEventQuery(c->pending.front().first) == CUDA_SUCCESS) {
+      d->cuEventDestroy_v2(c->pending.front().first);
+      c->pending.erase(c->pending.begin());
+    }
+    ncclResult_t async = ncclSuccess;
+    n.CommGetAsyncError(c->comm, &async);
+    const bool overdue = !c->pending.empty() &&
+                         std::chrono::steady_clock::now() - c->pending.front().second >
+                             std::chrono::milliseconds(c->timeout_ms);
+    if ((async != ncclSuccess && async != ncclInProgress) || overdue) {
+      c->abort_reason = overdue ? "a collective made no progress within the communicator timeout (peer lost?)"
+                                : std::string("NCCL asynchronous error ") + std::to_string((int)async);
+      n.CommAbort(c->comm);
+      c->comm = nullptr;
+      c->aborted = true;
+    }
+  }
+}
+
+tb_status track(Comm* c, Stream* st) {
+  const DriverApi* d = driver();
+  CUevent ev = nullptr;
+  TB_CU("cuEventCreate", d->cuEventCreate(&ev, CU_EVENT_DISABLE_TIMING));
+  TB_CU("cuEventRecord", d->cuEventRecord(ev, st->raw));
+  std::lock_guard<std::mutex> lock(c->mu);
+  c->pending.emplace_back(ev, std::chrono::steady_clock::now());
+  return TB_OK;
+}
+
+tb_status usable(Comm* c, const char* op) {
+  if (!c) return set_error(TB_ERR_INVALID, op, "null communicator");
+  std::lock_guard<std::mutex> lock(c->mu);
+  if (c->aborted || !c->comm)
+    return set_error(TB_ERR_NCCL, op, "communicator was aborted: " + c->abort_reason);
+  return TB_OK;
+}
+
+}  // namespace
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" {
+
+tb_status tb_comm_unique_id(uint8_t id[TB_COMM_ID_BYTES]) {
+  NcclApi& n = nccl();
+  if (!n.ok) return set_error(TB_ERR_NCCL, "load_nccl", n.error);
+  static_assert(sizeof(ncclUniqueId) == TB_COMM_ID_BYTES, "ncclUniqueId size");
+  ncclUniqueId uid;
+  ncclResult_t r = n.GetUniqueId(&uid);
+  if (r != ncclSuccess) return nccl_error("ncclGetUniqueId", r);
+  memcpy(id, &uid, TB_COMM_ID_BYTES);
+  return TB_OK;
+}
+
+tb_status tb_comm_init(tb_session* session, const uint8_t id[TB_COMM_ID_BYTES], int nranks, int rank,
+                       uint32_t timeout_ms, tb_comm** out) {
+  Session* s = reinterpret_cast<Session*>(session);
+  if (!s || !id || !out) return set_error(TB_ERR_INVALID, "comm_init", "null argument");
+  if (nranks < 1 || rank < 0 || rank >= nranks) return set_error(TB_ERR_INVALID, "comm_init", "bad rank or size");
+  NcclApi& n = nccl();
+  if (!n.ok) return set_error(TB_ERR_NCCL, "load_nccl", n.error);
+  tb_status rc = activate(s);
+  if (rc) return rc;
+  Comm* c = new Comm();
+  c->session = s;
+  c->rank = rank;
+  c->size = nranks;
+  c->timeout_ms = timeout_ms ? timeout_ms : 60000;
+  ncclUniqueId uid;
+  memcpy(&uid, id, TB_COMM_ID_BYTES);
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  ncclResult_t r = n.CommInitRankConfig(&c->comm, nranks, uid, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    delete c;
+    return nccl_error("ncclCommInitRankConfig", r);
+  }
+  rc = settle(c, "ncclCommInitRankConfig");
+  if (rc) {
+    if (c->comm) n.CommAbort(c->comm);
+    delete c;
+    return rc;
+  }
+  CUresult cr = driver()->cuMemAlloc_v2(&c->barrier_word, 64);
+  if (cr != CUDA_SUCCESS) {
+    n.CommAbort(c->comm);
+    delete c;
+    return cu_error("allocate", cr);
+  }
+  s->refs.fetch_add(1);
+  c->watchdog = std::thread(watchdog_loop, c);
+  *out = reinterpret_cast<tb_comm*>(c);
+  return TB_OK;
+}
+
+void tb_comm_release(tb_comm* comm) {
+  Comm* c = reinterpret_cast<Comm*>(comm);
+  if (!c) return;
+  {
+    std::lock_guard<std::mutex> lock(c->mu);
+    c->stop = true;
+  }
+  c->cv.notify_all();
+  if (c->watchdog.joinable()) c->watchdog.join();
+  const DriverApi* d = driver();
+  NcclApi& n = nccl();
+  if (d) d->cuCtxSetCurrent(c->session->context);
+  for (auto& p : c->pending) {
+    if (d) {
+      // Bounded: the watchdog is gone, so abort rather than wait on a collective that never finishes.
+      if (d->cuEventQuery(p.first) != CUDA_SUCCESS && c->comm) {
+        n.CommAbort(c->comm);
+        c->comm = nullptr;
+      }
+      d->cuEventDestroy_v2(p.first);
+    }
+  }
+  if (c->comm) n.CommDestroy(c->comm);
+  if (d && c->barrier_word) d->cuMemFree_v2(c->barrier_word);
+  Session* s = c->session;
+  delete c;
+  tb_session_release(reinterpret_cast<tb_session*>(s));
+}
+
+int tb_comm_rank(const tb_comm* comm) { return comm ? reinterpret_cast<const Comm*>(comm)->rank : -1; }
+int tb_comm_size(const tb_comm* comm) { return comm ? reinterpret_cast<const Comm*>(comm)->size : 0; }
+
+tb_status tb_comm_all_gather(tb_comm* comm, tb_stream* stream, tb_buffer* send, tb_buffer* recv,
+                             size_t bytes_per_rank, tb_event** out) {
+  Comm* c = reinterpret_cast<Comm*>(comm);
+  tb_status rc = usable(c, "all_gather");
+  if (rc) return rc;
+  Session* s = c->session;
+  Stream* st = nullptr;
+  Buffer *bs = nullptr, *br = nullptr;
+  if ((rc = check_stream(s, stream, &st)) || (rc = check_buffer(s, send, &bs)) || (rc = check_buffer(s, recv, &br)))
+    return rc;
+  if (bytes_per_rank > bs->bytes || bytes_per_rank * (size_t)c->size > br->bytes)
+    return set_error(TB_ERR_INVALID, "all_gather", "transfer exceeds allocation");
+  rc = activate(s);
+  if (rc) return rc;
+  ncclResult_t r = nccl().AllGather(reinterpret_cast<const void*>(bs->ptr), reinterpret_cast<void*>(br->ptr),
+                                    bytes_per_rank, ncclUint8, c->comm, st->raw);
+  if (r != ncclSuccess && r != ncclInProgress) return nccl_error("ncclAllGather", r);
+  if ((rc = settle(c, "ncclAllGather")) || (rc = track(c, st))) return rc;
+  return record_event(s, st, nullptr, out);
+}
+
+tb_status tb_comm_barrier(tb_comm* comm, tb_stream* stream) {
+  Comm* c = reinterpret_cast<Comm*>(comm);
+  tb_status rc = usable(c, "barrier");
+  if (rc) return rc;
+  Stream* st = nullptr;
+  if ((rc = check_stream(c->session, stream, &st))) return rc;
+  rc = activate(c->session);
+  if (rc) return rc;
+  void* p = reinterpret_cast<void*>(c->barrier_word);
+  ncclResult_t r = nccl().AllReduce(p, p, 1, ncclInt32, ncclSum, c->comm, st->raw);
+  if (r != ncclSuccess && r != ncclInProgress) return nccl_error("ncclAllReduce", r);
+  if ((rc = settle(c, "ncclAllReduce"))) return rc;
+  return track(c, st);
+}
+
+tb_status tb_op_gemm_sharded(tb_comm* comm, tb_stream* stream, const tb_tensor* lhs, const tb_tensor* rhs_shard,
+                             const tb_tensor* output, tb_buffer* workspace, tb_event** out) {
+  Comm* c = reinterpret_cast<Comm*>(comm);
+  tb_status rc = usable(c, "contract");
+  if (rc) return rc;
+  Session* s = c->session;
+  if (!lhs || !rhs_shard || !output) return contract("sharded GEMM requires A, a B shard and an output");
+  if (lhs->dtype != TB_BF16 || rhs_shard->dtype != TB_BF16 || output->dtype != TB_BF16)
+    return contract("sharded GEMM requires BF16 A, B shard and C");
+  if (lhs->rank != 2 || rhs_shard->rank != 2 || output->rank != 2 || !is_contiguous(lhs) ||
+      !is_contiguous(rhs_shard) || !is_contiguous(output))
+    return contract("sharded GEMM requires contiguous rank-2 tensors");
+  const uint64_t M = lhs->shape[0], K = lhs->shape[1], Np = rhs_shard->shape[0], p = (uint64_t)c->size;
+  if (rhs_shard->shape[1] != K) return contract("gemm inner dimensions must match");
+  if (output->shape[0] != M || output->shape[1] != Np * p) return contract("gemm output shape mismatch");
+  if (K % 8 != 0 || Np % 8 != 0) return unsupported("sharded GEMM needs K and N/p to be multiples of 8");
+  Stream* st = nullptr;
+  Buffer *ba = nullptr, *bb = nullptr, *bc = nullptr, *bw = nullptr;
+  if ((rc = check_stream(s, stream, &st)) || (rc = tensor_buffer(s, lhs, "gemm lhs", &ba)) ||
+      (rc = tensor_buffer(s, rhs_shard, "gemm rhs", &bb)) || (rc = tensor_buffer(s, output, "gemm output", &bc)) ||
+      (rc = check_buffer(s, workspace, &bw)))
+    return rc;
+  const size_t shard_bytes = M * Np * 2;
+  if (bw->bytes < shard_bytes * p) return contract("sharded GEMM workspace holds fewer than p*M*(N/p) elements");
+  rc = activate(s);
+  if (rc) return rc;
+  // 1. This rank's columns straight into its slot of the gather layout [p][M][N/p].
+  const CUdeviceptr slot = bw->ptr + (CUdeviceptr)c->rank * shard_bytes;
+  rc = launch_gemm_bf16_tn(s, st, ba->ptr, bb->ptr, slot, (int)M, (int)Np, (int)K, (long long)Np);
+  if (rc) return rc;
+  // 2. In-place all-gather of the shards over NVLink.
+  if (p > 1) {
+    ncclResult_t r = nccl().AllGather(reinterpret_cast<const void*>(slot), reinterpret_cast<void*>(bw->ptr),
+                                      shard_bytes, ncclUint8, c->comm, st->raw);
+    if (r != ncclSuccess && r != ncclInProgress) return nccl_error("ncclAllGather", r);
+    if ((rc = settle(c, "ncclAllGather")) || (rc = track(c, st))) return rc;
+  }
+  // 3. Column blocks -> row-major C[M, N].
+  CUfunction fn = nullptr;
+  rc = builtin_function(s, "layout", "gather_column_blocks_bf16", &fn);
+  if (rc) return rc;
+  CUdeviceptr src = bw->ptr, dst = bc->ptr;
+  int m = (int)M, np = (int)Np, parts = (int)p;
+  void* params[] = {&src, &dst, &m, &np, &parts};
+  const uint64_t vecs = M * Np * p / 8;
+  uint64_t grid = (vecs + 255) / 256;
+  if (grid > (uint64_t)s->sm_count * 16) grid = (uint64_t)s->sm_count * 16;
+  rc = launch_builtin(s, st, fn, (unsigned)grid, 1, 1, 256, 0, params, "gather_column_blocks_bf16");
+  if (rc) return rc;
+  return record_event(s, st, nullptr, out);
+}
+
+}  // extern "C"
