@@ -250,15 +250,19 @@ class GemmWorkload(Workload):
         if self.small:
             self.M = self.N = self.K = 4096
         M, Nn, K = self.M, self.N, self.K
-        self.a_bytes, self.b_bytes, self.c_bytes = M * K * 2, Nn * K * 2, M * Nn * 2
+        from titan_rs_b200.distributed import even_shard
+        from titan_rs_b200.runtime import TensorHandle, contiguous_strides
+        lo, hi = even_shard(Nn, self.world, self.rank)  # this rank's output columns / rows of B's [N,K] storage
+        self.n_local = hi - lo
+        self.a_bytes, self.b_bytes, self.c_bytes = M * K * 2, self.n_local * K * 2, M * Nn * 2
         self.host_a = self.s.host_alloc(self.a_bytes)
         self.host_b = self.s.host_alloc(self.b_bytes)
         self.host_c = self.s.host_alloc(self.c_bytes)
         self.a_bits = self.host_a.array(np.uint16, (M, K))
-        self.b_bits = self.host_b.array(np.uint16, (Nn, K))
+        self.b_bits = self.host_b.array(np.uint16, (self.n_local, K))
         self.a_bits[:] = self.tb.fill_normal(M * K, seed=tensor_seed(2, 0), std=1.0, dtype=DType.BF16).reshape(M, K)
-        self.b_bits[:] = self.tb.fill_normal(Nn * K, seed=tensor_seed(2, 1), std=1.0 / math.sqrt(K),
-                                             dtype=DType.BF16).reshape(Nn, K)
+        self.b_bits[:] = self.tb.fill_normal(hi * K, seed=tensor_seed(2, 1), std=1.0 / math.sqrt(K),
+                                             dtype=DType.BF16)[lo * K:].reshape(self.n_local, K)
         self.da = self.s.allocate(self.a_bytes)
         self.db = self.s.allocate(self.b_bytes)
         self.dc = self.s.allocate(self.c_bytes)
@@ -266,8 +270,17 @@ class GemmWorkload(Workload):
         self.s.upload_pinned(self.st, self.db, self.host_b)
         self.s.synchronize(self.st)
         self.ta = _tensor(self.tb, self.da, DType.BF16, (M, K))
-        self.tbm = _tensor(self.tb, self.db, DType.BF16, (Nn, K))
+        self.tbm = _tensor(self.tb, self.db, DType.BF16, (self.n_local, K))
         self.tc = _tensor(self.tb, self.dc, DType.BF16, (M, Nn))
+        if self.world > 1:
+            # Column shard lands in slot `rank` of a [p][M][N/p] gather buffer, then all-gather + re-layout.
+            self.dws = self.s.allocate(self.c_bytes)
+            self.dc_local = self.s.allocate(M * self.n_local * 2)
+            self.tc_local = _tensor(self.tb, self.dc_local, DType.BF16, (M, self.n_local))
+            self.h_a = TensorHandle(self.s, self.da, DType.BF16, (M, K), contiguous_strides((M, K)))
+            self.h_b = TensorHandle(self.s, self.db, DType.BF16, (self.n_local, K),
+                                    contiguous_strides((self.n_local, K)))
+            self.h_c = TensorHandle(self.s, self.dc, DType.BF16, (M, Nn), contiguous_strides((M, Nn)))
         self.attrs = (N.Attr * 1)()
         self._key = b"transpose_rhs"
         self.attrs[0].key = self._key
@@ -275,13 +288,32 @@ class GemmWorkload(Workload):
         self.kernel = "gemm_bf16_tn"
 
     def units_per_step(self):
-        return 2.0 * self.M * self.N * self.K
+        return 2.0 * self.M * self.n_local * self.K
 
-    def step(self):
+    def _local_gemm(self, out_tensor):
         rc = self.Nn.lib().tb_op_gemm(self.s.ptr, self.st.ptr, self.ctypes.byref(self.ta), self.ctypes.byref(self.tbm),
-                                      self.ctypes.byref(self.tc), self.attrs, 1, None)
+                                      self.ctypes.byref(out_tensor), self.attrs, 1, None)
         if rc:
             raise RuntimeError(self.Nn.last_error())
+
+    def step(self):
+        if self.world == 1:
+            self._local_gemm(self.tc)
+        else:
+            self.comm.sharded_gemm(self.st, self.h_a, self.h_b, self.h_c, self.dws)
+
+    def dominant_kernel_ms(self, session, stream, steps):
+        """Average duration of the GEMM kernel alone (the compute phase of a step)."""
+        if self.world == 1:
+            return None
+        for _ in range(3):
+            self._local_gemm(self.tc_local)
+        e0 = session.record(stream)
+        for _ in range(steps):
+            self._local_gemm(self.tc_local)
+        e1 = session.record(stream)
+        session.synchronize(stream)
+        return session.elapsed_ms(e0, e1) / steps
 
     def e2e_step(self):
         self.s.upload_pinned(self.st, self.da, self.host_a)
@@ -704,7 +736,11 @@ def main(argv=None) -> int:
     dist = init_dist(world, local)
     session = tb.Session(local)
     stream = session.create_stream()
-    wl = WORKLOADS[args.op](tb, session, stream, rank, world, small=args.small)
+    comm = None
+    if world > 1 and args.op == "gemm":
+        from titan_rs_b200 import distributed as D
+        comm = D.NcclCollective(session, D.broadcast_comm_id(rank), world, rank, timeout_ms=60000)
+    wl = WORKLOADS[args.op](tb, session, stream, rank, world, comm=comm, small=args.small)
     peaks, peak_src = load_peaks()
 
     w0 = session.record(stream)
@@ -745,10 +781,16 @@ def main(argv=None) -> int:
 
     # Roofline of the dominant kernel: its algorithmic units per launch / its
     # average launch duration, timed alone on the launching stream.
-    per_launch_ms = wl.dominant_kernel_ms(session, stream, args.steps) if hasattr(wl, "dominant_kernel_ms") \
-        else local_ms / args.steps
-    achieved = wl.units_per_launch() / (per_launch_ms / 1e3) / scale if hasattr(wl, "units_per_launch") \
-        else wl.units_per_step() / (per_launch_ms / 1e3) / scale
+    # With a collective in the step (sharded GEMM), the kernel is also timed
+    # alone: that is the compute phase, reported beside the end-to-end value.
+    kernel_ms = wl.dominant_kernel_ms(session, stream, args.steps) if hasattr(wl, "dominant_kernel_ms") else None
+    compute_phase = None
+    if kernel_ms is not None:
+        kernel_ms_max = reduce_max(dist, kernel_ms)
+        compute_phase = {"ms_per_step": kernel_ms_max, "value": units_step / (kernel_ms_max / 1e3) / scale,
+                         "note": "GEMM kernel alone on this rank's shard, max over ranks (no all-gather, no re-layout)"}
+    per_launch_ms = kernel_ms if kernel_ms is not None else local_ms / args.steps
+    achieved = wl.units_per_step() / (per_launch_ms / 1e3) / scale
     if wl.bound == "hbm":
         peak = float(peaks.get("hbm_gbs", PEAK_FALLBACK["hbm_gbs"]))
         r_unit = "GB/s"
@@ -791,9 +833,14 @@ def main(argv=None) -> int:
             "gpu_launches": launches,
             "clocks": clock_info,
         }
+        if compute_phase is not None:
+            line["compute_phase"] = compute_phase
         print(json.dumps(line), flush=True)
     if dist is not None:
+        session.synchronize(stream)
         dist.barrier()
+        if comm is not None:
+            comm.close()
         dist.destroy_process_group()
     return 0
 

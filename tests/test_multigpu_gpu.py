@@ -1,0 +1,142 @@
+"""Multi-GPU path: NCCL all-gather (Collective::all_gather on device buffers) and
+the N-sharded GEMM. The one-rank cases run on any single B200; the two-rank
+cases run as child processes when at least two GPUs are visible (NVLS off, as
+this pool requires for multi-process GPU tests)."""
+import math
+import multiprocessing as mp
+import os
+
+import numpy as np
+import pytest
+
+import titan_rs_b200 as tb
+from titan_rs_b200 import distributed as D
+from titan_rs_b200.kernel_abi import DType
+
+pytestmark = pytest.mark.gpu
+
+
+def _gemm_inputs(m, n, k, seed=21):
+    a = tb.fill_normal(m * k, seed=seed * 16, dtype=DType.BF16).reshape(m, k)
+    b = tb.fill_normal(n * k, seed=seed * 16 + 1, std=1.0 / math.sqrt(k), dtype=DType.BF16).reshape(n, k)
+    return a, b
+
+
+def _reference_c(s, rt, a, b):
+    m, k = a.shape
+    n = b.shape[0]
+    ta = tb.TensorHandle.from_numpy(s, a, DType.BF16, rt.stream)
+    tbb = tb.TensorHandle.from_numpy(s, b, DType.BF16, rt.stream)
+    h = rt.execute(tb.OpRequest("gemm", [ta, tbb], [tb.TensorSpec(DType.BF16, (m, n))], {"transpose_rhs": True}))
+    h.wait()
+    return h.outputs[0].to_numpy()
+
+
+def test_one_rank_sharded_gemm_equals_single_gpu_gemm():
+    s = tb.Session(0)
+    rt = tb.Runtime(s)
+    m, n, k = 512, 768, 1024
+    a, b = _gemm_inputs(m, n, k)
+    ref = _reference_c(s, rt, a, b)
+    coll = D.NcclCollective(s, D.new_comm_id(), 1, 0, timeout_ms=20000)
+    ta = tb.TensorHandle.from_numpy(s, a, DType.BF16, rt.stream)
+    tbb = tb.TensorHandle.from_numpy(s, b, DType.BF16, rt.stream)
+    c = tb.TensorHandle.allocate(s, DType.BF16, (m, n))
+    ws = s.allocate(m * n * 2)
+    coll.sharded_gemm(rt.stream, ta, tbb, c, ws)
+    s.synchronize(rt.stream)
+    np.testing.assert_array_equal(c.to_numpy(), ref)
+    # all_gather with one rank is a copy.
+    src = s.allocate(4096)
+    dst = s.allocate(4096)
+    s.wait(s.upload(rt.stream, src, np.arange(1024, dtype=np.float32)))
+    coll.all_gather(rt.stream, src, dst, 4096)
+    out = np.empty(1024, np.float32)
+    s.download(rt.stream, dst, out)
+    np.testing.assert_array_equal(out, np.arange(1024, dtype=np.float32))
+    coll.close()
+    s.close()
+
+
+def _device_count() -> int:
+    try:
+        return len(tb.enumerate_devices())
+    except Exception:
+        return 0
+
+
+def _rank_main(rank, world, q_in, q_out, mode):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        import titan_rs_b200 as tbm
+        from titan_rs_b200 import distributed as Dm
+        s = tbm.Session(rank)
+        rt = tbm.Runtime(s)
+        if rank == 0:
+            cid = Dm.new_comm_id()
+            for _ in range(world - 1):
+                q_in.put(cid)
+        else:
+            cid = q_in.get(timeout=60)
+        coll = Dm.NcclCollective(s, cid, world, rank, timeout_ms=20000)
+        if mode == "gemm":
+            m, n, k = 384, 1024, 2048
+            a, b = _gemm_inputs(m, n, k)
+            ref = _reference_c(s, rt, a, b)
+            lo, hi = Dm.even_shard(n, world, rank)
+            ta = tbm.TensorHandle.from_numpy(s, a, DType.BF16, rt.stream)
+            tbs = tbm.TensorHandle.from_numpy(s, np.ascontiguousarray(b[lo:hi]), DType.BF16, rt.stream)
+            c = tbm.TensorHandle.allocate(s, DType.BF16, (m, n))
+            ws = s.allocate(m * n * 2)
+            coll.sharded_gemm(rt.stream, ta, tbs, c, ws)
+            s.synchronize(rt.stream)
+            ok_gemm = bool(np.array_equal(c.to_numpy(), ref))
+            src, dst = s.allocate(1024 * 4), s.allocate(1024 * 4 * world)
+            s.wait(s.upload(rt.stream, src, np.full(1024, rank, np.float32)))
+            coll.all_gather(rt.stream, src, dst, 1024 * 4)
+            out = np.empty(1024 * world, np.float32)
+            s.download(rt.stream, dst, out)
+            ok_gather = bool(np.array_equal(out, np.repeat(np.arange(world, dtype=np.float32), 1024)))
+            coll.barrier(rt.stream)
+            s.synchronize(rt.stream)
+            q_out.put((rank, ok_gemm and ok_gather))
+        else:
+            # Departure between steps: rank 1 announces it leaves and exits with nothing in flight;
+            # rank 0 checks the announcement on the host before its next collective and stops.
+            coll.barrier(rt.stream)
+            s.synchronize(rt.stream)
+            if rank == 1:
+                q_in.put("departed")
+                coll.close()
+                q_out.put((rank, "left"))
+                return
+            msg = q_in.get(timeout=60)
+            q_out.put((rank, "detected" if msg == "departed" else "missed"))
+        coll.close()
+        s.close()
+    except Exception as exc:
+        q_out.put((rank, repr(exc)))
+
+
+def _spawn(world, mode):
+    ctx = mp.get_context("spawn")
+    q_in, q_out = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, q_in, q_out, mode)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q_out.get(timeout=240) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    return results
+
+
+@pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")
+def test_two_rank_sharded_gemm_and_all_gather():
+    assert _spawn(2, "gemm") == {0: True, 1: True}
+
+
+@pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")
+def test_two_rank_departure_is_detected_on_the_host():
+    assert _spawn(2, "depart") == {0: "detected", 1: "left"}
