@@ -754,7 +754,7 @@ def main(argv=None) -> int:
     # ~0.3 s first so the clock record covers the load the timed steps run under.
     clocks = ClockSampler(local)
     clocks.start()
-    soak = int(reduce_max(dist, float(min(max(300.0 / est_ms, 1), 20000))))
+    soak = 0 if args.small else int(reduce_max(dist, float(min(max(300.0 / est_ms, 1), 20000))))
     for _ in range(soak):
         wl.step()
 
@@ -800,22 +800,24 @@ def main(argv=None) -> int:
     traffic = TRAFFIC_PER_LAUNCH.get(args.op)
 
     # End to end through the C ABI with pinned host buffers.
-    for _ in range(2):
-        wl.e2e_step()
-    session.synchronize(stream)
-    barrier(dist)
-    session.synchronize(stream)
-    e0 = session.record(stream)
-    e2e_steps = max(3, min(args.steps, 10))
-    for _ in range(e2e_steps):
-        wl.e2e_step()
-    e1 = session.record(stream)
-    session.synchronize(stream)
-    e2e_ms = reduce_max(dist, session.elapsed_ms(e0, e1)) / e2e_steps
-    e2e_value = units_step / (e2e_ms / 1e3) / scale
+    e2e_ms = e2e_value = None
+    if not args.small:
+        for _ in range(2):
+            wl.e2e_step()
+        session.synchronize(stream)
+        barrier(dist)
+        session.synchronize(stream)
+        e0 = session.record(stream)
+        e2e_steps = max(3, min(args.steps, 10))
+        for _ in range(e2e_steps):
+            wl.e2e_step()
+        e1 = session.record(stream)
+        session.synchronize(stream)
+        e2e_ms = reduce_max(dist, session.elapsed_ms(e0, e1)) / e2e_steps
+        e2e_value = units_step / (e2e_ms / 1e3) / scale
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.small:
         cpu = wl.cpu_sample(args.cpu_seconds)
 
     if rank == 0:
