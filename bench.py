@@ -394,7 +394,7 @@ class SdpaWorkload(Workload):
         self._key = b"causal"
         self.attrs[0].key = self._key
         self.attrs[0].value = 1
-        self.kernel = "sdpa_fwd_bf16_d128"
+        self.kernel = "sdpa_fwd_bf16_d128_pair"
 
     def units_per_step(self):
         return 4.0 * self.bh_local * self.S * self.S * self.D / 2.0

@@ -42,8 +42,13 @@ def qkv_bf16(b, h, tq, tk, d, seed):
     return q, k, v
 
 
-def run_sdpa(session, rt, q, k, v, causal, dtype=DType.BF16):
+TC_CANDIDATES = ["sdpa_fwd_bf16_d128_pair", "sdpa_fwd_bf16_d128"]
+
+
+def run_sdpa(session, rt, q, k, v, causal, dtype=DType.BF16, candidate=None):
     attrs = {"causal": True} if causal else {}
+    if candidate:
+        attrs["candidate"] = candidate
     ins = [upload(session, rt.stream, t, dtype) for t in (q, k, v)]
     return run_op(rt, "scaled_dot_product_attention", ins, dtype, q.shape, attrs)
 
@@ -77,15 +82,16 @@ def test_sdpa_f32_rejects_mask_and_causal_like_the_reference(session, rt):
         assert e.value.phase == "contract" and "does not implement" in e.value.message
 
 
+@pytest.mark.parametrize("candidate", TC_CANDIDATES)
 @pytest.mark.parametrize("b,h,tq,tk,causal", [(1, 1, 128, 128, False), (1, 1, 128, 128, True), (1, 2, 256, 256, True),
                                               (2, 1, 384, 384, True), (1, 1, 200, 200, True), (1, 2, 130, 130, False),
                                               (1, 1, 256, 384, False), (1, 1, 256, 384, True),
                                               (1, 1, 384, 256, True), (2, 2, 1024, 1024, True)])
-def test_sdpa_bf16_tcgen05_matches_oracle(session, rt, b, h, tq, tk, causal):
+def test_sdpa_bf16_tcgen05_matches_oracle(session, rt, b, h, tq, tk, causal, candidate):
     d = 128
     q, k, v = qkv_bf16(b, h, tq, tk, d, seed=b * 1000 + h * 100 + tq + tk + causal)
-    res = run_sdpa(session, rt, q, k, v, causal)
-    assert res.candidate == "sdpa_fwd_bf16_d128"
+    res = run_sdpa(session, rt, q, k, v, causal, candidate=candidate)
+    assert res.candidate == candidate
     got = res.outputs[0].to_f32()
     ids = np.arange(b * h * tq)
     ref = oracle.sdpa_bf16_rows(q, k, v, b, h, tq, tk, d, causal, ids).reshape(b, h, tq, d)
@@ -102,12 +108,14 @@ def test_sdpa_bf16_generic_head_dim(session, rt):
     assert max_rel_err(res.outputs[0].to_f32(), ref) <= BF16_TOL
 
 
-def test_sdpa_bf16_full_c4_config(session, rt):
+@pytest.mark.parametrize("candidate", TC_CANDIDATES)
+def test_sdpa_bf16_full_c4_config(session, rt, candidate):
     """C4: causal B8 H32 S4096 D128, seed 3. Sampled full rows against the oracle, and
     the size-independent property that causal row 0 of every head equals V[..., 0, :]."""
     b, h, s, d = 8, 32, 4096, 128
     q, k, v = qkv_bf16(b, h, s, s, d, seed=3)
-    res = run_sdpa(session, rt, q, k, v, True)
+    res = run_sdpa(session, rt, q, k, v, True, candidate=candidate)
+    assert res.candidate == candidate
     got = res.outputs[0].to_numpy()
     rng = np.random.default_rng(3)
     bh = rng.integers(0, b * h, 48)
@@ -126,6 +134,13 @@ def test_sdpa_bf16_is_bit_reproducible(session, rt):
     a = run_sdpa(session, rt, q, k, v, True).outputs[0].to_numpy()
     b = run_sdpa(session, rt, q, k, v, True).outputs[0].to_numpy()
     np.testing.assert_array_equal(a, b)
+
+
+def test_sdpa_default_candidate_is_the_pair_kernel(session, rt):
+    q, k, v = qkv_bf16(1, 1, 256, 256, 128, seed=9)
+    assert run_sdpa(session, rt, q, k, v, True).candidate == "sdpa_fwd_bf16_d128_pair"
+    with pytest.raises(tb.ExecutionError, match="unknown attention candidate"):
+        run_sdpa(session, rt, q, k, v, True, candidate="no_such_kernel")
 
 
 def test_sdpa_contract_rejections(session, rt):

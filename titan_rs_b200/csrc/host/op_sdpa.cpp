@@ -43,6 +43,24 @@ tb_status launch_sdpa_bf16_d128(Session* s, Stream* st, CUdeviceptr q, CUdevicep
                         "sdpa_fwd_bf16_d128");
 }
 
+tb_status launch_sdpa_bf16_d128_pair(Session* s, Stream* st, CUdeviceptr q, CUdeviceptr k, CUdeviceptr v,
+                                     CUdeviceptr o, int bh, int tq, int tk, int causal) {
+  CUtensorMap mq, mk, mv;
+  tb_status rc;
+  if ((rc = tmap_bhtd(&mq, q, bh, tq, TB_SDPA_HD)) || (rc = tmap_bhtd(&mk, k, bh, tk, TB_SDPA_HD)) ||
+      (rc = tmap_bhtd(&mv, v, bh, tk, TB_SDPA_HD)))
+    return rc;
+  CUfunction fn = nullptr;
+  rc = builtin_function(s, "sdpa_bf16_pair", "sdpa_fwd_bf16_d128_pair", &fn);
+  if (rc) return rc;
+  float scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)TB_SDPA_HD));
+  CUdeviceptr status = s->status.device;
+  void* params[] = {&mq, &mk, &mv, &o, &tq, &tk, &causal, &scale_log2, &status};
+  const unsigned pairs = (unsigned)((tq + 2 * TB_SDPA_BM - 1) / (2 * TB_SDPA_BM));
+  return launch_builtin(s, st, fn, (unsigned)bh, pairs, 1, TB_SDPA2_THREADS, TB_SDPA2_SMEM_BYTES, params,
+                        "sdpa_fwd_bf16_d128_pair");
+}
+
 }  // namespace tb
 
 using namespace tb;
@@ -56,6 +74,7 @@ extern "C" tb_status tb_op_sdpa(tb_session* session, tb_stream* stream, const tb
     return contract("scaled dot-product attention requires exactly three rank-4 BHTD inputs");
   const uint32_t dt = q->dtype;
   bool causal = false;
+  const char* candidate = nullptr;  // optional: name of a registered kernel to run (autotuning / tests)
   if (dt == TB_F32) {
     if (num_attrs)
       return unsupported("CUDA scaled dot-product attention does not implement mask, causal, or other attributes");
@@ -64,6 +83,10 @@ extern "C" tb_status tb_op_sdpa(tb_session* session, tb_stream* stream, const tb
       if (attrs[i].key && strcmp(attrs[i].key, "causal") == 0 && !attrs[i].str && attrs[i].value >= 0 &&
           attrs[i].value <= 1) {
         causal = attrs[i].value != 0;
+        continue;
+      }
+      if (attrs[i].key && strcmp(attrs[i].key, "candidate") == 0 && attrs[i].str) {
+        candidate = attrs[i].str;
         continue;
       }
       return unsupported("CUDA scaled dot-product attention does not implement mask or attributes other than causal");
@@ -101,7 +124,15 @@ extern "C" tb_status tb_op_sdpa(tb_session* session, tb_stream* stream, const tb
   if (rc) return rc;
   CUdeviceptr pq = bq->ptr, pk = bk->ptr, pv = bv->ptr, po = bo->ptr;
   int b = (int)B, h = (int)H, tq = (int)Tq, tk = (int)Tk, d = (int)D, c = causal ? 1 : 0;
-  if (dt == TB_BF16 && D == TB_SDPA_HD && ((pq | pk | pv | po) & 15) == 0) {
+  const bool tc_ok = dt == TB_BF16 && D == TB_SDPA_HD && ((pq | pk | pv | po) & 15) == 0;
+  if (candidate && strcmp(candidate, "sdpa_fwd_bf16_d128_pair") != 0 && strcmp(candidate, "sdpa_fwd_bf16_d128") != 0 &&
+      strcmp(candidate, "sdpa_bf16_generic") != 0)
+    return contract(std::string("unknown attention candidate ") + candidate);
+  if (candidate && !tc_ok && strcmp(candidate, "sdpa_bf16_generic") != 0)
+    return unsupported(std::string("candidate ") + candidate + " does not take this shape or alignment");
+  if (tc_ok && (!candidate || strcmp(candidate, "sdpa_fwd_bf16_d128_pair") == 0)) {
+    rc = launch_sdpa_bf16_d128_pair(s, st, pq, pk, pv, po, b * h, tq, tk, c);
+  } else if (tc_ok && strcmp(candidate, "sdpa_fwd_bf16_d128") == 0) {
     rc = launch_sdpa_bf16_d128(s, st, pq, pk, pv, po, b * h, tq, tk, c);
   } else {
     const bool bf = dt == TB_BF16;

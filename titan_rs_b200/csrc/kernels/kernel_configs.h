@@ -18,3 +18,9 @@
 #define TB_SDPA_THREADS 192
 #define TB_SDPA_BARRIER_BYTES 256
 #define TB_SDPA_SMEM_BYTES (7 * 32768 + TB_SDPA_BARRIER_BYTES + 1024)
+
+// Two-query-tile SDPA (sdpa_bf16_pair.cu): Q 2x32 KB + K ring 2x32 KB + V ring 2x32 KB + barriers;
+// P lives in tensor memory. 12 warps: producer, MMA, 2 idle, two softmax warpgroups.
+#define TB_SDPA2_THREADS 384
+#define TB_SDPA2_BARRIER_BYTES 256
+#define TB_SDPA2_SMEM_BYTES (6 * 32768 + TB_SDPA2_BARRIER_BYTES + 1024)
