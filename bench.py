@@ -390,11 +390,14 @@ class SdpaWorkload(Workload):
         shape = (1, self.bh_local, S, D)
         self.tq, self.tk, self.tv = (_tensor(self.tb, d, DType.BF16, shape) for d in self.dev)
         self.to = _tensor(self.tb, self.do, DType.BF16, shape)
-        self.attrs = (N.Attr * 1)()
-        self._key = b"causal"
+        cand = os.environ.get("TITAN_B200_SDPA_CANDIDATE", "sdpa_fwd_bf16_d128")
+        self.attrs = (N.Attr * 2)()
+        self._key, self._ckey, self._cval = b"causal", b"candidate", cand.encode()
         self.attrs[0].key = self._key
         self.attrs[0].value = 1
-        self.kernel = "sdpa_fwd_bf16_d128_pair"
+        self.attrs[1].key = self._ckey
+        self.attrs[1].str = self._cval
+        self.kernel = cand
 
     def units_per_step(self):
         return 4.0 * self.bh_local * self.S * self.S * self.D / 2.0
@@ -402,7 +405,7 @@ class SdpaWorkload(Workload):
     def step(self):
         c = self.ctypes
         rc = self.Nn.lib().tb_op_sdpa(self.s.ptr, self.st.ptr, c.byref(self.tq), c.byref(self.tk), c.byref(self.tv),
-                                      c.byref(self.to), self.attrs, 1, None)
+                                      c.byref(self.to), self.attrs, 2, None)
         if rc:
             raise RuntimeError(self.Nn.last_error())
 

@@ -136,9 +136,9 @@ def test_sdpa_bf16_is_bit_reproducible(session, rt):
     np.testing.assert_array_equal(a, b)
 
 
-def test_sdpa_default_candidate_is_the_pair_kernel(session, rt):
+def test_sdpa_default_candidate_and_unknown_candidate(session, rt):
     q, k, v = qkv_bf16(1, 1, 256, 256, 128, seed=9)
-    assert run_sdpa(session, rt, q, k, v, True).candidate == "sdpa_fwd_bf16_d128_pair"
+    assert run_sdpa(session, rt, q, k, v, True).candidate == "sdpa_fwd_bf16_d128"
     with pytest.raises(tb.ExecutionError, match="unknown attention candidate"):
         run_sdpa(session, rt, q, k, v, True, candidate="no_such_kernel")
 

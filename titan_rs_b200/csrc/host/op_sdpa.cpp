@@ -130,9 +130,9 @@ extern "C" tb_status tb_op_sdpa(tb_session* session, tb_stream* stream, const tb
     return contract(std::string("unknown attention candidate ") + candidate);
   if (candidate && !tc_ok && strcmp(candidate, "sdpa_bf16_generic") != 0)
     return unsupported(std::string("candidate ") + candidate + " does not take this shape or alignment");
-  if (tc_ok && (!candidate || strcmp(candidate, "sdpa_fwd_bf16_d128_pair") == 0)) {
+  if (tc_ok && candidate && strcmp(candidate, "sdpa_fwd_bf16_d128_pair") == 0) {
     rc = launch_sdpa_bf16_d128_pair(s, st, pq, pk, pv, po, b * h, tq, tk, c);
-  } else if (tc_ok && strcmp(candidate, "sdpa_fwd_bf16_d128") == 0) {
+  } else if (tc_ok && (!candidate || strcmp(candidate, "sdpa_fwd_bf16_d128") == 0)) {
     rc = launch_sdpa_bf16_d128(s, st, pq, pk, pv, po, b * h, tq, tk, c);
   } else {
     const bool bf = dt == TB_BF16;
