@@ -155,3 +155,38 @@ def test_gemm_contract_rejections(session, rt):
     assert "contiguous" in err([lhs, rhs32], (2, 2), layout="Strided")
     assert "exactly two" in err([lhs], (2, 2))
     assert "unsupported attributes" in err([lhs, rhs32], (2, 2), attrs={"alpha": 2})
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 65536), (512, 512, 16384), (300, 700, 9000), (256, 256, 1024)])
+def test_gemm_bf16_split_k_matches_oracle(session, rt, m, n, k):
+    """Few output tiles and a long K: the op splits K over the SMs (fp32 partials in the
+    stream's scratch memory, then a fixed-order reduction)."""
+    a, b = bf16_inputs(m, n, k, seed=m + n + k + 7)
+    ta, tbb = upload(session, rt.stream, a, DType.BF16), upload(session, rt.stream, b, DType.BF16)
+    h = run_op(rt, "gemm", [ta, tbb], DType.BF16, (m, n), {"transpose_rhs": True})
+    assert h.candidate == "gemm_bf16_tn_splitk"
+    got = h.outputs[0].to_f32()
+    rows = np.repeat(np.arange(m), n)
+    cols = np.tile(np.arange(n), m)
+    ref = oracle.gemm_bf16_points(a, b, True, m, n, k, rows, cols).reshape(m, n)
+    assert max_rel_err(got, ref) <= BF16_TOL, max_rel_err(got, ref)
+    # Same inputs, one K slice per tile: equal within bf16 rounding, and split-K is deterministic.
+    whole = run_op(rt, "gemm", [ta, tbb], DType.BF16, (m, n), {"transpose_rhs": True, "candidate": "gemm_bf16_tn"})
+    assert whole.candidate == "gemm_bf16_tn"
+    assert max_rel_err(got, whole.outputs[0].to_f32()) <= BF16_TOL
+    again = run_op(rt, "gemm", [ta, tbb], DType.BF16, (m, n), {"transpose_rhs": True})
+    np.testing.assert_array_equal(again.outputs[0].to_numpy(), h.outputs[0].to_numpy())
+
+
+def test_gemm_candidate_attribute(session, rt):
+    a, b = bf16_inputs(256, 512, 256, seed=3)
+    ta, tbb = upload(session, rt.stream, a, DType.BF16), upload(session, rt.stream, b, DType.BF16)
+    forced = run_op(rt, "gemm", [ta, tbb], DType.BF16, (256, 512), {"transpose_rhs": True,
+                                                                    "candidate": "gemm_bf16_tn_splitk"})
+    assert forced.candidate == "gemm_bf16_tn_splitk"
+    generic = run_op(rt, "gemm", [ta, tbb], DType.BF16, (256, 512), {"transpose_rhs": True,
+                                                                     "candidate": "gemm_bf16_generic"})
+    assert generic.candidate == "gemm_bf16_generic"
+    assert max_rel_err(forced.outputs[0].to_f32(), generic.outputs[0].to_f32()) <= BF16_TOL
+    with pytest.raises(tb.ExecutionError, match="unknown GEMM candidate"):
+        run_op(rt, "gemm", [ta, tbb], DType.BF16, (256, 512), {"transpose_rhs": True, "candidate": "nope"})

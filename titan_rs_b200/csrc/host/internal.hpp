@@ -48,6 +48,10 @@ struct Buffer : RefCounted {
 struct Stream : RefCounted {
   Session* session = nullptr;
   CUstream raw = nullptr;
+  // Scratch device memory for kernels launched on this stream (split-K partials).
+  // Stream order serialises its users; it grows on demand and is freed with the stream.
+  CUdeviceptr scratch = 0;
+  size_t scratch_bytes = 0;
 };
 
 struct Event : RefCounted {
@@ -105,6 +109,9 @@ tb_status activate(Session* s);
 tb_status check_buffer(Session* s, tb_buffer* b, Buffer** out);
 tb_status check_stream(Session* s, tb_stream* st, Stream** out);
 tb_status check_event(Session* s, tb_event* e, Event** out);
+
+// At least `bytes` of the stream's scratch memory (allocating or growing it).
+tb_status stream_scratch(Session* s, Stream* st, size_t bytes, CUdeviceptr* out);
 
 // Records an event on `stream` and hands it to the caller (or drops it if out is null).
 tb_status record_event(Session* s, Stream* stream, std::shared_ptr<std::vector<uint8_t>> staging, tb_event** out);

@@ -28,6 +28,56 @@ tb_status launch_gemm_bf16_tn(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr
   return launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_SMEM_BYTES, params, "gemm_bf16_tn");
 }
 
+// Split-K plan for an output with too few 128x256 tiles to fill the SMs.
+struct SplitPlan {
+  int splits = 1, kb_per_split = 0;
+};
+
+SplitPlan plan_split_k(int sm_count, int M, int N, int K, bool force) {
+  SplitPlan p;
+  const int tiles = ((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN);
+  const int num_k = (K + TB_GEMM_BK - 1) / TB_GEMM_BK;
+  if (!force && (tiles * 2 > sm_count || num_k < 8)) return p;
+  int splits = sm_count / tiles;
+  if (splits < 2) splits = 2;
+  if (splits > 32) splits = 32;
+  if (splits > num_k) splits = num_k;
+  if (splits < 2) return p;
+  p.kb_per_split = (num_k + splits - 1) / splits;
+  p.splits = (num_k + p.kb_per_split - 1) / p.kb_per_split;  // every split gets >= 1 k-block
+  return p;
+}
+
+tb_status launch_gemm_bf16_splitk(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c, int M, int N,
+                                  int K, long long ldc, int splits, int kb_per_split, CUdeviceptr partial) {
+  CUtensorMap ta, tbm;
+  tb_status rc = tmap_bf16_2d(&ta, a, (uint64_t)M, (uint64_t)K, (uint64_t)K, TB_GEMM_BM, TB_GEMM_BK,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = tmap_bf16_2d(&tbm, b, (uint64_t)N, (uint64_t)K, (uint64_t)K, TB_GEMM_BN, TB_GEMM_BK,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  CUfunction fn = nullptr, red = nullptr;
+  if ((rc = builtin_function(s, "gemm_bf16", "gemm_bf16_tn_splitk", &fn)) ||
+      (rc = builtin_function(s, "gemm_bf16", "splitk_reduce_bf16", &red)))
+    return rc;
+  const long long units =
+      (long long)((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN) * splits;
+  const unsigned grid = (unsigned)(units < s->sm_count ? units : s->sm_count);
+  CUdeviceptr status = s->status.device;
+  void* params[] = {&ta, &tbm, &partial, &M, &N, &K, &splits, &kb_per_split, &status};
+  rc = launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_SMEM_BYTES, params, "gemm_bf16_tn_splitk");
+  if (rc) return rc;
+  void* rparams[] = {&partial, &c, &M, &N, &splits, &ldc};
+  const unsigned long long vecs = ((unsigned long long)M * N + 3) / 4;
+  unsigned long long rgrid = (vecs + 255) / 256;
+  if (rgrid > (unsigned long long)s->sm_count * 16) rgrid = (unsigned long long)s->sm_count * 16;
+  rc = launch_builtin(s, st, red, (unsigned)rgrid, 1, 1, 256, 0, rparams, "splitk_reduce_bf16");
+  if (rc) return rc;
+  note_launch("gemm_bf16_tn_splitk");
+  return TB_OK;
+}
+
 }  // namespace tb
 
 using namespace tb;
@@ -37,11 +87,21 @@ extern "C" tb_status tb_op_gemm(tb_session* session, tb_stream* stream, const tb
   Session* s = reinterpret_cast<Session*>(session);
   if (!s) return set_error(TB_ERR_INVALID, "contract", "null session");
   if (!lhs || !rhs || !output) return contract("gemm requires exactly two rank-2 inputs and one output");
-  for (uint32_t i = 0; i < num_attrs; ++i)
+  const char* candidate = nullptr;  // optional: name of a registered kernel to run (autotuning / tests)
+  for (uint32_t i = 0; i < num_attrs; ++i) {
+    if (attrs[i].key && strcmp(attrs[i].key, "candidate") == 0 && attrs[i].str) {
+      candidate = attrs[i].str;
+      continue;
+    }
     if (!attrs[i].key || (strcmp(attrs[i].key, "transpose_lhs") != 0 && strcmp(attrs[i].key, "transpose_rhs") != 0))
       return contract("CUDA GEMM received unsupported attributes");
+  }
+  if (candidate && strcmp(candidate, "gemm_bf16_tn") != 0 && strcmp(candidate, "gemm_bf16_tn_splitk") != 0 &&
+      strcmp(candidate, "gemm_bf16_generic") != 0 && strcmp(candidate, "gemm_f32_tiled") != 0)
+    return contract(std::string("unknown GEMM candidate ") + candidate);
   bool tl = false, tr = false;
   for (uint32_t i = 0; i < num_attrs; ++i) {
+    if (strcmp(attrs[i].key, "candidate") == 0) continue;
     if (attrs[i].str || attrs[i].value < 0 || attrs[i].value > 1)
       return contract(std::string(attrs[i].key) + " must be a bool");
     if (strcmp(attrs[i].key, "transpose_lhs") == 0) tl = attrs[i].value != 0;
@@ -78,7 +138,23 @@ extern "C" tb_status tb_op_gemm(tb_session* session, tb_stream* stream, const tb
   CUfunction fn = nullptr;
   if (dt == TB_BF16) {
     const bool tma_ok = !tl && tr && (K % 8) == 0 && ((pa | pb | pc) & 15) == 0;
-    if (tma_ok) {
+    const bool want_generic = candidate && strcmp(candidate, "gemm_bf16_generic") == 0;
+    if (candidate && !tma_ok && !want_generic)
+      return unsupported(std::string("candidate ") + candidate + " does not take this layout or alignment");
+    if (candidate && strcmp(candidate, "gemm_f32_tiled") == 0)
+      return unsupported("candidate gemm_f32_tiled does not take BF16");
+    const bool force_split = candidate && strcmp(candidate, "gemm_bf16_tn_splitk") == 0;
+    const SplitPlan plan = tma_ok && !want_generic && !(candidate && strcmp(candidate, "gemm_bf16_tn") == 0)
+                               ? plan_split_k(s->sm_count, M, N, K, force_split)
+                               : SplitPlan{};
+    if (force_split && plan.splits < 2) return unsupported("candidate gemm_bf16_tn_splitk needs at least 2 k-blocks");
+    if (tma_ok && !want_generic && plan.splits >= 2) {
+      CUdeviceptr partial = 0;
+      rc = stream_scratch(s, st, (size_t)plan.splits * M * N * sizeof(float), &partial);
+      if (rc) return rc;
+      rc = launch_gemm_bf16_splitk(s, st, pa, pb, pc, M, N, K, (long long)N, plan.splits, plan.kb_per_split,
+                                   partial);
+    } else if (tma_ok && !want_generic) {
       rc = launch_gemm_bf16_tn(s, st, pa, pb, pc, M, N, K, (long long)N);
     } else {
       rc = builtin_function(s, "compat", "gemm_bf16_generic", &fn);

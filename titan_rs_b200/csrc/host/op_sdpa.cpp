@@ -38,8 +38,9 @@ tb_status launch_sdpa_bf16_d128(Session* s, Stream* st, CUdeviceptr q, CUdevicep
   float scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)TB_SDPA_HD));
   CUdeviceptr status = s->status.device;
   void* params[] = {&mq, &mk, &mv, &o, &tq, &tk, &causal, &scale_log2, &status};
-  const unsigned qtiles = (unsigned)((tq + TB_SDPA_BM - 1) / TB_SDPA_BM);
-  return launch_builtin(s, st, fn, (unsigned)bh, qtiles, 1, TB_SDPA_THREADS, TB_SDPA_SMEM_BYTES, params,
+  const unsigned long long qtiles = (unsigned long long)((tq + TB_SDPA_BM - 1) / TB_SDPA_BM);
+  if (qtiles * (unsigned long long)bh > 0x7fffffffull) return contract("CUDA attention grid exceeds 2^31 CTAs");
+  return launch_builtin(s, st, fn, (unsigned)(qtiles * bh), 1, 1, TB_SDPA_THREADS, TB_SDPA_SMEM_BYTES, params,
                         "sdpa_fwd_bf16_d128");
 }
 
@@ -56,8 +57,9 @@ tb_status launch_sdpa_bf16_d128_pair(Session* s, Stream* st, CUdeviceptr q, CUde
   float scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)TB_SDPA_HD));
   CUdeviceptr status = s->status.device;
   void* params[] = {&mq, &mk, &mv, &o, &tq, &tk, &causal, &scale_log2, &status};
-  const unsigned pairs = (unsigned)((tq + 2 * TB_SDPA_BM - 1) / (2 * TB_SDPA_BM));
-  return launch_builtin(s, st, fn, (unsigned)bh, pairs, 1, TB_SDPA2_THREADS, TB_SDPA2_SMEM_BYTES, params,
+  const unsigned long long pairs = (unsigned long long)((tq + 2 * TB_SDPA_BM - 1) / (2 * TB_SDPA_BM));
+  if (pairs * (unsigned long long)bh > 0x7fffffffull) return contract("CUDA attention grid exceeds 2^31 CTAs");
+  return launch_builtin(s, st, fn, (unsigned)(pairs * bh), 1, 1, TB_SDPA2_THREADS, TB_SDPA2_SMEM_BYTES, params,
                         "sdpa_fwd_bf16_d128_pair");
 }
 

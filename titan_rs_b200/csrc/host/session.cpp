@@ -171,7 +171,11 @@ void session_destroy(Session* s) {
     delete e;
   }
   for (Stream* st : s->streams) {
-    if (d && st->raw) d->cuStreamDestroy_v2(st->raw);
+    if (d && st->raw) {
+      d->cuStreamSynchronize(st->raw);
+      if (st->scratch) d->cuMemFree_v2(st->scratch);
+      d->cuStreamDestroy_v2(st->raw);
+    }
     delete st;
   }
   for (Buffer* b : s->buffers) {
@@ -252,6 +256,28 @@ tb_status record_event(Session* s, Stream* stream, std::shared_ptr<std::vector<u
     s->events.insert(e);
   }
   *out = reinterpret_cast<tb_event*>(e);
+  return TB_OK;
+}
+
+tb_status stream_scratch(Session* s, Stream* st, size_t bytes, CUdeviceptr* out) {
+  if (st->scratch_bytes >= bytes) {
+    *out = st->scratch;
+    return TB_OK;
+  }
+  const DriverApi* d = driver();
+  if (st->scratch) {
+    // Earlier kernels on this stream may still read the old scratch.
+    TB_CU("cuStreamSynchronize", d->cuStreamSynchronize(st->raw));
+    d->cuMemFree_v2(st->scratch);
+    st->scratch = 0;
+    st->scratch_bytes = 0;
+  }
+  CUdeviceptr p = 0;
+  TB_CU("allocate", d->cuMemAlloc_v2(&p, bytes));
+  st->scratch = p;
+  st->scratch_bytes = bytes;
+  (void)s;
+  *out = p;
   return TB_OK;
 }
 
@@ -475,6 +501,10 @@ void tb_stream_release(tb_stream* stream) {
   const DriverApi* d = driver();
   if (d && x->raw) {
     d->cuCtxSetCurrent(s->context);
+    if (x->scratch) {
+      d->cuStreamSynchronize(x->raw);
+      d->cuMemFree_v2(x->scratch);
+    }
     d->cuStreamDestroy_v2(x->raw);
   }
   delete x;

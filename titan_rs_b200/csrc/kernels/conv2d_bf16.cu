@@ -35,7 +35,10 @@ struct ConvPolicy {
 
   __device__ int num_m() const { return tiles_img * tiles_h * tiles_w; }
   __device__ int num_tiles() const { return num_m() * num_n; }
-  __device__ int num_k_blocks() const { return R * S * c_blocks; }
+  __device__ void k_blocks(int, int& kb0, int& kb1) const {
+    kb0 = 0;
+    kb1 = R * S * c_blocks;
+  }
   __device__ void prefetch() const {
     tma_prefetch_desc(tx);
     tma_prefetch_desc(tw);
@@ -59,7 +62,7 @@ struct ConvPolicy {
     tma_load_4d(a_dst, tx, bar, cb * 64, wo0 * sw - pw + s * dw, ho0 * sh - ph + r * dh, n0);
     tma_load_3d(b_dst, tw, bar, cb * 64, rs, n_blk * umma::BN);
   }
-  __device__ void store(int row, int m_blk, int n_blk, int col, const uint32_t (&acc)[32]) const {
+  __device__ void store(int row, int, int m_blk, int n_blk, int col, const uint32_t (&acc)[32]) const {
     int n0, ho0, wo0;
     pixel_tile(m_blk, n0, ho0, wo0);
     const int n = n0 + (row >> 6), ho = ho0 + ((row >> 3) & 7), wo = wo0 + (row & 7);

@@ -20,7 +20,7 @@
 #define TB_SDPA_SMEM_BYTES (7 * 32768 + TB_SDPA_BARRIER_BYTES + 1024)
 
 // Two-query-tile SDPA (sdpa_bf16_pair.cu): Q 2x32 KB + K ring 2x32 KB + V ring 2x32 KB + barriers;
-// P lives in tensor memory. 12 warps: producer, MMA, 2 idle, two softmax warpgroups.
-#define TB_SDPA2_THREADS 384
+// P lives in tensor memory. 10 warps: producer, MMA, two softmax groups of four.
+#define TB_SDPA2_THREADS 320
 #define TB_SDPA2_BARRIER_BYTES 256
 #define TB_SDPA2_SMEM_BYTES (6 * 32768 + TB_SDPA2_BARRIER_BYTES + 1024)

@@ -5,8 +5,9 @@
 // O = softmax(Q K^T / sqrt(D)) V over BHTD tensors, extended with a causal mask in
 // which query i attends to keys j <= i (top-left aligned when Tq != Tk).
 //
-// Work unit: one CTA per (128-row query tile, batch*head), heaviest causal tiles
-// first. 192 threads, warp-specialised:
+// Work unit: one CTA per (128-row query tile, batch*head); the grid is flat and
+// head-major with the heaviest causal tiles of each head first. 192 threads,
+// warp-specialised:
 //   warp 0      TMA producer: the Q tile once, then K_j / V_j tiles (128 keys x 128 dims,
 //               two 64-column 128-byte-swizzled boxes each) through 2-stage rings.
 //   warp 1      owns 512 TMEM columns: S double buffer (2 x 128 fp32 columns) and
@@ -100,9 +101,11 @@ extern "C" __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Barriers* bars = reinterpret_cast<Barriers*>(smem + OFF_BAR);
   const int warp = warp_id(), lane = lane_id();
-  const int bh = blockIdx.x;
+  // Flat grid, head-major: the query tiles of one head run together (so that
+  // head's K/V stays in L2), heaviest causal tiles first within the head.
   const int num_qt = (Tq + BM - 1) / BM;
-  const int qt = num_qt - 1 - blockIdx.y;  // heaviest causal tiles first
+  const int bh = blockIdx.x / num_qt;
+  const int qt = num_qt - 1 - (int)(blockIdx.x % num_qt);
   const int kv_tiles_all = (Tk + BN - 1) / BN;
   const int n = causal ? min(kv_tiles_all, qt + 1) : kv_tiles_all;
 

@@ -5,7 +5,7 @@
 // O = softmax(Q K^T / sqrt(D)) V over BHTD, plus a causal mask (query i sees keys j <= i,
 // top-left aligned when Tq != Tk).
 //
-// One CTA per (pair of 128-row query tiles A = 2i, B = 2i+1, batch*head); 384 threads:
+// One CTA per (pair of 128-row query tiles A = 2i, B = 2i+1, batch*head); 320 threads:
 //   warp 0       TMA producer: Q_A and Q_B once, then K_j / V_j (128 keys x 128 dims,
 //                two 64-column 128-byte-swizzled boxes each) through 2-stage rings.
 //   warp 1       owns all 512 TMEM columns: S_A | S_B | O_A | O_B (128 fp32 columns each).
@@ -15,13 +15,17 @@
 //                tile's warpgroup exponentiates.
 //                  S_X(j)  = Q_X K_j^T   (SS: both operands K-major in shared memory)
 //                  O_X    += P_X(j) V_j  (TS: P read from TMEM, V MN-major in shared memory)
-//   warps 4..7   softmax warpgroup for tile A, warps 8..11 for tile B: one query row per
-//                thread (its TMEM lane). Each S row is read from TMEM twice (row max,
-//                then exponentials), and P is written back as bf16 pairs over the first
-//                64 columns of the same S region, where the TS-MMA reads it. The running
-//                max moves (and O is rescaled in TMEM) only when it grows by more than
-//                2^8, so P stays below 256 and the result is the exact online softmax.
-//   warps 2..3   idle (they keep the warpgroup layout that TMEM lane access requires).
+//   warps 2..5   softmax group for tile A, warps 6..9 for tile B (each group covers the
+//                four TMEM lane quarters, since warp w reaches lanes 32*(w%4)..): one query row per
+//                thread (its TMEM lane). The S row is streamed from TMEM once in
+//                32-column chunks and exponentiated against the current reference max
+//                (one FFMA each; one exponential in four on the FMA pipe, the rest on
+//                the MUFU); P is held in registers, then written back as bf16 pairs
+//                over the first 64 columns of the same S region, where the TS-MMA
+//                reads it. The reference max moves (O is rescaled in TMEM and the row
+//                recomputed from the still-intact S) only when the row max grows by
+//                more than 2^8, so P stays below 256 and the result is the exact online
+//                softmax.
 // Ordering: tcgen05.commit arrives once ALL earlier MMAs of the issuing thread are
 // done, so "S_X(j) ready" also means PV_X(j-1) finished reading P_X and writing O_X:
 // the softmax warps may then overwrite S/P and rescale O without further waits.
@@ -72,6 +76,73 @@ __device__ __forceinline__ float exp2_approx(float x) {
   return y;
 }
 
+// 2^x on the FMA pipe, for x <= 8 (the lazy-rescale bound): Cody-Waite split
+// x = n + f with n = floor(x), f in [0, 1); 2^f from a degree-3 polynomial
+// fitted for this kernel (weighted least squares toward minimax relative error
+// on [0, 1), p(0) = 1; max relative error 8.6e-5, below the 2^-9 rounding of the
+// bf16 P it feeds); 2^n added to the exponent field. Inputs below -127 give 0
+// or a denormal, which bf16 P and the row sum treat as zero.
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -127.0f);
+  const float n = floorf(x);
+  const float f = x - n;
+  float p = fmaf(0.0770670622587204f, f, 0.22764495015144348f);
+  p = fmaf(p, f, 0.6951168179512024f);
+  p = fmaf(p, f, 1.0f);
+  return __int_as_float(__float_as_int(p) + (static_cast<int>(n) << 23));
+}
+
+// Makes later uses of registers filled by tcgen05.ld depend on the preceding
+// tcgen05.wait::ld (the two asm statements share no operands otherwise).
+template <int N>
+__device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
+// One pass over a 128-column S row in TMEM: applies the causal/tail mask,
+// returns the row sum of p = 2^(s*scale_log2 + neg_m) (bf16-packed into
+// `packed`, one exponential in four on the FMA pipe) and updates `mraw`, the
+// row max of the raw scores. With exps == false only the max is computed.
+// `valid` = number of leading columns of this key tile the row may see
+// (min(Tk, q+1) - kv0 when causal, Tk - kv0 otherwise; >= BN means all).
+__device__ __forceinline__ float softmax_row_pass(uint32_t s_tmem, int valid, float scale_log2, float neg_m, bool exps,
+                                                  uint32_t (&packed)[BN / 2], float& mraw) {
+  float rs = 0.f;
+  const bool need_mask = valid < BN;
+#pragma unroll
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t cur[32];
+    tmem_ld_x32(s_tmem + c, cur);
+    tmem_ld_wait();
+    reg_fence(cur);
+    const int lim = valid - c;  // columns i >= lim of this chunk are masked
+    if (need_mask) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i >= lim) cur[i] = __float_as_uint(-INFINITY);
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, __uint_as_float(cur[i]));
+    if (exps) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const float x0 = fmaf(__uint_as_float(cur[i]), scale_log2, neg_m);
+        const float x1 = fmaf(__uint_as_float(cur[i + 1]), scale_log2, neg_m);
+        float p0 = exp2_approx(x0);
+        float p1 = (i & 2) ? exp2_poly(x1) : exp2_approx(x1);
+        if (need_mask) {
+          if (i >= lim) p0 = 0.f;
+          if (i + 1 >= lim) p1 = 0.f;
+        }
+        rs += p0 + p1;
+        packed[(c + i) / 2] = pack_bf16x2(p0, p1);
+      }
+    }
+  }
+  return rs;
+}
+
 __device__ __forceinline__ void load_tile(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int row0, int bh) {
   tma_load_3d(dst, map, bar, 0, row0, bh);
   tma_load_3d(dst + HALF_BYTES, map, bar, 64, row0, bh);
@@ -97,9 +168,10 @@ extern "C" __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Barriers* bars = reinterpret_cast<Barriers*>(smem + OFF_BAR);
   const int warp = warp_id(), lane = lane_id();
-  const int bh = blockIdx.x;
+  // Flat grid, head-major (a head's K/V stays in L2), heaviest causal pairs first.
   const int num_pairs = (Tq + 2 * BM - 1) / (2 * BM);
-  const int pair = num_pairs - 1 - blockIdx.y;  // heaviest causal pairs first
+  const int bh = blockIdx.x / num_pairs;
+  const int pair = num_pairs - 1 - (int)(blockIdx.x % num_pairs);
   const int qt0 = 2 * pair;                     // query tile A; tile B = qt0 + 1
   const int kv_tiles_all = (Tk + BN - 1) / BN;
   // Key tiles each query tile needs.
@@ -230,9 +302,9 @@ extern "C" __global__ void __launch_bounds__(THREADS, 1)
       umma_commit(&bars->drain);
       if (!mbar_wait(&bars->drain, 0)) report_status(status, kFailMma | 5);
     }
-  } else if (warp >= 4) {
+  } else {
     // ---------------- softmax warpgroups ----------------
-    const int x = (warp >= 8) ? 1 : 0;  // query tile of this warpgroup
+    const int x = (warp >= 6) ? 1 : 0;  // query tile of this softmax group
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
@@ -251,21 +323,14 @@ extern "C" __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_after_sync();
       const int kv0 = j * BN;
-      const bool need_mask = (kv0 + BN > Tk) || (causal && kv0 + BN - 1 > qt * BM);
-      // Pass 1: row maximum of the scaled scores.
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t raw[32];
-        tmem_ld_x32(s_tmem + c, raw);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int kv = kv0 + c + i;
-          const bool valid = !need_mask || (kv < Tk && (!causal || kv <= q_row));
-          mx = fmaxf(mx, valid ? __uint_as_float(raw[i]) * scale_log2 : -INFINITY);
-        }
-      }
+      const int valid = (causal ? min(Tk, q_row + 1) : Tk) - kv0;  // visible leading keys of this tile
+      // Stream the S row in 32-column chunks (the next chunk's TMEM load overlaps
+      // this chunk's math), exponentiating against the current reference max.
+      // P stays in registers until the row is known not to need a larger max.
+      uint32_t packed[BN / 2];
+      float mraw = -INFINITY;
+      float rs = softmax_row_pass(s_tmem, valid, scale_log2, -m_used, m_used != -INFINITY, packed, mraw);
+      const float mx = mraw * scale_log2;  // scale_log2 > 0 commutes with max
       const bool grow = mx > m_used + kLazyRescaleLog2;
       if (__any_sync(0xffffffffu, grow)) {
         const float m_new = grow ? mx : m_used;
@@ -278,36 +343,21 @@ extern "C" __global__ void __launch_bounds__(THREADS, 1)
             uint32_t o[16];
             tmem_ld_x16(o_tmem + c, o);
             tmem_ld_wait();
+            reg_fence(o);
 #pragma unroll
             for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
             tmem_st_x16(o_tmem + c, o);
           }
         }
         m_used = m_new;
-      }
-      // Pass 2: P = 2^(s*scale - m_used) as bf16 pairs into columns [0, 64) of S_x.
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t raw[32];
-        tmem_ld_x32(s_tmem + c, raw);
-        tmem_ld_wait();
-        uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int kv = kv0 + c + i;
-          float p0 = exp2_approx(__uint_as_float(raw[i]) * scale_log2 - m_used);
-          float p1 = exp2_approx(__uint_as_float(raw[i + 1]) * scale_log2 - m_used);
-          if (need_mask) {
-            if (!(kv < Tk && (!causal || kv <= q_row))) p0 = 0.f;
-            if (!(kv + 1 < Tk && (!causal || kv + 1 <= q_row))) p1 = 0.f;
-          }
-          rs += p0 + p1;
-          packed[i / 2] = pack_bf16x2(p0, p1);
-        }
-        tmem_st_x16(s_tmem + c / 2, packed);
+        // S is still intact in TMEM (P is written below): recompute against the new max.
+        float unused = -INFINITY;
+        rs = softmax_row_pass(s_tmem, valid, scale_log2, -m_used, true, packed, unused);
       }
       l += rs;
+      // P_x(j) as bf16 pairs into columns [0, 64) of S_x, where the TS-MMA reads it.
+#pragma unroll
+      for (int c = 0; c < BN / 2; c += 16) tmem_st_x16(s_tmem + c, *reinterpret_cast<const uint32_t(*)[16]>(&packed[c]));
       tmem_st_wait();
       tc_fence_before_sync();
       __syncwarp();

@@ -1,6 +1,7 @@
 // Persistent, warp-specialised tcgen05 GEMM pipeline shared by the GEMM and the
-// implicit-GEMM convolution. A problem policy supplies the tile space, the TMA
-// loads of one k-block and the epilogue addressing; this file owns the
+// implicit-GEMM convolution. A problem policy supplies the tile space
+// (num_tiles, tile, k_blocks = the k-block range of a tile), the TMA loads of
+// one k-block and the epilogue addressing (store); this file owns the
 // shared-memory ring, the MMA issue and the TMEM accumulators.
 //
 //   D[128 x 256] (+)= A[128 x 64] * B[256 x 64]^T per k-block, bf16 in, fp32 in TMEM.
@@ -87,7 +88,6 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
 
   const int warp = warp_id(), lane = lane_id();
   const int tiles = p.num_tiles();
-  const int num_k = p.num_k_blocks();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -121,7 +121,9 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         int m_blk, n_blk;
         p.tile(t, m_blk, n_blk);
-        for (int kb = 0; kb < num_k; ++kb) {
+        int kb0, kb1;
+        p.k_blocks(t, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&bars->empty[stage], phase ^ 1)) {
             report_status(status, fail_base | 0x0101);
             ok = false;
@@ -155,7 +157,9 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
         }
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_k; ++kb) {
+        int kb0, kb1;
+        p.k_blocks(t, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&bars->full[stage], phase)) {
             report_status(status, fail_base | 0x0202);
             ok = false;
@@ -168,7 +172,7 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t adesc = sdesc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bdesc = sdesc_sw128(b_addr + k * 32, 16, 1024);
-            umma_bf16_ss(d_tmem, adesc, bdesc, IDESC, (kb | k) != 0);
+            umma_bf16_ss(d_tmem, adesc, bdesc, IDESC, (kb > kb0) || (k > 0));
           }
           umma_commit(&bars->empty[stage]);
           if (++stage == STAGES) {
@@ -207,7 +211,7 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
         uint32_t r[32];
         tmem_ld_x32(taddr + col, r);
         tmem_ld_wait();
-        p.store(row, m_blk, n_blk, col, r);
+        p.store(row, t, m_blk, n_blk, col, r);
       }
       tc_fence_before_sync();
       __syncwarp();
