@@ -73,13 +73,17 @@ def test_gemm_f32_c1_config_exact(session, rt):
     np.testing.assert_array_equal(h.outputs[0].to_numpy(), oracle.gemm(a, b))
 
 
+@pytest.mark.parametrize("candidate", [None, "gemm_bf16_tn"])
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 128), (200, 300, 72), (1, 8, 8), (129, 257, 1032),
                                    (1000, 1000, 1000), (512, 256, 8192), (300, 1024, 136)])
-def test_gemm_bf16_tcgen05_matches_oracle(session, rt, m, n, k):
+def test_gemm_bf16_tcgen05_matches_oracle(session, rt, m, n, k, candidate):
     a, b = bf16_inputs(m, n, k, seed=m + n + k)
+    attrs = {"transpose_rhs": True}
+    if candidate:
+        attrs["candidate"] = candidate
     h = run_op(rt, "gemm", [upload(session, rt.stream, a, DType.BF16), upload(session, rt.stream, b, DType.BF16)],
-               DType.BF16, (m, n), {"transpose_rhs": True})
-    assert h.candidate == "gemm_bf16_tn"
+               DType.BF16, (m, n), attrs)
+    assert h.candidate == candidate if candidate else h.candidate in ("gemm_bf16_tn", "gemm_bf16_tn_splitk")
     got = h.outputs[0].to_f32()
     rows = np.repeat(np.arange(m), n)
     cols = np.tile(np.arange(n), m)
