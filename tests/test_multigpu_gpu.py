@@ -27,7 +27,9 @@ def _reference_c(s, rt, a, b):
     n = b.shape[0]
     ta = tb.TensorHandle.from_numpy(s, a, DType.BF16, rt.stream)
     tbb = tb.TensorHandle.from_numpy(s, b, DType.BF16, rt.stream)
-    h = rt.execute(tb.OpRequest("gemm", [ta, tbb], [tb.TensorSpec(DType.BF16, (m, n))], {"transpose_rhs": True}))
+    # The sharded path runs the whole-K kernel on each shard; compare with the same kernel.
+    h = rt.execute(tb.OpRequest("gemm", [ta, tbb], [tb.TensorSpec(DType.BF16, (m, n))],
+                                {"transpose_rhs": True, "candidate": "gemm_bf16_tn"}))
     h.wait()
     return h.outputs[0].to_numpy()
 
