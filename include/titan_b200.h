@@ -291,6 +291,22 @@ tb_status tb_comm_barrier(tb_comm* comm, tb_stream* stream);
 tb_status tb_op_gemm_sharded(tb_comm* comm, tb_stream* stream, const tb_tensor* lhs, const tb_tensor* rhs_shard,
                              const tb_tensor* output, tb_buffer* workspace, tb_event** out);
 
+/* ---------------- Allocation-free split-K GEMM ---------------- */
+
+/* No counterpart in the reference. The split-K bf16 GEMM of tb_op_gemm
+ * (C[M,N] = A[M,K] x B^T, A row-major, B stored [N,K], C row-major, fp32
+ * accumulation) for callers that must not let a library allocate device memory,
+ * such as a server that plans all of HBM up front. Its fp32 partials live in a
+ * fixed 32 MiB device array inside the library instead of memory allocated per
+ * stream, so it rejects splits*M*N above 8,388,608 partials (TB_ERR_INVALID) and
+ * calls no allocator. `stream` is a CUstream of the current device; a, b, c are
+ * 16-byte-aligned device pointers; K % 8 == 0; splits = 0 chooses as tb_op_gemm
+ * does. The first call on a device fetches the array's address (do it before any
+ * stream capture). All calls share the array: calls that can overlap on the GPU
+ * race and must be serialised by the caller. */
+tb_status tb_gemm_bf16_splitk_noalloc(uint64_t stream, const void* a, const void* b, void* c, int m, int n, int k,
+                                      int splits);
+
 /* ---------------- Seeded synthetic inputs (host side) ---------------- */
 
 /* Counter-based generator: element i depends only on (seed, i), so any slice is

@@ -130,6 +130,7 @@ _SIGNATURES = {
     "tb_comm_barrier": (_S, [_P, _P]),
     "tb_op_gemm_sharded": (_S, [_P, _P, ctypes.POINTER(Tensor), ctypes.POINTER(Tensor), ctypes.POINTER(Tensor), _P,
                                 _PP]),
+    "tb_gemm_bf16_splitk_noalloc": (_S, [_U64, _P, _P, _P, _S, _S, _S, _S]),
     "tb_fill_normal": (_S, [_P, _U32, _SZ, _U64, ctypes.c_double, ctypes.c_double, _S]),
     "tb_fill_uniform": (_S, [_P, _U32, _SZ, _U64, ctypes.c_double, ctypes.c_double, _S]),
 }

@@ -75,8 +75,9 @@ def build(verbose: bool = False, force: bool = False) -> pathlib.Path:
     kernel_srcs = sorted(KERNELS.glob("*.cu"))
     headers = sorted(KERNELS.glob("*.cuh")) + sorted(HOST.glob("*.hpp")) + [ROOT / "include" / "titan_b200.h"]
     host_srcs = sorted(HOST.glob("*.cpp"))
+    runtime_srcs = sorted((CSRC / "noalloc").glob("*.cu"))
     stamp = OUT_DIR / "stamp"
-    digest = _digest(kernel_srcs + headers + host_srcs + [pathlib.Path(__file__)])
+    digest = _digest(kernel_srcs + headers + host_srcs + runtime_srcs + [pathlib.Path(__file__)])
     if not force and LIB.exists() and stamp.exists() and stamp.read_text() == digest:
         return LIB
 
@@ -116,11 +117,19 @@ def build(verbose: bool = False, force: bool = False) -> pathlib.Path:
               "-I", cuda_inc, "-I", str(ROOT / "include"), "-DTB_BUILDING_LIBRARY", "-c", str(src), "-o", str(obj)])
         return obj
 
+    def compile_runtime_unit(src: pathlib.Path) -> pathlib.Path:
+        # Host+device translation units that use the CUDA runtime API (static cudart).
+        obj = OUT_DIR / (src.stem + ".o")
+        _run([_nvcc(), "-c", *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", str(KERNELS),
+              "-I", str(ROOT / "include"), str(src), "-o", str(obj)])
+        return obj
+
     with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(compile_host, host_srcs + [embed]))
+        objs += list(ex.map(compile_runtime_unit, runtime_srcs))
     tmp = LIB.with_suffix(".so.tmp")
-    _run([_cxx(), "-shared", "-o", str(tmp), *map(str, objs), "-ldl", "-lpthread",
-          "-Wl,--version-script=" + str(HOST / "exports.map")])
+    _run([_cxx(), "-shared", "-o", str(tmp), *map(str, objs), "-L/usr/local/cuda/lib64", "-lcudart_static", "-lrt",
+          "-ldl", "-lpthread", "-Wl,--version-script=" + str(HOST / "exports.map")])
     os.replace(tmp, LIB)
     stamp.write_text(digest)
     return LIB
