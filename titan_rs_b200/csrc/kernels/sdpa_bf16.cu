@@ -251,23 +251,18 @@ extern "C" __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) mbar_arrive(&bars->s_empty[st]);
 
       const int kv0 = j * BN;
-      const bool need_mask = (kv0 + BN > Tk) || (causal && kv0 + BN - 1 > qt * BM);
-      float mx = -INFINITY;
-      if (need_mask) {
+      // Leading keys of this tile the row may see; four max accumulators keep the
+      // reduction off one long dependency chain.
+      const int valid = (causal ? min(Tk, q_row + 1) : Tk) - kv0;
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (valid < BN) {
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          const int kv = kv0 + c;
-          const bool valid = kv < Tk && (!causal || kv <= q_row);
-          s[c] = valid ? s[c] * scale_log2 : -INFINITY;
-          mx = fmaxf(mx, s[c]);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          s[c] *= scale_log2;
-          mx = fmaxf(mx, s[c]);
-        }
+        for (int c = 0; c < BN; ++c)
+          if (c >= valid) s[c] = -INFINITY;
       }
+#pragma unroll
+      for (int c = 0; c < BN; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
       // Lazy rescale: move the reference maximum only when it grows by > 2^8.
       const bool grow = mx > m_used + kLazyRescaleLog2;
       if (__any_sync(0xffffffffu, grow)) {
@@ -295,17 +290,18 @@ extern "C" __global__ void __launch_bounds__(THREADS, 1)
         }
         m_used = m_new;
       }
-      // P = 2^(s - m_used) (bf16), l += rowsum(P) in fp32.
+      // P = 2^(s*scale - m_used) (one FFMA each, bf16), l += rowsum(P) in fp32.
       uint32_t packed[BN / 2];
-      float rs = 0.f;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+      const float neg_m = -m_used;
 #pragma unroll
       for (int c = 0; c < BN; c += 2) {
-        const float p0 = exp2_approx(s[c] - m_used);
-        const float p1 = exp2_approx(s[c + 1] - m_used);
-        rs += p0 + p1;
+        const float p0 = exp2_approx(fmaf(s[c], scale_log2, neg_m));
+        const float p1 = exp2_approx(fmaf(s[c + 1], scale_log2, neg_m));
+        rs4[(c >> 1) & 3] += p0 + p1;
         packed[c / 2] = pack_bf16x2(p0, p1);
       }
-      l += rs;
+      l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       ok = __all_sync(0xffffffffu, mbar_wait(&bars->p_empty[st], ph ^ 1));
       if (!ok) {
         if (lane == 0) report_status(status, kFailSoftmax | 3);

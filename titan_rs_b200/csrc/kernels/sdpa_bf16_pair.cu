@@ -108,7 +108,10 @@ __device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
 // (min(Tk, q+1) - kv0 when causal, Tk - kv0 otherwise; >= BN means all).
 __device__ __forceinline__ float softmax_row_pass(uint32_t s_tmem, int valid, float scale_log2, float neg_m, bool exps,
                                                   uint32_t (&packed)[BN / 2], float& mraw) {
-  float rs = 0.f;
+  // Four independent max / sum accumulators keep the reductions off one long
+  // dependency chain.
+  float rs[4] = {0.f, 0.f, 0.f, 0.f};
+  float mx[4] = {mraw, -INFINITY, -INFINITY, -INFINITY};
   const bool need_mask = valid < BN;
 #pragma unroll
   for (int c = 0; c < BN; c += 32) {
@@ -123,7 +126,7 @@ __device__ __forceinline__ float softmax_row_pass(uint32_t s_tmem, int valid, fl
         if (i >= lim) cur[i] = __float_as_uint(-INFINITY);
     }
 #pragma unroll
-    for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, __uint_as_float(cur[i]));
+    for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(cur[i]));
     if (exps) {
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
@@ -135,11 +138,29 @@ __device__ __forceinline__ float softmax_row_pass(uint32_t s_tmem, int valid, fl
           if (i >= lim) p0 = 0.f;
           if (i + 1 >= lim) p1 = 0.f;
         }
-        rs += p0 + p1;
+        rs[(i >> 1) & 3] += p0 + p1;
         packed[(c + i) / 2] = pack_bf16x2(p0, p1);
       }
     }
   }
+  mraw = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+  return (rs[0] + rs[1]) + (rs[2] + rs[3]);
+}
+
+// P as bf16 pairs into columns [0, 64) of the S region (warp-collective).
+__device__ __forceinline__ void store_p(uint32_t s_tmem, const uint32_t (&packed)[BN / 2]) {
+#pragma unroll
+  for (int c = 0; c < BN / 2; c += 16) tmem_st_x16(s_tmem + c, *reinterpret_cast<const uint32_t(*)[16]>(&packed[c]));
+}
+
+// The rare recompute after the reference max moved: exponentials against the
+// new max, P written to TMEM here. Kept out of line (with its own P registers)
+// so the common path keeps its registers.
+__device__ __noinline__ float softmax_row_recompute_store(uint32_t s_tmem, int valid, float scale_log2, float neg_m) {
+  uint32_t packed[BN / 2];
+  float unused = -INFINITY;
+  const float rs = softmax_row_pass(s_tmem, valid, scale_log2, neg_m, true, packed, unused);
+  store_p(s_tmem, packed);
   return rs;
 }
 
@@ -351,13 +372,12 @@ extern "C" __global__ void __launch_bounds__(THREADS, 1)
         }
         m_used = m_new;
         // S is still intact in TMEM (P is written below): recompute against the new max.
-        float unused = -INFINITY;
-        rs = softmax_row_pass(s_tmem, valid, scale_log2, -m_used, true, packed, unused);
+        rs = softmax_row_recompute_store(s_tmem, valid, scale_log2, -m_used);
+      } else {
+        // P_x(j) as bf16 pairs into columns [0, 64) of S_x, where the TS-MMA reads it.
+        store_p(s_tmem, packed);
       }
       l += rs;
-      // P_x(j) as bf16 pairs into columns [0, 64) of S_x, where the TS-MMA reads it.
-#pragma unroll
-      for (int c = 0; c < BN / 2; c += 16) tmem_st_x16(s_tmem + c, *reinterpret_cast<const uint32_t(*)[16]>(&packed[c]));
       tmem_st_wait();
       tc_fence_before_sync();
       __syncwarp();
