@@ -390,7 +390,7 @@ class SdpaWorkload(Workload):
         shape = (1, self.bh_local, S, D)
         self.tq, self.tk, self.tv = (_tensor(self.tb, d, DType.BF16, shape) for d in self.dev)
         self.to = _tensor(self.tb, self.do, DType.BF16, shape)
-        cand = os.environ.get("TITAN_B200_SDPA_CANDIDATE", "sdpa_fwd_bf16_d128")
+        cand = os.environ.get("TITAN_B200_SDPA_CANDIDATE", "sdpa_fwd_bf16_d128_pair")
         self.attrs = (N.Attr * 2)()
         self._key, self._ckey, self._cval = b"causal", b"candidate", cand.encode()
         self.attrs[0].key = self._key
@@ -426,7 +426,7 @@ class SdpaWorkload(Workload):
                             "scale 1/sqrt(128), FLOPs = 4*B*H*S^2*D/2",
                 "B": self.B, "H": self.H, "S": self.S, "D": self.D,
                 "parallelism": f"bh-shard{self.world}" if self.world > 1 else "single",
-                "l2": "inputs 768 MiB > 126 MB L2"}
+                "l2": f"inputs {3 * self.nbytes / 2**20:.0f} MiB per GPU vs 126 MB L2"}
 
     def cpu_sample(self, budget_s):
         import oracle

@@ -42,7 +42,7 @@ def qkv_bf16(b, h, tq, tk, d, seed):
     return q, k, v
 
 
-TC_CANDIDATES = ["sdpa_fwd_bf16_d128_pair", "sdpa_fwd_bf16_d128"]
+TC_CANDIDATES = ["sdpa_fwd_bf16_d128_bn64", "sdpa_fwd_bf16_d128_pair", "sdpa_fwd_bf16_d128"]
 
 
 def run_sdpa(session, rt, q, k, v, causal, dtype=DType.BF16, candidate=None):
@@ -138,7 +138,7 @@ def test_sdpa_bf16_is_bit_reproducible(session, rt):
 
 def test_sdpa_default_candidate_and_unknown_candidate(session, rt):
     q, k, v = qkv_bf16(1, 1, 256, 256, 128, seed=9)
-    assert run_sdpa(session, rt, q, k, v, True).candidate == "sdpa_fwd_bf16_d128"
+    assert run_sdpa(session, rt, q, k, v, True).candidate == "sdpa_fwd_bf16_d128_pair"
     with pytest.raises(tb.ExecutionError, match="unknown attention candidate"):
         run_sdpa(session, rt, q, k, v, True, candidate="no_such_kernel")
 

@@ -1,7 +1,11 @@
 // "scaled_dot_product_attention" operator entry: the contract of
 // execute_cuda_attention and the CPU reference (titan-runtime/src/lib.rs:2575-2705,
 // 1090-1151), then the kernel choice:
-//   BF16, D == 128, 16-byte aligned  -> sdpa_fwd_bf16_d128 (tcgen05, TMA, TMEM); causal optional
+//   BF16, D == 128, 16-byte aligned  -> sdpa_fwd_bf16_d128_pair (tcgen05, TMA, TMEM; two query
+//                                       tiles per CTA); causal optional. Candidates
+//                                       sdpa_fwd_bf16_d128 (one query tile, P through shared
+//                                       memory) and sdpa_fwd_bf16_d128_bn64 (64-key tiles, two
+//                                       CTAs per SM) take the same inputs
 //   BF16, other head dims            -> sdpa_bf16_generic (CUDA cores)
 //   F32                              -> scaled_dot_product_attention_f32 (reference ABI kernel);
 //                                       mask/causal rejected as the reference does
@@ -12,10 +16,10 @@
 
 namespace tb {
 
-tb_status tmap_bhtd(CUtensorMap* map, CUdeviceptr base, uint64_t bh, uint64_t t, uint64_t d) {
+tb_status tmap_bhtd(CUtensorMap* map, CUdeviceptr base, uint64_t bh, uint64_t t, uint64_t d, uint32_t box_rows = 128) {
   cuuint64_t dims[3] = {d, t, bh};
   cuuint64_t strides[2] = {d * 2, t * d * 2};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, box_rows, 1};
   cuuint32_t elem[3] = {1, 1, 1};
   TB_CU("cuTensorMapEncodeTiled",
         driver()->cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, reinterpret_cast<void*>(base), dims,
@@ -61,6 +65,25 @@ tb_status launch_sdpa_bf16_d128_pair(Session* s, Stream* st, CUdeviceptr q, CUde
   if (pairs * (unsigned long long)bh > 0x7fffffffull) return contract("CUDA attention grid exceeds 2^31 CTAs");
   return launch_builtin(s, st, fn, (unsigned)(pairs * bh), 1, 1, TB_SDPA2_THREADS, TB_SDPA2_SMEM_BYTES, params,
                         "sdpa_fwd_bf16_d128_pair");
+}
+
+tb_status launch_sdpa_bf16_d128_bn64(Session* s, Stream* st, CUdeviceptr q, CUdeviceptr k, CUdeviceptr v,
+                                     CUdeviceptr o, int bh, int tq, int tk, int causal) {
+  CUtensorMap mq, mk, mv;
+  tb_status rc;
+  if ((rc = tmap_bhtd(&mq, q, bh, tq, TB_SDPA_HD, 128)) || (rc = tmap_bhtd(&mk, k, bh, tk, TB_SDPA_HD, TB_SDPA3_BN)) ||
+      (rc = tmap_bhtd(&mv, v, bh, tk, TB_SDPA_HD, TB_SDPA3_BN)))
+    return rc;
+  CUfunction fn = nullptr;
+  rc = builtin_function(s, "sdpa_bf16_bn64", "sdpa_fwd_bf16_d128_bn64", &fn);
+  if (rc) return rc;
+  float scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)TB_SDPA_HD));
+  CUdeviceptr status = s->status.device;
+  void* params[] = {&mq, &mk, &mv, &o, &tq, &tk, &causal, &scale_log2, &status};
+  const unsigned long long qtiles = (unsigned long long)((tq + TB_SDPA_BM - 1) / TB_SDPA_BM);
+  if (qtiles * (unsigned long long)bh > 0x7fffffffull) return contract("CUDA attention grid exceeds 2^31 CTAs");
+  return launch_builtin(s, st, fn, (unsigned)(qtiles * bh), 1, 1, TB_SDPA3_THREADS, TB_SDPA3_SMEM_BYTES, params,
+                        "sdpa_fwd_bf16_d128_bn64");
 }
 
 }  // namespace tb
@@ -128,13 +151,15 @@ extern "C" tb_status tb_op_sdpa(tb_session* session, tb_stream* stream, const tb
   int b = (int)B, h = (int)H, tq = (int)Tq, tk = (int)Tk, d = (int)D, c = causal ? 1 : 0;
   const bool tc_ok = dt == TB_BF16 && D == TB_SDPA_HD && ((pq | pk | pv | po) & 15) == 0;
   if (candidate && strcmp(candidate, "sdpa_fwd_bf16_d128_pair") != 0 && strcmp(candidate, "sdpa_fwd_bf16_d128") != 0 &&
-      strcmp(candidate, "sdpa_bf16_generic") != 0)
+      strcmp(candidate, "sdpa_fwd_bf16_d128_bn64") != 0 && strcmp(candidate, "sdpa_bf16_generic") != 0)
     return contract(std::string("unknown attention candidate ") + candidate);
   if (candidate && !tc_ok && strcmp(candidate, "sdpa_bf16_generic") != 0)
     return unsupported(std::string("candidate ") + candidate + " does not take this shape or alignment");
-  if (tc_ok && candidate && strcmp(candidate, "sdpa_fwd_bf16_d128_pair") == 0) {
+  if (tc_ok && (!candidate || strcmp(candidate, "sdpa_fwd_bf16_d128_pair") == 0)) {
     rc = launch_sdpa_bf16_d128_pair(s, st, pq, pk, pv, po, b * h, tq, tk, c);
-  } else if (tc_ok && (!candidate || strcmp(candidate, "sdpa_fwd_bf16_d128") == 0)) {
+  } else if (tc_ok && strcmp(candidate, "sdpa_fwd_bf16_d128_bn64") == 0) {
+    rc = launch_sdpa_bf16_d128_bn64(s, st, pq, pk, pv, po, b * h, tq, tk, c);
+  } else if (tc_ok && strcmp(candidate, "sdpa_fwd_bf16_d128") == 0) {
     rc = launch_sdpa_bf16_d128(s, st, pq, pk, pv, po, b * h, tq, tk, c);
   } else {
     const bool bf = dt == TB_BF16;

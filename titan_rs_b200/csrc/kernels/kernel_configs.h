@@ -24,3 +24,10 @@
 #define TB_SDPA2_THREADS 320
 #define TB_SDPA2_BARRIER_BYTES 256
 #define TB_SDPA2_SMEM_BYTES (6 * 32768 + TB_SDPA2_BARRIER_BYTES + 1024)
+
+// 64-key-tile SDPA (sdpa_bf16_bn64.cu), two CTAs per SM: Q 32 KB + K ring 2x16 KB +
+// V ring 2x16 KB + barriers; 256 TMEM columns per CTA.
+#define TB_SDPA3_BN 64
+#define TB_SDPA3_THREADS 192
+#define TB_SDPA3_BARRIER_BYTES 256
+#define TB_SDPA3_SMEM_BYTES (32768 + 4 * 16384 + TB_SDPA3_BARRIER_BYTES + 1024)

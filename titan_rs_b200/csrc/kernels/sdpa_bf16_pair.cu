@@ -17,21 +17,21 @@
 //                  O_X    += P_X(j) V_j  (TS: P read from TMEM, V MN-major in shared memory)
 //   warps 2..5   softmax group for tile A, warps 6..9 for tile B (each group covers the
 //                four TMEM lane quarters, since warp w reaches lanes 32*(w%4)..): one query row per
-//                thread (its TMEM lane). The S row is streamed from TMEM once in
-//                32-column chunks and exponentiated against the current reference max
-//                (one FFMA each; one exponential in four on the FMA pipe, the rest on
-//                the MUFU); P is held in registers, then written back as bf16 pairs
-//                over the first 64 columns of the same S region, where the TS-MMA
-//                reads it. The reference max moves (O is rescaled in TMEM and the row
-//                recomputed from the still-intact S) only when the row max grows by
-//                more than 2^8, so P stays below 256 and the result is the exact online
-//                softmax.
+//                thread (its TMEM lane). Per key tile, pass 1 reads the 128 scores
+//                from TMEM in 32-column chunks for the row max; pass 2 exponentiates
+//                against the reference max (packed FFMA2 for s*scale - m; a share of
+//                the exponentials on the FMA/ALU pipes, the rest on the MUFU) and
+//                writes P as bf16 pairs over the first 64 columns of the same S
+//                region, where the TS-MMA reads it. The reference max moves, and O is
+//                rescaled in TMEM, only when the row max grows by more than 2^8, so
+//                P stays below 256 and the result is the exact online softmax.
 // Ordering: tcgen05.commit arrives once ALL earlier MMAs of the issuing thread are
 // done, so "S_X(j) ready" also means PV_X(j-1) finished reading P_X and writing O_X:
 // the softmax warps may then overwrite S/P and rescale O without further waits.
 //
 // Every wait is bounded; on a timeout the kernel records a code in `status`,
 // drains its copies and MMAs, frees TMEM and exits.
+#include "attn_math.cuh"
 #include "kernel_configs.h"
 #include "sm100.cuh"
 
@@ -45,7 +45,11 @@ constexpr int HALF_BYTES = TILE_BYTES / 2;
 constexpr int THREADS = TB_SDPA2_THREADS;
 constexpr uint32_t IDESC_S = idesc_bf16_f32(BM, BN, false);
 constexpr uint32_t IDESC_O = idesc_bf16_f32(BM, HD, true);  // B = V, MN-major
-constexpr float kLazyRescaleLog2 = 8.0f;
+// The common path keeps the reference max of a row until a key tile's row sum of
+// exponentials exceeds this; every P of the row is then at most 2^32 (bf16 and
+// fp32 keep their relative precision at any scale, and O stays far from fp32
+// overflow: at most 2^38 times max|V| over 64 key tiles of 2^32 each).
+constexpr float kSumLimit = 4294967296.0f;
 
 struct Barriers {
   uint64_t q_full;
@@ -70,28 +74,6 @@ constexpr uint32_t kFailProducer = 0x50010000u;
 constexpr uint32_t kFailMma = 0x50020000u;
 constexpr uint32_t kFailSoftmax = 0x50030000u;
 
-__device__ __forceinline__ float exp2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// 2^x on the FMA pipe, for x <= 8 (the lazy-rescale bound): Cody-Waite split
-// x = n + f with n = floor(x), f in [0, 1); 2^f from a degree-3 polynomial
-// fitted for this kernel (weighted least squares toward minimax relative error
-// on [0, 1), p(0) = 1; max relative error 8.6e-5, below the 2^-9 rounding of the
-// bf16 P it feeds); 2^n added to the exponent field. Inputs below -127 give 0
-// or a denormal, which bf16 P and the row sum treat as zero.
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -127.0f);
-  const float n = floorf(x);
-  const float f = x - n;
-  float p = fmaf(0.0770670622587204f, f, 0.22764495015144348f);
-  p = fmaf(p, f, 0.6951168179512024f);
-  p = fmaf(p, f, 1.0f);
-  return __int_as_float(__float_as_int(p) + (static_cast<int>(n) << 23));
-}
-
 // Makes later uses of registers filled by tcgen05.ld depend on the preceding
 // tcgen05.wait::ld (the two asm statements share no operands otherwise).
 template <int N>
@@ -100,68 +82,120 @@ __device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
   for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
 }
 
-// One pass over a 128-column S row in TMEM: applies the causal/tail mask,
-// returns the row sum of p = 2^(s*scale_log2 + neg_m) (bf16-packed into
-// `packed`, one exponential in four on the FMA pipe) and updates `mraw`, the
-// row max of the raw scores. With exps == false only the max is computed.
-// `valid` = number of leading columns of this key tile the row may see
-// (min(Tk, q+1) - kv0 when causal, Tk - kv0 otherwise; >= BN means all).
-__device__ __forceinline__ float softmax_row_pass(uint32_t s_tmem, int valid, float scale_log2, float neg_m, bool exps,
-                                                  uint32_t (&packed)[BN / 2], float& mraw) {
-  // Four independent max / sum accumulators keep the reductions off one long
-  // dependency chain.
-  float rs[4] = {0.f, 0.f, 0.f, 0.f};
-  float mx[4] = {mraw, -INFINITY, -INFINITY, -INFINITY};
-  const bool need_mask = valid < BN;
+// Sets columns >= lim of a 32-column S chunk to -inf (its exponential is exactly 0
+// on both exponential paths).
+__device__ __forceinline__ void mask_chunk(uint32_t (&cur)[32], int lim) {
 #pragma unroll
+  for (int i = 0; i < 32; ++i)
+    if (i >= lim) cur[i] = __float_as_uint(-INFINITY);
+}
+
+// Masks the chunk when the tile needs it and folds it into four max accumulators.
+__device__ __forceinline__ void mask_max_chunk(uint32_t (&cur)[32], int lim, bool need_mask, float (&mx)[4]) {
+  if (need_mask) mask_chunk(cur, lim);
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) mx[q] = fmax3f(mx[q], __uint_as_float(cur[i + 2 * q]), __uint_as_float(cur[i + 2 * q + 1]));
+  }
+}
+
+// p = 2^(s * scale_log2 - m) for one 32-column S chunk (kPolyPairsOf8 pairs in
+// every 8 on the FMA/ALU pipes, the rest on the MUFU), added to the four packed
+// row-sum accumulators and stored as 16 columns of bf16 pairs at p_tmem.
+template <int kPolyPairsOf8>
+__device__ __forceinline__ void exp_chunk_store(const uint32_t (&cur)[32], float2 scale2, float2 neg_m2, float2 (&rs)[4],
+                                                uint32_t p_tmem) {
+  uint32_t packed[16];
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    const float2 x = __ffma2_rn(make_float2(__uint_as_float(cur[i]), __uint_as_float(cur[i + 1])), scale2, neg_m2);
+    const float2 p = ((i >> 1) & 7) < kPolyPairsOf8 ? exp2_poly2(x) : make_float2(exp2_mufu(x.x), exp2_mufu(x.y));
+    rs[(i >> 1) & 3] = __fadd2_rn(rs[(i >> 1) & 3], p);
+    packed[i / 2] = pack_bf16x2(p.x, p.y);
+  }
+  tmem_st_x16(p_tmem, packed);
+}
+
+// Rescale of O by alpha for one row: 128 fp32 columns in TMEM.
+__device__ __forceinline__ void rescale_o(uint32_t o_tmem, float alpha) {
+#pragma unroll 1
+  for (int c = 0; c < HD; c += 16) {
+    uint32_t o[16];
+    tmem_ld_x16(o_tmem + c, o);
+    tmem_ld_wait();
+    reg_fence(o);
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      const float2 v =
+          __fmul2_rn(make_float2(__uint_as_float(o[i]), __uint_as_float(o[i + 1])), make_float2(alpha, alpha));
+      o[i] = __float_as_uint(v.x);
+      o[i + 1] = __float_as_uint(v.y);
+    }
+    tmem_st_x16(o_tmem + c, o);
+  }
+}
+
+// The rare path of a key tile, taken by the whole warp when some row's sum of
+// exponentials against the current reference max exceeded kSumLimit (or was not
+// finite: the first key tile, whose reference max is still -inf). S is still
+// intact in TMEM: the row max of the masked scores becomes the new reference,
+// O and l are rescaled, and P is recomputed and stored. Returns the row sum.
+// Out of line, so the common path keeps its registers.
+template <int kPolyPairsOf8>
+__device__ __noinline__ float softmax_tile_rescale(uint32_t s_tmem, uint32_t o_tmem, int valid, float scale_log2,
+                                                   bool o_live, float& m_used, float& l) {
+  const bool need_mask = valid < BN;
+  float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
   for (int c = 0; c < BN; c += 32) {
     uint32_t cur[32];
     tmem_ld_x32(s_tmem + c, cur);
     tmem_ld_wait();
     reg_fence(cur);
-    const int lim = valid - c;  // columns i >= lim of this chunk are masked
-    if (need_mask) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (i >= lim) cur[i] = __float_as_uint(-INFINITY);
-    }
-#pragma unroll
-    for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(cur[i]));
-    if (exps) {
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        const float x0 = fmaf(__uint_as_float(cur[i]), scale_log2, neg_m);
-        const float x1 = fmaf(__uint_as_float(cur[i + 1]), scale_log2, neg_m);
-        float p0 = exp2_approx(x0);
-        float p1 = (i & 2) ? exp2_poly(x1) : exp2_approx(x1);
-        if (need_mask) {
-          if (i >= lim) p0 = 0.f;
-          if (i + 1 >= lim) p1 = 0.f;
-        }
-        rs[(i >> 1) & 3] += p0 + p1;
-        packed[(c + i) / 2] = pack_bf16x2(p0, p1);
-      }
-    }
+    mask_max_chunk(cur, valid - c, need_mask, mx4);
   }
-  mraw = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-  return (rs[0] + rs[1]) + (rs[2] + rs[3]);
+  const float mx = fmaxf(fmax3f(mx4[0], mx4[1], mx4[2]), mx4[3]) * scale_log2;  // scale_log2 > 0 commutes with max
+  const float m_new = fmaxf(m_used, mx);
+  const float alpha = exp2_mufu(m_used - m_new);  // 0 when m_used was -inf; 1 when the max did not move
+  l *= alpha;
+  if (o_live) rescale_o(o_tmem, alpha);
+  m_used = m_new;
+  const float2 scale2 = make_float2(scale_log2, scale_log2), neg_m2 = make_float2(-m_new, -m_new);
+  float2 rs4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+  uint32_t ca[32], cb[32];
+  // P chunk c lands on S columns [16c, 16c + 16): load each pair of chunks before
+  // storing any P over it.
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 64) {
+    tmem_ld_x32(s_tmem + c, ca);
+    tmem_ld_x32(s_tmem + c + 32, cb);
+    tmem_ld_wait();
+    reg_fence(ca);
+    reg_fence(cb);
+    if (need_mask) {
+      mask_chunk(ca, valid - c);
+      mask_chunk(cb, valid - c - 32);
+    }
+    exp_chunk_store<kPolyPairsOf8>(ca, scale2, neg_m2, rs4, s_tmem + c / 2);
+    exp_chunk_store<kPolyPairsOf8>(cb, scale2, neg_m2, rs4, s_tmem + c / 2 + 16);
+  }
+  const float2 r = __fadd2_rn(__fadd2_rn(rs4[0], rs4[1]), __fadd2_rn(rs4[2], rs4[3]));
+  return r.x + r.y;
 }
 
-// P as bf16 pairs into columns [0, 64) of the S region (warp-collective).
-__device__ __forceinline__ void store_p(uint32_t s_tmem, const uint32_t (&packed)[BN / 2]) {
+// Common-path exponentials of one 32-column chunk into 16 packed bf16 pairs (not
+// yet stored), with the row sum accumulated.
+template <int kPolyPairsOf8>
+__device__ __forceinline__ void exp_chunk(const uint32_t (&cur)[32], float2 scale2, float2 neg_m2, float2 (&rs)[4],
+                                          uint32_t* packed) {
 #pragma unroll
-  for (int c = 0; c < BN / 2; c += 16) tmem_st_x16(s_tmem + c, *reinterpret_cast<const uint32_t(*)[16]>(&packed[c]));
-}
-
-// The rare recompute after the reference max moved: exponentials against the
-// new max, P written to TMEM here. Kept out of line (with its own P registers)
-// so the common path keeps its registers.
-__device__ __noinline__ float softmax_row_recompute_store(uint32_t s_tmem, int valid, float scale_log2, float neg_m) {
-  uint32_t packed[BN / 2];
-  float unused = -INFINITY;
-  const float rs = softmax_row_pass(s_tmem, valid, scale_log2, neg_m, true, packed, unused);
-  store_p(s_tmem, packed);
-  return rs;
+  for (int i = 0; i < 32; i += 2) {
+    const float2 x = __ffma2_rn(make_float2(__uint_as_float(cur[i]), __uint_as_float(cur[i + 1])), scale2, neg_m2);
+    const float2 p = ((i >> 1) & 7) < kPolyPairsOf8 ? exp2_poly2(x) : make_float2(exp2_mufu(x.x), exp2_mufu(x.y));
+    rs[(i >> 1) & 3] = __fadd2_rn(rs[(i >> 1) & 3], p);
+    packed[i / 2] = pack_bf16x2(p.x, p.y);
+  }
 }
 
 __device__ __forceinline__ void load_tile(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int row0, int bh) {
@@ -177,14 +211,41 @@ __device__ __forceinline__ uint64_t v_desc(uint32_t tile_addr, int k) {
   return sdesc_sw128(tile_addr + k * 2048, HALF_BYTES, 1024);
 }
 
+// Moves a shared-memory descriptor's start address by `units` 16-byte units. The
+// start-address field is the descriptor's low 14 bits and every address here is
+// below 256 KB, so a 32-bit add on the low word never carries out of the field.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t units) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(static_cast<uint32_t>(d) + units), "r"(static_cast<uint32_t>(d >> 32)));
+  return r;
+}
+
+// O (+)= P V for one 128-key tile: P from TMEM (bf16 pairs, 8 columns per 16 keys),
+// V MN-major in shared memory (16 keys = 2 KB per slice).
+__device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint64_t vd, bool accumulate) {
+  umma_bf16_ts(o_tmem, p_tmem, vd, IDESC_O, accumulate ? 1u : 0u);
+#pragma unroll
+  for (int k = 1; k < BN / 16; ++k) umma_bf16_ts(o_tmem, p_tmem + k * 8, desc_add(vd, k * (2048 >> 4)), IDESC_O, 1u);
+}
+
+// S = Q K^T for one 128-key tile: both operands K-major, 16 dims per slice (two
+// 64-dim boxes of HALF_BYTES; 32 bytes per slice inside a box).
+__device__ __forceinline__ void issue_s(uint32_t s_tmem, uint64_t qd, uint64_t kd) {
+#pragma unroll
+  for (int k = 0; k < HD / 16; ++k) {
+    const uint32_t off = (k >> 2) * (HALF_BYTES >> 4) + (k & 3) * 2;
+    umma_bf16_ss(s_tmem, desc_add(qd, off), desc_add(kd, off), IDESC_S, k > 0 ? 1u : 0u);
+  }
+}
+
 }  // namespace
 
 // q, k, v, o: [BH, T, 128] bf16 (3-D tensor maps {128, T, BH}, box {64, 128, 1}).
 // scale_log2 = log2(e) / sqrt(D).
-extern "C" __global__ void __launch_bounds__(THREADS, 1)
-    sdpa_fwd_bf16_d128_pair(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
-                            const __grid_constant__ CUtensorMap tmap_v, __nv_bfloat16* __restrict__ out, int Tq,
-                            int Tk, int causal, float scale_log2, uint32_t* status) {
+template <int kPolyPairsOf8>
+__device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const CUtensorMap& tmap_k,
+                                               const CUtensorMap& tmap_v, __nv_bfloat16* __restrict__ out, int Tq,
+                                               int Tk, int causal, float scale_log2, uint32_t* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Barriers* bars = reinterpret_cast<Barriers*>(smem + OFF_BAR);
@@ -264,41 +325,41 @@ extern "C" __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
+      // One lane issues every MMA, so its instruction stream is kept short: all
+      // descriptors are formed here once, and each MMA only adds a compile-time
+      // K-slice offset to the low word of one of them.
       bool ok = mbar_wait(&bars->q_full, 0);
       if (!ok) report_status(status, kFailMma | 1);
-      const uint32_t q_addr[2] = {smem_addr(smem + OFF_Q), smem_addr(smem + OFF_Q + TILE_BYTES)};
-      const int n_tiles[2] = {n_a, n_b};
+      const uint64_t qd_a = kmajor_desc(smem_addr(smem + OFF_Q), 0);
+      const uint64_t qd_b = kmajor_desc(smem_addr(smem + OFF_Q + TILE_BYTES), 0);
+      const uint64_t kd0 = kmajor_desc(smem_addr(smem + OFF_K), 0);
+      const uint64_t vd0 = v_desc(smem_addr(smem + OFF_V), 0);
       // j = key tile whose scores are issued this iteration; PV of tile j-1 goes first.
       for (int j = 0; j <= n_b && ok; ++j) {
         const int st = j & 1, pst = (j - 1) & 1;
         const uint32_t ph = (j >> 1) & 1, pph = ((j - 1) >> 1) & 1;
-        bool k_ready = false, v_ready = false;
-        for (int x = 0; x < 2 && ok; ++x) {
-          // O_x += P_x(j-1) V_{j-1}
-          if (j >= 1 && j - 1 < n_tiles[x]) {
-            if (!v_ready) {
-              if (!mbar_wait(&bars->v_full[pst], pph)) {
-                report_status(status, kFailMma | 2);
-                ok = false;
-                break;
-              }
-              v_ready = true;
-            }
+        const uint64_t kd = desc_add(kd0, st * (TILE_BYTES >> 4));
+        const uint64_t vd = desc_add(vd0, pst * (TILE_BYTES >> 4));
+        const bool pv_a = j >= 1 && j - 1 < n_a, pv_b = j >= 1 && j - 1 < n_b;  // n_a <= n_b
+        const bool s_a = j < n_a, s_b = j < n_b;
+        if (pv_b && !mbar_wait(&bars->v_full[pst], pph)) {
+          report_status(status, kFailMma | 2);
+          ok = false;
+          break;
+        }
+        bool k_ready = false;
+        // Tile A: O_A += P_A(j-1) V_{j-1}, then S_A(j) = Q_A K_j^T; then the same for tile B.
+        for (int x = 0; x < 2; ++x) {
+          if (x ? pv_b : pv_a) {
             if (!mbar_wait(&bars->p_full[x], (j - 1) & 1)) {
               report_status(status, kFailMma | 3);
               ok = false;
               break;
             }
             tc_fence_after_sync();
-            const uint32_t v_addr = smem_addr(smem + OFF_V + pst * TILE_BYTES);
-            const uint32_t p_tmem = tmem + x * BN;  // P_x: first 64 columns of S_x (bf16 pairs)
-            const uint32_t o_tmem = tmem + (2 + x) * BN;
-#pragma unroll
-            for (int k = 0; k < BN / 16; ++k)
-              umma_bf16_ts(o_tmem, p_tmem + k * 8, v_desc(v_addr, k), IDESC_O, (j - 1 > 0) || (k > 0));
+            issue_pv(tmem + (2 + x) * BN, tmem + x * BN, vd, j - 1 > 0);
           }
-          // S_x(j) = Q_x K_j^T
-          if (j < n_tiles[x]) {
+          if (x ? s_b : s_a) {
             if (!k_ready) {
               if (!mbar_wait(&bars->k_full[st], ph)) {
                 report_status(status, kFailMma | 4);
@@ -308,15 +369,12 @@ extern "C" __global__ void __launch_bounds__(THREADS, 1)
               k_ready = true;
               tc_fence_after_sync();
             }
-            const uint32_t k_addr = smem_addr(smem + OFF_K + st * TILE_BYTES);
-#pragma unroll
-            for (int k = 0; k < HD / 16; ++k)
-              umma_bf16_ss(tmem + x * BN, kmajor_desc(q_addr[x], k), kmajor_desc(k_addr, k), IDESC_S, k > 0);
+            issue_s(tmem + x * BN, x ? qd_b : qd_a, kd);
             umma_commit(&bars->s_full[x]);
           }
         }
         if (!ok) break;
-        if (v_ready) umma_commit(&bars->v_empty[pst]);
+        if (pv_b) umma_commit(&bars->v_empty[pst]);
         if (k_ready) umma_commit(&bars->k_empty[st]);
       }
       umma_commit(&bars->o_final);
@@ -334,6 +392,7 @@ extern "C" __global__ void __launch_bounds__(THREADS, 1)
     const int qt = qt0 + x;
     const int q_row = qt * BM + r;
     const int n = x ? n_b : n_a;
+    const float2 scale2 = make_float2(scale_log2, scale_log2);
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
@@ -343,39 +402,48 @@ extern "C" __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after_sync();
-      const int kv0 = j * BN;
-      const int valid = (causal ? min(Tk, q_row + 1) : Tk) - kv0;  // visible leading keys of this tile
-      // Stream the S row in 32-column chunks (the next chunk's TMEM load overlaps
-      // this chunk's math), exponentiating against the current reference max.
-      // P stays in registers until the row is known not to need a larger max.
+      const int valid = (causal ? min(Tk, q_row + 1) : Tk) - j * BN;  // visible leading keys of this tile
+      const bool need_mask = valid < BN;
+      // One streamed pass: exponentials against the current reference max, P held
+      // in registers until the row sums show that no P exceeds kSumLimit.
+      const float2 neg_m2 = make_float2(-m_used, -m_used);
+      float2 rs4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       uint32_t packed[BN / 2];
-      float mraw = -INFINITY;
-      float rs = softmax_row_pass(s_tmem, valid, scale_log2, -m_used, m_used != -INFINITY, packed, mraw);
-      const float mx = mraw * scale_log2;  // scale_log2 > 0 commutes with max
-      const bool grow = mx > m_used + kLazyRescaleLog2;
-      if (__any_sync(0xffffffffu, grow)) {
-        const float m_new = grow ? mx : m_used;
-        const float alpha = exp2_approx(m_used - m_new);
-        l *= alpha;
-        if (j > 0) {
-          // O_x = sum_{t<j} P_x(t) V_t is complete (S_x(j) was committed after PV_x(j-1)).
-#pragma unroll 1
-          for (int c = 0; c < HD; c += 16) {
-            uint32_t o[16];
-            tmem_ld_x16(o_tmem + c, o);
-            tmem_ld_wait();
-            reg_fence(o);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st_x16(o_tmem + c, o);
-          }
-        }
-        m_used = m_new;
-        // S is still intact in TMEM (P is written below): recompute against the new max.
-        rs = softmax_row_recompute_store(s_tmem, valid, scale_log2, -m_used);
+      uint32_t ca[32], cb[32];
+      tmem_ld_x32(s_tmem, ca);
+      tmem_ld_x32(s_tmem + 32, cb);
+      tmem_ld_wait();
+      reg_fence(ca);
+      reg_fence(cb);
+      if (need_mask) {
+        mask_chunk(ca, valid);
+        mask_chunk(cb, valid - 32);
+      }
+      exp_chunk<kPolyPairsOf8>(ca, scale2, neg_m2, rs4, &packed[0]);
+      tmem_ld_x32(s_tmem + 64, ca);
+      exp_chunk<kPolyPairsOf8>(cb, scale2, neg_m2, rs4, &packed[16]);
+      tmem_ld_x32(s_tmem + 96, cb);
+      tmem_ld_wait();
+      reg_fence(ca);
+      reg_fence(cb);
+      if (need_mask) {
+        mask_chunk(ca, valid - 64);
+        mask_chunk(cb, valid - 96);
+      }
+      exp_chunk<kPolyPairsOf8>(ca, scale2, neg_m2, rs4, &packed[32]);
+      exp_chunk<kPolyPairsOf8>(cb, scale2, neg_m2, rs4, &packed[48]);
+      const float2 rsum = __fadd2_rn(__fadd2_rn(rs4[0], rs4[1]), __fadd2_rn(rs4[2], rs4[3]));
+      float rs = rsum.x + rsum.y;
+      // rs <= kSumLimit bounds every P of the row by kSumLimit (all terms are >= 0);
+      // otherwise (or not finite) the warp takes the rescale path.
+      if (__any_sync(0xffffffffu, !(rs <= kSumLimit))) {
+        // O_x = sum_{t<j} P_x(t) V_t is complete (S_x(j) was committed after PV_x(j-1)).
+        rs = softmax_tile_rescale<kPolyPairsOf8>(s_tmem, o_tmem, valid, scale_log2, j > 0, m_used, l);
       } else {
         // P_x(j) as bf16 pairs into columns [0, 64) of S_x, where the TS-MMA reads it.
-        store_p(s_tmem, packed);
+#pragma unroll
+        for (int c = 0; c < BN / 2; c += 16)
+          tmem_st_x16(s_tmem + c, *reinterpret_cast<const uint32_t(*)[16]>(&packed[c]));
       }
       l += rs;
       tmem_st_wait();
@@ -396,6 +464,7 @@ extern "C" __global__ void __launch_bounds__(THREADS, 1)
           uint32_t o[32];
           tmem_ld_x32(o_tmem + c, o);
           tmem_ld_wait();
+          reg_fence(o);
           if (q_row < Tq) {
             uint4* d4 = reinterpret_cast<uint4*>(dst + c);
 #pragma unroll
@@ -421,3 +490,15 @@ extern "C" __global__ void __launch_bounds__(THREADS, 1)
     tmem_dealloc(tmem, 512);
   }
 }
+
+#define TB_SDPA_PAIR_ENTRY(name, poly)                                                                              \
+  extern "C" __global__ void __launch_bounds__(THREADS, 1)                                                       \
+      name(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,             \
+           const __grid_constant__ CUtensorMap tmap_v, __nv_bfloat16* __restrict__ out, int Tq, int Tk, int causal, \
+           float scale_log2, uint32_t* status) {                                                                 \
+    sdpa_pair_body<poly>(tmap_q, tmap_k, tmap_v, out, Tq, Tk, causal, scale_log2, status);                       \
+  }
+
+// Two score pairs in every eight take the FMA/ALU exponential (measured fastest of
+// 1, 2 and 3 on the C4 workload).
+TB_SDPA_PAIR_ENTRY(sdpa_fwd_bf16_d128_pair, 2)
