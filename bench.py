@@ -800,7 +800,8 @@ def main(argv=None) -> int:
     else:
         peak = float(peaks.get("bf16_tflops", PEAK_FALLBACK["bf16_tflops"]))
         r_unit = "TFLOP/s"
-    traffic = TRAFFIC_PER_LAUNCH.get(args.op)
+    # Captured on the 1-GPU configuration of each kernel; a shard has other traffic.
+    traffic = TRAFFIC_PER_LAUNCH.get(wl.kernel) if wl.world == 1 and not args.small else None
 
     # End to end through the C ABI with pinned host buffers.
     e2e_ms = e2e_value = None
@@ -850,8 +851,15 @@ def main(argv=None) -> int:
     return 0
 
 
-# DRAM bytes per launch from one ncu capture (profiles/), or None when not yet captured.
-TRAFFIC_PER_LAUNCH: dict = {}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one full-size launch of
+# each default kernel at N=1, from the 1-pass ncu captures summarised in
+# profiles/dram_traffic_full_size.md. Kernels not listed report null.
+TRAFFIC_PER_LAUNCH: dict = {
+    "softmax_f32_warp32": 536.99e6 + 480.30e6,
+    "gemm_bf16_tn": 997.83e6 + 127.29e6,
+    "sdpa_fwd_bf16_d128_pair": 806.43e6 + 253.34e6,
+    "conv2d_fprop_bf16_nhwc": 104.21e6 + 53.92e6,
+}
 
 
 if __name__ == "__main__":

@@ -347,7 +347,14 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
           ok = false;
           break;
         }
-        bool k_ready = false;
+        // K_j was loaded long before P_A(j-1) is ready: wait for it first, so that
+        // S_A(j) issues right behind PV_A(j-1).
+        const bool k_ready = s_b;
+        if (k_ready && !mbar_wait(&bars->k_full[st], ph)) {
+          report_status(status, kFailMma | 4);
+          ok = false;
+          break;
+        }
         // Tile A: O_A += P_A(j-1) V_{j-1}, then S_A(j) = Q_A K_j^T; then the same for tile B.
         for (int x = 0; x < 2; ++x) {
           if (x ? pv_b : pv_a) {
@@ -360,15 +367,7 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
             issue_pv(tmem + (2 + x) * BN, tmem + x * BN, vd, j - 1 > 0);
           }
           if (x ? s_b : s_a) {
-            if (!k_ready) {
-              if (!mbar_wait(&bars->k_full[st], ph)) {
-                report_status(status, kFailMma | 4);
-                ok = false;
-                break;
-              }
-              k_ready = true;
-              tc_fence_after_sync();
-            }
+            tc_fence_after_sync();
             issue_s(tmem + x * BN, x ? qd_b : qd_a, kd);
             umma_commit(&bars->s_full[x]);
           }
