@@ -272,15 +272,22 @@ class GemmWorkload(Workload):
         self.ta = _tensor(self.tb, self.da, DType.BF16, (M, K))
         self.tbm = _tensor(self.tb, self.db, DType.BF16, (self.n_local, K))
         self.tc = _tensor(self.tb, self.dc, DType.BF16, (M, Nn))
+        # N > 1: "p2p" (default) = one fused kernel storing this rank's columns into every
+        # rank's registered C over NVLink; "nccl" = GEMM into slot `rank` of a [p][M][N/p]
+        # gather buffer, NCCL all-gather, re-layout kernel.
+        self.allgather = os.environ.get("TITAN_B200_ALLGATHER", "p2p")
+        if self.allgather not in ("p2p", "nccl"):
+            raise SystemExit("TITAN_B200_ALLGATHER must be p2p or nccl")
         if self.world > 1:
-            # Column shard lands in slot `rank` of a [p][M][N/p] gather buffer, then all-gather + re-layout.
-            self.dws = self.s.allocate(self.c_bytes)
+            self.dws = self.s.allocate(self.c_bytes) if self.allgather == "nccl" else None
             self.dc_local = self.s.allocate(M * self.n_local * 2)
             self.tc_local = _tensor(self.tb, self.dc_local, DType.BF16, (M, self.n_local))
             self.h_a = TensorHandle(self.s, self.da, DType.BF16, (M, K), contiguous_strides((M, K)))
             self.h_b = TensorHandle(self.s, self.db, DType.BF16, (self.n_local, K),
                                     contiguous_strides((self.n_local, K)))
             self.h_c = TensorHandle(self.s, self.dc, DType.BF16, (M, Nn), contiguous_strides((M, Nn)))
+            if self.allgather == "p2p":
+                self.comm.register_buffer(self.st, self.dc)  # collective: every rank maps every rank's C
         self.attrs = (N.Attr * 1)()
         self._key = b"transpose_rhs"
         self.attrs[0].key = self._key
@@ -328,9 +335,13 @@ class GemmWorkload(Workload):
         return self.c_bytes
 
     def config(self):
-        return {"workload": f"C3 bf16 GEMM M=N=K={self.M}, A row-major N(0,1), B column-major N(0,1/K), seed 2",
-                "M": self.M, "N": self.N, "K": self.K, "parallelism": f"N-shard{self.world}" if self.world > 1
-                else "single", "l2": "inputs 256 MiB > 126 MB L2"}
+        cfg = {"workload": f"C3 bf16 GEMM M=N=K={self.M}, A row-major N(0,1), B column-major N(0,1/K), seed 2",
+               "M": self.M, "N": self.N, "K": self.K, "parallelism": f"N-shard{self.world}" if self.world > 1
+               else "single", "l2": "inputs 256 MiB > 126 MB L2"}
+        if self.world > 1:
+            cfg["allgather"] = ("fused gemm_bf16_tn_allgather: NVLink peer stores into registered C"
+                                if self.allgather == "p2p" else "NCCL all-gather + re-layout kernel")
+        return cfg
 
     def cpu_sample(self, budget_s):
         import oracle

@@ -284,10 +284,25 @@ tb_status tb_comm_all_gather(tb_comm* comm, tb_stream* stream, tb_buffer* send, 
 /* Device-side barrier across the communicator (a 1-element all-reduce). */
 tb_status tb_comm_barrier(tb_comm* comm, tb_stream* stream);
 
+/* No counterpart in the reference, whose all_gather concatenates host vectors
+ * (titan-distributed/src/lib.rs:95-99). Collective: every rank calls it with its own
+ * buffer, in the same order. Maps each rank's buffer into every other rank's
+ * address space (CUDA IPC, peer access over NVLink) so that operators such as
+ * tb_op_gemm_sharded can store into the peers' copies directly. Synchronizes
+ * `stream`. The buffer stays retained until tb_comm_deregister_buffer or
+ * tb_comm_release; all ranks must deregister before any rank frees its buffer. */
+tb_status tb_comm_register_buffer(tb_comm* comm, tb_stream* stream, tb_buffer* buffer);
+tb_status tb_comm_deregister_buffer(tb_comm* comm, tb_buffer* buffer);
+
 /* N-sharded GEMM: this rank owns output columns [rank*N/p, (rank+1)*N/p).
  * lhs is the full A[M,K]; rhs_shard is B's shard as [N/p, K] (column-major B);
- * output is the full C[M,N] on every rank after the call. `workspace` holds
- * p*M*(N/p) elements of the output dtype. */
+ * output is the full C[M,N] on every rank after the call.
+ * When the output buffer is registered (tb_comm_register_buffer) on every rank,
+ * one fused kernel (gemm_bf16_tn_allgather) stores this rank's columns into all
+ * ranks' C over NVLink between two barriers, and `workspace` may be NULL.
+ * Otherwise `workspace` holds p*M*(N/p) elements of the output dtype: the GEMM
+ * fills this rank's slot, NCCL all-gathers the slots and a layout kernel writes C.
+ * Every rank must take the same form. */
 tb_status tb_op_gemm_sharded(tb_comm* comm, tb_stream* stream, const tb_tensor* lhs, const tb_tensor* rhs_shard,
                              const tb_tensor* output, tb_buffer* workspace, tb_event** out);
 

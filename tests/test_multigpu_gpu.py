@@ -60,6 +60,33 @@ def test_one_rank_sharded_gemm_equals_single_gpu_gemm():
     s.close()
 
 
+def test_one_rank_fused_sharded_gemm_equals_single_gpu_gemm():
+    """A registered output takes the fused kernel (gemm_bf16_tn_allgather); with one rank
+    it must equal the plain whole-K GEMM bit for bit, call after call."""
+    s = tb.Session(0)
+    rt = tb.Runtime(s)
+    m, n, k = 640, 1280, 1536
+    a, b = _gemm_inputs(m, n, k, seed=23)
+    ref = _reference_c(s, rt, a, b)
+    coll = D.NcclCollective(s, D.new_comm_id(), 1, 0, timeout_ms=20000)
+    ta = tb.TensorHandle.from_numpy(s, a, DType.BF16, rt.stream)
+    tbb = tb.TensorHandle.from_numpy(s, b, DType.BF16, rt.stream)
+    c = tb.TensorHandle.allocate(s, DType.BF16, (m, n))
+    coll.register_buffer(rt.stream, c.buffer)
+    with pytest.raises(tb.HalError, match="already registered"):
+        coll.register_buffer(rt.stream, c.buffer)
+    for _ in range(2):
+        coll.sharded_gemm(rt.stream, ta, tbb, c, None)
+        s.synchronize(rt.stream)
+        assert tb.last_candidate() == "gemm_bf16_tn_allgather"
+        np.testing.assert_array_equal(c.to_numpy(), ref)
+    coll.deregister_buffer(c.buffer)
+    with pytest.raises(tb.HalError, match="not registered"):
+        coll.deregister_buffer(c.buffer)
+    coll.close()
+    s.close()
+
+
 def _device_count() -> int:
     try:
         return len(tb.enumerate_devices())
@@ -102,6 +129,26 @@ def _rank_main(rank, world, q_in, q_out, mode):
             coll.barrier(rt.stream)
             s.synchronize(rt.stream)
             q_out.put((rank, ok_gemm and ok_gather))
+        elif mode == "gemm_p2p":
+            # Fused GEMM + all-gather into registered outputs, twice with different inputs.
+            m, n, k = 520, 1536, 1024  # M is not a multiple of the 128-row tile
+            lo, hi = Dm.even_shard(n, world, rank)
+            c = tbm.TensorHandle.allocate(s, DType.BF16, (m, n))
+            coll.register_buffer(rt.stream, c.buffer)
+            ok = True
+            for seed in (31, 32):
+                a, b = _gemm_inputs(m, n, k, seed=seed)
+                ref = _reference_c(s, rt, a, b)
+                ta = tbm.TensorHandle.from_numpy(s, a, DType.BF16, rt.stream)
+                tbs = tbm.TensorHandle.from_numpy(s, np.ascontiguousarray(b[lo:hi]), DType.BF16, rt.stream)
+                coll.sharded_gemm(rt.stream, ta, tbs, c, None)
+                s.synchronize(rt.stream)
+                ok = ok and tbm.last_candidate() == "gemm_bf16_tn_allgather"
+                ok = ok and bool(np.array_equal(c.to_numpy(), ref))
+            coll.barrier(rt.stream)
+            s.synchronize(rt.stream)
+            coll.deregister_buffer(c.buffer)
+            q_out.put((rank, ok))
         else:
             # Departure between steps: rank 1 announces it leaves and exits with nothing in flight;
             # rank 0 checks the announcement on the host before its next collective and stops.
@@ -137,6 +184,11 @@ def _spawn(world, mode):
 @pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")
 def test_two_rank_sharded_gemm_and_all_gather():
     assert _spawn(2, "gemm") == {0: True, 1: True}
+
+
+@pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")
+def test_two_rank_fused_sharded_gemm_over_peer_stores():
+    assert _spawn(2, "gemm_p2p") == {0: True, 1: True}
 
 
 @pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")

@@ -2,6 +2,13 @@
 // (projects/titan-distributed/src/lib.rs:95-99, LocalRing :129-134) on device
 // buffers through NCCL, plus the N-sharded GEMM that uses it.
 //
+// The sharded GEMM has two forms. With an output buffer registered on every rank
+// (tb_comm_register_buffer: CUDA IPC mappings of each rank's buffer in every other
+// rank), one fused kernel computes this rank's column block and stores each output
+// chunk straight into every rank's row-major C over NVLink, between two barriers.
+// Otherwise the GEMM writes a [p][M][N/p] workspace slot, NCCL all-gathers it in
+// place and a layout kernel writes the row-major C.
+//
 // NCCL is opened with dlopen like the CUDA driver, so the library still loads
 // where NCCL is absent. Communicators are non-blocking (ncclConfig_t.blocking = 0).
 // A watchdog thread per communicator watches the event recorded after each
@@ -23,6 +30,8 @@ namespace tb {
 
 tb_status launch_gemm_bf16_tn(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c, int M, int N,
                               int K, long long ldc);
+tb_status launch_gemm_bf16_tn_allgather(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, const CUdeviceptr* outs,
+                                        int ranks, int self, int M, int N, int K, long long ldc, long long col0);
 
 namespace {
 
@@ -76,6 +85,14 @@ tb_status nccl_error(const char* op, ncclResult_t r) {
 
 }  // namespace
 
+// A buffer registered on every rank: where each rank's copy is mapped in this process.
+struct PeerMapping {
+  Buffer* local = nullptr;            // retained while registered
+  std::vector<CUdeviceptr> base;      // per rank; this rank's entry is local->ptr
+  std::vector<uint64_t> bytes;        // per rank
+  std::vector<CUdeviceptr> opened;    // per rank: IPC mapping to close (0 for this rank)
+};
+
 struct Comm {
   Session* session = nullptr;
   ncclComm_t comm = nullptr;
@@ -90,6 +107,7 @@ struct Comm {
   bool aborted = false;
   std::string abort_reason;
   std::vector<std::pair<CUevent, std::chrono::steady_clock::time_point>> pending;
+  std::vector<PeerMapping> mappings;  // registered buffers (caller's thread only)
 };
 
 namespace {
@@ -158,6 +176,38 @@ tb_status usable(Comm* c, const char* op) {
     return set_error(TB_ERR_NCCL, op, "communicator was aborted: " + c->abort_reason);
   return TB_OK;
 }
+
+// Stream-ordered barrier: a one-element NCCL all-reduce.
+tb_status enqueue_barrier(Comm* c, Stream* st) {
+  void* p = reinterpret_cast<void*>(c->barrier_word);
+  ncclResult_t r = nccl().AllReduce(p, p, 1, ncclInt32, ncclSum, c->comm, st->raw);
+  if (r != ncclSuccess && r != ncclInProgress) return nccl_error("ncclAllReduce", r);
+  tb_status rc = settle(c, "ncclAllReduce");
+  if (rc) return rc;
+  return track(c, st);
+}
+
+void unmap(PeerMapping& m) {
+  const DriverApi* d = driver();
+  for (CUdeviceptr p : m.opened)
+    if (p && d) d->cuIpcCloseMemHandle(p);
+  m.opened.clear();
+  if (m.local) tb_buffer_release(reinterpret_cast<tb_buffer*>(m.local));
+  m.local = nullptr;
+}
+
+const PeerMapping* find_mapping(const Comm* c, const Buffer* b) {
+  for (const PeerMapping& m : c->mappings)
+    if (m.local == b) return &m;
+  return nullptr;
+}
+
+// What one rank publishes about its registered buffer.
+struct MappingRecord {
+  CUipcMemHandle handle;
+  uint64_t offset;  // of the buffer inside its allocation
+  uint64_t bytes;
+};
 
 }  // namespace
 }  // namespace tb
@@ -240,6 +290,7 @@ void tb_comm_release(tb_comm* comm) {
       d->cuEventDestroy_v2(p.first);
     }
   }
+  for (PeerMapping& m : c->mappings) unmap(m);
   if (c->comm) n.CommDestroy(c->comm);
   if (d && c->barrier_word) d->cuMemFree_v2(c->barrier_word);
   Session* s = c->session;
@@ -279,11 +330,88 @@ tb_status tb_comm_barrier(tb_comm* comm, tb_stream* stream) {
   if ((rc = check_stream(c->session, stream, &st))) return rc;
   rc = activate(c->session);
   if (rc) return rc;
-  void* p = reinterpret_cast<void*>(c->barrier_word);
-  ncclResult_t r = nccl().AllReduce(p, p, 1, ncclInt32, ncclSum, c->comm, st->raw);
-  if (r != ncclSuccess && r != ncclInProgress) return nccl_error("ncclAllReduce", r);
-  if ((rc = settle(c, "ncclAllReduce"))) return rc;
-  return track(c, st);
+  return enqueue_barrier(c, st);
+}
+
+tb_status tb_comm_register_buffer(tb_comm* comm, tb_stream* stream, tb_buffer* buffer) {
+  Comm* c = reinterpret_cast<Comm*>(comm);
+  tb_status rc = usable(c, "register");
+  if (rc) return rc;
+  Session* s = c->session;
+  Stream* st = nullptr;
+  Buffer* b = nullptr;
+  if ((rc = check_stream(s, stream, &st)) || (rc = check_buffer(s, buffer, &b))) return rc;
+  if (find_mapping(c, b)) return set_error(TB_ERR_INVALID, "register", "buffer is already registered with this communicator");
+  rc = activate(s);
+  if (rc) return rc;
+  const DriverApi* d = driver();
+  const int p = c->size;
+  PeerMapping m;
+  m.base.assign(p, 0);
+  m.bytes.assign(p, 0);
+  m.opened.assign(p, 0);
+  m.base[c->rank] = b->ptr;
+  m.bytes[c->rank] = b->bytes;
+  if (p > 1) {
+    // Publish (IPC handle of the allocation, offset, size) and gather everyone's.
+    CUdeviceptr alloc_base = 0;
+    size_t alloc_size = 0;
+    TB_CU("cuMemGetAddressRange", d->cuMemGetAddressRange_v2(&alloc_base, &alloc_size, b->ptr));
+    MappingRecord mine{};
+    TB_CU("cuIpcGetMemHandle", d->cuIpcGetMemHandle(&mine.handle, alloc_base));
+    mine.offset = b->ptr - alloc_base;
+    mine.bytes = b->bytes;
+    std::vector<MappingRecord> all(p);
+    CUdeviceptr dev = 0;
+    TB_CU("allocate", d->cuMemAlloc_v2(&dev, sizeof(MappingRecord) * p));
+    const CUdeviceptr slot = dev + sizeof(MappingRecord) * c->rank;
+    CUresult cr = d->cuMemcpyHtoDAsync_v2(slot, &mine, sizeof(mine), st->raw);
+    ncclResult_t r = ncclSuccess;
+    if (cr == CUDA_SUCCESS) {
+      r = nccl().AllGather(reinterpret_cast<const void*>(slot), reinterpret_cast<void*>(dev), sizeof(MappingRecord),
+                           ncclUint8, c->comm, st->raw);
+      if (r == ncclSuccess || r == ncclInProgress) rc = settle(c, "ncclAllGather");
+      if ((r == ncclSuccess || r == ncclInProgress) && rc == TB_OK)
+        cr = d->cuMemcpyDtoHAsync_v2(all.data(), dev, sizeof(MappingRecord) * p, st->raw);
+      if (cr == CUDA_SUCCESS) cr = d->cuStreamSynchronize(st->raw);
+    }
+    d->cuMemFree_v2(dev);
+    if (cr != CUDA_SUCCESS) return cu_error("register", cr);
+    if (r != ncclSuccess && r != ncclInProgress) return nccl_error("ncclAllGather", r);
+    if (rc) return rc;
+    for (int j = 0; j < p; ++j) {
+      if (j == c->rank) continue;
+      CUdeviceptr peer = 0;
+      cr = d->cuIpcOpenMemHandle_v2(&peer, all[j].handle, CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS);
+      if (cr != CUDA_SUCCESS) {
+        unmap(m);
+        return cu_error("cuIpcOpenMemHandle", cr);
+      }
+      m.opened[j] = peer;
+      m.base[j] = peer + all[j].offset;
+      m.bytes[j] = all[j].bytes;
+    }
+  }
+  tb_buffer_retain(buffer);
+  m.local = b;
+  c->mappings.push_back(std::move(m));
+  return TB_OK;
+}
+
+tb_status tb_comm_deregister_buffer(tb_comm* comm, tb_buffer* buffer) {
+  Comm* c = reinterpret_cast<Comm*>(comm);
+  if (!c) return set_error(TB_ERR_INVALID, "deregister", "null communicator");
+  Buffer* b = nullptr;
+  tb_status rc = check_buffer(c->session, buffer, &b);
+  if (rc) return rc;
+  for (size_t i = 0; i < c->mappings.size(); ++i) {
+    if (c->mappings[i].local != b) continue;
+    activate(c->session);
+    unmap(c->mappings[i]);
+    c->mappings.erase(c->mappings.begin() + (long)i);
+    return TB_OK;
+  }
+  return set_error(TB_ERR_INVALID, "deregister", "buffer is not registered with this communicator");
 }
 
 tb_status tb_op_gemm_sharded(tb_comm* comm, tb_stream* stream, const tb_tensor* lhs, const tb_tensor* rhs_shard,
@@ -305,9 +433,26 @@ tb_status tb_op_gemm_sharded(tb_comm* comm, tb_stream* stream, const tb_tensor* 
   Stream* st = nullptr;
   Buffer *ba = nullptr, *bb = nullptr, *bc = nullptr, *bw = nullptr;
   if ((rc = check_stream(s, stream, &st)) || (rc = tensor_buffer(s, lhs, "gemm lhs", &ba)) ||
-      (rc = tensor_buffer(s, rhs_shard, "gemm rhs", &bb)) || (rc = tensor_buffer(s, output, "gemm output", &bc)) ||
-      (rc = check_buffer(s, workspace, &bw)))
+      (rc = tensor_buffer(s, rhs_shard, "gemm rhs", &bb)) || (rc = tensor_buffer(s, output, "gemm output", &bc)))
     return rc;
+  const PeerMapping* mapping = find_mapping(c, bc);
+  if (mapping) {
+    // Fused: every rank's C is mapped here; this rank's column block goes to all of them.
+    for (int j = 0; j < (int)p; ++j)
+      if (mapping->bytes[j] < M * Np * p * 2) return contract("a rank's registered output is smaller than C");
+    if (p > TB_MAX_RANKS) return unsupported("fused all-gather supports at most 8 ranks");
+    rc = activate(s);
+    if (rc) return rc;
+    // Every rank is done with its previous C before anyone writes into it...
+    if ((rc = enqueue_barrier(c, st))) return rc;
+    rc = launch_gemm_bf16_tn_allgather(s, st, ba->ptr, bb->ptr, mapping->base.data(), (int)p, c->rank, (int)M,
+                                       (int)Np, (int)K, (long long)(Np * p), (long long)(Np * (uint64_t)c->rank));
+    if (rc) return rc;
+    // ...and every rank's stores have landed before anyone reads it.
+    if ((rc = enqueue_barrier(c, st))) return rc;
+    return record_event(s, st, nullptr, out);
+  }
+  if ((rc = check_buffer(s, workspace, &bw))) return rc;
   const size_t shard_bytes = M * Np * 2;
   if (bw->bytes < shard_bytes * p) return contract("sharded GEMM workspace holds fewer than p*M*(N/p) elements");
   rc = activate(s);

@@ -50,7 +50,11 @@ namespace tb {
   X(cuTensorMapEncodeTiled)            \
   X(cuGetErrorString)                  \
   X(cuGetErrorName)                    \
-  X(cuPointerGetAttribute)
+  X(cuPointerGetAttribute)             \
+  X(cuMemGetAddressRange_v2)           \
+  X(cuIpcGetMemHandle)                 \
+  X(cuIpcOpenMemHandle_v2)             \
+  X(cuIpcCloseMemHandle)
 
 struct DriverApi {
 #define TB_DECLARE(name) decltype(&::name) name = nullptr;

@@ -28,6 +28,37 @@ tb_status launch_gemm_bf16_tn(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr
   return launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_SMEM_BYTES, params, "gemm_bf16_tn");
 }
 
+// Fused N-sharded GEMM + all-gather: this rank's [M, N] column block of the row-major
+// C[M, ldc] at column col0, stored into every rank's C (outs[i] = rank i's base).
+tb_status launch_gemm_bf16_tn_allgather(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, const CUdeviceptr* outs,
+                                        int ranks, int self, int M, int N, int K, long long ldc, long long col0) {
+  if (ranks < 1 || ranks > TB_MAX_RANKS) return unsupported("fused all-gather supports 1 to 8 ranks");
+  // The kernel stores whole 16-byte segments (8 columns) into every rank's C.
+  if (ldc % 8 != 0 || col0 % 8 != 0 || N % 8 != 0) return unsupported("fused all-gather needs 8-column alignment");
+  for (int i = 0; i < ranks; ++i)
+    if (outs[i] & 15) return unsupported("fused all-gather needs 16-byte aligned outputs");
+  CUtensorMap ta, tbm;
+  tb_status rc = tmap_bf16_2d(&ta, a, (uint64_t)M, (uint64_t)K, (uint64_t)K, TB_GEMM_BM, TB_GEMM_BK,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = tmap_bf16_2d(&tbm, b, (uint64_t)N, (uint64_t)K, (uint64_t)K, TB_GEMM_BN, TB_GEMM_BK,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  CUfunction fn = nullptr;
+  rc = builtin_function(s, "gemm_bf16", "gemm_bf16_tn_allgather", &fn);
+  if (rc) return rc;
+  struct {
+    CUdeviceptr base[TB_MAX_RANKS];
+  } rank_outputs = {};
+  for (int i = 0; i < ranks; ++i) rank_outputs.base[i] = outs[i];
+  const long long tiles = (long long)((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN);
+  const unsigned grid = (unsigned)(tiles < s->sm_count ? tiles : s->sm_count);
+  CUdeviceptr status = s->status.device;
+  void* params[] = {&ta, &tbm, &rank_outputs, &ranks, &self, &M, &N, &K, &ldc, &col0, &status};
+  return launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_AG_SMEM_BYTES, params,
+                        "gemm_bf16_tn_allgather");
+}
+
 // Split-K plan for an output with too few 128x256 tiles to fill the SMs.
 struct SplitPlan {
   int splits = 1, kb_per_split = 0;

@@ -71,6 +71,7 @@ struct ConvPolicy {
     __nv_bfloat16* dst = y + (((long long)n * Ho + ho) * Wo + wo) * Cout + co;
     umma::store_bf16_chunk(dst, Cout - co, vec_ok, acc, bias ? bias + co : nullptr);
   }
+  __device__ void finish() const {}
 };
 
 }  // namespace

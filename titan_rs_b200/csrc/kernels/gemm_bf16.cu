@@ -12,6 +12,10 @@
 // and B columns in L2. K tails and M/N tails come back from TMA as zeros; the
 // epilogue masks them.
 //
+// Fused all-gather (gemm_bf16_tn_allgather): the N-sharded GEMM of one rank whose
+// epilogue stores every output chunk into all ranks' row-major C (NVLink peer stores
+// through CUDA IPC mappings), so the gather overlaps the remaining tiles' math.
+//
 // Split-K (gemm_bf16_tn_splitk + splitk_reduce_bf16): when the output has too
 // few 128x256 tiles to occupy the SMs, each tile's K range is cut into slices
 // that run as separate work units writing fp32 partials to scratch memory; the
@@ -21,6 +25,7 @@
 namespace {
 constexpr uint32_t kFailGemm = 0x47000000u;
 constexpr uint32_t kFailSplitK = 0x4B000000u;
+constexpr uint32_t kFailAllGather = 0x47410000u;
 }  // namespace
 
 extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
@@ -38,6 +43,30 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
   p.num_m = (M + tb::umma::BM - 1) / tb::umma::BM;
   p.num_n = (N + tb::umma::BN - 1) / tb::umma::BN;
   tb::umma::run(p, status, kFailGemm);
+}
+
+// Fused GEMM + all-gather: this rank's N-shard (B rows [N, K]) of C[M, ldc], written
+// at column col0 into every rank's C through `outs` (its own entry included).
+extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
+    gemm_bf16_tn_allgather(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                           const __grid_constant__ tb::gemm::RankOutputs outs, int ranks, int self, int M, int N,
+                           int K, long long ldc, long long col0, uint32_t* status) {
+  tb::gemm::AllGatherPolicy p;
+  p.ta = &tmap_a;
+  p.tb = &tmap_b;
+  p.c = nullptr;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = ldc;
+  p.vec_ok = true;  // the host requires 16-byte aligned bases, ldc % 8 == 0, col0 % 8 == 0 and N % 8 == 0
+  p.num_m = (M + tb::umma::BM - 1) / tb::umma::BM;
+  p.num_n = (N + tb::umma::BN - 1) / tb::umma::BN;
+  p.outs = &outs;
+  p.ranks = ranks;
+  p.self = self;
+  p.col0 = col0;
+  tb::umma::run(p, status, kFailAllGather);
 }
 
 extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)

@@ -8,6 +8,9 @@
 //                  written to `partial` laid out [splits][M][N].
 //   splitk_reduce  C[m, n] = bf16( sum_{s < splits} partial[s][m][n] ), summed in
 //                  split order, so the result is deterministic.
+//   AllGatherPolicy  the GEMM of one rank's column block, fused with the all-gather:
+//                  every packed output chunk is stored into each rank's copy of the
+//                  row-major C (peer copies through CUDA IPC mappings over NVLink).
 #pragma once
 
 #include "umma_pipeline.cuh"
@@ -44,6 +47,60 @@ struct GemmPolicy {
     if (gr >= M || gc >= N) return;
     umma::store_bf16_chunk(c + (long long)gr * ldc + gc, N - gc, vec_ok, r, nullptr);
   }
+  __device__ void finish() const {}
+};
+
+// Output bases of every rank's C for the fused GEMM + all-gather (index = rank).
+struct RankOutputs {
+  __nv_bfloat16* base[TB_MAX_RANKS];
+};
+
+// This rank computes C[:, col0 : col0 + N] of the row-major C[M, ldc] that every rank
+// holds, and writes each output row segment into all `ranks` copies. Stores to a peer
+// cross NVLink, where many small scattered writes waste the link, so each epilogue warp
+// first collects its 32 rows x 128 columns (4 accumulator chunks) in shared memory
+// (16-byte segments XOR-swizzled by row, so neither the row-wise writes nor the
+// segment-wise reads conflict) and then writes them out with 16 lanes per 256-byte
+// row segment: this rank's own copy first, then its successors', so at any moment the
+// ranks write to different peers.
+struct AllGatherPolicy : GemmPolicy {
+  const RankOutputs* outs;  // kernel parameter space
+  int ranks, self;
+  long long col0;
+
+  __device__ void store(int row, int, int m_blk, int n_blk, int col, const uint32_t (&r)[32]) const {
+    const int lane = row & 31;
+    uint8_t* stage = umma::epilogue_smem() + (row >> 5) * (32 * 256);  // this warp's [32 rows][256 B]
+    const int first_seg = (col & 127) >> 3;                              // 0, 4, 8, 12
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 v;
+      v.x = pack_bf16x2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
+      v.y = pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
+      v.z = pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
+      v.w = pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
+      *reinterpret_cast<uint4*>(stage + lane * 256 + (((first_seg + q) ^ (lane & 15)) << 4)) = v;
+    }
+    if ((col & 127) != 96) return;  // the 128-column half is complete after its fourth chunk
+    __syncwarp();
+    const int seg = lane & 15;                                // 16-byte segment (8 columns) of a row
+    const int gc = n_blk * umma::BN + (col & ~127) + seg * 8;  // this lane's local column
+    const int row0 = m_blk * umma::BM + (row & ~31);
+    for (int it = 0; it < 16; ++it) {
+      const int rr = 2 * it + (lane >> 4);
+      const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 256 + ((seg ^ (rr & 15)) << 4));
+      const int gr = row0 + rr;
+      if (gr < M && gc < N) {
+        const long long off = (long long)gr * ldc + col0 + gc;
+        for (int i = 0, d = self; i < ranks; ++i, d = (d + 1 == ranks) ? 0 : d + 1)
+          *reinterpret_cast<uint4*>(outs->base[d] + off) = v;
+      }
+    }
+    __syncwarp();  // the next half overwrites the staging block
+  }
+  // The peer stores of this thread are performed system-wide before the kernel ends,
+  // hence before the barrier that follows it on the stream signals any peer.
+  __device__ void finish() const { __threadfence_system(); }
 };
 
 struct SplitKPolicy {
@@ -89,6 +146,7 @@ struct SplitKPolicy {
         if (gc + j < N) dst[j] = __uint_as_float(r[j]);
     }
   }
+  __device__ void finish() const {}
 };
 
 __device__ __forceinline__ void run_splitk(const CUtensorMap* ta, const CUtensorMap* tb, float* partial, int M, int N,

@@ -10,6 +10,12 @@
 #define TB_GEMM_BARRIER_BYTES 128
 #define TB_GEMM_SMEM_BYTES (TB_GEMM_STAGES * (TB_GEMM_BM + TB_GEMM_BN) * TB_GEMM_BK * 2 + 1024 + TB_GEMM_BARRIER_BYTES)
 
+// Ranks the fused GEMM + all-gather writes to (one node), and its epilogue staging:
+// 4 warps x 32 rows x 128 bf16 columns beyond the pipeline's shared memory.
+#define TB_MAX_RANKS 8
+#define TB_GEMM_AG_STAGE_BYTES (4 * 32 * 256)
+#define TB_GEMM_AG_SMEM_BYTES (TB_GEMM_SMEM_BYTES + TB_GEMM_AG_STAGE_BYTES)
+
 // Causal SDPA forward (sdpa_bf16.cu): 128-row query tiles, 128-key tiles, head dim 128.
 // Shared memory: Q 32 KB + K ring 2x32 KB + V ring 2x32 KB + P 2x32 KB + barriers.
 #define TB_SDPA_BM 128

@@ -39,6 +39,16 @@ struct Barriers {
 static_assert(sizeof(Barriers) <= TB_GEMM_BARRIER_BYTES, "barrier block overflows its reservation");
 static_assert(STAGES * STAGE_BYTES + 1024 + TB_GEMM_BARRIER_BYTES == TB_GEMM_SMEM_BYTES, "smem layout");
 static_assert(TB_GEMM_SMEM_BYTES <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
+// Dynamic shared memory past the ring and the barriers (from the 1 KB-aligned base) is
+// free for a policy's epilogue staging; its kernel is launched with the extra bytes.
+constexpr int EPILOGUE_SMEM_OFFSET = STAGES * STAGE_BYTES + TB_GEMM_BARRIER_BYTES;
+static_assert(TB_GEMM_AG_SMEM_BYTES <= 232448, "fused all-gather staging exceeds the 227 KB limit");
+
+__device__ __forceinline__ uint8_t* epilogue_smem() {
+  extern __shared__ uint8_t smem_raw[];
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023)) +
+         EPILOGUE_SMEM_OFFSET;
+}
 
 // Grouped rasterisation: `group` M-blocks share each sweep over the N-blocks.
 __device__ __forceinline__ void grouped_tile(int t, int num_m, int num_n, int group, int& m_blk, int& n_blk) {
@@ -221,6 +231,7 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
         acc_phase ^= 1;
       }
     }
+    p.finish();
   }
 
   __syncthreads();

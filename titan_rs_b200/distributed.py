@@ -211,11 +211,22 @@ class NcclCollective:
     def barrier(self, stream: Stream) -> None:
         _check(N.lib().tb_comm_barrier(self.ptr, stream.ptr))
 
-    def sharded_gemm(self, stream: Stream, a, b_shard, c, workspace: Buffer) -> None:
-        """C = A B^T with B's rows (output columns) sharded over the ranks; C complete on every rank."""
+    def register_buffer(self, stream: Stream, buffer: Buffer) -> None:
+        """Collective: map every rank's `buffer` into every other rank (CUDA IPC over NVLink)."""
+        _check(N.lib().tb_comm_register_buffer(self.ptr, stream.ptr, buffer.ptr))
+
+    def deregister_buffer(self, buffer: Buffer) -> None:
+        _check(N.lib().tb_comm_deregister_buffer(self.ptr, buffer.ptr))
+
+    def sharded_gemm(self, stream: Stream, a, b_shard, c, workspace: Buffer | None) -> None:
+        """C = A B^T with B's rows (output columns) sharded over the ranks; C complete on every rank.
+
+        With C's buffer registered on every rank (`register_buffer`) one fused kernel
+        stores this rank's columns into all ranks' C over NVLink and `workspace` may be
+        None; otherwise the GEMM fills a workspace slot that NCCL all-gathers."""
         ta, tb_, tc = a.c_tensor(), b_shard.c_tensor(), c.c_tensor()
         _check(N.lib().tb_op_gemm_sharded(self.ptr, stream.ptr, ctypes.byref(ta), ctypes.byref(tb_),
-                                          ctypes.byref(tc), workspace.ptr, None))
+                                          ctypes.byref(tc), workspace.ptr if workspace is not None else None, None))
 
     def close(self) -> None:
         if self.ptr:

@@ -33,6 +33,11 @@ def _check(status: int) -> None:
         raise HalError(status, op, detail)
 
 
+def last_candidate() -> str:
+    """Name of the kernel the calling thread's most recent operator launched."""
+    return (N.lib().tb_last_candidate() or b"").decode()
+
+
 def driver_available() -> bool:
     """True when libcuda loads and reports devices (the reference's no_cuda_environment inverse)."""
     try:
