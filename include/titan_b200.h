@@ -286,11 +286,13 @@ tb_status tb_comm_barrier(tb_comm* comm, tb_stream* stream);
 
 /* No counterpart in the reference, whose all_gather concatenates host vectors
  * (titan-distributed/src/lib.rs:95-99). Collective: every rank calls it with its own
- * buffer, in the same order. Maps each rank's buffer into every other rank's
- * address space (CUDA IPC, peer access over NVLink) so that operators such as
- * tb_op_gemm_sharded can store into the peers' copies directly. Synchronizes
- * `stream`. The buffer stays retained until tb_comm_deregister_buffer or
- * tb_comm_release; all ranks must deregister before any rank frees its buffer. */
+ * buffer, in the same order. Maps each rank's buffer, and a 128-byte signal block
+ * of flags, into every other rank's address space (CUDA IPC, peer access over
+ * NVLink) so that operators such as tb_op_gemm_sharded can store into the peers'
+ * copies directly and synchronise inside their kernels. Fails with
+ * TB_ERR_UNSUPPORTED when two ranks share a GPU. Synchronizes `stream`. The buffer
+ * stays retained until tb_comm_deregister_buffer or tb_comm_release; all ranks must
+ * deregister before any rank frees its buffer. */
 tb_status tb_comm_register_buffer(tb_comm* comm, tb_stream* stream, tb_buffer* buffer);
 tb_status tb_comm_deregister_buffer(tb_comm* comm, tb_buffer* buffer);
 
@@ -299,7 +301,9 @@ tb_status tb_comm_deregister_buffer(tb_comm* comm, tb_buffer* buffer);
  * output is the full C[M,N] on every rank after the call.
  * When the output buffer is registered (tb_comm_register_buffer) on every rank,
  * one fused kernel (gemm_bf16_tn_allgather) stores this rank's columns into all
- * ranks' C over NVLink between two barriers, and `workspace` may be NULL.
+ * ranks' C over NVLink; it waits at its start until every rank has reached the call
+ * and completes only when every rank's stores have landed (flags in the signal
+ * blocks, each wait bounded at ~1 s with an error status), and `workspace` may be NULL.
  * Otherwise `workspace` holds p*M*(N/p) elements of the output dtype: the GEMM
  * fills this rank's slot, NCCL all-gathers the slots and a layout kernel writes C.
  * Every rank must take the same form. */

@@ -149,6 +149,36 @@ def _rank_main(rank, world, q_in, q_out, mode):
             s.synchronize(rt.stream)
             coll.deregister_buffer(c.buffer)
             q_out.put((rank, ok))
+        elif mode == "p2p_absent":
+            # Rank 1 registers its output but never makes the call: rank 0's fused kernel
+            # gives up its entry wait after ~1 s (a flag nothing sets), reports the code, and
+            # its context stays usable.
+            m, n, k = 256, 512, 256
+            c = tbm.TensorHandle.allocate(s, DType.BF16, (m, n))
+            coll.register_buffer(rt.stream, c.buffer)
+            if rank == 0:
+                a, b = _gemm_inputs(m, n, k, seed=33)
+                lo, hi = Dm.even_shard(n, world, rank)
+                ta = tbm.TensorHandle.from_numpy(s, a, DType.BF16, rt.stream)
+                tbs = tbm.TensorHandle.from_numpy(s, np.ascontiguousarray(b[lo:hi]), DType.BF16, rt.stream)
+                coll.sharded_gemm(rt.stream, ta, tbs, c, None)
+                try:
+                    s.synchronize(rt.stream)
+                    outcome = "no error"
+                except tbm.HalError as e:
+                    outcome = "timeout" if "47410501" in str(e) else repr(e)
+                # The context still runs work.
+                probe = s.allocate(64)
+                s.wait(s.upload(rt.stream, probe, np.arange(16, dtype=np.float32)))
+                back = np.empty(16, np.float32)
+                s.download(rt.stream, probe, back)
+                usable = bool(np.array_equal(back, np.arange(16, dtype=np.float32)))
+                q_in.put("done")
+                q_out.put((rank, (outcome, usable)))
+            else:
+                q_in.get(timeout=120)
+                q_out.put((rank, "absent"))
+            coll.deregister_buffer(c.buffer)
         else:
             # Departure between steps: rank 1 announces it leaves and exits with nothing in flight;
             # rank 0 checks the announcement on the host before its next collective and stops.
@@ -189,6 +219,11 @@ def test_two_rank_sharded_gemm_and_all_gather():
 @pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")
 def test_two_rank_fused_sharded_gemm_over_peer_stores():
     assert _spawn(2, "gemm_p2p") == {0: True, 1: True}
+
+
+@pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")
+def test_two_rank_fused_gemm_gives_up_when_a_peer_never_arrives():
+    assert _spawn(2, "p2p_absent") == {0: ("timeout", True), 1: "absent"}
 
 
 @pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")

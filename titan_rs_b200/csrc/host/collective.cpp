@@ -3,9 +3,11 @@
 // buffers through NCCL, plus the N-sharded GEMM that uses it.
 //
 // The sharded GEMM has two forms. With an output buffer registered on every rank
-// (tb_comm_register_buffer: CUDA IPC mappings of each rank's buffer in every other
-// rank), one fused kernel computes this rank's column block and stores each output
-// chunk straight into every rank's row-major C over NVLink, between two barriers.
+// (tb_comm_register_buffer: CUDA IPC mappings of each rank's buffer, and of a small
+// signal block, in every other rank), one fused kernel computes this rank's column
+// block and stores each output chunk straight into every rank's row-major C over
+// NVLink; the ranks meet through flags in the signal blocks at the kernel's start
+// and end, so the call is a single launch.
 // Otherwise the GEMM writes a [p][M][N/p] workspace slot, NCCL all-gathers it in
 // place and a layout kernel writes the row-major C.
 //
@@ -31,7 +33,8 @@ namespace tb {
 tb_status launch_gemm_bf16_tn(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c, int M, int N,
                               int K, long long ldc);
 tb_status launch_gemm_bf16_tn_allgather(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, const CUdeviceptr* outs,
-                                        int ranks, int self, int M, int N, int K, long long ldc, long long col0);
+                                        const CUdeviceptr* signals, int ranks, int self, uint32_t epoch, int M, int N,
+                                        int K, long long ldc, long long col0);
 
 namespace {
 
@@ -85,12 +88,17 @@ tb_status nccl_error(const char* op, ncclResult_t r) {
 
 }  // namespace
 
-// A buffer registered on every rank: where each rank's copy is mapped in this process.
+// A buffer registered on every rank: where each rank's copy, and each rank's signal
+// block (TB_SIGNAL_BLOCK_BYTES of flags, see kernels/peer_signal.cuh), are mapped here.
 struct PeerMapping {
-  Buffer* local = nullptr;            // retained while registered
-  std::vector<CUdeviceptr> base;      // per rank; this rank's entry is local->ptr
-  std::vector<uint64_t> bytes;        // per rank
-  std::vector<CUdeviceptr> opened;    // per rank: IPC mapping to close (0 for this rank)
+  Buffer* local = nullptr;             // retained while registered
+  std::vector<CUdeviceptr> base;       // per rank; this rank's entry is local->ptr
+  std::vector<uint64_t> bytes;         // per rank
+  std::vector<CUdeviceptr> opened;     // per rank: IPC mapping to close (0 for this rank)
+  CUdeviceptr signal_local = 0;        // this rank's signal block (owned)
+  std::vector<CUdeviceptr> signal;     // per rank
+  std::vector<CUdeviceptr> signal_opened;
+  uint32_t epoch = 0;                  // fused calls made with this buffer (same on every rank)
 };
 
 struct Comm {
@@ -192,21 +200,28 @@ void unmap(PeerMapping& m) {
   for (CUdeviceptr p : m.opened)
     if (p && d) d->cuIpcCloseMemHandle(p);
   m.opened.clear();
+  for (CUdeviceptr p : m.signal_opened)
+    if (p && d) d->cuIpcCloseMemHandle(p);
+  m.signal_opened.clear();
+  if (m.signal_local && d) d->cuMemFree_v2(m.signal_local);
+  m.signal_local = 0;
   if (m.local) tb_buffer_release(reinterpret_cast<tb_buffer*>(m.local));
   m.local = nullptr;
 }
 
-const PeerMapping* find_mapping(const Comm* c, const Buffer* b) {
-  for (const PeerMapping& m : c->mappings)
+PeerMapping* find_mapping(Comm* c, const Buffer* b) {
+  for (PeerMapping& m : c->mappings)
     if (m.local == b) return &m;
   return nullptr;
 }
 
 // What one rank publishes about its registered buffer.
 struct MappingRecord {
-  CUipcMemHandle handle;
-  uint64_t offset;  // of the buffer inside its allocation
+  CUipcMemHandle handle;         // the buffer's allocation
+  CUipcMemHandle signal_handle;  // the rank's signal block
+  uint64_t offset;               // of the buffer inside its allocation
   uint64_t bytes;
+  int32_t pci_domain, pci_bus, pci_device, pad;
 };
 
 }  // namespace
@@ -352,13 +367,31 @@ tb_status tb_comm_register_buffer(tb_comm* comm, tb_stream* stream, tb_buffer* b
   m.opened.assign(p, 0);
   m.base[c->rank] = b->ptr;
   m.bytes[c->rank] = b->bytes;
+  m.signal.assign(p, 0);
+  m.signal_opened.assign(p, 0);
+  TB_CU("allocate", d->cuMemAlloc_v2(&m.signal_local, TB_SIGNAL_BLOCK_BYTES));
+  m.signal[c->rank] = m.signal_local;
+  CUresult zr = d->cuMemsetD32Async(m.signal_local, 0, TB_SIGNAL_BLOCK_BYTES / 4, st->raw);
+  if (zr == CUDA_SUCCESS) zr = d->cuStreamSynchronize(st->raw);
+  if (zr != CUDA_SUCCESS) {
+    unmap(m);
+    return cu_error("register", zr);
+  }
   if (p > 1) {
     // Publish (IPC handle of the allocation, offset, size) and gather everyone's.
     CUdeviceptr alloc_base = 0;
     size_t alloc_size = 0;
     TB_CU("cuMemGetAddressRange", d->cuMemGetAddressRange_v2(&alloc_base, &alloc_size, b->ptr));
     MappingRecord mine{};
-    TB_CU("cuIpcGetMemHandle", d->cuIpcGetMemHandle(&mine.handle, alloc_base));
+    CUresult hr = d->cuIpcGetMemHandle(&mine.handle, alloc_base);
+    if (hr == CUDA_SUCCESS) hr = d->cuIpcGetMemHandle(&mine.signal_handle, m.signal_local);
+    if (hr == CUDA_SUCCESS) hr = d->cuDeviceGetAttribute(&mine.pci_domain, CU_DEVICE_ATTRIBUTE_PCI_DOMAIN_ID, s->device);
+    if (hr == CUDA_SUCCESS) hr = d->cuDeviceGetAttribute(&mine.pci_bus, CU_DEVICE_ATTRIBUTE_PCI_BUS_ID, s->device);
+    if (hr == CUDA_SUCCESS) hr = d->cuDeviceGetAttribute(&mine.pci_device, CU_DEVICE_ATTRIBUTE_PCI_DEVICE_ID, s->device);
+    if (hr != CUDA_SUCCESS) {
+      unmap(m);
+      return cu_error("register", hr);
+    }
     mine.offset = b->ptr - alloc_base;
     mine.bytes = b->bytes;
     std::vector<MappingRecord> all(p);
@@ -376,18 +409,37 @@ tb_status tb_comm_register_buffer(tb_comm* comm, tb_stream* stream, tb_buffer* b
       if (cr == CUDA_SUCCESS) cr = d->cuStreamSynchronize(st->raw);
     }
     d->cuMemFree_v2(dev);
-    if (cr != CUDA_SUCCESS) return cu_error("register", cr);
-    if (r != ncclSuccess && r != ncclInProgress) return nccl_error("ncclAllGather", r);
-    if (rc) return rc;
+    if (cr != CUDA_SUCCESS || (r != ncclSuccess && r != ncclInProgress) || rc) {
+      unmap(m);
+      if (cr != CUDA_SUCCESS) return cu_error("register", cr);
+      if (r != ncclSuccess && r != ncclInProgress) return nccl_error("ncclAllGather", r);
+      return rc;
+    }
+    // The fused kernels of different ranks wait on each other's flags, which is only
+    // safe when every rank has its own GPU.
+    for (int i = 0; i < p; ++i)
+      for (int j = i + 1; j < p; ++j)
+        if (all[i].pci_domain == all[j].pci_domain && all[i].pci_bus == all[j].pci_bus &&
+            all[i].pci_device == all[j].pci_device) {
+          unmap(m);
+          return set_error(TB_ERR_UNSUPPORTED, "register",
+                           "ranks " + std::to_string(i) + " and " + std::to_string(j) +
+                               " share a GPU; peer-store collectives need one GPU per rank");
+        }
     for (int j = 0; j < p; ++j) {
       if (j == c->rank) continue;
-      CUdeviceptr peer = 0;
+      CUdeviceptr peer = 0, peer_signal = 0;
       cr = d->cuIpcOpenMemHandle_v2(&peer, all[j].handle, CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS);
+      if (cr == CUDA_SUCCESS) {
+        m.opened[j] = peer;
+        cr = d->cuIpcOpenMemHandle_v2(&peer_signal, all[j].signal_handle, CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS);
+      }
       if (cr != CUDA_SUCCESS) {
         unmap(m);
         return cu_error("cuIpcOpenMemHandle", cr);
       }
-      m.opened[j] = peer;
+      m.signal_opened[j] = peer_signal;
+      m.signal[j] = peer_signal;
       m.base[j] = peer + all[j].offset;
       m.bytes[j] = all[j].bytes;
     }
@@ -435,7 +487,7 @@ tb_status tb_op_gemm_sharded(tb_comm* comm, tb_stream* stream, const tb_tensor* 
   if ((rc = check_stream(s, stream, &st)) || (rc = tensor_buffer(s, lhs, "gemm lhs", &ba)) ||
       (rc = tensor_buffer(s, rhs_shard, "gemm rhs", &bb)) || (rc = tensor_buffer(s, output, "gemm output", &bc)))
     return rc;
-  const PeerMapping* mapping = find_mapping(c, bc);
+  PeerMapping* mapping = find_mapping(c, bc);
   if (mapping) {
     // Fused: every rank's C is mapped here; this rank's column block goes to all of them.
     for (int j = 0; j < (int)p; ++j)
@@ -443,13 +495,11 @@ tb_status tb_op_gemm_sharded(tb_comm* comm, tb_stream* stream, const tb_tensor* 
     if (p > TB_MAX_RANKS) return unsupported("fused all-gather supports at most 8 ranks");
     rc = activate(s);
     if (rc) return rc;
-    // Every rank is done with its previous C before anyone writes into it...
-    if ((rc = enqueue_barrier(c, st))) return rc;
-    rc = launch_gemm_bf16_tn_allgather(s, st, ba->ptr, bb->ptr, mapping->base.data(), (int)p, c->rank, (int)M,
-                                       (int)Np, (int)K, (long long)(Np * p), (long long)(Np * (uint64_t)c->rank));
+    rc = launch_gemm_bf16_tn_allgather(s, st, ba->ptr, bb->ptr, mapping->base.data(), mapping->signal.data(), (int)p,
+                                       c->rank, mapping->epoch + 1, (int)M, (int)Np, (int)K, (long long)(Np * p),
+                                       (long long)(Np * (uint64_t)c->rank));
     if (rc) return rc;
-    // ...and every rank's stores have landed before anyone reads it.
-    if ((rc = enqueue_barrier(c, st))) return rc;
+    ++mapping->epoch;
     return record_event(s, st, nullptr, out);
   }
   if ((rc = check_buffer(s, workspace, &bw))) return rc;

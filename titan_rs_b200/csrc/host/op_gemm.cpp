@@ -29,9 +29,11 @@ tb_status launch_gemm_bf16_tn(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr
 }
 
 // Fused N-sharded GEMM + all-gather: this rank's [M, N] column block of the row-major
-// C[M, ldc] at column col0, stored into every rank's C (outs[i] = rank i's base).
+// C[M, ldc] at column col0, stored into every rank's C (outs[i] = rank i's base); the
+// ranks synchronise through their signal blocks (signals[i] = rank i's) for call `epoch`.
 tb_status launch_gemm_bf16_tn_allgather(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, const CUdeviceptr* outs,
-                                        int ranks, int self, int M, int N, int K, long long ldc, long long col0) {
+                                        const CUdeviceptr* signals, int ranks, int self, uint32_t epoch, int M, int N,
+                                        int K, long long ldc, long long col0) {
   if (ranks < 1 || ranks > TB_MAX_RANKS) return unsupported("fused all-gather supports 1 to 8 ranks");
   // The kernel stores whole 16-byte segments (8 columns) into every rank's C.
   if (ldc % 8 != 0 || col0 % 8 != 0 || N % 8 != 0) return unsupported("fused all-gather needs 8-column alignment");
@@ -49,12 +51,15 @@ tb_status launch_gemm_bf16_tn_allgather(Session* s, Stream* st, CUdeviceptr a, C
   if (rc) return rc;
   struct {
     CUdeviceptr base[TB_MAX_RANKS];
-  } rank_outputs = {};
-  for (int i = 0; i < ranks; ++i) rank_outputs.base[i] = outs[i];
+  } rank_outputs = {}, rank_signals = {};
+  for (int i = 0; i < ranks; ++i) {
+    rank_outputs.base[i] = outs[i];
+    rank_signals.base[i] = signals[i];
+  }
   const long long tiles = (long long)((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN);
   const unsigned grid = (unsigned)(tiles < s->sm_count ? tiles : s->sm_count);
   CUdeviceptr status = s->status.device;
-  void* params[] = {&ta, &tbm, &rank_outputs, &ranks, &self, &M, &N, &K, &ldc, &col0, &status};
+  void* params[] = {&ta, &tbm, &rank_outputs, &rank_signals, &ranks, &self, &epoch, &M, &N, &K, &ldc, &col0, &status};
   return launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_AG_SMEM_BYTES, params,
                         "gemm_bf16_tn_allgather");
 }

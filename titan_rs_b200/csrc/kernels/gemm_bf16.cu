@@ -14,13 +14,15 @@
 //
 // Fused all-gather (gemm_bf16_tn_allgather): the N-sharded GEMM of one rank whose
 // epilogue stores every output chunk into all ranks' row-major C (NVLink peer stores
-// through CUDA IPC mappings), so the gather overlaps the remaining tiles' math.
+// through CUDA IPC mappings), so the gather overlaps the remaining tiles' math; the
+// ranks synchronise through flags in each other's memory (peer_signal.cuh).
 //
 // Split-K (gemm_bf16_tn_splitk + splitk_reduce_bf16): when the output has too
 // few 128x256 tiles to occupy the SMs, each tile's K range is cut into slices
 // that run as separate work units writing fp32 partials to scratch memory; the
 // reduction sums them in a fixed order.
 #include "gemm_policies.cuh"
+#include "peer_signal.cuh"
 
 namespace {
 constexpr uint32_t kFailGemm = 0x47000000u;
@@ -47,26 +49,56 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
 
 // Fused GEMM + all-gather: this rank's N-shard (B rows [N, K]) of C[M, ldc], written
 // at column col0 into every rank's C through `outs` (its own entry included).
+// Call `epoch` of the registered output, synchronised with the other ranks in-kernel:
+//   entry  CTA 0 announces the epoch in every peer's signal block; each CTA waits until
+//          every peer has announced it (so every peer is done with its C) before it
+//          computes and stores anything;
+//   exit   the last CTA to finish (all stores fenced system-wide) tells every peer its
+//          stores have landed and waits until every peer has said the same, so the
+//          kernel completes only when this rank's C is whole.
 extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
     gemm_bf16_tn_allgather(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                           const __grid_constant__ tb::gemm::RankOutputs outs, int ranks, int self, int M, int N,
-                           int K, long long ldc, long long col0, uint32_t* status) {
-  tb::gemm::AllGatherPolicy p;
-  p.ta = &tmap_a;
-  p.tb = &tmap_b;
-  p.c = nullptr;
-  p.M = M;
-  p.N = N;
-  p.K = K;
-  p.ldc = ldc;
-  p.vec_ok = true;  // the host requires 16-byte aligned bases, ldc % 8 == 0, col0 % 8 == 0 and N % 8 == 0
-  p.num_m = (M + tb::umma::BM - 1) / tb::umma::BM;
-  p.num_n = (N + tb::umma::BN - 1) / tb::umma::BN;
-  p.outs = &outs;
-  p.ranks = ranks;
-  p.self = self;
-  p.col0 = col0;
-  tb::umma::run(p, status, kFailAllGather);
+                           const __grid_constant__ tb::gemm::RankOutputs outs,
+                           const __grid_constant__ tb::RankSignals sig, int ranks, int self, uint32_t epoch, int M,
+                           int N, int K, long long ldc, long long col0, uint32_t* status) {
+  __shared__ int entry_ok;
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) tb::signal_peers(sig, ranks, self, epoch, false);
+    entry_ok = tb::wait_peers(sig, ranks, self, epoch, false) ? 1 : 0;
+    if (!entry_ok) tb::report_status(status, kFailAllGather | 0x0501);
+  }
+  __syncthreads();
+  if (entry_ok) {
+    tb::gemm::AllGatherPolicy p;
+    p.ta = &tmap_a;
+    p.tb = &tmap_b;
+    p.c = nullptr;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.ldc = ldc;
+    p.vec_ok = true;  // the host requires 16-byte aligned bases, ldc % 8 == 0, col0 % 8 == 0 and N % 8 == 0
+    p.num_m = (M + tb::umma::BM - 1) / tb::umma::BM;
+    p.num_n = (N + tb::umma::BN - 1) / tb::umma::BN;
+    p.outs = &outs;
+    p.ranks = ranks;
+    p.self = self;
+    p.col0 = col0;
+    tb::umma::run(p, status, kFailAllGather);
+  }
+  if (threadIdx.x == 0) {
+    // Every epilogue thread fenced its stores (AllGatherPolicy::finish) before run()'s
+    // final __syncthreads.
+    __threadfence_system();
+    tb::SignalBlock* mine = sig.block[self];
+    if (atomicAdd(&mine->arrivals, 1u) == gridDim.x - 1) {
+      mine->arrivals = 0;  // the next call starts after this kernel (stream order)
+      if (entry_ok) {
+        tb::signal_peers(sig, ranks, self, epoch, true);
+        if (!tb::wait_peers(sig, ranks, self, epoch, true)) tb::report_status(status, kFailAllGather | 0x0502);
+      }
+    }
+  }
 }
 
 extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)

@@ -13,6 +13,7 @@
 // Ranks the fused GEMM + all-gather writes to (one node), and its epilogue staging:
 // 4 warps x 32 rows x 128 bf16 columns beyond the pipeline's shared memory.
 #define TB_MAX_RANKS 8
+#define TB_SIGNAL_BLOCK_BYTES 128
 #define TB_GEMM_AG_STAGE_BYTES (4 * 32 * 256)
 #define TB_GEMM_AG_SMEM_BYTES (TB_GEMM_SMEM_BYTES + TB_GEMM_AG_STAGE_BYTES)
 
