@@ -5,6 +5,8 @@
 //     groups 1, Cin % 8 == 0, Cout % 8 == 0, stride 1, 16-byte aligned
 //                                          -> conv2d_fprop_bf16_nhwc (tcgen05 implicit GEMM)
 //     otherwise                            -> conv2d_bf16_nhwc_generic (CUDA cores)
+// A `candidate` attribute (not a reference attribute; the autotuner's) names one of
+// these kernels; a kernel that does not take the problem is TB_ERR_UNSUPPORTED.
 #include "../kernels/kernel_configs.h"
 #include "ops_common.hpp"
 
@@ -59,8 +61,9 @@ extern "C" tb_status tb_op_conv2d(tb_session* session, tb_stream* stream, const 
   if (!input || !weight || !output)
     return contract("CUDA Conv2D requires input, weight, optional bias, and one output");
   static const char* kKnown[] = {"stride_h", "stride_w", "pad_h", "pad_w", "dilation_h", "dilation_w", "groups",
-                                 "layout"};
+                                 "layout",   "candidate"};
   const char* layout = nullptr;
+  const char* candidate = nullptr;  // optional registered kernel name (autotuner)
   for (uint32_t i = 0; i < num_attrs; ++i) {
     bool known = false;
     for (const char* k : kKnown) known = known || (attrs[i].key && strcmp(attrs[i].key, k) == 0);
@@ -69,7 +72,14 @@ extern "C" tb_status tb_op_conv2d(tb_session* session, tb_stream* stream, const 
       if (!attrs[i].str) return contract("conv2d layout must be a string");
       layout = attrs[i].str;
     }
+    if (strcmp(attrs[i].key, "candidate") == 0) {
+      if (!attrs[i].str) return contract("conv2d candidate must be a string");
+      candidate = attrs[i].str;
+    }
   }
+  if (candidate && strcmp(candidate, "conv2d_fprop_bf16_nhwc") != 0 &&
+      strcmp(candidate, "conv2d_bf16_nhwc_generic") != 0 && strcmp(candidate, "conv2d_f32") != 0)
+    return contract(std::string("unknown conv2d candidate ") + candidate);
   const bool nhwc = layout && strcmp(layout, "NHWC") == 0;
   if (layout && !nhwc && strcmp(layout, "NCHW") != 0) return contract("conv2d layout must be NCHW or NHWC");
   const uint32_t dt = input->dtype;
@@ -138,6 +148,8 @@ extern "C" tb_status tb_op_conv2d(tb_session* session, tb_stream* stream, const 
   uint64_t grid = (total + 255) / 256;
   if (grid > (uint64_t)s->sm_count * 32) grid = (uint64_t)s->sm_count * 32;
   CUfunction fn = nullptr;
+  if (candidate && (f32 != (strcmp(candidate, "conv2d_f32") == 0)))
+    return unsupported(std::string("candidate ") + candidate + " does not take this dtype");
   if (f32) {
     rc = builtin_function(s, "compat", "conv2d_f32", &fn);
     if (rc) return rc;
@@ -146,7 +158,10 @@ extern "C" tb_status tb_op_conv2d(tb_session* session, tb_stream* stream, const 
     rc = launch_builtin(s, st, fn, (unsigned)grid, 1, 1, 256, 0, params, "conv2d_f32");
   } else {
     const bool tc_ok = G == 1 && C % 8 == 0 && K % 8 == 0 && SH == 1 && SW == 1 && ((px | pw_ | py) & 15) == 0;
-    if (tc_ok) {
+    const bool want_generic = candidate && strcmp(candidate, "conv2d_bf16_nhwc_generic") == 0;
+    if (candidate && !want_generic && !tc_ok)
+      return unsupported(std::string("candidate ") + candidate + " does not take this shape, stride or alignment");
+    if (tc_ok && !want_generic) {
       rc = launch_conv2d_bf16(s, st, px, pw_, pb, py, N, H, Wd, C, K, R, S, Ho, Wo, SH, SW, PH, PW, DH, DW);
     } else {
       rc = builtin_function(s, "compat", "conv2d_bf16_nhwc_generic", &fn);

@@ -1,5 +1,8 @@
 // "softmax" operator entry: the contract of execute_cuda_softmax
-// (titan-runtime/src/lib.rs:1504-1596), then the B200 kernel choice.
+// (titan-runtime/src/lib.rs:1504-1596), then the B200 kernel choice. Besides the
+// reference's `axis`, the operator takes `candidate` (a registered kernel name:
+// softmax_f32_warp{1,2,4,8,16,32} for rows of at most that many x 128 columns, or
+// softmax_f32_stream), which the autotuner uses.
 #include "ops_common.hpp"
 
 using namespace tb;
@@ -9,9 +12,16 @@ extern "C" tb_status tb_op_softmax(tb_session* session, tb_stream* stream, const
   Session* s = reinterpret_cast<Session*>(session);
   if (!s) return set_error(TB_ERR_INVALID, "contract", "null session");
   if (!input || !output) return contract("CUDA softmax requires exactly one input and one output");
-  for (uint32_t i = 0; i < num_attrs; ++i)
+  const char* candidate = nullptr;
+  for (uint32_t i = 0; i < num_attrs; ++i) {
+    if (attrs[i].key && strcmp(attrs[i].key, "candidate") == 0) {
+      if (!attrs[i].str) return contract("softmax candidate must be a string");
+      candidate = attrs[i].str;
+      continue;
+    }
     if (!attrs[i].key || strcmp(attrs[i].key, "axis") != 0)
       return contract("CUDA softmax only accepts the axis attribute");
+  }
   if (input->dtype != TB_F32 || output->dtype != TB_F32)
     return contract("CUDA softmax requires F32 input and output");
   if (input->rank == 0 || input->rank > TB_MAX_RANK) return contract("CUDA softmax requires a non-scalar input");
@@ -45,14 +55,34 @@ extern "C" tb_status tb_op_softmax(tb_session* session, tb_stream* stream, const
   CUdeviceptr pin = bin->ptr, pout = bout->ptr;
   void* params[] = {&pin, &pout, &r, &c};
   const bool aligned = ((pin | pout) & 15u) == 0;
+  const bool reg_ok = aligned && cols % 4 == 0 && cols <= 4096;
+  // Register-path variants: one warp per row, up to `nv` x 128 columns.
+  static const struct {
+    const char* name;
+    uint64_t nv;
+  } kWarp[] = {{"softmax_f32_warp1", 1},  {"softmax_f32_warp2", 2},   {"softmax_f32_warp4", 4},
+               {"softmax_f32_warp8", 8},  {"softmax_f32_warp16", 16}, {"softmax_f32_warp32", 32}};
+  const char* entry = nullptr;  // a register-path variant, or null for the streaming kernel
+  if (candidate) {
+    bool known = strcmp(candidate, "softmax_f32_stream") == 0;
+    for (const auto& w : kWarp) {
+      if (strcmp(candidate, w.name) != 0) continue;
+      known = true;
+      if (!reg_ok || cols > 128 * w.nv)
+        return unsupported(std::string("candidate ") + candidate + " does not take this shape or alignment");
+      entry = w.name;
+    }
+    if (!known) return contract(std::string("unknown softmax candidate ") + candidate);
+  } else if (reg_ok) {
+    entry = cols <= 128    ? "softmax_f32_warp1"
+            : cols <= 256  ? "softmax_f32_warp2"
+            : cols <= 512  ? "softmax_f32_warp4"
+            : cols <= 1024 ? "softmax_f32_warp8"
+            : cols <= 2048 ? "softmax_f32_warp16"
+                           : "softmax_f32_warp32";
+  }
   CUfunction fn = nullptr;
-  if (aligned && cols % 4 == 0 && cols <= 4096) {
-    const char* entry = cols <= 128    ? "softmax_f32_warp1"
-                        : cols <= 256  ? "softmax_f32_warp2"
-                        : cols <= 512  ? "softmax_f32_warp4"
-                        : cols <= 1024 ? "softmax_f32_warp8"
-                        : cols <= 2048 ? "softmax_f32_warp16"
-                                       : "softmax_f32_warp32";
+  if (entry) {
     rc = builtin_function(s, "softmax", entry, &fn);
     if (rc) return rc;
     // 4 rows (warps) per 128-thread CTA; one CTA per 4 rows.

@@ -180,11 +180,22 @@ _ARITY_MSG = {"softmax": "CUDA softmax requires exactly one input and one output
 
 
 class Runtime:
-    """Dispatches OpRequests for the hot-path operators to the B200 kernels."""
+    """Dispatches OpRequests for the hot-path operators to the B200 kernels.
 
-    def __init__(self, session: Session, stream: Optional[Stream] = None):
+    With an `autotuner` (autotune.Autotuner), a request without an explicit `candidate`
+    attribute runs the candidate its exact TuneKey selected; the first request of a key
+    tunes it (capability, correctness against the first capable candidate, event-timed
+    benchmark, selection) and persists the decision. This is the runtime candidate
+    dispatch the reference leaves unwired (titan-runtime/src/lib.rs:3493-3495)."""
+
+    def __init__(self, session: Session, stream: Optional[Stream] = None, autotuner=None, budget=None):
         self.session = session
         self.stream = stream or session.create_stream()
+        self.autotuner = autotuner
+        self.budget = budget
+        self.last_tune = None  # TuneResult of the most recent search (None on cache hits)
+        self._device_key = None
+        self._artifact = None
 
     def execute(self, request: OpRequest, output: Optional[TensorHandle] = None) -> ExecutionHandle:
         name = request.operator
@@ -203,9 +214,24 @@ class Runtime:
                 output = TensorHandle.allocate(self.session, spec.dtype, spec.shape)
             except HalError as e:
                 raise ExecutionError(name, "allocate", str(e), e.status) from e
+        attrs = dict(request.attrs)
+        self.last_tune = None
+        if self.autotuner is not None and "candidate" not in attrs:
+            chosen = self._tuned_candidate(request, output, attrs)
+            if chosen:
+                attrs["candidate"] = chosen
+        ev = self._launch(name, request, output, attrs)
+        L = N.lib()
+        return ExecutionHandle([TensorHandle(self.session, output.buffer, spec.dtype, tuple(spec.shape),
+                                             contiguous_strides(spec.shape))],
+                               L.tb_last_candidate().decode(), L.tb_last_candidate().decode(),
+                               Event(self.session, ev))
+
+    def _launch(self, name: str, request: OpRequest, output: TensorHandle, attrs_dict: dict) -> int:
+        spec = request.outputs[0]
         out_c = c_tensor(output.buffer, spec.dtype, spec.shape, spec.resolved_strides())
         ins = [t.c_tensor() for t in request.inputs]
-        attrs, nattrs, _keep = _attrs(request.attrs)
+        attrs, nattrs, _keep = _attrs(attrs_dict)
         ev = ctypes.c_void_p(0)
         L = N.lib()
         fn = getattr(L, _OPS[name])
@@ -225,11 +251,67 @@ class Runtime:
         if st != N.TB_OK:
             op, detail = N.last_error()
             raise ExecutionError(name, op or "launch", detail, st)
-        handle = ExecutionHandle([TensorHandle(self.session, output.buffer, spec.dtype, tuple(spec.shape),
-                                               contiguous_strides(spec.shape))],
-                                 L.tb_last_candidate().decode(), L.tb_last_candidate().decode(),
-                                 Event(self.session, ev.value))
-        return handle
+        return ev.value
+
+    # ---- candidate dispatch ----
+    def tune_key(self, request: OpRequest):
+        """The exact TuneKey of a request (shapes, strides, dtypes, semantic attributes, device, library)."""
+        from . import autotune as A
+        if self._device_key is None:
+            fp = self.session.fingerprint()
+            self._device_key = f"{fp['model']}/{fp['capability_revision']}/{fp['sm_count']}sm"
+            self._artifact = A.library_identity()
+        spec = request.outputs[0]
+        shape = ",".join(str(list(t.shape)) for t in request.inputs) + "->" + str(list(spec.shape))
+        dtype = ",".join(t.dtype.name for t in request.inputs) + "->" + spec.dtype.name
+        sem = {k: v for k, v in sorted(request.attrs.items()) if k != "candidate"}
+        layout = (";".join(str(list(t.strides)) for t in request.inputs) + "->" + str(list(spec.resolved_strides()))
+                  + ";" + ",".join(f"{k}={v}" for k, v in sem.items()))
+        return A.TuneKey(operator=request.operator, device=self._device_key, shape=shape, dtype=dtype,
+                         layout=layout, artifact=self._artifact)
+
+    def _tuned_candidate(self, request: OpRequest, output: TensorHandle, attrs: dict) -> Optional[str]:
+        from . import autotune as A
+        name = request.operator
+        cands = A.CANDIDATES.get((name, request.inputs[0].dtype.name))
+        if not cands:
+            return None
+        key = self.tune_key(request)
+        hit = self.autotuner.get(key)
+        if hit is not None:
+            return hit.candidate
+        spec = request.outputs[0]
+
+        def run(c):
+            try:
+                self._launch(name, request, output, {**attrs, "candidate": c})
+                self.session.synchronize(self.stream)
+            except ExecutionError as e:
+                if e.status == N.TB_ERR_UNSUPPORTED:
+                    raise A.CandidateUnsupported(e.message) from e
+                raise
+
+        def read_output():
+            return TensorHandle(self.session, output.buffer, spec.dtype, tuple(spec.shape),
+                                contiguous_strides(spec.shape)).to_f32(self.stream)
+
+        def time_ns(c, warmups, samples):
+            cand_attrs = {**attrs, "candidate": c}
+            for _ in range(warmups):
+                self._launch(name, request, output, cand_attrs)
+            marks = [self.session.record(self.stream)]
+            for _ in range(samples):
+                self._launch(name, request, output, cand_attrs)
+                marks.append(self.session.record(self.stream))
+            self.session.synchronize(self.stream)
+            return [self.session.elapsed_ms(marks[i], marks[i + 1]) * 1e6 for i in range(samples)]
+
+        tol = A.TOLERANCE.get(spec.dtype.name, 1e-2)
+        result = self.autotuner.tune(key, cands[0], cands[1], run, read_output, time_ns, tol,
+                                     self.budget or A.TuneBudget())
+        self.autotuner.flush()
+        self.last_tune = result
+        return result.entry.candidate
 
 
 def fill_normal(count: int, seed: int, mean: float = 0.0, std: float = 1.0, dtype: DType = DType.F32,
