@@ -10,7 +10,7 @@
 //                two 64-column 128-byte-swizzled boxes each) through 2-stage rings.
 //   warp 1       owns all 512 TMEM columns: S_A | S_B | O_A | O_B (128 fp32 columns each).
 //                One lane issues, per key tile j,
-//                  PV_A(j-1) then S_A(j), PV_B(j-1) then S_B(j)
+//                  PV_A(j-1) (two halves) then S_A(j), PV_B(j-1) then S_B(j)
 //                so the tensor core works on one tile's products while the other
 //                tile's warpgroup exponentiates.
 //                  S_X(j)  = Q_X K_j^T   (SS: both operands K-major in shared memory)
@@ -22,9 +22,11 @@
 //                against the reference max (packed FFMA2 for s*scale - m; a share of
 //                the exponentials on the FMA/ALU pipes, the rest on the MUFU) and
 //                writes P as bf16 pairs over the first 64 columns of the same S
-//                region, where the TS-MMA reads it. The reference max moves, and O is
-//                rescaled in TMEM, only when the row max grows by more than 2^8, so
-//                P stays below 256 and the result is the exact online softmax.
+//                region, where the TS-MMA reads it: keys [0, 64) first, announced on
+//                p_half so the MMA lane issues their half of PV while the warps finish
+//                keys [64, 128) (p_full). The reference max moves, and O is rescaled
+//                in TMEM, only when the row max grows by more than 2^8, so P stays
+//                below 256 and the result is the exact online softmax.
 // Ordering: tcgen05.commit arrives once ALL earlier MMAs of the issuing thread are
 // done, so "S_X(j) ready" also means PV_X(j-1) finished reading P_X and writing O_X:
 // the softmax warps may then overwrite S/P and rescale O without further waits.
@@ -45,18 +47,18 @@ constexpr int HALF_BYTES = TILE_BYTES / 2;
 constexpr int THREADS = TB_SDPA2_THREADS;
 constexpr uint32_t IDESC_S = idesc_bf16_f32(BM, BN, false);
 constexpr uint32_t IDESC_O = idesc_bf16_f32(BM, HD, true);  // B = V, MN-major
-// The common path keeps the reference max of a row until a key tile's row sum of
-// exponentials exceeds this; every P of the row is then at most 2^32 (bf16 and
-// fp32 keep their relative precision at any scale, and O stays far from fp32
-// overflow: at most 2^38 times max|V| over 64 key tiles of 2^32 each).
-constexpr float kSumLimit = 4294967296.0f;
+// The reference max of a row moves (and O is rescaled) only when a key tile's row
+// max exceeds it by more than 2^8, so P <= 256 and the result is the exact online
+// softmax with the rescale skipped on most tiles.
+constexpr float kLazyRescaleLog2 = 8.0f;
 
 struct Barriers {
   uint64_t q_full;
   uint64_t k_full[2], k_empty[2];
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2];  // per query tile (A, B)
-  uint64_t p_full[2];  // per query tile
+  uint64_t p_half[2];  // per query tile: P of keys [0, 64) is in TMEM
+  uint64_t p_full[2];  // per query tile: P of keys [64, 128) is in TMEM
   uint64_t o_final;
   uint64_t drain;
   uint32_t tmem_base;
@@ -136,68 +138,6 @@ __device__ __forceinline__ void rescale_o(uint32_t o_tmem, float alpha) {
   }
 }
 
-// The rare path of a key tile, taken by the whole warp when some row's sum of
-// exponentials against the current reference max exceeded kSumLimit (or was not
-// finite: the first key tile, whose reference max is still -inf). S is still
-// intact in TMEM: the row max of the masked scores becomes the new reference,
-// O and l are rescaled, and P is recomputed and stored. Returns the row sum.
-// Out of line, so the common path keeps its registers.
-template <int kPolyPairsOf8>
-__device__ __noinline__ float softmax_tile_rescale(uint32_t s_tmem, uint32_t o_tmem, int valid, float scale_log2,
-                                                   bool o_live, float& m_used, float& l) {
-  const bool need_mask = valid < BN;
-  float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll 1
-  for (int c = 0; c < BN; c += 32) {
-    uint32_t cur[32];
-    tmem_ld_x32(s_tmem + c, cur);
-    tmem_ld_wait();
-    reg_fence(cur);
-    mask_max_chunk(cur, valid - c, need_mask, mx4);
-  }
-  const float mx = fmaxf(fmax3f(mx4[0], mx4[1], mx4[2]), mx4[3]) * scale_log2;  // scale_log2 > 0 commutes with max
-  const float m_new = fmaxf(m_used, mx);
-  const float alpha = exp2_mufu(m_used - m_new);  // 0 when m_used was -inf; 1 when the max did not move
-  l *= alpha;
-  if (o_live) rescale_o(o_tmem, alpha);
-  m_used = m_new;
-  const float2 scale2 = make_float2(scale_log2, scale_log2), neg_m2 = make_float2(-m_new, -m_new);
-  float2 rs4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-  uint32_t ca[32], cb[32];
-  // P chunk c lands on S columns [16c, 16c + 16): load each pair of chunks before
-  // storing any P over it.
-#pragma unroll 1
-  for (int c = 0; c < BN; c += 64) {
-    tmem_ld_x32(s_tmem + c, ca);
-    tmem_ld_x32(s_tmem + c + 32, cb);
-    tmem_ld_wait();
-    reg_fence(ca);
-    reg_fence(cb);
-    if (need_mask) {
-      mask_chunk(ca, valid - c);
-      mask_chunk(cb, valid - c - 32);
-    }
-    exp_chunk_store<kPolyPairsOf8>(ca, scale2, neg_m2, rs4, s_tmem + c / 2);
-    exp_chunk_store<kPolyPairsOf8>(cb, scale2, neg_m2, rs4, s_tmem + c / 2 + 16);
-  }
-  const float2 r = __fadd2_rn(__fadd2_rn(rs4[0], rs4[1]), __fadd2_rn(rs4[2], rs4[3]));
-  return r.x + r.y;
-}
-
-// Common-path exponentials of one 32-column chunk into 16 packed bf16 pairs (not
-// yet stored), with the row sum accumulated.
-template <int kPolyPairsOf8>
-__device__ __forceinline__ void exp_chunk(const uint32_t (&cur)[32], float2 scale2, float2 neg_m2, float2 (&rs)[4],
-                                          uint32_t* packed) {
-#pragma unroll
-  for (int i = 0; i < 32; i += 2) {
-    const float2 x = __ffma2_rn(make_float2(__uint_as_float(cur[i]), __uint_as_float(cur[i + 1])), scale2, neg_m2);
-    const float2 p = ((i >> 1) & 7) < kPolyPairsOf8 ? exp2_poly2(x) : make_float2(exp2_mufu(x.x), exp2_mufu(x.y));
-    rs[(i >> 1) & 3] = __fadd2_rn(rs[(i >> 1) & 3], p);
-    packed[i / 2] = pack_bf16x2(p.x, p.y);
-  }
-}
-
 __device__ __forceinline__ void load_tile(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int row0, int bh) {
   tma_load_3d(dst, map, bar, 0, row0, bh);
   tma_load_3d(dst + HALF_BYTES, map, bar, 64, row0, bh);
@@ -220,12 +160,12 @@ __device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t units) {
   return r;
 }
 
-// O (+)= P V for one 128-key tile: P from TMEM (bf16 pairs, 8 columns per 16 keys),
-// V MN-major in shared memory (16 keys = 2 KB per slice).
-__device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint64_t vd, bool accumulate) {
-  umma_bf16_ts(o_tmem, p_tmem, vd, IDESC_O, accumulate ? 1u : 0u);
+// O (+)= P V for keys [64 h, 64 h + 64) of a 128-key tile: P from TMEM (bf16 pairs,
+// 8 columns per 16 keys), V MN-major in shared memory (16 keys = 2 KB per slice).
+__device__ __forceinline__ void issue_pv_half(uint32_t o_tmem, uint32_t p_tmem, uint64_t vd, int h, bool accumulate) {
 #pragma unroll
-  for (int k = 1; k < BN / 16; ++k) umma_bf16_ts(o_tmem, p_tmem + k * 8, desc_add(vd, k * (2048 >> 4)), IDESC_O, 1u);
+  for (int k = 4 * h; k < 4 * h + 4; ++k)
+    umma_bf16_ts(o_tmem, p_tmem + k * 8, desc_add(vd, k * (2048 >> 4)), IDESC_O, (k > 0 || accumulate) ? 1u : 0u);
 }
 
 // S = Q K^T for one 128-key tile: both operands K-major, 16 dims per slice (two
@@ -268,6 +208,7 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
       mbar_init(&bars->v_full[i], 1);
       mbar_init(&bars->v_empty[i], 1);
       mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->p_half[i], 4);
       mbar_init(&bars->p_full[i], 4);
     }
     mbar_init(&bars->o_final, 1);
@@ -358,13 +299,21 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
         // Tile A: O_A += P_A(j-1) V_{j-1}, then S_A(j) = Q_A K_j^T; then the same for tile B.
         for (int x = 0; x < 2; ++x) {
           if (x ? pv_b : pv_a) {
-            if (!mbar_wait(&bars->p_full[x], (j - 1) & 1)) {
+            // The first half of P_x(j-1) arrives while its warps still exponentiate the second.
+            if (!mbar_wait(&bars->p_half[x], (j - 1) & 1)) {
               report_status(status, kFailMma | 3);
               ok = false;
               break;
             }
             tc_fence_after_sync();
-            issue_pv(tmem + (2 + x) * BN, tmem + x * BN, vd, j - 1 > 0);
+            issue_pv_half(tmem + (2 + x) * BN, tmem + x * BN, vd, 0, j - 1 > 0);
+            if (!mbar_wait(&bars->p_full[x], (j - 1) & 1)) {
+              report_status(status, kFailMma | 6);
+              ok = false;
+              break;
+            }
+            tc_fence_after_sync();
+            issue_pv_half(tmem + (2 + x) * BN, tmem + x * BN, vd, 1, true);
           }
           if (x ? s_b : s_a) {
             tc_fence_after_sync();
@@ -403,48 +352,59 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
       tc_fence_after_sync();
       const int valid = (causal ? min(Tk, q_row + 1) : Tk) - j * BN;  // visible leading keys of this tile
       const bool need_mask = valid < BN;
-      // One streamed pass: exponentials against the current reference max, P held
-      // in registers until the row sums show that no P exceeds kSumLimit.
-      const float2 neg_m2 = make_float2(-m_used, -m_used);
-      float2 rs4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      uint32_t packed[BN / 2];
-      uint32_t ca[32], cb[32];
+      // Pass 1: the row max over all 128 columns; chunks 0 and 1 stay in registers.
+      uint32_t ca[32], cb[32], ct[32];
       tmem_ld_x32(s_tmem, ca);
       tmem_ld_x32(s_tmem + 32, cb);
+      tmem_ld_x32(s_tmem + 64, ct);
       tmem_ld_wait();
       reg_fence(ca);
       reg_fence(cb);
-      if (need_mask) {
-        mask_chunk(ca, valid);
-        mask_chunk(cb, valid - 32);
-      }
-      exp_chunk<kPolyPairsOf8>(ca, scale2, neg_m2, rs4, &packed[0]);
-      tmem_ld_x32(s_tmem + 64, ca);
-      exp_chunk<kPolyPairsOf8>(cb, scale2, neg_m2, rs4, &packed[16]);
-      tmem_ld_x32(s_tmem + 96, cb);
+      reg_fence(ct);
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      mask_max_chunk(ca, valid, need_mask, mx4);
+      mask_max_chunk(cb, valid - 32, need_mask, mx4);
+      mask_max_chunk(ct, valid - 64, need_mask, mx4);
+      tmem_ld_x32(s_tmem + 96, ct);
       tmem_ld_wait();
-      reg_fence(ca);
-      reg_fence(cb);
-      if (need_mask) {
-        mask_chunk(ca, valid - 64);
-        mask_chunk(cb, valid - 96);
+      reg_fence(ct);
+      mask_max_chunk(ct, valid - 96, need_mask, mx4);
+      const float mx = fmaxf(fmax3f(mx4[0], mx4[1], mx4[2]), mx4[3]) * scale_log2;  // scale_log2 > 0 commutes with max
+      const bool grow = mx > m_used + kLazyRescaleLog2;
+      if (__any_sync(0xffffffffu, grow)) {
+        const float m_new = grow ? mx : m_used;
+        const float alpha = exp2_mufu(m_used - m_new);  // 0 on the first tile
+        l *= alpha;
+        // O_x = sum_{t<j} P_x(t) V_t is complete (S_x(j) was committed after PV_x(j-1)),
+        // and no PV of this tile starts before p_half below.
+        if (j > 0) rescale_o(o_tmem, alpha);
+        m_used = m_new;
       }
-      exp_chunk<kPolyPairsOf8>(ca, scale2, neg_m2, rs4, &packed[32]);
-      exp_chunk<kPolyPairsOf8>(cb, scale2, neg_m2, rs4, &packed[48]);
+      // Pass 2: P_x(j) as bf16 pairs over columns [0, 64) of S_x, where the TS-MMA reads
+      // it. Keys [0, 64) first (S chunks 0 and 1, in registers; their P covers columns
+      // [0, 32), which pass 1 has read), then p_half lets the MMA warp start on them
+      // while keys [64, 128) (columns the P never touches) are reloaded and done.
+      const float2 neg_m2 = make_float2(-m_used, -m_used);
+      float2 rs4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      tmem_ld_x32(s_tmem + 64, ct);
+      exp_chunk_store<kPolyPairsOf8>(ca, scale2, neg_m2, rs4, s_tmem);
+      exp_chunk_store<kPolyPairsOf8>(cb, scale2, neg_m2, rs4, s_tmem + 16);
+      tmem_st_wait();
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_half[x]);
+      tmem_ld_x32(s_tmem + 96, ca);
+      tmem_ld_wait();
+      reg_fence(ct);
+      reg_fence(ca);
+      if (need_mask) {
+        mask_chunk(ct, valid - 64);
+        mask_chunk(ca, valid - 96);
+      }
+      exp_chunk_store<kPolyPairsOf8>(ct, scale2, neg_m2, rs4, s_tmem + 32);
+      exp_chunk_store<kPolyPairsOf8>(ca, scale2, neg_m2, rs4, s_tmem + 48);
       const float2 rsum = __fadd2_rn(__fadd2_rn(rs4[0], rs4[1]), __fadd2_rn(rs4[2], rs4[3]));
-      float rs = rsum.x + rsum.y;
-      // rs <= kSumLimit bounds every P of the row by kSumLimit (all terms are >= 0);
-      // otherwise (or not finite) the warp takes the rescale path.
-      if (__any_sync(0xffffffffu, !(rs <= kSumLimit))) {
-        // O_x = sum_{t<j} P_x(t) V_t is complete (S_x(j) was committed after PV_x(j-1)).
-        rs = softmax_tile_rescale<kPolyPairsOf8>(s_tmem, o_tmem, valid, scale_log2, j > 0, m_used, l);
-      } else {
-        // P_x(j) as bf16 pairs into columns [0, 64) of S_x, where the TS-MMA reads it.
-#pragma unroll
-        for (int c = 0; c < BN / 2; c += 16)
-          tmem_st_x16(s_tmem + c, *reinterpret_cast<const uint32_t(*)[16]>(&packed[c]));
-      }
-      l += rs;
+      l += rsum.x + rsum.y;
       tmem_st_wait();
       tc_fence_before_sync();
       __syncwarp();
