@@ -310,6 +310,20 @@ tb_status tb_comm_deregister_buffer(tb_comm* comm, tb_buffer* buffer);
 tb_status tb_op_gemm_sharded(tb_comm* comm, tb_stream* stream, const tb_tensor* lhs, const tb_tensor* rhs_shard,
                              const tb_tensor* output, tb_buffer* workspace, tb_event** out);
 
+/* ---------------- Fused GEMM epilogue ---------------- */
+
+/* "gemm.bias_act": C = act(A B^T + bias) in one launch. Fuses the reference's gemm
+ * (titan-runtime/src/lib.rs:955-989) with broadcast.add of a per-column bias and its
+ * gelu (:625-640, erf by Abramowitz & Stegun 7.1.26) or silu (:3064) operators:
+ * the bias is added and the activation applied to the fp32 accumulator, which is
+ * rounded to bf16 once. A BF16 [M,K] row-major, B BF16 stored [N,K] (attribute
+ * transpose_rhs = 1), C BF16 [M,N]; bias F32 [N] or NULL; attributes activation
+ * ("none" | "gelu" | "silu"), transpose_lhs (0), transpose_rhs, candidate
+ * ("gemm_bf16_tn_bias_act"). Other layouts are TB_ERR_UNSUPPORTED. */
+tb_status tb_op_gemm_bias_act(tb_session* session, tb_stream* stream, const tb_tensor* lhs, const tb_tensor* rhs,
+                              const tb_tensor* bias, const tb_tensor* output, const tb_attr* attrs,
+                              uint32_t num_attrs, tb_event** out);
+
 /* ---------------- Allocation-free split-K GEMM ---------------- */
 
 /* No counterpart in the reference. The split-K bf16 GEMM of tb_op_gemm

@@ -167,6 +167,30 @@ def sdpa(q, k, v, causal=False) -> np.ndarray:
     return out
 
 
+def gelu(x: np.ndarray) -> np.ndarray:
+    """titan-runtime/src/lib.rs:625-640: 0.5 x (1 + erf(x / sqrt 2)) with erf from the
+    Abramowitz & Stegun 7.1.26 polynomial evaluated in f64 and rounded to f32, as the
+    reference's `erf_approximation` does; x / sqrt 2 is the f32 product (FRAC_1_SQRT_2)."""
+    x = np.asarray(x, dtype=np.float32)
+    z32 = (x * np.float32(0.70710678118654752)).astype(np.float32)
+    sign = np.sign(z32).astype(np.float64)
+    z = np.abs(z32).astype(np.float64)
+    t = 1.0 / (1.0 + 0.3275911 * z)
+    p = 1.061405429
+    p = p * t - 1.453152027
+    p = p * t + 1.421413741
+    p = p * t - 0.284496736
+    p = p * t + 0.254829592
+    erf = (sign * (1.0 - p * t * np.exp(-z * z))).astype(np.float32)
+    return (np.float32(0.5) * x * (np.float32(1.0) + erf)).astype(np.float32)
+
+
+def silu(x: np.ndarray) -> np.ndarray:
+    """titan-runtime/src/lib.rs:3064: value / (1 + exp(-value)) in f32."""
+    x = np.asarray(x, dtype=np.float32)
+    return (x / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
+
+
 def gemm_bf16_points(a_bits, b_bits, b_col_major, m, n, k, rows, cols, threads=0) -> np.ndarray:
     rows = np.ascontiguousarray(rows, dtype=np.int64)
     cols = np.ascontiguousarray(cols, dtype=np.int64)

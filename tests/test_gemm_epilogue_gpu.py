@@ -1,0 +1,89 @@
+"""gemm.bias_act (the GEMM with a fused bias + GELU/SiLU epilogue) on the B200 against
+the oracle: the reference's gemm (titan-runtime/src/lib.rs:955-989) on the same bf16
+inputs, plus the bias, then its gelu (:625-640) or silu (:3064) in f32. Tolerance:
+the bf16 bound max|err| <= 1e-2 * max|ref|."""
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+import titan_rs_b200 as tb
+from titan_rs_b200 import _native as N
+from titan_rs_b200.kernel_abi import DType
+
+from gpu_util import max_rel_err, run_op, upload
+
+pytestmark = pytest.mark.gpu
+BF16_TOL = 1e-2
+
+
+@pytest.fixture(scope="module")
+def session():
+    s = tb.Session(0)
+    yield s
+    s.close()
+
+
+@pytest.fixture(scope="module")
+def rt(session):
+    return tb.Runtime(session)
+
+
+def _inputs(m, n, k, seed):
+    a = tb.fill_normal(m * k, seed=seed * 16, dtype=DType.BF16)
+    b = tb.fill_normal(n * k, seed=seed * 16 + 1, std=1.0 / math.sqrt(k), dtype=DType.BF16)
+    bias = tb.fill_normal(n, seed=seed * 16 + 2, std=0.5)
+    return a, b, bias
+
+
+def _reference(a, b, bias, m, n, k, act):
+    rows, cols = np.divmod(np.arange(m * n), n)
+    acc = oracle.gemm_bf16_points(a, b, True, m, n, k, rows, cols).reshape(m, n)
+    if bias is not None:
+        acc = (acc + bias[None, :]).astype(np.float32)
+    return {"none": lambda x: x, "gelu": oracle.gelu, "silu": oracle.silu}[act](acc)
+
+
+@pytest.mark.parametrize("act", ["none", "gelu", "silu"])
+@pytest.mark.parametrize("with_bias", [True, False])
+@pytest.mark.parametrize("m,n,k", [(300, 520, 1024), (128, 256, 64), (517, 264, 2048)])
+def test_gemm_bias_act_matches_oracle(session, rt, m, n, k, act, with_bias):
+    a, b, bias = _inputs(m, n, k, seed=m + n + k)
+    ins = [upload(session, rt.stream, a.reshape(m, k), DType.BF16), upload(session, rt.stream, b.reshape(n, k), DType.BF16)]
+    if with_bias:
+        ins.append(upload(session, rt.stream, bias))
+    h = run_op(rt, "gemm.bias_act", ins, DType.BF16, (m, n), {"transpose_rhs": True, "activation": act})
+    assert h.candidate == "gemm_bf16_tn_bias_act"
+    got = h.outputs[0].to_f32()
+    ref = _reference(a, b, bias if with_bias else None, m, n, k, act)
+    assert np.isfinite(got).all()
+    assert max_rel_err(got, ref) <= BF16_TOL, max_rel_err(got, ref)
+
+
+def test_no_bias_no_activation_equals_plain_gemm_bitwise(session, rt):
+    m, n, k = 640, 512, 1024
+    a, b, _ = _inputs(m, n, k, seed=5)
+    ta, tbb = upload(session, rt.stream, a.reshape(m, k), DType.BF16), upload(session, rt.stream, b.reshape(n, k), DType.BF16)
+    fused = run_op(rt, "gemm.bias_act", [ta, tbb], DType.BF16, (m, n), {"transpose_rhs": True, "activation": "none"})
+    plain = run_op(rt, "gemm", [ta, tbb], DType.BF16, (m, n), {"transpose_rhs": True, "candidate": "gemm_bf16_tn"})
+    np.testing.assert_array_equal(fused.outputs[0].to_numpy(), plain.outputs[0].to_numpy())
+
+
+def test_gemm_bias_act_contract(session, rt):
+    m, n, k = 64, 128, 64
+    a, b, bias = _inputs(m, n, k, seed=9)
+    ta, tbb = upload(session, rt.stream, a.reshape(m, k), DType.BF16), upload(session, rt.stream, b.reshape(n, k), DType.BF16)
+
+    def err(inputs, attrs, shape=(m, n)):
+        with pytest.raises(tb.ExecutionError) as e:
+            run_op(rt, "gemm.bias_act", inputs, DType.BF16, shape, attrs)
+        return e.value
+
+    e = err([ta, tbb, upload(session, rt.stream, bias[: n // 2])], {"transpose_rhs": True})
+    assert e.phase == "contract" and "F32 [N]" in e.message
+    assert "activation" in err([ta, tbb], {"transpose_rhs": True, "activation": "relu"}).message
+    assert "unsupported attributes" in err([ta, tbb], {"transpose_rhs": True, "axis": 1}).message
+    e = err([ta, upload(session, rt.stream, b.reshape(k, n), DType.BF16)], {"activation": "gelu"})
+    assert e.status == N.TB_ERR_UNSUPPORTED and "transpose_rhs" in e.message
+    assert "output shape" in err([ta, tbb], {"transpose_rhs": True}, shape=(m, n + 8)).message

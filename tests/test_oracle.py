@@ -156,3 +156,17 @@ def test_softmax_mt_matches_single_thread():
     rng = np.random.default_rng(1)
     x = (rng.standard_normal((64, 257)) * 2).astype(np.float32)
     np.testing.assert_array_equal(oracle.softmax_rows_mt(x), oracle.softmax(x))
+
+
+def test_gelu_and_silu_match_the_reference_known_answers():
+    """projects/titan-runtime/tests/cpu_reference_ops.rs:438-442."""
+    x = np.array([-1.0, 0.0, 1.0], np.float32)
+    s = oracle.silu(x)
+    assert abs(s[0] + 0.26894143) < 1e-6 and s[1] == 0.0 and abs(s[2] - 0.7310586) < 1e-6
+    g = oracle.gelu(x)
+    assert abs(g[0] + 0.15865526) < 2e-6 and g[1] == 0.0 and abs(g[2] - 0.8413447) < 2e-6
+    # The erf polynomial (|error| <= 1.5e-7) against the exact GELU over a range.
+    from math import erf
+    xs = np.linspace(-8, 8, 4001, dtype=np.float32)
+    exact = np.array([0.5 * v * (1 + erf(v / 2 ** 0.5)) for v in xs.astype(np.float64)])
+    assert np.max(np.abs(oracle.gelu(xs) - exact)) < 2e-6

@@ -130,6 +130,8 @@ _SIGNATURES = {
     "tb_comm_barrier": (_S, [_P, _P]),
     "tb_comm_register_buffer": (_S, [_P, _P, _P]),
     "tb_comm_deregister_buffer": (_S, [_P, _P]),
+    "tb_op_gemm_bias_act": (_S, [_P, _P, ctypes.POINTER(Tensor), ctypes.POINTER(Tensor), ctypes.POINTER(Tensor),
+                                 ctypes.POINTER(Tensor), ctypes.POINTER(Attr), _U32, _PP]),
     "tb_op_gemm_sharded": (_S, [_P, _P, ctypes.POINTER(Tensor), ctypes.POINTER(Tensor), ctypes.POINTER(Tensor), _P,
                                 _PP]),
     "tb_gemm_bf16_splitk_noalloc": (_S, [_U64, _P, _P, _P, _S, _S, _S, _S]),

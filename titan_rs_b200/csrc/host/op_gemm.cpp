@@ -211,3 +211,80 @@ extern "C" tb_status tb_op_gemm(tb_session* session, tb_stream* stream, const tb
   if (rc) return rc;
   return record_event(s, st, nullptr, out);
 }
+
+// "gemm.bias_act": C = act(A B^T + bias) in one tcgen05 GEMM whose epilogue adds the
+// fp32 bias and applies the activation on the fp32 accumulator before the single bf16
+// rounding (the GEMM-epilogue fusion of the reference's gemm, broadcast.add, gelu and
+// silu operators: titan-runtime/src/lib.rs:955-989, 625-640, 3064).
+extern "C" tb_status tb_op_gemm_bias_act(tb_session* session, tb_stream* stream, const tb_tensor* lhs,
+                                         const tb_tensor* rhs, const tb_tensor* bias, const tb_tensor* output,
+                                         const tb_attr* attrs, uint32_t num_attrs, tb_event** out) {
+  Session* s = reinterpret_cast<Session*>(session);
+  if (!s) return set_error(TB_ERR_INVALID, "contract", "null session");
+  if (!lhs || !rhs || !output) return contract("gemm.bias_act requires two rank-2 inputs, an optional bias and one output");
+  bool tl = false, tr = false;
+  int act = TB_ACT_NONE;
+  for (uint32_t i = 0; i < num_attrs; ++i) {
+    const char* key = attrs[i].key;
+    if (!key) return contract("gemm.bias_act received an unnamed attribute");
+    if (strcmp(key, "candidate") == 0) {
+      if (!attrs[i].str || strcmp(attrs[i].str, "gemm_bf16_tn_bias_act") != 0)
+        return contract(std::string("unknown gemm.bias_act candidate ") + (attrs[i].str ? attrs[i].str : "(null)"));
+    } else if (strcmp(key, "activation") == 0) {
+      if (!attrs[i].str) return contract("gemm.bias_act activation must be a string");
+      if (strcmp(attrs[i].str, "none") == 0) act = TB_ACT_NONE;
+      else if (strcmp(attrs[i].str, "gelu") == 0) act = TB_ACT_GELU;
+      else if (strcmp(attrs[i].str, "silu") == 0) act = TB_ACT_SILU;
+      else return contract(std::string("gemm.bias_act activation must be none, gelu or silu, not ") + attrs[i].str);
+    } else if (strcmp(key, "transpose_lhs") == 0 || strcmp(key, "transpose_rhs") == 0) {
+      if (attrs[i].str || attrs[i].value < 0 || attrs[i].value > 1) return contract(std::string(key) + " must be a bool");
+      (strcmp(key, "transpose_lhs") == 0 ? tl : tr) = attrs[i].value != 0;
+    } else {
+      return contract("gemm.bias_act received unsupported attributes");
+    }
+  }
+  if (lhs->dtype != TB_BF16 || rhs->dtype != TB_BF16 || output->dtype != TB_BF16)
+    return contract("gemm.bias_act requires BF16 A, B and C");
+  if (lhs->rank != 2 || rhs->rank != 2) return contract("gemm requires exactly two rank-2 inputs");
+  if (!is_contiguous(lhs) || !is_contiguous(rhs) || output->rank != 2 || !is_contiguous(output))
+    return contract("gemm.bias_act requires contiguous rank-2 tensors");
+  const uint64_t m = tl ? lhs->shape[1] : lhs->shape[0];
+  const uint64_t k = tl ? lhs->shape[0] : lhs->shape[1];
+  const uint64_t rk = tr ? rhs->shape[1] : rhs->shape[0];
+  const uint64_t n = tr ? rhs->shape[0] : rhs->shape[1];
+  if (k != rk) return contract("gemm inner dimensions must match");
+  if (output->shape[0] != m || output->shape[1] != n) return contract("gemm output shape mismatch");
+  if (m == 0 || n == 0 || k == 0) return contract("CUDA GEMM M, N, and K must be non-zero");
+  if (m > 0x7fffffffull || n > 0x7fffffffull || k > 0x7fffffffull) return contract("CUDA GEMM M exceeds u32 ABI");
+  if (bias && (bias->dtype != TB_F32 || bias->rank != 1 || bias->shape[0] != n || !is_contiguous(bias)))
+    return contract("gemm.bias_act bias must be a contiguous F32 [N] tensor");
+  Stream* st = nullptr;
+  tb_status rc = check_stream(s, stream, &st);
+  if (rc) return rc;
+  Buffer *ba = nullptr, *bb = nullptr, *bc = nullptr, *bbias = nullptr;
+  if ((rc = tensor_buffer(s, lhs, "gemm lhs", &ba)) || (rc = tensor_buffer(s, rhs, "gemm rhs", &bb)) ||
+      (rc = tensor_buffer(s, output, "gemm output", &bc)) || (bias && (rc = tensor_buffer(s, bias, "gemm bias", &bbias))))
+    return rc;
+  const CUdeviceptr pa = ba->ptr, pb = bb->ptr, pc = bc->ptr;
+  if (tl || !tr || k % 8 != 0 || ((pa | pb | pc) & 15) != 0)
+    return unsupported("gemm.bias_act needs A [M,K] row-major, B stored [N,K] (transpose_rhs), K % 8 == 0 and "
+                       "16-byte aligned tensors");
+  rc = activate(s);
+  if (rc) return rc;
+  int M = (int)m, N = (int)n, K = (int)k;
+  CUtensorMap ta, tbm;
+  if ((rc = tmap_bf16_2d(&ta, pa, m, k, k, TB_GEMM_BM, TB_GEMM_BK, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = tmap_bf16_2d(&tbm, pb, n, k, k, TB_GEMM_BN, TB_GEMM_BK, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  CUfunction fn = nullptr;
+  rc = builtin_function(s, "gemm_bf16", "gemm_bf16_tn_bias_act", &fn);
+  if (rc) return rc;
+  const long long tiles = (long long)((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN);
+  const unsigned grid = (unsigned)(tiles < s->sm_count ? tiles : s->sm_count);
+  CUdeviceptr c = pc, pbias = bbias ? bbias->ptr : 0, status = s->status.device;
+  long long ldc = N;
+  void* params[] = {&ta, &tbm, &c, &pbias, &act, &M, &N, &K, &ldc, &status};
+  rc = launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_SMEM_BYTES, params, "gemm_bf16_tn_bias_act");
+  if (rc) return rc;
+  return record_event(s, st, nullptr, out);
+}

@@ -47,6 +47,28 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
   tb::umma::run(p, status, kFailGemm);
 }
 
+// GEMM with a fused epilogue: C = act(A B^T + bias) (bias fp32 [N] or null; act an
+// epilogue_math.cuh Activation), rounded to bf16 once.
+extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
+    gemm_bf16_tn_bias_act(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                          __nv_bfloat16* __restrict__ c, const float* __restrict__ bias, int act, int M, int N, int K,
+                          long long ldc, uint32_t* status) {
+  tb::gemm::GemmPolicy p;
+  p.ta = &tmap_a;
+  p.tb = &tmap_b;
+  p.c = c;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = ldc;
+  p.vec_ok = (ldc % 8) == 0 && (reinterpret_cast<uintptr_t>(c) & 15) == 0;
+  p.num_m = (M + tb::umma::BM - 1) / tb::umma::BM;
+  p.num_n = (N + tb::umma::BN - 1) / tb::umma::BN;
+  p.bias = bias;
+  p.act = act;
+  tb::umma::run(p, status, kFailGemm);
+}
+
 // Fused GEMM + all-gather: this rank's N-shard (B rows [N, K]) of C[M, ldc], written
 // at column col0 into every rank's C through `outs` (its own entry included).
 // Call `epoch` of the registered output, synchronised with the other ranks in-kernel:

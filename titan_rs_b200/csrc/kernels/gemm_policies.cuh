@@ -1,7 +1,8 @@
 // Problem policies for the tcgen05 GEMM pipeline (umma_pipeline.cuh) and the
 // split-K reduction, shared by every translation unit that instantiates them.
 //
-//   GemmPolicy     C[M,N] bf16 = A[M,K] x B^T, B stored [N,K] (column-major B).
+//   GemmPolicy     C[M,N] bf16 = act(A[M,K] x B^T + bias), B stored [N,K] (column-major B);
+//                  bias and act optional (the fused epilogue of gemm.bias_act).
 //   SplitKPolicy   fp32 partial tiles of the same product; work unit
 //                  t = split * (num_m * num_n) + output tile, each split covering
 //                  kb_per_split k-blocks of 64 (the last one possibly fewer, none empty),
@@ -26,6 +27,8 @@ struct GemmPolicy {
   long long ldc;
   bool vec_ok;
   int num_m, num_n;
+  const float* bias = nullptr;  // optional fp32 [N], added to the accumulator
+  int act = kActNone;           // optional activation after the bias
 
   __device__ int num_tiles() const { return num_m * num_n; }
   __device__ void k_blocks(int, int& kb0, int& kb1) const {
@@ -45,7 +48,7 @@ struct GemmPolicy {
     const int gr = m_blk * umma::BM + row;
     const int gc = n_blk * umma::BN + col;
     if (gr >= M || gc >= N) return;
-    umma::store_bf16_chunk(c + (long long)gr * ldc + gc, N - gc, vec_ok, r, nullptr);
+    umma::store_bf16_chunk(c + (long long)gr * ldc + gc, N - gc, vec_ok, r, bias ? bias + gc : nullptr, act);
   }
   __device__ void finish() const {}
 };

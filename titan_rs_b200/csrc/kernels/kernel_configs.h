@@ -38,3 +38,8 @@
 #define TB_SDPA3_THREADS 192
 #define TB_SDPA3_BARRIER_BYTES 256
 #define TB_SDPA3_SMEM_BYTES (32768 + 4 * 16384 + TB_SDPA3_BARRIER_BYTES + 1024)
+
+// Epilogue activations (epilogue_math.cuh), shared with the host operators.
+#define TB_ACT_NONE 0
+#define TB_ACT_GELU 1
+#define TB_ACT_SILU 2

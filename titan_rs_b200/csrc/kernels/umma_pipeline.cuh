@@ -15,6 +15,7 @@
 // the status word, drains its copies and MMAs, frees TMEM and exits.
 #pragma once
 
+#include "epilogue_math.cuh"
 #include "kernel_configs.h"
 #include "sm100.cuh"
 
@@ -61,9 +62,10 @@ __device__ __forceinline__ void grouped_tile(int t, int num_m, int num_n, int gr
   n_blk = r / gm;
 }
 
-// Packs 32 fp32 accumulator columns (+ optional per-column bias) into bf16 and stores them.
+// Packs 32 fp32 accumulator columns (+ optional per-column bias, then an optional
+// activation, epilogue_math.cuh) into bf16 and stores them.
 __device__ __forceinline__ void store_bf16_chunk(__nv_bfloat16* dst, int valid_cols, bool vec_ok,
-                                                 const uint32_t (&r)[32], const float* bias) {
+                                                 const uint32_t (&r)[32], const float* bias, int act = kActNone) {
   float f[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
@@ -71,6 +73,10 @@ __device__ __forceinline__ void store_bf16_chunk(__nv_bfloat16* dst, int valid_c
 #pragma unroll
     for (int j = 0; j < 32; ++j)
       if (j < valid_cols) f[j] += bias[j];
+  }
+  if (act != kActNone) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = activate(f[j], act);
   }
   if (vec_ok && valid_cols >= 32) {
     uint4* d4 = reinterpret_cast<uint4*>(dst);

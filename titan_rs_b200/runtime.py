@@ -171,12 +171,14 @@ def _attrs(attrs: dict):
 
 
 _OPS = {"softmax": "tb_op_softmax", "gemm": "tb_op_gemm", "scaled_dot_product_attention": "tb_op_sdpa",
-        "conv2d": "tb_op_conv2d"}
-_ARITY = {"softmax": (1, 1), "gemm": (2, 2), "scaled_dot_product_attention": (3, 3), "conv2d": (2, 3)}
+        "conv2d": "tb_op_conv2d", "gemm.bias_act": "tb_op_gemm_bias_act"}
+_ARITY = {"softmax": (1, 1), "gemm": (2, 2), "scaled_dot_product_attention": (3, 3), "conv2d": (2, 3),
+          "gemm.bias_act": (2, 3)}
 _ARITY_MSG = {"softmax": "CUDA softmax requires exactly one input and one output",
               "gemm": "gemm requires exactly two rank-2 inputs",
               "scaled_dot_product_attention": "scaled dot-product attention requires exactly three rank-4 BHTD inputs",
-              "conv2d": "conv2d requires rank-4 NCHW input, rank-4 OIHW weight, and optional bias"}
+              "conv2d": "conv2d requires rank-4 NCHW input, rank-4 OIHW weight, and optional bias",
+              "gemm.bias_act": "gemm.bias_act requires two rank-2 inputs, an optional bias and one output"}
 
 
 class Runtime:
@@ -244,6 +246,10 @@ class Runtime:
         elif name == "scaled_dot_product_attention":
             st = fn(self.session.ptr, self.stream.ptr, ctypes.byref(ins[0]), ctypes.byref(ins[1]),
                     ctypes.byref(ins[2]), ctypes.byref(out_c), attrs, nattrs, ctypes.byref(ev))
+        elif name == "gemm.bias_act":
+            bias = ctypes.byref(ins[2]) if len(ins) > 2 else None
+            st = fn(self.session.ptr, self.stream.ptr, ctypes.byref(ins[0]), ctypes.byref(ins[1]), bias,
+                    ctypes.byref(out_c), attrs, nattrs, ctypes.byref(ev))
         else:
             bias = ctypes.byref(ins[2]) if len(ins) > 2 else None
             st = fn(self.session.ptr, self.stream.ptr, ctypes.byref(ins[0]), ctypes.byref(ins[1]), bias,
