@@ -123,7 +123,22 @@ def test_conv2d_bf16_implicit_gemm_matches_oracle(session, rt, n, hh, ww, cin, c
                seed=n + hh + cin + cout + r)
 
 
-@pytest.mark.parametrize("stride,groups,cin", [((2, 2), 1, 64), ((1, 1), 2, 64), ((1, 1), 1, 12)])
+@pytest.mark.parametrize("n,hh,ww,cin,cout,r,s,stride,pad,dil,bias", [
+    (2, 9, 10, 64, 32, 3, 3, (2, 2), (1, 1), (1, 1), True),     # the reference's stride-2 case, tensor cores
+    (2, 56, 56, 64, 128, 3, 3, (2, 2), (1, 1), (1, 1), False),  # ResNet-style downsampling
+    (3, 17, 23, 128, 256, 3, 3, (2, 1), (1, 1), (1, 1), True),  # mixed strides, ragged tiles
+    (2, 20, 20, 64, 64, 1, 1, (2, 2), (0, 0), (1, 1), False),   # 1x1 projection shortcut
+    (1, 31, 29, 64, 256, 5, 5, (3, 3), (2, 2), (1, 1), False),  # stride 3
+    (2, 24, 24, 64, 128, 3, 3, (2, 2), (2, 2), (2, 2), True),   # stride 2 + dilation 2
+])
+def test_conv2d_bf16_strided_implicit_gemm_matches_oracle(session, rt, n, hh, ww, cin, cout, r, s, stride, pad, dil,
+                                                          bias):
+    """Strides reach the tensor-core kernel as TMA traversal strides (input box 8*s wide)."""
+    check_nhwc(session, rt, n, hh, ww, cin, cout, r, s, stride, pad, dil, bias, "conv2d_fprop_bf16_nhwc",
+               seed=n + hh + cin + cout + stride[0])
+
+
+@pytest.mark.parametrize("stride,groups,cin", [((1, 1), 2, 64), ((1, 1), 1, 12), ((2, 2), 1, 12)])
 def test_conv2d_bf16_generic_path(session, rt, stride, groups, cin):
     check_nhwc(session, rt, 2, 9, 10, cin, 32, 3, 3, stride, (1, 1), (1, 1), True, "conv2d_bf16_nhwc_generic",
                seed=5 + groups + cin, groups=groups)

@@ -2,7 +2,7 @@
 // conv2d (titan-runtime/src/lib.rs:2406-2573, 991-1088), then the kernel choice:
 //   F32 (NCHW input, OIHW weight)        -> conv2d_f32 (reference ABI kernel, bit-exact)
 //   BF16 with layout="NHWC" (KRSC weight):
-//     groups 1, Cin % 8 == 0, Cout % 8 == 0, stride 1, 16-byte aligned
+//     groups 1, Cin % 8 == 0, Cout % 8 == 0, stride <= 8, 16-byte aligned
 //                                          -> conv2d_fprop_bf16_nhwc (tcgen05 implicit GEMM)
 //     otherwise                            -> conv2d_bf16_nhwc_generic (CUDA cores)
 // A `candidate` attribute (not a reference attribute; the autotuner's) names one of
@@ -157,7 +157,9 @@ extern "C" tb_status tb_op_conv2d(tb_session* session, tb_stream* stream, const 
                       &has_bias};
     rc = launch_builtin(s, st, fn, (unsigned)grid, 1, 1, 256, 0, params, "conv2d_f32");
   } else {
-    const bool tc_ok = G == 1 && C % 8 == 0 && K % 8 == 0 && SH == 1 && SW == 1 && ((px | pw_ | py) & 15) == 0;
+    // Strides reach the kernel as TMA traversal strides, which must be at most 8.
+    const bool tc_ok = G == 1 && C % 8 == 0 && K % 8 == 0 && SH >= 1 && SH <= 8 && SW >= 1 && SW <= 8 &&
+                       ((px | pw_ | py) & 15) == 0;
     const bool want_generic = candidate && strcmp(candidate, "conv2d_bf16_nhwc_generic") == 0;
     if (candidate && !want_generic && !tc_ok)
       return unsupported(std::string("candidate ") + candidate + " does not take this shape, stride or alignment");
