@@ -1,0 +1,71 @@
+"""Graph compile passes and binding errors (no GPU): the ExecutionPlan mirror of
+projects/titan-runtime/src/lib.rs:176-276, 3472-3483 and the gemm-epilogue fusion."""
+import pytest
+
+from titan_rs_b200 import graph as G
+from titan_rs_b200.kernel_abi import DType
+from titan_rs_b200.runtime import ExecutionError, TensorSpec
+
+
+def spec(dtype, *shape):
+    return TensorSpec(dtype, tuple(shape))
+
+
+def mlp_graph(act="gelu", bias_dtype=DType.F32, output_intermediate=False, transpose_rhs=True):
+    # x[8,16] W1[32,16] b1[32] -> gemm -> add -> act -> h[8,32]; W2[4,32] b2[4] -> gemm -> add -> y[8,4]
+    values = {0: spec(DType.BF16, 8, 16), 1: spec(DType.BF16, 32, 16), 2: spec(bias_dtype, 32),
+              3: spec(DType.BF16, 8, 32), 4: spec(DType.BF16, 8, 32), 5: spec(DType.BF16, 8, 32),
+              6: spec(DType.BF16, 4, 32), 7: spec(DType.F32, 4), 8: spec(DType.BF16, 8, 4), 9: spec(DType.BF16, 8, 4)}
+    nodes = [G.GraphNode(10, "gemm", [0, 1], [3], {"transpose_rhs": transpose_rhs}),
+             G.GraphNode(11, "broadcast.add", [3, 2], [4]),
+             G.GraphNode(12, act, [4], [5]),
+             G.GraphNode(13, "gemm", [5, 6], [8], {"transpose_rhs": True}),
+             G.GraphNode(14, "broadcast.add", [7, 8], [9])]
+    outputs = [9] + ([4] if output_intermediate else [])
+    return G.Graph([0, 1, 2, 6, 7], outputs, values, nodes)
+
+
+def test_fusion_turns_each_gemm_chain_into_one_node():
+    plan = G.compile(mlp_graph())
+    ops = [(n.operator, n.inputs, n.outputs, n.attrs) for n in plan.graph.nodes]
+    assert ops == [("gemm.bias_act", [0, 1, 2], [5], {"transpose_rhs": True, "activation": "gelu"}),
+                   ("gemm.bias_act", [5, 6, 7], [9], {"transpose_rhs": True, "activation": "none"})]
+    assert 3 not in plan.graph.values and 4 not in plan.graph.values and 8 not in plan.graph.values
+    fusion = [r for r in plan.reports if r.name == "fusion.gemm_epilogue"][0]
+    assert fusion.changed and len(fusion.notes) == 2
+
+
+def test_fusion_keeps_what_it_cannot_absorb():
+    # A visible intermediate stops the chain at that value.
+    g = G.compile(mlp_graph(output_intermediate=True)).graph
+    assert [n.operator for n in g.nodes] == ["gemm.bias_act", "gelu", "gemm.bias_act"]
+    assert g.nodes[0].attrs["activation"] == "none" and g.nodes[0].outputs == [4]
+    # A bf16 bias or an untransposed B is left alone.
+    assert [n.operator for n in G.compile(mlp_graph(bias_dtype=DType.BF16)).graph.nodes][:3] == \
+        ["gemm", "broadcast.add", "gelu"]
+    assert G.compile(mlp_graph(transpose_rhs=False)).graph.nodes[0].operator == "gemm"
+    assert G.compile(mlp_graph(act="silu")).graph.nodes[0].attrs["activation"] == "silu"
+
+
+def test_dead_code_and_empty_graph():
+    g = mlp_graph()
+    g.outputs = [5]  # the second layer is dead
+    plan = G.compile(g)
+    assert [n.id for n in plan.graph.nodes] == [10]
+    assert [r.changed for r in plan.reports if r.name == "dce"] == [True]
+    empty = G.Graph([0], [0], {0: spec(DType.F32, 4)}, [G.GraphNode(1, "softmax", [0], [1])])
+    empty.values[1] = spec(DType.F32, 4)
+    with pytest.raises(ExecutionError) as e:
+        G.compile(empty)
+    assert e.value.phase == "compile" and "no nodes" in e.value.message
+
+
+def test_validation_and_binding_errors():
+    g = mlp_graph()
+    g.nodes[0].inputs = [0, 99]
+    with pytest.raises(ExecutionError, match="before it is produced"):
+        G.compile(g)
+    plan = G.compile(mlp_graph())
+    with pytest.raises(ExecutionError) as e:
+        plan.execute(runtime=None, bindings={0: object()})
+    assert e.value.phase == "bind" and "missing binding for input value 1" in e.value.message
