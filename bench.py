@@ -12,7 +12,8 @@ Inputs are seeded synthetic data (no dataset exists for this path).
 
 `value` is the device-timed whole-job throughput with inputs resident in HBM;
 `e2e` is the same metric through the C ABI with pinned-host inputs copied in and
-the result copied out inside every timed step. `--impl reference` times the CPU
+the result copied out inside every timed step (steps pipelined over two streams, so one
+step's upload overlaps the previous step's download). `--impl reference` times the CPU
 restatement of the reference's scalar operator (oracle/) on the host cores.
 """
 from __future__ import annotations
@@ -131,7 +132,10 @@ class Workload:
     def step(self):
         raise NotImplementedError
 
-    def e2e_step(self):
+    def e2e_upload(self, stream):
+        raise NotImplementedError
+
+    def e2e_download(self, stream):
         raise NotImplementedError
 
     def h2d_bytes(self) -> int:
@@ -193,10 +197,11 @@ class SoftmaxWorkload(Workload):
         if rc:
             raise RuntimeError(self.N.last_error())
 
-    def e2e_step(self):
-        self.s.upload_pinned(self.st, self.din, self.host_in)
-        self.step()
-        self.s.download_pinned(self.st, self.dout, self.host_out)
+    def e2e_upload(self, stream):
+        self.s.upload_pinned(stream, self.din, self.host_in)
+
+    def e2e_download(self, stream):
+        self.s.download_pinned(stream, self.dout, self.host_out)
 
     def h2d_bytes(self):
         return self.nbytes
@@ -322,11 +327,12 @@ class GemmWorkload(Workload):
         session.synchronize(stream)
         return session.elapsed_ms(e0, e1) / steps
 
-    def e2e_step(self):
-        self.s.upload_pinned(self.st, self.da, self.host_a)
-        self.s.upload_pinned(self.st, self.db, self.host_b)
-        self.step()
-        self.s.download_pinned(self.st, self.dc, self.host_c)
+    def e2e_upload(self, stream):
+        self.s.upload_pinned(stream, self.da, self.host_a)
+        self.s.upload_pinned(stream, self.db, self.host_b)
+
+    def e2e_download(self, stream):
+        self.s.download_pinned(stream, self.dc, self.host_c)
 
     def h2d_bytes(self):
         return self.a_bytes + self.b_bytes
@@ -420,11 +426,12 @@ class SdpaWorkload(Workload):
         if rc:
             raise RuntimeError(self.Nn.last_error())
 
-    def e2e_step(self):
+    def e2e_upload(self, stream):
         for h, d in zip(self.hosts, self.dev):
-            self.s.upload_pinned(self.st, d, h)
-        self.step()
-        self.s.download_pinned(self.st, self.do, self.host_o)
+            self.s.upload_pinned(stream, d, h)
+
+    def e2e_download(self, stream):
+        self.s.download_pinned(stream, self.do, self.host_o)
 
     def h2d_bytes(self):
         return 3 * self.nbytes
@@ -532,12 +539,13 @@ class ConvWorkload(Workload):
         if rc:
             raise RuntimeError(self.Nn.last_error())
 
-    def e2e_step(self):
-        self.s.upload_pinned(self.st, self.dx[0], self.host_x)
-        self.s.upload_pinned(self.st, self.dw, self.host_w)
-        self.i = 0
-        self.step()
-        self.s.download_pinned(self.st, self.dy[0], self.host_y)
+    def e2e_upload(self, stream):
+        self.s.upload_pinned(stream, self.dx[0], self.host_x)
+        self.s.upload_pinned(stream, self.dw, self.host_w)
+        self.i = 0  # the next step() uses input/output pair 0
+
+    def e2e_download(self, stream):
+        self.s.download_pinned(stream, self.dy[0], self.host_y)
 
     def h2d_bytes(self):
         return self.x_bytes + self.w_bytes
@@ -814,19 +822,36 @@ def main(argv=None) -> int:
     # Captured on the 1-GPU configuration of each kernel; a shard has other traffic.
     traffic = TRAFFIC_PER_LAUNCH.get(wl.kernel) if wl.world == 1 and not args.small else None
 
-    # End to end through the C ABI with pinned host buffers.
+    # End to end through the C ABI with pinned host buffers: every step copies its inputs
+    # in and its result out. Steps are pipelined as a server would run them: uploads and
+    # the operator on the main stream, downloads on a second stream, so step i+1's upload
+    # overlaps step i's download (PCIe is full duplex); the operator of step i+1 waits
+    # for step i's download, since it overwrites the result buffer.
     e2e_ms = e2e_value = None
     if not args.small:
-        for _ in range(2):
-            wl.e2e_step()
+        out_stream = session.create_stream()
+
+        def e2e_run(steps):
+            prev_download = None
+            for _ in range(steps):
+                wl.e2e_upload(stream)
+                if prev_download is not None:
+                    session.wait_event(stream, prev_download)
+                wl.step()
+                session.wait_event(out_stream, session.record(stream))
+                wl.e2e_download(out_stream)
+                prev_download = session.record(out_stream)
+
+        e2e_run(2)
         session.synchronize(stream)
+        session.synchronize(out_stream)
         barrier(dist)
         session.synchronize(stream)
         e0 = session.record(stream)
         e2e_steps = max(3, min(args.steps, 10))
-        for _ in range(e2e_steps):
-            wl.e2e_step()
-        e1 = session.record(stream)
+        e2e_run(e2e_steps)
+        e1 = session.record(out_stream)
+        session.synchronize(out_stream)
         session.synchronize(stream)
         e2e_ms = reduce_max(dist, session.elapsed_ms(e0, e1)) / e2e_steps
         e2e_value = units_step / (e2e_ms / 1e3) / scale
