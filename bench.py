@@ -293,18 +293,24 @@ class GemmWorkload(Workload):
             self.h_c = TensorHandle(self.s, self.dc, DType.BF16, (M, Nn), contiguous_strides((M, Nn)))
             if self.allgather == "p2p":
                 self.comm.register_buffer(self.st, self.dc)  # collective: every rank maps every rank's C
-        self.attrs = (N.Attr * 1)()
-        self._key = b"transpose_rhs"
+        # Optional kernel choice for the single-GPU GEMM (an operator candidate name);
+        # unset, the operator picks its default kernel.
+        cand = os.environ.get("TITAN_B200_GEMM_CANDIDATE", "")
+        self.attrs = (N.Attr * 2)()
+        self.n_attrs = 2 if cand else 1
+        self._key, self._ckey, self._cval = b"transpose_rhs", b"candidate", cand.encode()
         self.attrs[0].key = self._key
         self.attrs[0].value = 1
-        self.kernel = "gemm_bf16_tn"
+        self.attrs[1].key = self._ckey
+        self.attrs[1].str = self._cval
+        self.kernel = cand or "gemm_bf16_tn_2sm"  # the operator's choice at 8192^3
 
     def units_per_step(self):
         return 2.0 * self.M * self.n_local * self.K
 
     def _local_gemm(self, out_tensor):
         rc = self.Nn.lib().tb_op_gemm(self.s.ptr, self.st.ptr, self.ctypes.byref(self.ta), self.ctypes.byref(self.tbm),
-                                      self.ctypes.byref(out_tensor), self.attrs, 1, None)
+                                      self.ctypes.byref(out_tensor), self.attrs, self.n_attrs, None)
         if rc:
             raise RuntimeError(self.Nn.last_error())
 
@@ -893,6 +899,7 @@ def main(argv=None) -> int:
 TRAFFIC_PER_LAUNCH: dict = {
     "softmax_f32_warp32": 536.99e6 + 480.30e6,
     "gemm_bf16_tn": 997.83e6 + 127.29e6,
+    "gemm_bf16_tn_2sm": 1088.31e6 + 127.76e6,
     "sdpa_fwd_bf16_d128_pair": 806.43e6 + 253.34e6,
     "conv2d_fprop_bf16_nhwc": 104.21e6 + 53.92e6,
 }

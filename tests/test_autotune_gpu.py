@@ -37,7 +37,7 @@ def test_gemm_tunes_once_and_matches_the_explicit_candidate(session, tmp_path):
     h = rt.execute(req).wait()
     res = rt.last_tune
     assert res is not None and tuner.tunings == 1
-    assert {x.candidate for x in res.measured} == {"gemm_bf16_tn", "gemm_bf16_tn_splitk"}
+    assert {x.candidate for x in res.measured} == {"gemm_bf16_tn_2sm", "gemm_bf16_tn", "gemm_bf16_tn_splitk"}
     assert _stages(res)["gemm_bf16_generic"] == "selection"
     assert h.candidate == res.entry.candidate
     got = h.outputs[0].to_numpy()

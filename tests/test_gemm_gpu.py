@@ -73,9 +73,9 @@ def test_gemm_f32_c1_config_exact(session, rt):
     np.testing.assert_array_equal(h.outputs[0].to_numpy(), oracle.gemm(a, b))
 
 
-@pytest.mark.parametrize("candidate", [None, "gemm_bf16_tn"])
+@pytest.mark.parametrize("candidate", [None, "gemm_bf16_tn", "gemm_bf16_tn_2sm"])
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 128), (200, 300, 72), (1, 8, 8), (129, 257, 1032),
-                                   (1000, 1000, 1000), (512, 256, 8192), (300, 1024, 136)])
+                                   (1000, 1000, 1000), (512, 256, 8192), (300, 1024, 136), (2304, 4352, 520)])
 def test_gemm_bf16_tcgen05_matches_oracle(session, rt, m, n, k, candidate):
     a, b = bf16_inputs(m, n, k, seed=m + n + k)
     attrs = {"transpose_rhs": True}
@@ -83,7 +83,8 @@ def test_gemm_bf16_tcgen05_matches_oracle(session, rt, m, n, k, candidate):
         attrs["candidate"] = candidate
     h = run_op(rt, "gemm", [upload(session, rt.stream, a, DType.BF16), upload(session, rt.stream, b, DType.BF16)],
                DType.BF16, (m, n), attrs)
-    assert h.candidate == candidate if candidate else h.candidate in ("gemm_bf16_tn", "gemm_bf16_tn_splitk")
+    assert h.candidate == candidate if candidate else h.candidate in ("gemm_bf16_tn_2sm", "gemm_bf16_tn",
+                                                                      "gemm_bf16_tn_splitk")
     got = h.outputs[0].to_f32()
     rows = np.repeat(np.arange(m), n)
     cols = np.tile(np.arange(n), m)
@@ -105,15 +106,21 @@ def test_gemm_bf16_row_major_b_and_transposed_a(session, rt):
     assert max_rel_err(h.outputs[0].to_f32(), ref) <= BF16_TOL
 
 
-def test_gemm_bf16_full_c3_config(session, rt):
+@pytest.mark.parametrize("candidate", [None, "gemm_bf16_tn_2sm"])
+def test_gemm_bf16_full_c3_config(session, rt, candidate):
     """C3: 8192^3, A N(0,1), B column-major N(0,1/8192), seed 2. Sampled points against the
     oracle, then two size-independent properties over every element: finiteness and the
     column-checksum identity 1^T C = (1^T A) B (fp64)."""
     M = N = K = 8192
     a = tb.fill_normal(M * K, seed=2 * 16 + 0, dtype=DType.BF16).reshape(M, K)
     b = tb.fill_normal(N * K, seed=2 * 16 + 1, std=1.0 / math.sqrt(K), dtype=DType.BF16).reshape(N, K)
+    attrs = {"transpose_rhs": True}
+    if candidate:
+        attrs["candidate"] = candidate
     h = run_op(rt, "gemm", [upload(session, rt.stream, a, DType.BF16), upload(session, rt.stream, b, DType.BF16)],
-               DType.BF16, (M, N), {"transpose_rhs": True})
+               DType.BF16, (M, N), attrs)
+    if candidate:
+        assert h.candidate == candidate
     got = h.outputs[0].to_f32()
     rng = np.random.default_rng(2)
     rows = rng.integers(0, M, 4096)

@@ -30,8 +30,8 @@
 
 namespace tb {
 
-tb_status launch_gemm_bf16_tn(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c, int M, int N,
-                              int K, long long ldc);
+tb_status launch_gemm_bf16_default(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c, int M, int N,
+                                   int K, long long ldc);
 tb_status launch_gemm_bf16_tn_allgather(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, const CUdeviceptr* outs,
                                         const CUdeviceptr* signals, int ranks, int self, uint32_t epoch, int M, int N,
                                         int K, long long ldc, long long col0);
@@ -509,7 +509,7 @@ tb_status tb_op_gemm_sharded(tb_comm* comm, tb_stream* stream, const tb_tensor* 
   if (rc) return rc;
   // 1. This rank's columns straight into its slot of the gather layout [p][M][N/p].
   const CUdeviceptr slot = bw->ptr + (CUdeviceptr)c->rank * shard_bytes;
-  rc = launch_gemm_bf16_tn(s, st, ba->ptr, bb->ptr, slot, (int)M, (int)Np, (int)K, (long long)Np);
+  rc = launch_gemm_bf16_default(s, st, ba->ptr, bb->ptr, slot, (int)M, (int)Np, (int)K, (long long)Np);
   if (rc) return rc;
   // 2. In-place all-gather of the shards over NVLink.
   if (p > 1) {

@@ -47,6 +47,7 @@ namespace tb {
   X(cuFuncSetAttribute)                \
   X(cuLaunchKernel)                    \
   X(cuLaunchKernelEx)                  \
+  X(cuOccupancyMaxActiveClusters)      \
   X(cuTensorMapEncodeTiled)            \
   X(cuGetErrorString)                  \
   X(cuGetErrorName)                    \

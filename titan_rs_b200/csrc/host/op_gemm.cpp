@@ -1,7 +1,9 @@
 // "gemm" operator entry: the contract of execute_cuda_gemm and the CPU gemm
 // (titan-runtime/src/lib.rs:2289-2404, 955-989), then the kernel choice:
 //   BF16, A row-major, B column-major (transpose_rhs), K % 8 == 0, 16-byte
-//        aligned buffers        -> gemm_bf16_tn (tcgen05, TMA, TMEM)
+//        aligned buffers        -> gemm_bf16_tn_2sm (tcgen05 on CTA pairs, TMA, TMEM) when the
+//                                  output fills the SMs, gemm_bf16_tn (one SM per tile) when it
+//                                  does not, gemm_bf16_tn_splitk when too few tiles exist
 //   BF16, any other layout      -> gemm_bf16_generic (CUDA cores)
 //   F32                         -> gemm_f32_tiled (CUDA cores, bit-exact with the CPU reference)
 #include "../kernels/kernel_configs.h"
@@ -26,6 +28,59 @@ tb_status launch_gemm_bf16_tn(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr
   CUdeviceptr status = s->status.device;
   void* params[] = {&ta, &tbm, &c, &M, &N, &K, &ldc, &status};
   return launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_SMEM_BYTES, params, "gemm_bf16_tn");
+}
+
+// 2-SM form: clusters of two CTAs on 256x256 tiles (gemm_bf16_tn_2sm). The persistent
+// grid is as many pairs as can be resident at once (the driver's cluster occupancy), at
+// most one per tile.
+tb_status launch_gemm_bf16_tn_2sm(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c, int M, int N,
+                                  int K, long long ldc) {
+  CUtensorMap ta, tbm;
+  tb_status rc = tmap_bf16_2d(&ta, a, (uint64_t)M, (uint64_t)K, (uint64_t)K, 128, TB_GEMM_BK,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = tmap_bf16_2d(&tbm, b, (uint64_t)N, (uint64_t)K, (uint64_t)K, 128, TB_GEMM_BK, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  CUfunction fn = nullptr;
+  rc = builtin_function(s, "gemm_bf16", "gemm_bf16_tn_2sm", &fn);
+  if (rc) return rc;
+  const DriverApi* d = driver();
+  TB_CU("cuFuncSetAttribute",
+        d->cuFuncSetAttribute(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)TB_GEMM2_SMEM_BYTES));
+  CUlaunchConfig cfg{};
+  cfg.gridDimX = (unsigned)s->sm_count & ~1u;
+  cfg.gridDimY = cfg.gridDimZ = 1;
+  cfg.blockDimX = TB_GEMM_THREADS;
+  cfg.blockDimY = cfg.blockDimZ = 1;
+  cfg.sharedMemBytes = TB_GEMM2_SMEM_BYTES;
+  cfg.hStream = st->raw;
+  CUlaunchAttribute attr{};
+  attr.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+  attr.value.clusterDim.x = 2;
+  attr.value.clusterDim.y = 1;
+  attr.value.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  TB_CU("cuOccupancyMaxActiveClusters", d->cuOccupancyMaxActiveClusters(&clusters, fn, &cfg));
+  if (clusters < 1) return unsupported("no CTA pair of gemm_bf16_tn_2sm fits on this device");
+  const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+  const unsigned pairs = (unsigned)(tiles < clusters ? tiles : clusters);
+  CUdeviceptr status = s->status.device;
+  void* params[] = {&ta, &tbm, &c, &M, &N, &K, &ldc, &status};
+  return launch_builtin(s, st, fn, 2 * pairs, 1, 1, TB_GEMM_THREADS, TB_GEMM2_SMEM_BYTES, params, "gemm_bf16_tn_2sm",
+                        2);
+}
+
+// The unsplit tensor-core GEMM the operator runs by default: the 2-SM kernel once the
+// output holds at least a full wave of 128x256 tiles (it moves a third less operand data
+// per FLOP from L2 into shared memory), else the 1-SM kernel, whose 128-row tiles waste
+// less of a short M.
+tb_status launch_gemm_bf16_default(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c, int M, int N,
+                                   int K, long long ldc) {
+  const long long tiles = (long long)((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN);
+  if (M >= 256 && tiles >= s->sm_count) return launch_gemm_bf16_tn_2sm(s, st, a, b, c, M, N, K, ldc);
+  return launch_gemm_bf16_tn(s, st, a, b, c, M, N, K, ldc);
 }
 
 // Fused N-sharded GEMM + all-gather: this rank's [M, N] column block of the row-major
@@ -132,8 +187,9 @@ extern "C" tb_status tb_op_gemm(tb_session* session, tb_stream* stream, const tb
     if (!attrs[i].key || (strcmp(attrs[i].key, "transpose_lhs") != 0 && strcmp(attrs[i].key, "transpose_rhs") != 0))
       return contract("CUDA GEMM received unsupported attributes");
   }
-  if (candidate && strcmp(candidate, "gemm_bf16_tn") != 0 && strcmp(candidate, "gemm_bf16_tn_splitk") != 0 &&
-      strcmp(candidate, "gemm_bf16_generic") != 0 && strcmp(candidate, "gemm_f32_tiled") != 0)
+  if (candidate && strcmp(candidate, "gemm_bf16_tn") != 0 && strcmp(candidate, "gemm_bf16_tn_2sm") != 0 &&
+      strcmp(candidate, "gemm_bf16_tn_splitk") != 0 && strcmp(candidate, "gemm_bf16_generic") != 0 &&
+      strcmp(candidate, "gemm_f32_tiled") != 0)
     return contract(std::string("unknown GEMM candidate ") + candidate);
   bool tl = false, tr = false;
   for (uint32_t i = 0; i < num_attrs; ++i) {
@@ -180,7 +236,8 @@ extern "C" tb_status tb_op_gemm(tb_session* session, tb_stream* stream, const tb
     if (candidate && strcmp(candidate, "gemm_f32_tiled") == 0)
       return unsupported("candidate gemm_f32_tiled does not take BF16");
     const bool force_split = candidate && strcmp(candidate, "gemm_bf16_tn_splitk") == 0;
-    const SplitPlan plan = tma_ok && !want_generic && !(candidate && strcmp(candidate, "gemm_bf16_tn") == 0)
+    const bool want_2sm = candidate && strcmp(candidate, "gemm_bf16_tn_2sm") == 0;
+    const SplitPlan plan = tma_ok && !want_generic && !want_2sm && !(candidate && strcmp(candidate, "gemm_bf16_tn") == 0)
                                ? plan_split_k(s->sm_count, M, N, K, force_split)
                                : SplitPlan{};
     if (force_split && plan.splits < 2) return unsupported("candidate gemm_bf16_tn_splitk needs at least 2 k-blocks");
@@ -190,8 +247,12 @@ extern "C" tb_status tb_op_gemm(tb_session* session, tb_stream* stream, const tb
       if (rc) return rc;
       rc = launch_gemm_bf16_splitk(s, st, pa, pb, pc, M, N, K, (long long)N, plan.splits, plan.kb_per_split,
                                    partial);
-    } else if (tma_ok && !want_generic) {
+    } else if (want_2sm) {
+      rc = launch_gemm_bf16_tn_2sm(s, st, pa, pb, pc, M, N, K, (long long)N);
+    } else if (tma_ok && !want_generic && candidate) {
       rc = launch_gemm_bf16_tn(s, st, pa, pb, pc, M, N, K, (long long)N);
+    } else if (tma_ok && !want_generic) {
+      rc = launch_gemm_bf16_default(s, st, pa, pb, pc, M, N, K, (long long)N);
     } else {
       rc = builtin_function(s, "compat", "gemm_bf16_generic", &fn);
       if (rc) return rc;

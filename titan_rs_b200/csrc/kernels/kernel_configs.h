@@ -10,6 +10,14 @@
 #define TB_GEMM_BARRIER_BYTES 128
 #define TB_GEMM_SMEM_BYTES (TB_GEMM_STAGES * (TB_GEMM_BM + TB_GEMM_BN) * TB_GEMM_BK * 2 + 1024 + TB_GEMM_BARRIER_BYTES)
 
+// 2-SM bf16 GEMM (gemm_bf16_tn_2sm): CTA pairs computing 256x256 tiles with
+// tcgen05.mma.cta_group::2; 32 KB per-CTA stages, pair tiles visited in groups of
+// TB_GEMM2_GROUP 256-row blocks.
+#define TB_GEMM2_STAGES 6
+#define TB_GEMM2_GROUP 8
+#define TB_GEMM2_BARRIER_BYTES 256
+#define TB_GEMM2_SMEM_BYTES (TB_GEMM2_STAGES * 2 * 128 * TB_GEMM_BK * 2 + 1024 + TB_GEMM2_BARRIER_BYTES)
+
 // Ranks the fused GEMM + all-gather writes to (one node), and its epilogue staging:
 // 4 warps x 32 rows x 128 bf16 columns beyond the pipeline's shared memory.
 #define TB_MAX_RANKS 8

@@ -1,0 +1,306 @@
+// Persistent tcgen05 GEMM pipeline on CTA pairs (2-SM MMA, `cta_group::2`).
+//
+// A cluster of two CTAs on two SMs computes one 256 x 256 output tile:
+//   D[256 x 256] (+)= A[256 x 64] * B[256 x 64]^T per k-block, bf16 in, fp32 in TMEM.
+// CTA rank r of the pair holds A rows [128 r, 128 r + 128) and B rows (output
+// columns) [128 r, 128 r + 128) of the tile in its shared memory, at the same
+// offsets in both CTAs. One lane of the even CTA issues tcgen05.mma.cta_group::2
+// with M = 256, N = 256: the tensor cores of both SMs read both CTAs' B halves and
+// each SM its own A half, and each CTA's TMEM receives its own 128 rows x 256
+// columns. Per SM, one k-block moves 32 KB from L2 instead of 48 KB for the
+// single-SM 128 x 256 tile at the same work per SM.
+//
+//   warp 0      TMA producer in each CTA: its A and B halves into its own stage; the
+//               transaction bytes of both CTAs land on the even CTA's `full` barrier
+//               (2-SM tensor loads, each CTA reading only its own tiles).
+//   warp 1      TMEM owner in each CTA (tcgen05.alloc.cta_group::2, 512 columns = two
+//               128 x 256 fp32 accumulators); in the even CTA one lane issues the MMAs
+//               and commits with .multicast::cluster to both CTAs' `empty` and
+//               `acc_full` barriers.
+//   warps 2..5  epilogue of each CTA's 128 rows; after draining an accumulator they
+//               arrive on the even CTA's `acc_empty` (4 local + 4 remote arrivals).
+// Every mbarrier wait is bounded; both CTAs always reach the two cluster barriers
+// (after barrier initialisation, and before TMEM is freed), so a failure in one role
+// ends as a status code, not a hang.
+#pragma once
+
+#include "umma_pipeline.cuh"
+
+namespace tb {
+namespace umma2 {
+
+constexpr int BM = 128;   // rows per CTA (256 per pair)
+constexpr int BN = 256;   // output columns per pair tile
+constexpr int BK = 64;
+constexpr int STAGES = TB_GEMM2_STAGES;
+constexpr int A_BYTES = BM * BK * 2;            // 16 KB
+constexpr int B_BYTES = (BN / 2) * BK * 2;      // 16 KB: this CTA's half of B
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 32 KB per CTA
+constexpr int TMEM_COLS = 2 * BN;
+constexpr uint32_t IDESC = idesc_bf16_f32(2 * BM, BN);
+
+template <int Stages>
+struct Barriers {
+  uint64_t full[Stages];    // even CTA: both CTAs' bytes of a stage have landed
+  uint64_t empty[Stages];   // each CTA: the pair's MMAs are done with this CTA's stage
+  uint64_t acc_full[2];     // each CTA: its accumulator rows are ready
+  uint64_t acc_empty[2];    // even CTA: both CTAs' epilogues drained the accumulator
+  uint64_t drain;
+  uint32_t tmem_base;
+};
+// Dynamic shared memory of a kernel with `stages` ring stages (1 KB of alignment slack included).
+__host__ __device__ constexpr int smem_bytes(int stages) { return stages * STAGE_BYTES + 1024 + TB_GEMM2_BARRIER_BYTES; }
+static_assert(sizeof(Barriers<8>) <= TB_GEMM2_BARRIER_BYTES, "barrier block overflows its reservation");
+static_assert(smem_bytes(STAGES) == TB_GEMM2_SMEM_BYTES, "smem layout");
+static_assert(TB_GEMM2_SMEM_BYTES <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Shared::cluster address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t smem, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// 2-D tile load into this CTA's shared memory whose completion bytes go to the even
+// CTA's barrier (`bar_cluster` is that barrier's shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int32_t x,
+                                                 int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_bf16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                  uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on `bar` (same offset) in every CTA of `cta_mask` once the pair's MMAs so far are done.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_addr(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+
+// Arrives on the issuing CTA's `bar` once the pair's MMAs so far are done.
+__device__ __forceinline__ void umma_commit_pair_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)), "r"(cols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t tmem, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(cols) : "memory");
+}
+
+// C[M, N] bf16 (leading dimension ldc) = act(A[M, K] B^T + bias), B stored [N, K].
+struct Problem {
+  const CUtensorMap* ta;
+  const CUtensorMap* tb;
+  __nv_bfloat16* c;
+  const float* bias;
+  int act;
+  int M, N, K;
+  long long ldc;
+  bool vec_ok;
+};
+
+template <int Stages = STAGES, int Group = TB_GEMM2_GROUP>
+__device__ __forceinline__ void run_gemm(const Problem& p, uint32_t* status, uint32_t fail_base) {
+  static_assert(smem_bytes(Stages) <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Barriers<Stages>* bars = reinterpret_cast<Barriers<Stages>*>(smem + Stages * STAGE_BYTES);
+  const int warp = warp_id(), lane = lane_id();
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int num_m = (p.M + 2 * BM - 1) / (2 * BM);  // 256-row pair tiles
+  const int num_n = (p.N + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int num_k = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Stages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->acc_full[a], 1);
+      mbar_init(&bars->acc_empty[a], 8);  // 4 epilogue warps in each CTA
+    }
+    mbar_init(&bars->drain, 1);
+    fence_barrier_init();  // .release.cluster: visible to the peer CTA
+  }
+  cluster_sync();  // both CTAs' barriers exist before anything arrives remotely
+  if (warp == 1) {
+    tmem_alloc_pair(&bars->tmem_base, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs) ----------------
+      tma_prefetch_desc(p.ta);
+      tma_prefetch_desc(p.tb);
+      uint32_t issued[Stages] = {};
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += pairs) {
+        int m_blk, n_blk;
+        umma::grouped_tile(t, num_m, num_n, Group, m_blk, n_blk);
+        const int row0 = m_blk * 2 * BM + (int)rank * BM;
+        const int col0 = n_blk * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&bars->empty[stage], phase ^ 1)) {
+            report_status(status, fail_base | 0x0101);
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = smem + stage * STAGE_BYTES;
+          const uint32_t full_even = map_to_rank(smem_addr(&bars->full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&bars->full[stage], 2 * STAGE_BYTES);
+          tma_load_2d_pair(a_dst, p.ta, full_even, kb * BK, row0);
+          tma_load_2d_pair(a_dst + A_BYTES, p.tb, full_even, kb * BK, col0);
+          ++issued[stage];
+          if (++stage == Stages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok && leader) {
+        // The issued copies land on this CTA's `full` barriers: wait for them before TMEM goes.
+        for (int s = 0; s < Stages; ++s)
+          if (issued[s] && !mbar_wait(&bars->full[s], (issued[s] - 1) & 1)) report_status(status, fail_base | 0x0102);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (even CTA) ----------------
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      const uint32_t stage0 = smem_addr(smem);
+      for (int t = pair; t < tiles && ok; t += pairs) {
+        if (!mbar_wait(&bars->acc_empty[acc], acc_phase ^ 1)) {
+          report_status(status, fail_base | 0x0201);
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&bars->full[stage], phase)) {
+            report_status(status, fail_base | 0x0202);
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t a_addr = stage0 + stage * STAGE_BYTES;
+          const uint64_t a_desc = sdesc_sw128(a_addr, 16, 1024);
+          const uint64_t b_desc = sdesc_sw128(a_addr + A_BYTES, 16, 1024);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)  // 32 bytes of K per 16-element step inside the 128-byte row
+            umma_bf16_ss_pair(d_tmem, a_desc + (uint64_t)(k * 2), b_desc + (uint64_t)(k * 2), IDESC,
+                              (kb > 0) || (k > 0));
+          umma_commit_pair(&bars->empty[stage], 0x3);
+          if (++stage == Stages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&bars->acc_full[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      umma_commit_pair_local(&bars->drain);
+      if (!mbar_wait(&bars->drain, 0)) report_status(status, fail_base | 0x0203);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+    const int quarter = warp & 3;
+    const uint32_t acc_empty_even[2] = {map_to_rank(smem_addr(&bars->acc_empty[0]), 0),
+                                        map_to_rank(smem_addr(&bars->acc_empty[1]), 0)};
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair; t < tiles; t += pairs) {
+      int m_blk, n_blk;
+      umma::grouped_tile(t, num_m, num_n, Group, m_blk, n_blk);
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full[acc], acc_phase));
+      if (!ok) {
+        if (lane == 0) report_status(status, fail_base | 0x0301);
+        break;
+      }
+      tc_fence_after_sync();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      const int gr = m_blk * 2 * BM + (int)rank * BM + quarter * 32 + lane;
+#pragma unroll 1
+      for (int col = 0; col < BN; col += 32) {
+        uint32_t r[32];
+        tmem_ld_x32(taddr + col, r);
+        tmem_ld_wait();
+        const int gc = n_blk * BN + col;
+        if (gr < p.M && gc < p.N)
+          umma::store_bf16_chunk(p.c + (long long)gr * p.ldc + gc, p.N - gc, p.vec_ok, r,
+                                 p.bias ? p.bias + gc : nullptr, p.act);
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(&bars->acc_empty[acc]);
+        else mbar_arrive_remote(acc_empty_even[acc]);
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before_sync();
+  cluster_sync();  // no CTA frees TMEM or exits while its pair's MMAs may still use its memory
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace umma2
+}  // namespace tb
