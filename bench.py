@@ -520,18 +520,24 @@ class ConvWorkload(Workload):
         self.ty = [_tensor(self.tb, d, DType.BF16, (self.n_local, H, W, K)) for d in self.dy]
         self.tw = _tensor(self.tb, self.dw, DType.BF16, (K, self.R, self.S, C))
         names = ["stride_h", "stride_w", "pad_h", "pad_w", "dilation_h", "dilation_w", "groups", "layout"]
-        vals = [1, 1, 1, 1, 1, 1, 1, None]
+        vals = [1, 1, 1, 1, 1, 1, 1, b"NHWC"]
+        # Optional kernel choice (an operator candidate name); unset, the operator picks.
+        cand = os.environ.get("TITAN_B200_CONV_CANDIDATE", "")
+        if cand:
+            names.append("candidate")
+            vals.append(cand.encode())
         self._keys = [n.encode() for n in names]
-        self._nhwc = b"NHWC"
+        self._strs = [v for v in vals if isinstance(v, bytes)]  # kept alive for the C strings
         self.attrs = (N.Attr * len(names))()
         for i, (key, v) in enumerate(zip(self._keys, vals)):
             self.attrs[i].key = key
-            if v is None:
-                self.attrs[i].str = self._nhwc
+            if isinstance(v, bytes):
+                self.attrs[i].str = v
             else:
                 self.attrs[i].value = v
         self.i = 0
-        self.kernel = "conv2d_fprop_bf16_nhwc"
+        # The operator's choice at C5 (and at every batch shard of up to 8 GPUs).
+        self.kernel = cand or "conv2d_fprop_bf16_nhwc_2sm"
 
     def units_per_step(self):
         return 2.0 * self.n_local * self.H * self.W * self.K * self.C * self.R * self.S
@@ -902,6 +908,7 @@ TRAFFIC_PER_LAUNCH: dict = {
     "gemm_bf16_tn_2sm": 1088.31e6 + 127.76e6,
     "sdpa_fwd_bf16_d128_pair": 806.43e6 + 253.34e6,
     "conv2d_fprop_bf16_nhwc": 104.21e6 + 53.92e6,
+    "conv2d_fprop_bf16_nhwc_2sm": 104.09e6 + 55.92e6,
 }
 
 

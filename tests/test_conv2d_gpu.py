@@ -86,7 +86,8 @@ def nhwc_inputs(n, hh, ww, cin, cout, r, s, seed, with_bias=False):
     return x, w, b
 
 
-def check_nhwc(session, rt, n, hh, ww, cin, cout, r, s, stride, pad, dil, with_bias, expect_candidate, seed, groups=1):
+def check_nhwc(session, rt, n, hh, ww, cin, cout, r, s, stride, pad, dil, with_bias, expect_candidate, seed, groups=1,
+               candidate=None):
     x, w, b = nhwc_inputs(n, hh, ww, cin, cout, r, s, seed, with_bias)
     if groups > 1:
         w = np.ascontiguousarray(w[..., : cin // groups])
@@ -94,7 +95,10 @@ def check_nhwc(session, rt, n, hh, ww, cin, cout, r, s, stride, pad, dil, with_b
     ins = [upload(session, rt.stream, x, DType.BF16), upload(session, rt.stream, w, DType.BF16)]
     if b is not None:
         ins.append(upload(session, rt.stream, b, DType.F32))
-    res = run_op(rt, "conv2d", ins, DType.BF16, (n, ho, wo, cout), conv_attrs(stride, pad, dil, groups, "NHWC"))
+    attrs = conv_attrs(stride, pad, dil, groups, "NHWC")
+    if candidate:
+        attrs["candidate"] = candidate
+    res = run_op(rt, "conv2d", ins, DType.BF16, (n, ho, wo, cout), attrs)
     assert res.candidate == expect_candidate
     got = res.outputs[0].to_f32()
     if groups == 1:
@@ -118,9 +122,12 @@ def check_nhwc(session, rt, n, hh, ww, cin, cout, r, s, stride, pad, dil, with_b
     (2, 12, 12, 64, 256, 3, 3, (2, 2), (2, 2), False),      # dilation 2
     (4, 7, 7, 32, 64, 5, 3, (2, 1), (1, 1), True),          # non-square filter, Cin 32
 ])
-def test_conv2d_bf16_implicit_gemm_matches_oracle(session, rt, n, hh, ww, cin, cout, r, s, pad, dil, bias):
-    check_nhwc(session, rt, n, hh, ww, cin, cout, r, s, (1, 1), pad, dil, bias, "conv2d_fprop_bf16_nhwc",
-               seed=n + hh + cin + cout + r)
+@pytest.mark.parametrize("candidate", [None, "conv2d_fprop_bf16_nhwc_2sm"])
+def test_conv2d_bf16_implicit_gemm_matches_oracle(session, rt, n, hh, ww, cin, cout, r, s, pad, dil, bias, candidate):
+    """Small outputs take the 1-SM kernel by default; the 2-SM kernel is forced by name
+    (its odd CTA of a final pair past the last 128-pixel block must store nothing)."""
+    check_nhwc(session, rt, n, hh, ww, cin, cout, r, s, (1, 1), pad, dil, bias, candidate or "conv2d_fprop_bf16_nhwc",
+               seed=n + hh + cin + cout + r, candidate=candidate)
 
 
 @pytest.mark.parametrize("n,hh,ww,cin,cout,r,s,stride,pad,dil,bias", [
@@ -131,11 +138,12 @@ def test_conv2d_bf16_implicit_gemm_matches_oracle(session, rt, n, hh, ww, cin, c
     (1, 31, 29, 64, 256, 5, 5, (3, 3), (2, 2), (1, 1), False),  # stride 3
     (2, 24, 24, 64, 128, 3, 3, (2, 2), (2, 2), (2, 2), True),   # stride 2 + dilation 2
 ])
+@pytest.mark.parametrize("candidate", [None, "conv2d_fprop_bf16_nhwc_2sm"])
 def test_conv2d_bf16_strided_implicit_gemm_matches_oracle(session, rt, n, hh, ww, cin, cout, r, s, stride, pad, dil,
-                                                          bias):
+                                                          bias, candidate):
     """Strides reach the tensor-core kernel as TMA traversal strides (input box 8*s wide)."""
-    check_nhwc(session, rt, n, hh, ww, cin, cout, r, s, stride, pad, dil, bias, "conv2d_fprop_bf16_nhwc",
-               seed=n + hh + cin + cout + stride[0])
+    check_nhwc(session, rt, n, hh, ww, cin, cout, r, s, stride, pad, dil, bias, candidate or "conv2d_fprop_bf16_nhwc",
+               seed=n + hh + cin + cout + stride[0], candidate=candidate)
 
 
 @pytest.mark.parametrize("stride,groups,cin", [((1, 1), 2, 64), ((1, 1), 1, 12), ((2, 2), 1, 12)])
@@ -144,14 +152,20 @@ def test_conv2d_bf16_generic_path(session, rt, stride, groups, cin):
                seed=5 + groups + cin, groups=groups)
 
 
-def test_conv2d_bf16_full_c5_config(session, rt):
-    """C5: x [64,56,56,256] N(0,1), w [256,3,3,256] N(0, 2/2304), seed 4, stride 1, pad 1."""
+@pytest.mark.parametrize("candidate", [None, "conv2d_fprop_bf16_nhwc"])
+def test_conv2d_bf16_full_c5_config(session, rt, candidate):
+    """C5: x [64,56,56,256] N(0,1), w [256,3,3,256] N(0, 2/2304), seed 4, stride 1, pad 1.
+    The default at this size is the 2-SM kernel; the 1-SM kernel is forced by name."""
     n, hh, ww, cin, cout = 64, 56, 56, 256, 256
     x = tb.fill_normal(n * hh * ww * cin, seed=4 * 16, dtype=DType.BF16).reshape(n, hh, ww, cin)
     w = tb.fill_normal(cout * 9 * cin, seed=4 * 16 + 1, std=math.sqrt(2.0 / 2304), dtype=DType.BF16)
     w = w.reshape(cout, 3, 3, cin)
     ins = [upload(session, rt.stream, x, DType.BF16), upload(session, rt.stream, w, DType.BF16)]
-    res = run_op(rt, "conv2d", ins, DType.BF16, (n, hh, ww, cout), conv_attrs((1, 1), (1, 1), (1, 1), 1, "NHWC"))
+    attrs = conv_attrs((1, 1), (1, 1), (1, 1), 1, "NHWC")
+    if candidate:
+        attrs["candidate"] = candidate
+    res = run_op(rt, "conv2d", ins, DType.BF16, (n, hh, ww, cout), attrs)
+    assert res.candidate == (candidate or "conv2d_fprop_bf16_nhwc_2sm")
     got = res.outputs[0].to_f32()
     rng = np.random.default_rng(4)
     idx = rng.integers(0, n * hh * ww * cout, 4096)

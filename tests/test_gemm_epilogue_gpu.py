@@ -45,28 +45,47 @@ def _reference(a, b, bias, m, n, k, act):
     return {"none": lambda x: x, "gelu": oracle.gelu, "silu": oracle.silu}[act](acc)
 
 
+@pytest.mark.parametrize("candidate", [None, "gemm_bf16_tn_bias_act_2sm"])
 @pytest.mark.parametrize("act", ["none", "gelu", "silu"])
 @pytest.mark.parametrize("with_bias", [True, False])
 @pytest.mark.parametrize("m,n,k", [(300, 520, 1024), (128, 256, 64), (517, 264, 2048)])
-def test_gemm_bias_act_matches_oracle(session, rt, m, n, k, act, with_bias):
+def test_gemm_bias_act_matches_oracle(session, rt, m, n, k, act, with_bias, candidate):
     a, b, bias = _inputs(m, n, k, seed=m + n + k)
     ins = [upload(session, rt.stream, a.reshape(m, k), DType.BF16), upload(session, rt.stream, b.reshape(n, k), DType.BF16)]
     if with_bias:
         ins.append(upload(session, rt.stream, bias))
-    h = run_op(rt, "gemm.bias_act", ins, DType.BF16, (m, n), {"transpose_rhs": True, "activation": act})
-    assert h.candidate == "gemm_bf16_tn_bias_act"
+    attrs = {"transpose_rhs": True, "activation": act}
+    if candidate:
+        attrs["candidate"] = candidate
+    h = run_op(rt, "gemm.bias_act", ins, DType.BF16, (m, n), attrs)
+    assert h.candidate == (candidate or "gemm_bf16_tn_bias_act")
     got = h.outputs[0].to_f32()
     ref = _reference(a, b, bias if with_bias else None, m, n, k, act)
     assert np.isfinite(got).all()
     assert max_rel_err(got, ref) <= BF16_TOL, max_rel_err(got, ref)
 
 
-def test_no_bias_no_activation_equals_plain_gemm_bitwise(session, rt):
+def test_bias_act_defaults_to_pairs_on_large_outputs(session, rt):
+    """1024 x 4864 holds 152 tiles of 128 x 256 (>= one wave of 148 SMs): the 2-SM kernel."""
+    m, n, k = 1024, 4864, 256
+    a, b, bias = _inputs(m, n, k, seed=6)
+    ins = [upload(session, rt.stream, a.reshape(m, k), DType.BF16), upload(session, rt.stream, b.reshape(n, k), DType.BF16),
+           upload(session, rt.stream, bias)]
+    h = run_op(rt, "gemm.bias_act", ins, DType.BF16, (m, n), {"transpose_rhs": True, "activation": "gelu"})
+    assert h.candidate == "gemm_bf16_tn_bias_act_2sm"
+    ref = _reference(a, b, bias, m, n, k, "gelu")
+    assert max_rel_err(h.outputs[0].to_f32(), ref) <= BF16_TOL
+
+
+@pytest.mark.parametrize("fused_cand,plain_cand", [("gemm_bf16_tn_bias_act", "gemm_bf16_tn"),
+                                                   ("gemm_bf16_tn_bias_act_2sm", "gemm_bf16_tn_2sm")])
+def test_no_bias_no_activation_equals_plain_gemm_bitwise(session, rt, fused_cand, plain_cand):
     m, n, k = 640, 512, 1024
     a, b, _ = _inputs(m, n, k, seed=5)
     ta, tbb = upload(session, rt.stream, a.reshape(m, k), DType.BF16), upload(session, rt.stream, b.reshape(n, k), DType.BF16)
-    fused = run_op(rt, "gemm.bias_act", [ta, tbb], DType.BF16, (m, n), {"transpose_rhs": True, "activation": "none"})
-    plain = run_op(rt, "gemm", [ta, tbb], DType.BF16, (m, n), {"transpose_rhs": True, "candidate": "gemm_bf16_tn"})
+    fused = run_op(rt, "gemm.bias_act", [ta, tbb], DType.BF16, (m, n),
+                   {"transpose_rhs": True, "activation": "none", "candidate": fused_cand})
+    plain = run_op(rt, "gemm", [ta, tbb], DType.BF16, (m, n), {"transpose_rhs": True, "candidate": plain_cand})
     np.testing.assert_array_equal(fused.outputs[0].to_numpy(), plain.outputs[0].to_numpy())
 
 

@@ -3,7 +3,9 @@
 //   F32 (NCHW input, OIHW weight)        -> conv2d_f32 (reference ABI kernel, bit-exact)
 //   BF16 with layout="NHWC" (KRSC weight):
 //     groups 1, Cin % 8 == 0, Cout % 8 == 0, stride <= 8, 16-byte aligned
-//                                          -> conv2d_fprop_bf16_nhwc (tcgen05 implicit GEMM)
+//                                          -> conv2d_fprop_bf16_nhwc_2sm (tcgen05 implicit GEMM on
+//                                             CTA pairs) when the output fills the SMs, else
+//                                             conv2d_fprop_bf16_nhwc (one SM per tile)
 //     otherwise                            -> conv2d_bf16_nhwc_generic (CUDA cores)
 // A `candidate` attribute (not a reference attribute; the autotuner's) names one of
 // these kernels; a kernel that does not take the problem is TB_ERR_UNSUPPORTED.
@@ -12,9 +14,15 @@
 
 namespace tb {
 
+// pairs: -1 = choose (CTA pairs once the output holds a full wave of 128x256 tiles),
+// 0 = conv2d_fprop_bf16_nhwc, 1 = conv2d_fprop_bf16_nhwc_2sm.
 tb_status launch_conv2d_bf16(Session* s, Stream* st, CUdeviceptr x, CUdeviceptr w, CUdeviceptr bias, CUdeviceptr y,
                              int batch, int H, int W, int C, int Cout, int R, int S, int Ho, int Wo, int sh, int sw,
-                             int ph, int pw, int dh, int dw) {
+                             int ph, int pw, int dh, int dw, int pairs) {
+  const long long m_tiles = (long long)((batch + 1) / 2) * ((Ho + 7) / 8) * ((Wo + 7) / 8);
+  const long long n_tiles = (Cout + TB_GEMM_BN - 1) / TB_GEMM_BN;
+  const long long tiles = m_tiles * n_tiles;
+  if (pairs < 0) pairs = (m_tiles >= 2 && tiles >= s->sm_count) ? 1 : 0;
   CUtensorMap tx, tw;
   {
     cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)batch};
@@ -30,7 +38,7 @@ tb_status launch_conv2d_bf16(Session* s, Stream* st, CUdeviceptr x, CUdeviceptr 
   {
     cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)R * S, (cuuint64_t)Cout};
     cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)R * S * C * 2};
-    cuuint32_t box[3] = {64, 1, TB_GEMM_BN};
+    cuuint32_t box[3] = {64, 1, pairs ? 128u : (cuuint32_t)TB_GEMM_BN};
     cuuint32_t elem[3] = {1, 1, 1};
     TB_CU("cuTensorMapEncodeTiled",
           driver()->cuTensorMapEncodeTiled(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, reinterpret_cast<void*>(w), dims,
@@ -39,14 +47,16 @@ tb_status launch_conv2d_bf16(Session* s, Stream* st, CUdeviceptr x, CUdeviceptr 
                                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE));
   }
   CUfunction fn = nullptr;
-  tb_status rc = builtin_function(s, "conv2d_bf16", "conv2d_fprop_bf16_nhwc", &fn);
+  const char* name = pairs ? "conv2d_fprop_bf16_nhwc_2sm" : "conv2d_fprop_bf16_nhwc";
+  tb_status rc = builtin_function(s, "conv2d_bf16", name, &fn);
   if (rc) return rc;
-  const long long m_tiles = (long long)((batch + 1) / 2) * ((Ho + 7) / 8) * ((Wo + 7) / 8);
-  const long long tiles = m_tiles * ((Cout + TB_GEMM_BN - 1) / TB_GEMM_BN);
-  const unsigned grid = (unsigned)(tiles < s->sm_count ? tiles : s->sm_count);
   CUdeviceptr status = s->status.device;
   void* params[] = {&tx, &tw, &y, &bias, &batch, &C, &Cout, &R, &S, &Ho, &Wo, &sh, &sw, &ph, &pw, &dh, &dw, &status};
-  return launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_SMEM_BYTES, params, "conv2d_fprop_bf16_nhwc");
+  if (pairs)
+    return launch_builtin_pairs(s, st, fn, (m_tiles + 1) / 2 * n_tiles, TB_GEMM_THREADS, TB_GEMM2_SMEM_BYTES, params,
+                                name);
+  const unsigned grid = (unsigned)(tiles < s->sm_count ? tiles : s->sm_count);
+  return launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_SMEM_BYTES, params, name);
 }
 
 }  // namespace tb
@@ -78,7 +88,8 @@ extern "C" tb_status tb_op_conv2d(tb_session* session, tb_stream* stream, const 
     }
   }
   if (candidate && strcmp(candidate, "conv2d_fprop_bf16_nhwc") != 0 &&
-      strcmp(candidate, "conv2d_bf16_nhwc_generic") != 0 && strcmp(candidate, "conv2d_f32") != 0)
+      strcmp(candidate, "conv2d_fprop_bf16_nhwc_2sm") != 0 && strcmp(candidate, "conv2d_bf16_nhwc_generic") != 0 &&
+      strcmp(candidate, "conv2d_f32") != 0)
     return contract(std::string("unknown conv2d candidate ") + candidate);
   const bool nhwc = layout && strcmp(layout, "NHWC") == 0;
   if (layout && !nhwc && strcmp(layout, "NCHW") != 0) return contract("conv2d layout must be NCHW or NHWC");
@@ -164,7 +175,8 @@ extern "C" tb_status tb_op_conv2d(tb_session* session, tb_stream* stream, const 
     if (candidate && !want_generic && !tc_ok)
       return unsupported(std::string("candidate ") + candidate + " does not take this shape, stride or alignment");
     if (tc_ok && !want_generic) {
-      rc = launch_conv2d_bf16(s, st, px, pw_, pb, py, N, H, Wd, C, K, R, S, Ho, Wo, SH, SW, PH, PW, DH, DW);
+      const int pairs = !candidate ? -1 : strcmp(candidate, "conv2d_fprop_bf16_nhwc_2sm") == 0 ? 1 : 0;
+      rc = launch_conv2d_bf16(s, st, px, pw_, pb, py, N, H, Wd, C, K, R, S, Ho, Wo, SH, SW, PH, PW, DH, DW, pairs);
     } else {
       rc = builtin_function(s, "compat", "conv2d_bf16_nhwc_generic", &fn);
       if (rc) return rc;

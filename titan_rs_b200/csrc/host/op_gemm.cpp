@@ -44,32 +44,10 @@ tb_status launch_gemm_bf16_tn_2sm(Session* s, Stream* st, CUdeviceptr a, CUdevic
   CUfunction fn = nullptr;
   rc = builtin_function(s, "gemm_bf16", "gemm_bf16_tn_2sm", &fn);
   if (rc) return rc;
-  const DriverApi* d = driver();
-  TB_CU("cuFuncSetAttribute",
-        d->cuFuncSetAttribute(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)TB_GEMM2_SMEM_BYTES));
-  CUlaunchConfig cfg{};
-  cfg.gridDimX = (unsigned)s->sm_count & ~1u;
-  cfg.gridDimY = cfg.gridDimZ = 1;
-  cfg.blockDimX = TB_GEMM_THREADS;
-  cfg.blockDimY = cfg.blockDimZ = 1;
-  cfg.sharedMemBytes = TB_GEMM2_SMEM_BYTES;
-  cfg.hStream = st->raw;
-  CUlaunchAttribute attr{};
-  attr.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
-  attr.value.clusterDim.x = 2;
-  attr.value.clusterDim.y = 1;
-  attr.value.clusterDim.z = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
-  int clusters = 0;
-  TB_CU("cuOccupancyMaxActiveClusters", d->cuOccupancyMaxActiveClusters(&clusters, fn, &cfg));
-  if (clusters < 1) return unsupported("no CTA pair of gemm_bf16_tn_2sm fits on this device");
-  const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
-  const unsigned pairs = (unsigned)(tiles < clusters ? tiles : clusters);
+  const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
   CUdeviceptr status = s->status.device;
   void* params[] = {&ta, &tbm, &c, &M, &N, &K, &ldc, &status};
-  return launch_builtin(s, st, fn, 2 * pairs, 1, 1, TB_GEMM_THREADS, TB_GEMM2_SMEM_BYTES, params, "gemm_bf16_tn_2sm",
-                        2);
+  return launch_builtin_pairs(s, st, fn, pair_tiles, TB_GEMM_THREADS, TB_GEMM2_SMEM_BYTES, params, "gemm_bf16_tn_2sm");
 }
 
 // The unsplit tensor-core GEMM the operator runs by default: the 2-SM kernel once the
@@ -285,12 +263,15 @@ extern "C" tb_status tb_op_gemm_bias_act(tb_session* session, tb_stream* stream,
   if (!lhs || !rhs || !output) return contract("gemm.bias_act requires two rank-2 inputs, an optional bias and one output");
   bool tl = false, tr = false;
   int act = TB_ACT_NONE;
+  const char* candidate = nullptr;
   for (uint32_t i = 0; i < num_attrs; ++i) {
     const char* key = attrs[i].key;
     if (!key) return contract("gemm.bias_act received an unnamed attribute");
     if (strcmp(key, "candidate") == 0) {
-      if (!attrs[i].str || strcmp(attrs[i].str, "gemm_bf16_tn_bias_act") != 0)
+      if (!attrs[i].str || (strcmp(attrs[i].str, "gemm_bf16_tn_bias_act") != 0 &&
+                            strcmp(attrs[i].str, "gemm_bf16_tn_bias_act_2sm") != 0))
         return contract(std::string("unknown gemm.bias_act candidate ") + (attrs[i].str ? attrs[i].str : "(null)"));
+      candidate = attrs[i].str;
     } else if (strcmp(key, "activation") == 0) {
       if (!attrs[i].str) return contract("gemm.bias_act activation must be a string");
       if (strcmp(attrs[i].str, "none") == 0) act = TB_ACT_NONE;
@@ -333,19 +314,29 @@ extern "C" tb_status tb_op_gemm_bias_act(tb_session* session, tb_stream* stream,
   rc = activate(s);
   if (rc) return rc;
   int M = (int)m, N = (int)n, K = (int)k;
+  // Same choice as the plain GEMM: CTA pairs once the output fills the SMs.
+  const long long tiles = (long long)((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN);
+  const bool pairs = candidate ? strcmp(candidate, "gemm_bf16_tn_bias_act_2sm") == 0
+                               : (M >= 256 && tiles >= s->sm_count);
+  const uint32_t box_rows_b = pairs ? 128 : TB_GEMM_BN;
   CUtensorMap ta, tbm;
   if ((rc = tmap_bf16_2d(&ta, pa, m, k, k, TB_GEMM_BM, TB_GEMM_BK, CU_TENSOR_MAP_SWIZZLE_128B)) ||
-      (rc = tmap_bf16_2d(&tbm, pb, n, k, k, TB_GEMM_BN, TB_GEMM_BK, CU_TENSOR_MAP_SWIZZLE_128B)))
+      (rc = tmap_bf16_2d(&tbm, pb, n, k, k, box_rows_b, TB_GEMM_BK, CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   CUfunction fn = nullptr;
-  rc = builtin_function(s, "gemm_bf16", "gemm_bf16_tn_bias_act", &fn);
+  const char* name = pairs ? "gemm_bf16_tn_bias_act_2sm" : "gemm_bf16_tn_bias_act";
+  rc = builtin_function(s, "gemm_bf16", name, &fn);
   if (rc) return rc;
-  const long long tiles = (long long)((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN);
-  const unsigned grid = (unsigned)(tiles < s->sm_count ? tiles : s->sm_count);
   CUdeviceptr c = pc, pbias = bbias ? bbias->ptr : 0, status = s->status.device;
   long long ldc = N;
   void* params[] = {&ta, &tbm, &c, &pbias, &act, &M, &N, &K, &ldc, &status};
-  rc = launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_SMEM_BYTES, params, "gemm_bf16_tn_bias_act");
+  if (pairs) {
+    const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+    rc = launch_builtin_pairs(s, st, fn, pair_tiles, TB_GEMM_THREADS, TB_GEMM2_SMEM_BYTES, params, name);
+  } else {
+    const unsigned grid = (unsigned)(tiles < s->sm_count ? tiles : s->sm_count);
+    rc = launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_SMEM_BYTES, params, name);
+  }
   if (rc) return rc;
   return record_event(s, st, nullptr, out);
 }

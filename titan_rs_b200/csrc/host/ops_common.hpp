@@ -117,6 +117,34 @@ inline tb_status launch_builtin(Session* s, Stream* st, CUfunction fn, unsigned 
   return TB_OK;
 }
 
+// Launches a persistent kernel built on the 2-SM pipeline (clusters of two CTAs along x):
+// as many pairs as the driver's cluster occupancy allows at once, at most `pair_tiles`.
+inline tb_status launch_builtin_pairs(Session* s, Stream* st, CUfunction fn, long long pair_tiles, unsigned bx,
+                                      unsigned shared_bytes, void** params, const char* candidate) {
+  const DriverApi* d = driver();
+  TB_CU("cuFuncSetAttribute",
+        d->cuFuncSetAttribute(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)shared_bytes));
+  CUlaunchConfig cfg{};
+  cfg.gridDimX = (unsigned)s->sm_count & ~1u;
+  cfg.gridDimY = cfg.gridDimZ = 1;
+  cfg.blockDimX = bx;
+  cfg.blockDimY = cfg.blockDimZ = 1;
+  cfg.sharedMemBytes = shared_bytes;
+  cfg.hStream = st->raw;
+  CUlaunchAttribute attr{};
+  attr.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+  attr.value.clusterDim.x = 2;
+  attr.value.clusterDim.y = 1;
+  attr.value.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  TB_CU("cuOccupancyMaxActiveClusters", d->cuOccupancyMaxActiveClusters(&clusters, fn, &cfg));
+  if (clusters < 1) return unsupported(std::string("no CTA pair of ") + candidate + " fits on this device");
+  const unsigned pairs = (unsigned)(pair_tiles < clusters ? pair_tiles : clusters);
+  return launch_builtin(s, st, fn, 2 * pairs, 1, 1, bx, shared_bytes, params, candidate, 2);
+}
+
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix with leading
 // dimension `ld` elements; box = [box_rows, box_cols] with 128-byte swizzle.
 inline tb_status tmap_bf16_2d(CUtensorMap* map, CUdeviceptr base, uint64_t rows, uint64_t cols, uint64_t ld,

@@ -17,14 +17,18 @@
 // The shared pipeline (umma_pipeline.cuh) does the rest; the epilogue writes
 // each accumulator row to its NHWC output pixel, 32 channels per 128-bit burst.
 #include "umma_pipeline.cuh"
+#include "umma_pipeline_2sm.cuh"
 
 namespace {
 
 using namespace tb;
 
 constexpr uint32_t kFailConv = 0x43000000u;
+constexpr uint32_t kFailConv2 = 0x43320000u;
 
-struct ConvPolicy {
+// Problem geometry shared by the 1-SM and 2-SM policies. A 128-row M block m_blk is
+// 2 images x 8 output rows x 8 output columns.
+struct ConvGeometry {
   const CUtensorMap* tx;
   const CUtensorMap* tw;
   __nv_bfloat16* y;
@@ -34,17 +38,9 @@ struct ConvPolicy {
   bool vec_ok;
 
   __device__ int num_m() const { return tiles_img * tiles_h * tiles_w; }
-  __device__ int num_tiles() const { return num_m() * num_n; }
-  __device__ void k_blocks(int, int& kb0, int& kb1) const {
-    kb0 = 0;
-    kb1 = R * S * c_blocks;
-  }
   __device__ void prefetch() const {
     tma_prefetch_desc(tx);
     tma_prefetch_desc(tw);
-  }
-  __device__ void tile(int t, int& m_blk, int& n_blk) const {
-    umma::grouped_tile(t, num_m(), num_n, 16, m_blk, n_blk);
   }
   __device__ void pixel_tile(int m_blk, int& n0, int& ho0, int& wo0) const {
     const int wi = m_blk % tiles_w;
@@ -54,38 +50,78 @@ struct ConvPolicy {
     ho0 = hi * 8;
     wo0 = wi * 8;
   }
-  __device__ void load(uint8_t* a_dst, uint8_t* b_dst, uint64_t* bar, int m_blk, int n_blk, int kb) const {
-    const int rs = kb / c_blocks, cb = kb - rs * c_blocks;
+  // Input-box coordinates {c, w, h, n} of k-block kb = (r, s, channel block) for M block m_blk.
+  __device__ void a_coords(int m_blk, int kb, int& x, int& w, int& h, int& n, int& rs) const {
+    rs = kb / c_blocks;
+    const int cb = kb - rs * c_blocks;
     const int r = rs / S, s = rs - r * S;
-    int n0, ho0, wo0;
-    pixel_tile(m_blk, n0, ho0, wo0);
-    tma_load_4d(a_dst, tx, bar, cb * 64, wo0 * sw - pw + s * dw, ho0 * sh - ph + r * dh, n0);
-    tma_load_3d(b_dst, tw, bar, cb * 64, rs, n_blk * umma::BN);
+    int ho0, wo0;
+    pixel_tile(m_blk, n, ho0, wo0);
+    x = cb * 64;
+    w = wo0 * sw - pw + s * dw;
+    h = ho0 * sh - ph + r * dh;
   }
-  __device__ void store(int row, int, int m_blk, int n_blk, int col, const uint32_t (&acc)[32]) const {
+  // Row `row` of M block m_blk is output pixel (n, ho, wo); 32 channels from co.
+  __device__ void store_row(int row, int m_blk, int co, const uint32_t (&acc)[32]) const {
     int n0, ho0, wo0;
     pixel_tile(m_blk, n0, ho0, wo0);
     const int n = n0 + (row >> 6), ho = ho0 + ((row >> 3) & 7), wo = wo0 + (row & 7);
-    const int co = n_blk * umma::BN + col;
     if (n >= batch || ho >= Ho || wo >= Wo || co >= Cout) return;
     __nv_bfloat16* dst = y + (((long long)n * Ho + ho) * Wo + wo) * Cout + co;
     umma::store_bf16_chunk(dst, Cout - co, vec_ok, acc, bias ? bias + co : nullptr);
+  }
+};
+
+struct ConvPolicy : ConvGeometry {
+  __device__ int num_tiles() const { return num_m() * num_n; }
+  __device__ void k_blocks(int, int& kb0, int& kb1) const {
+    kb0 = 0;
+    kb1 = R * S * c_blocks;
+  }
+  __device__ void tile(int t, int& m_blk, int& n_blk) const {
+    umma::grouped_tile(t, num_m(), num_n, 16, m_blk, n_blk);
+  }
+  __device__ void load(uint8_t* a_dst, uint8_t* b_dst, uint64_t* bar, int m_blk, int n_blk, int kb) const {
+    int x, w, h, n, rs;
+    a_coords(m_blk, kb, x, w, h, n, rs);
+    tma_load_4d(a_dst, tx, bar, x, w, h, n);
+    tma_load_3d(b_dst, tw, bar, x, rs, n_blk * umma::BN);
+  }
+  __device__ void store(int row, int, int m_blk, int n_blk, int col, const uint32_t (&acc)[32]) const {
+    store_row(row, m_blk, n_blk * umma::BN + col, acc);
+  }
+  __device__ void finish() const {}
+};
+
+// The 2-SM form: each CTA of a pair loads its own 128-pixel input box and its half
+// (128 output channels) of the 256-channel weight box; the weight map's box is
+// {64, 1, 128}. The odd CTA of a final pair past the last M block reads zeros and
+// stores nothing.
+struct Conv2Policy : ConvGeometry {
+  __device__ int m_blocks() const { return num_m(); }
+  __device__ int n_blocks() const { return num_n; }
+  __device__ int k_blocks() const { return R * S * c_blocks; }
+  __device__ void load(uint8_t* a_dst, uint8_t* b_dst, uint32_t bar, int m_blk, int n_blk, int half, int kb) const {
+    int x, w, h, n, rs;
+    a_coords(m_blk, kb, x, w, h, n, rs);
+    umma2::tma_load_4d_pair(a_dst, tx, bar, x, w, h, n);
+    umma2::tma_load_3d_pair(b_dst, tw, bar, x, rs, n_blk * umma2::BN + half * 128);
+  }
+  __device__ void store(int row, int m_blk, int n_blk, int col, const uint32_t (&acc)[32]) const {
+    store_row(row, m_blk, n_blk * umma2::BN + col, acc);
   }
   __device__ void finish() const {}
 };
 
 }  // namespace
 
-// x: 4-D map {C, W, H, N}, box {64, 8*sw, 8*sh, 2}, element strides {1, sw, sh, 1};
-// w: 3-D map {C, R*S, Cout}, box {64, 1, 256}; both 128-byte swizzled.
-extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
-    conv2d_fprop_bf16_nhwc(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
-                           __nv_bfloat16* __restrict__ y, const float* __restrict__ bias, int batch, int C, int Cout,
-                           int R, int S, int Ho, int Wo, int sh, int sw, int ph, int pw, int dh, int dw,
-                           uint32_t* status) {
-  ConvPolicy p;
-  p.tx = &tmap_x;
-  p.tw = &tmap_w;
+
+// Fills the geometry from the kernel arguments (identical for both forms).
+__device__ __forceinline__ void conv_geometry(ConvGeometry& p, const CUtensorMap* tx, const CUtensorMap* tw,
+                                              __nv_bfloat16* y, const float* bias, int batch, int C, int Cout, int R,
+                                              int S, int Ho, int Wo, int sh, int sw, int ph, int pw, int dh, int dw) {
+  p.tx = tx;
+  p.tw = tw;
   p.y = y;
   p.bias = bias;
   p.batch = batch;
@@ -105,7 +141,30 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
   p.tiles_h = (Ho + 7) / 8;
   p.tiles_w = (Wo + 7) / 8;
   p.c_blocks = (C + 63) / 64;
-  p.num_n = (Cout + umma::BN - 1) / umma::BN;
+  p.num_n = (Cout + 255) / 256;
   p.vec_ok = (Cout % 8) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+}
+
+// x: 4-D map {C, W, H, N}, box {64, 8*sw, 8*sh, 2}, element strides {1, sw, sh, 1};
+// w: 3-D map {C, R*S, Cout}, box {64, 1, 256}; both 128-byte swizzled.
+extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
+    conv2d_fprop_bf16_nhwc(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                           __nv_bfloat16* __restrict__ y, const float* __restrict__ bias, int batch, int C, int Cout,
+                           int R, int S, int Ho, int Wo, int sh, int sw, int ph, int pw, int dh, int dw,
+                           uint32_t* status) {
+  ConvPolicy p;
+  conv_geometry(p, &tmap_x, &tmap_w, y, bias, batch, C, Cout, R, S, Ho, Wo, sh, sw, ph, pw, dh, dw);
   umma::run(p, status, kFailConv);
+}
+
+// The same convolution on CTA pairs (launched with clusters of 2 along x); the weight
+// map's box is {64, 1, 128}.
+extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
+    conv2d_fprop_bf16_nhwc_2sm(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                               __nv_bfloat16* __restrict__ y, const float* __restrict__ bias, int batch, int C,
+                               int Cout, int R, int S, int Ho, int Wo, int sh, int sw, int ph, int pw, int dh, int dw,
+                               uint32_t* status) {
+  Conv2Policy p;
+  conv_geometry(p, &tmap_x, &tmap_w, y, bias, batch, C, Cout, R, S, Ho, Wo, sh, sw, ph, pw, dh, dw);
+  umma2::run(p, status, kFailConv2);
 }

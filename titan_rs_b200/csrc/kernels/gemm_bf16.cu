@@ -23,7 +23,6 @@
 // reduction sums them in a fixed order.
 #include "gemm_policies.cuh"
 #include "peer_signal.cuh"
-#include "umma_pipeline_2sm.cuh"
 
 namespace {
 constexpr uint32_t kFailGemm = 0x47000000u;
@@ -52,25 +51,39 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
 // The same product on CTA pairs (umma_pipeline_2sm.cuh): 256x256 tiles, each CTA
 // loading a 128-row A block and half of the 256-row B block per k-block. Launched
 // with clusters of 2 along x; tensor maps with 128-row boxes for A and B.
-#define TB_GEMM2_ENTRY(name, stages, group)                                                                     \
-  extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)                                              \
-      name(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,              \
-           __nv_bfloat16* __restrict__ c, int M, int N, int K, long long ldc, uint32_t* status) {               \
-    tb::umma2::Problem p;                                                                                       \
-    p.ta = &tmap_a;                                                                                             \
-    p.tb = &tmap_b;                                                                                             \
-    p.c = c;                                                                                                    \
-    p.bias = nullptr;                                                                                           \
-    p.act = tb::kActNone;                                                                                       \
-    p.M = M;                                                                                                    \
-    p.N = N;                                                                                                    \
-    p.K = K;                                                                                                    \
-    p.ldc = ldc;                                                                                                \
-    p.vec_ok = (ldc % 8) == 0 && (reinterpret_cast<uintptr_t>(c) & 15) == 0;                                    \
-    tb::umma2::run_gemm<stages, group>(p, status, kFailGemm2);                                                  \
-  }
+extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
+    gemm_bf16_tn_2sm(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                     __nv_bfloat16* __restrict__ c, int M, int N, int K, long long ldc, uint32_t* status) {
+  tb::gemm::Gemm2Policy p;
+  p.ta = &tmap_a;
+  p.tb = &tmap_b;
+  p.c = c;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = ldc;
+  p.vec_ok = (ldc % 8) == 0 && (reinterpret_cast<uintptr_t>(c) & 15) == 0;
+  tb::umma2::run(p, status, kFailGemm2);
+}
 
-TB_GEMM2_ENTRY(gemm_bf16_tn_2sm, TB_GEMM2_STAGES, TB_GEMM2_GROUP)
+// gemm_bf16_tn_bias_act on the 2-SM pipeline.
+extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
+    gemm_bf16_tn_bias_act_2sm(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                              __nv_bfloat16* __restrict__ c, const float* __restrict__ bias, int act, int M, int N,
+                              int K, long long ldc, uint32_t* status) {
+  tb::gemm::Gemm2Policy p;
+  p.ta = &tmap_a;
+  p.tb = &tmap_b;
+  p.c = c;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = ldc;
+  p.vec_ok = (ldc % 8) == 0 && (reinterpret_cast<uintptr_t>(c) & 15) == 0;
+  p.bias = bias;
+  p.act = act;
+  tb::umma2::run(p, status, kFailGemm2);
+}
 
 // GEMM with a fused epilogue: C = act(A B^T + bias) (bias fp32 [N] or null; act an
 // epilogue_math.cuh Activation), rounded to bf16 once.

@@ -12,9 +12,12 @@
 //   AllGatherPolicy  the GEMM of one rank's column block, fused with the all-gather:
 //                  every packed output chunk is stored into each rank's copy of the
 //                  row-major C (peer copies through CUDA IPC mappings over NVLink).
+//   Gemm2Policy    GemmPolicy's product on the 2-SM pipeline (umma_pipeline_2sm.cuh):
+//                  tensor maps with 128-row boxes for A and B.
 #pragma once
 
 #include "umma_pipeline.cuh"
+#include "umma_pipeline_2sm.cuh"
 
 namespace tb {
 namespace gemm {
@@ -47,6 +50,36 @@ struct GemmPolicy {
   __device__ void store(int row, int, int m_blk, int n_blk, int col, const uint32_t (&r)[32]) const {
     const int gr = m_blk * umma::BM + row;
     const int gc = n_blk * umma::BN + col;
+    if (gr >= M || gc >= N) return;
+    umma::store_bf16_chunk(c + (long long)gr * ldc + gc, N - gc, vec_ok, r, bias ? bias + gc : nullptr, act);
+  }
+  __device__ void finish() const {}
+};
+
+struct Gemm2Policy {
+  const CUtensorMap* ta;
+  const CUtensorMap* tb;
+  __nv_bfloat16* c;
+  int M, N, K;
+  long long ldc;
+  bool vec_ok;
+  const float* bias = nullptr;
+  int act = kActNone;
+
+  __device__ int m_blocks() const { return (M + 127) / 128; }
+  __device__ int n_blocks() const { return (N + umma2::BN - 1) / umma2::BN; }
+  __device__ int k_blocks() const { return (K + umma2::BK - 1) / umma2::BK; }
+  __device__ void prefetch() const {
+    tma_prefetch_desc(ta);
+    tma_prefetch_desc(tb);
+  }
+  __device__ void load(uint8_t* a_dst, uint8_t* b_dst, uint32_t bar, int m_blk, int n_blk, int half, int kb) const {
+    umma2::tma_load_2d_pair(a_dst, ta, bar, kb * umma2::BK, m_blk * 128);
+    umma2::tma_load_2d_pair(b_dst, tb, bar, kb * umma2::BK, n_blk * umma2::BN + half * 128);
+  }
+  __device__ void store(int row, int m_blk, int n_blk, int col, const uint32_t (&r)[32]) const {
+    const int gr = m_blk * 128 + row;
+    const int gc = n_blk * umma2::BN + col;
     if (gr >= M || gc >= N) return;
     umma::store_bf16_chunk(c + (long long)gr * ldc + gc, N - gc, vec_ok, r, bias ? bias + gc : nullptr, act);
   }

@@ -86,6 +86,24 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int32_t x,
+                                                 int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int32_t x,
+                                                 int32_t y, int32_t z, int32_t w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5, %6}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
 __device__ __forceinline__ void umma_bf16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                                   uint32_t accumulate) {
   asm volatile(
@@ -122,20 +140,16 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t tmem, uint32_t cols) 
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(cols) : "memory");
 }
 
-// C[M, N] bf16 (leading dimension ldc) = act(A[M, K] B^T + bias), B stored [N, K].
-struct Problem {
-  const CUtensorMap* ta;
-  const CUtensorMap* tb;
-  __nv_bfloat16* c;
-  const float* bias;
-  int act;
-  int M, N, K;
-  long long ldc;
-  bool vec_ok;
-};
-
-template <int Stages = STAGES, int Group = TB_GEMM2_GROUP>
-__device__ __forceinline__ void run_gemm(const Problem& p, uint32_t* status, uint32_t fail_base) {
+// A problem policy supplies the tile space in 128-row blocks (m_blocks) and 256-column
+// blocks (n_blocks), the k-block count (k_blocks), the loads of one CTA's operands for one k-block
+// and the epilogue addressing:
+//   load(a_dst, b_dst, bar, m_blk, n_blk, half, kb)  A rows of 128-row block m_blk and
+//        B rows [256 n_blk + 128 half, +128), completing on `bar` (the even CTA's `full`,
+//        a shared::cluster address) with the *_pair tensor loads;
+//   store(row, m_blk, n_blk, col, acc)  32 fp32 accumulator columns of one row.
+// Pair tile t covers 128-row blocks 2 pm and 2 pm + 1 (CTA rank 0 and 1).
+template <class Policy, int Stages = STAGES, int Group = TB_GEMM2_GROUP>
+__device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t fail_base) {
   static_assert(smem_bytes(Stages) <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -143,11 +157,11 @@ __device__ __forceinline__ void run_gemm(const Problem& p, uint32_t* status, uin
   const int warp = warp_id(), lane = lane_id();
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
-  const int num_m = (p.M + 2 * BM - 1) / (2 * BM);  // 256-row pair tiles
-  const int num_n = (p.N + BN - 1) / BN;
-  const int tiles = num_m * num_n;
+  const int num_pm = (p.m_blocks() + 1) / 2;  // 256-row pair tiles
+  const int num_n = p.n_blocks();
+  const int tiles = num_pm * num_n;
   const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
-  const int num_k = (p.K + BK - 1) / BK;
+  const int num_k = p.k_blocks();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Stages; ++s) {
@@ -174,17 +188,15 @@ __device__ __forceinline__ void run_gemm(const Problem& p, uint32_t* status, uin
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer (both CTAs) ----------------
-      tma_prefetch_desc(p.ta);
-      tma_prefetch_desc(p.tb);
+      p.prefetch();
       uint32_t issued[Stages] = {};
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       for (int t = pair; t < tiles && ok; t += pairs) {
         int m_blk, n_blk;
-        umma::grouped_tile(t, num_m, num_n, Group, m_blk, n_blk);
-        const int row0 = m_blk * 2 * BM + (int)rank * BM;
-        const int col0 = n_blk * BN + (int)rank * (BN / 2);
+        umma::grouped_tile(t, num_pm, num_n, Group, m_blk, n_blk);
+        m_blk = 2 * m_blk + (int)rank;
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&bars->empty[stage], phase ^ 1)) {
             report_status(status, fail_base | 0x0101);
@@ -194,8 +206,7 @@ __device__ __forceinline__ void run_gemm(const Problem& p, uint32_t* status, uin
           uint8_t* a_dst = smem + stage * STAGE_BYTES;
           const uint32_t full_even = map_to_rank(smem_addr(&bars->full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&bars->full[stage], 2 * STAGE_BYTES);
-          tma_load_2d_pair(a_dst, p.ta, full_even, kb * BK, row0);
-          tma_load_2d_pair(a_dst + A_BYTES, p.tb, full_even, kb * BK, col0);
+          p.load(a_dst, a_dst + A_BYTES, full_even, m_blk, n_blk, (int)rank, kb);
           ++issued[stage];
           if (++stage == Stages) {
             stage = 0;
@@ -262,7 +273,8 @@ __device__ __forceinline__ void run_gemm(const Problem& p, uint32_t* status, uin
     uint32_t acc_phase = 0;
     for (int t = pair; t < tiles; t += pairs) {
       int m_blk, n_blk;
-      umma::grouped_tile(t, num_m, num_n, Group, m_blk, n_blk);
+      umma::grouped_tile(t, num_pm, num_n, Group, m_blk, n_blk);
+      m_blk = 2 * m_blk + (int)rank;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&bars->acc_full[acc], acc_phase));
       if (!ok) {
         if (lane == 0) report_status(status, fail_base | 0x0301);
@@ -270,16 +282,13 @@ __device__ __forceinline__ void run_gemm(const Problem& p, uint32_t* status, uin
       }
       tc_fence_after_sync();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
-      const int gr = m_blk * 2 * BM + (int)rank * BM + quarter * 32 + lane;
+      const int row = quarter * 32 + lane;
 #pragma unroll 1
       for (int col = 0; col < BN; col += 32) {
         uint32_t r[32];
         tmem_ld_x32(taddr + col, r);
         tmem_ld_wait();
-        const int gc = n_blk * BN + col;
-        if (gr < p.M && gc < p.N)
-          umma::store_bf16_chunk(p.c + (long long)gr * p.ldc + gc, p.N - gc, p.vec_ok, r,
-                                 p.bias ? p.bias + gc : nullptr, p.act);
+        p.store(row, m_blk, n_blk, col, r);
       }
       tc_fence_before_sync();
       __syncwarp();
@@ -292,6 +301,7 @@ __device__ __forceinline__ void run_gemm(const Problem& p, uint32_t* status, uin
         acc_phase ^= 1;
       }
     }
+    p.finish();
   }
 
   tc_fence_before_sync();
