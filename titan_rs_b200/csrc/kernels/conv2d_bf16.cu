@@ -101,14 +101,49 @@ struct Conv2Policy : ConvGeometry {
   __device__ int m_blocks() const { return num_m(); }
   __device__ int n_blocks() const { return num_n; }
   __device__ int k_blocks() const { return R * S * c_blocks; }
-  __device__ void load(uint8_t* a_dst, uint8_t* b_dst, uint32_t bar, int m_blk, int n_blk, int half, int kb) const {
-    int x, w, h, n, rs;
-    a_coords(m_blk, kb, x, w, h, n, rs);
-    umma2::tma_load_4d_pair(a_dst, tx, bar, x, w, h, n);
-    umma2::tma_load_3d_pair(b_dst, tw, bar, x, rs, n_blk * umma2::BN + half * 128);
+  // Walks k-blocks in the order kb = (r * S + s) * c_blocks + cb with counters.
+  struct Loader {
+    const CUtensorMap *tx, *tw;
+    int w0, h0, n0, co;      // input box origin for tap (0, 0); first output channel
+    int r, s, cb, rs;        // current tap and channel block
+    int S, c_blocks, dh, dw;
+    __device__ void load(uint8_t* a_dst, uint8_t* b_dst, uint32_t bar) {
+      umma2::tma_load_4d_pair(a_dst, tx, bar, cb * 64, w0 + s * dw, h0 + r * dh, n0);
+      umma2::tma_load_3d_pair(b_dst, tw, bar, cb * 64, rs, co);
+      if (++cb == c_blocks) {
+        cb = 0;
+        ++rs;
+        if (++s == S) {
+          s = 0;
+          ++r;
+        }
+      }
+    }
+  };
+  __device__ Loader loader(int m_blk, int n_blk, int half) const {
+    int n0, ho0, wo0;
+    pixel_tile(m_blk, n0, ho0, wo0);
+    return Loader{tx, tw, wo0 * sw - pw, ho0 * sh - ph, n0, n_blk * umma2::BN + half * 128, 0, 0, 0, 0,
+                  S, c_blocks, dh, dw};
   }
-  __device__ void store(int row, int m_blk, int n_blk, int col, const uint32_t (&acc)[32]) const {
-    store_row(row, m_blk, n_blk * umma2::BN + col, acc);
+  struct Storer {
+    __nv_bfloat16* dst;  // output pixel at the tile's first channel; null outside the output
+    const float* bias;
+    int cols;            // valid channels from the tile's first channel
+    bool vec_ok;
+    __device__ void store(int col, const uint32_t (&acc)[32]) const {
+      if (!dst || col >= cols) return;
+      umma::store_bf16_chunk(dst + col, cols - col, vec_ok, acc, bias ? bias + col : nullptr);
+    }
+  };
+  __device__ Storer storer(int row, int m_blk, int n_blk) const {
+    int n0, ho0, wo0;
+    pixel_tile(m_blk, n0, ho0, wo0);
+    const int n = n0 + (row >> 6), ho = ho0 + ((row >> 3) & 7), wo = wo0 + (row & 7);
+    const int co = n_blk * umma2::BN;
+    const bool in = n < batch && ho < Ho && wo < Wo;
+    return Storer{in ? y + (((long long)n * Ho + ho) * Wo + wo) * Cout + co : nullptr, bias ? bias + co : nullptr,
+                  Cout - co, vec_ok};
   }
   __device__ void finish() const {}
 };

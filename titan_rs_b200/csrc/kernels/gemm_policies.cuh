@@ -73,15 +73,33 @@ struct Gemm2Policy {
     tma_prefetch_desc(ta);
     tma_prefetch_desc(tb);
   }
-  __device__ void load(uint8_t* a_dst, uint8_t* b_dst, uint32_t bar, int m_blk, int n_blk, int half, int kb) const {
-    umma2::tma_load_2d_pair(a_dst, ta, bar, kb * umma2::BK, m_blk * 128);
-    umma2::tma_load_2d_pair(b_dst, tb, bar, kb * umma2::BK, n_blk * umma2::BN + half * 128);
+  struct Loader {
+    const CUtensorMap *ta, *tb;
+    int row, col, k;
+    __device__ void load(uint8_t* a_dst, uint8_t* b_dst, uint32_t bar) {
+      umma2::tma_load_2d_pair(a_dst, ta, bar, k, row);
+      umma2::tma_load_2d_pair(b_dst, tb, bar, k, col);
+      k += umma2::BK;
+    }
+  };
+  __device__ Loader loader(int m_blk, int n_blk, int half) const {
+    return Loader{ta, tb, m_blk * 128, n_blk * umma2::BN + half * 128, 0};
   }
-  __device__ void store(int row, int m_blk, int n_blk, int col, const uint32_t (&r)[32]) const {
+  struct Storer {
+    __nv_bfloat16* dst;  // row start at the tile's first column; null when the row is past M
+    const float* bias;   // at the tile's first column, or null
+    int cols;            // valid columns from the tile's first column
+    int act;
+    bool vec_ok;
+    __device__ void store(int col, const uint32_t (&r)[32]) const {
+      if (!dst || col >= cols) return;
+      umma::store_bf16_chunk(dst + col, cols - col, vec_ok, r, bias ? bias + col : nullptr, act);
+    }
+  };
+  __device__ Storer storer(int row, int m_blk, int n_blk) const {
     const int gr = m_blk * 128 + row;
-    const int gc = n_blk * umma2::BN + col;
-    if (gr >= M || gc >= N) return;
-    umma::store_bf16_chunk(c + (long long)gr * ldc + gc, N - gc, vec_ok, r, bias ? bias + gc : nullptr, act);
+    const int gc = n_blk * umma2::BN;
+    return Storer{gr < M ? c + (long long)gr * ldc + gc : nullptr, bias ? bias + gc : nullptr, N - gc, act, vec_ok};
   }
   __device__ void finish() const {}
 };

@@ -141,12 +141,15 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t tmem, uint32_t cols) 
 }
 
 // A problem policy supplies the tile space in 128-row blocks (m_blocks) and 256-column
-// blocks (n_blocks), the k-block count (k_blocks), the loads of one CTA's operands for one k-block
-// and the epilogue addressing:
-//   load(a_dst, b_dst, bar, m_blk, n_blk, half, kb)  A rows of 128-row block m_blk and
-//        B rows [256 n_blk + 128 half, +128), completing on `bar` (the even CTA's `full`,
-//        a shared::cluster address) with the *_pair tensor loads;
-//   store(row, m_blk, n_blk, col, acc)  32 fp32 accumulator columns of one row.
+// blocks (n_blocks), the k-block count (k_blocks), and two per-tile cursors that do
+// their index arithmetic once per tile, so the single producer lane spends its time
+// issuing copies (a runtime integer division per k-block costs more than the copy):
+//   loader(m_blk, n_blk, half) -> L;  L.load(a_dst, b_dst, bar) loads the next k-block:
+//        A rows of 128-row block m_blk and B rows [256 n_blk + 128 half, +128), completing
+//        on `bar` (the even CTA's `full`, a shared::cluster address) with the *_pair
+//        tensor loads;
+//   storer(row, m_blk, n_blk) -> W;  W.store(col, acc) stores 32 fp32 accumulator
+//        columns [col, col + 32) of one row.
 // Pair tile t covers 128-row blocks 2 pm and 2 pm + 1 (CTA rank 0 and 1).
 template <class Policy, int Stages = STAGES, int Group = TB_GEMM2_GROUP>
 __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t fail_base) {
@@ -189,14 +192,17 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
     if (lane == 0) {
       // ---------------- TMA producer (both CTAs) ----------------
       p.prefetch();
-      uint32_t issued[Stages] = {};
+      uint32_t issued = 0;  // k-blocks loaded so far; stage s was filled (issued + Stages - 1 - s) / Stages times
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      // The even CTA's `full` barriers as shared::cluster addresses (consecutive, 8 bytes apart).
+      const uint32_t full_even0 = map_to_rank(smem_addr(&bars->full[0]), 0);
       for (int t = pair; t < tiles && ok; t += pairs) {
         int m_blk, n_blk;
         umma::grouped_tile(t, num_pm, num_n, Group, m_blk, n_blk);
         m_blk = 2 * m_blk + (int)rank;
+        auto ld = p.loader(m_blk, n_blk, (int)rank);
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&bars->empty[stage], phase ^ 1)) {
             report_status(status, fail_base | 0x0101);
@@ -204,10 +210,9 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
             break;
           }
           uint8_t* a_dst = smem + stage * STAGE_BYTES;
-          const uint32_t full_even = map_to_rank(smem_addr(&bars->full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&bars->full[stage], 2 * STAGE_BYTES);
-          p.load(a_dst, a_dst + A_BYTES, full_even, m_blk, n_blk, (int)rank, kb);
-          ++issued[stage];
+          ld.load(a_dst, a_dst + A_BYTES, full_even0 + 8u * (uint32_t)stage);
+          ++issued;
           if (++stage == Stages) {
             stage = 0;
             phase ^= 1;
@@ -216,8 +221,10 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
       }
       if (!ok && leader) {
         // The issued copies land on this CTA's `full` barriers: wait for them before TMEM goes.
-        for (int s = 0; s < Stages; ++s)
-          if (issued[s] && !mbar_wait(&bars->full[s], (issued[s] - 1) & 1)) report_status(status, fail_base | 0x0102);
+        for (int s = 0; s < Stages; ++s) {
+          const uint32_t fills = (issued + Stages - 1 - s) / Stages;
+          if (fills && !mbar_wait(&bars->full[s], (fills - 1) & 1)) report_status(status, fail_base | 0x0102);
+        }
       }
     }
   } else if (warp == 1) {
@@ -282,13 +289,13 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
       }
       tc_fence_after_sync();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
-      const int row = quarter * 32 + lane;
+      const auto st = p.storer(quarter * 32 + lane, m_blk, n_blk);
 #pragma unroll 1
       for (int col = 0; col < BN; col += 32) {
         uint32_t r[32];
         tmem_ld_x32(taddr + col, r);
         tmem_ld_wait();
-        p.store(row, m_blk, n_blk, col, r);
+        st.store(col, r);
       }
       tc_fence_before_sync();
       __syncwarp();
