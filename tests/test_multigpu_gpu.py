@@ -22,14 +22,14 @@ def _gemm_inputs(m, n, k, seed=21):
     return a, b
 
 
-def _reference_c(s, rt, a, b):
+def _reference_c(s, rt, a, b, candidate="gemm_bf16_tn"):
     m, k = a.shape
     n = b.shape[0]
     ta = tb.TensorHandle.from_numpy(s, a, DType.BF16, rt.stream)
     tbb = tb.TensorHandle.from_numpy(s, b, DType.BF16, rt.stream)
-    # The sharded path runs the whole-K kernel on each shard; compare with the same kernel.
+    # The sharded path runs a whole-K kernel on each shard; compare with the same kernel family.
     h = rt.execute(tb.OpRequest("gemm", [ta, tbb], [tb.TensorSpec(DType.BF16, (m, n))],
-                                {"transpose_rhs": True, "candidate": "gemm_bf16_tn"}))
+                                {"transpose_rhs": True, "candidate": candidate}))
     h.wait()
     return h.outputs[0].to_numpy()
 
@@ -60,14 +60,20 @@ def test_one_rank_sharded_gemm_equals_single_gpu_gemm():
     s.close()
 
 
-def test_one_rank_fused_sharded_gemm_equals_single_gpu_gemm():
-    """A registered output takes the fused kernel (gemm_bf16_tn_allgather); with one rank
-    it must equal the plain whole-K GEMM bit for bit, call after call."""
+# (m, n, k, fused kernel, plain kernel of the same family): 25 output tiles of 128x256
+# take the 1-SM kernel; 323 (with M and N tails) take CTA pairs.
+FUSED_CASES = [(640, 1280, 1536, "gemm_bf16_tn_allgather", "gemm_bf16_tn"),
+               (2056, 4856, 1024, "gemm_bf16_tn_allgather_2sm", "gemm_bf16_tn_2sm")]
+
+
+@pytest.mark.parametrize("m,n,k,fused,plain", FUSED_CASES)
+def test_one_rank_fused_sharded_gemm_equals_single_gpu_gemm(m, n, k, fused, plain):
+    """A registered output takes the fused kernel; with one rank it must equal the plain
+    whole-K GEMM of the same pipeline bit for bit, call after call."""
     s = tb.Session(0)
     rt = tb.Runtime(s)
-    m, n, k = 640, 1280, 1536
     a, b = _gemm_inputs(m, n, k, seed=23)
-    ref = _reference_c(s, rt, a, b)
+    ref = _reference_c(s, rt, a, b, plain)
     coll = D.NcclCollective(s, D.new_comm_id(), 1, 0, timeout_ms=20000)
     ta = tb.TensorHandle.from_numpy(s, a, DType.BF16, rt.stream)
     tbb = tb.TensorHandle.from_numpy(s, b, DType.BF16, rt.stream)
@@ -78,7 +84,7 @@ def test_one_rank_fused_sharded_gemm_equals_single_gpu_gemm():
     for _ in range(2):
         coll.sharded_gemm(rt.stream, ta, tbb, c, None)
         s.synchronize(rt.stream)
-        assert tb.last_candidate() == "gemm_bf16_tn_allgather"
+        assert tb.last_candidate() == fused
         np.testing.assert_array_equal(c.to_numpy(), ref)
     coll.deregister_buffer(c.buffer)
     with pytest.raises(tb.HalError, match="not registered"):
@@ -129,31 +135,37 @@ def _rank_main(rank, world, q_in, q_out, mode):
             coll.barrier(rt.stream)
             s.synchronize(rt.stream)
             q_out.put((rank, ok_gemm and ok_gather))
-        elif mode == "gemm_p2p":
+        elif mode in ("gemm_p2p", "gemm_p2p_pairs"):
             # Fused GEMM + all-gather into registered outputs, twice with different inputs.
-            m, n, k = 520, 1536, 1024  # M is not a multiple of the 128-row tile
+            if mode == "gemm_p2p":
+                m, n, k = 520, 1536, 1024  # M is not a multiple of the 128-row tile
+                fused, plain = "gemm_bf16_tn_allgather", "gemm_bf16_tn"
+            else:
+                m, n, k = 2056, 9712, 1024  # 323 tiles per shard, M and N tails: CTA pairs
+                fused, plain = "gemm_bf16_tn_allgather_2sm", "gemm_bf16_tn_2sm"
             lo, hi = Dm.even_shard(n, world, rank)
             c = tbm.TensorHandle.allocate(s, DType.BF16, (m, n))
             coll.register_buffer(rt.stream, c.buffer)
             ok = True
             for seed in (31, 32):
                 a, b = _gemm_inputs(m, n, k, seed=seed)
-                ref = _reference_c(s, rt, a, b)
+                ref = _reference_c(s, rt, a, b, plain)
                 ta = tbm.TensorHandle.from_numpy(s, a, DType.BF16, rt.stream)
                 tbs = tbm.TensorHandle.from_numpy(s, np.ascontiguousarray(b[lo:hi]), DType.BF16, rt.stream)
                 coll.sharded_gemm(rt.stream, ta, tbs, c, None)
                 s.synchronize(rt.stream)
-                ok = ok and tbm.last_candidate() == "gemm_bf16_tn_allgather"
+                ok = ok and tbm.last_candidate() == fused
                 ok = ok and bool(np.array_equal(c.to_numpy(), ref))
             coll.barrier(rt.stream)
             s.synchronize(rt.stream)
             coll.deregister_buffer(c.buffer)
             q_out.put((rank, ok))
-        elif mode == "p2p_absent":
+        elif mode in ("p2p_absent", "p2p_absent_pairs"):
             # Rank 1 registers its output but never makes the call: rank 0's fused kernel
             # gives up its entry wait after ~1 s (a flag nothing sets), reports the code, and
-            # its context stays usable.
-            m, n, k = 256, 512, 256
+            # its context stays usable. With CTA pairs the CTAs still run the pair pipeline
+            # (stores off), so every cluster barrier is reached.
+            m, n, k = (256, 512, 256) if mode == "p2p_absent" else (2056, 9712, 512)
             c = tbm.TensorHandle.allocate(s, DType.BF16, (m, n))
             coll.register_buffer(rt.stream, c.buffer)
             if rank == 0:
@@ -222,8 +234,14 @@ def test_two_rank_fused_sharded_gemm_over_peer_stores():
 
 
 @pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")
-def test_two_rank_fused_gemm_gives_up_when_a_peer_never_arrives():
-    assert _spawn(2, "p2p_absent") == {0: ("timeout", True), 1: "absent"}
+def test_two_rank_fused_sharded_gemm_on_cta_pairs():
+    assert _spawn(2, "gemm_p2p_pairs") == {0: True, 1: True}
+
+
+@pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("mode", ["p2p_absent", "p2p_absent_pairs"])
+def test_two_rank_fused_gemm_gives_up_when_a_peer_never_arrives(mode):
+    assert _spawn(2, mode) == {0: ("timeout", True), 1: "absent"}
 
 
 @pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")

@@ -72,15 +72,19 @@ tb_status launch_gemm_bf16_tn_allgather(Session* s, Stream* st, CUdeviceptr a, C
   if (ldc % 8 != 0 || col0 % 8 != 0 || N % 8 != 0) return unsupported("fused all-gather needs 8-column alignment");
   for (int i = 0; i < ranks; ++i)
     if (outs[i] & 15) return unsupported("fused all-gather needs 16-byte aligned outputs");
+  // CTA pairs under the same rule as the plain GEMM (gemm_bf16_tn_allgather_2sm).
+  const long long tiles = (long long)((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN);
+  const bool pairs = M >= 256 && tiles >= s->sm_count;
   CUtensorMap ta, tbm;
   tb_status rc = tmap_bf16_2d(&ta, a, (uint64_t)M, (uint64_t)K, (uint64_t)K, TB_GEMM_BM, TB_GEMM_BK,
                               CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = tmap_bf16_2d(&tbm, b, (uint64_t)N, (uint64_t)K, (uint64_t)K, TB_GEMM_BN, TB_GEMM_BK,
+  rc = tmap_bf16_2d(&tbm, b, (uint64_t)N, (uint64_t)K, (uint64_t)K, pairs ? 128u : (uint32_t)TB_GEMM_BN, TB_GEMM_BK,
                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   CUfunction fn = nullptr;
-  rc = builtin_function(s, "gemm_bf16", "gemm_bf16_tn_allgather", &fn);
+  const char* name = pairs ? "gemm_bf16_tn_allgather_2sm" : "gemm_bf16_tn_allgather";
+  rc = builtin_function(s, "gemm_bf16", name, &fn);
   if (rc) return rc;
   struct {
     CUdeviceptr base[TB_MAX_RANKS];
@@ -89,12 +93,14 @@ tb_status launch_gemm_bf16_tn_allgather(Session* s, Stream* st, CUdeviceptr a, C
     rank_outputs.base[i] = outs[i];
     rank_signals.base[i] = signals[i];
   }
-  const long long tiles = (long long)((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN);
-  const unsigned grid = (unsigned)(tiles < s->sm_count ? tiles : s->sm_count);
   CUdeviceptr status = s->status.device;
   void* params[] = {&ta, &tbm, &rank_outputs, &rank_signals, &ranks, &self, &epoch, &M, &N, &K, &ldc, &col0, &status};
-  return launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_AG_SMEM_BYTES, params,
-                        "gemm_bf16_tn_allgather");
+  if (pairs) {
+    const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+    return launch_builtin_pairs(s, st, fn, pair_tiles, TB_GEMM_THREADS, TB_GEMM2_AG_SMEM_BYTES, params, name);
+  }
+  const unsigned grid = (unsigned)(tiles < s->sm_count ? tiles : s->sm_count);
+  return launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_AG_SMEM_BYTES, params, name);
 }
 
 // Split-K plan for an output with too few 128x256 tiles to fill the SMs.

@@ -29,6 +29,7 @@ constexpr uint32_t kFailGemm = 0x47000000u;
 constexpr uint32_t kFailGemm2 = 0x47320000u;
 constexpr uint32_t kFailSplitK = 0x4B000000u;
 constexpr uint32_t kFailAllGather = 0x47410000u;
+constexpr uint32_t kFailAllGather2 = 0x47420000u;
 }  // namespace
 
 extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
@@ -149,6 +150,51 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
   if (threadIdx.x == 0) {
     // Every epilogue thread fenced its stores (AllGatherPolicy::finish) before run()'s
     // final __syncthreads.
+    __threadfence_system();
+    tb::SignalBlock* mine = sig.block[self];
+    if (atomicAdd(&mine->arrivals, 1u) == gridDim.x - 1) {
+      mine->arrivals = 0;  // the next call starts after this kernel (stream order)
+      if (entry_ok) {
+        tb::signal_peers(sig, ranks, self, epoch, true);
+        if (!tb::wait_peers(sig, ranks, self, epoch, true)) tb::report_status(status, kFailAllGather | 0x0502);
+      }
+    }
+  }
+}
+
+// The fused GEMM + all-gather on CTA pairs (clusters of 2 along x, 128-row boxes for A
+// and B). Same handshake as gemm_bf16_tn_allgather; a CTA whose entry wait fails still
+// runs the pair pipeline (its partner waits for it at cluster barriers) with stores off.
+extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
+    gemm_bf16_tn_allgather_2sm(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                               const __grid_constant__ tb::gemm::RankOutputs outs,
+                               const __grid_constant__ tb::RankSignals sig, int ranks, int self, uint32_t epoch, int M,
+                               int N, int K, long long ldc, long long col0, uint32_t* status) {
+  __shared__ int entry_ok;
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) tb::signal_peers(sig, ranks, self, epoch, false);
+    entry_ok = tb::wait_peers(sig, ranks, self, epoch, false) ? 1 : 0;
+    if (!entry_ok) tb::report_status(status, kFailAllGather | 0x0501);
+  }
+  __syncthreads();
+  tb::gemm::AllGather2Policy p;
+  p.ta = &tmap_a;
+  p.tb = &tmap_b;
+  p.c = nullptr;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = ldc;
+  p.vec_ok = true;  // the host requires 16-byte aligned bases, ldc % 8 == 0, col0 % 8 == 0 and N % 8 == 0
+  p.outs = &outs;
+  p.ranks = ranks;
+  p.self = self;
+  p.col0 = col0;
+  p.enabled = entry_ok != 0;
+  tb::umma2::run(p, status, kFailAllGather2);
+  if (threadIdx.x == 0) {
+    // Every epilogue thread fenced its stores (AllGather2Policy::finish) before run()'s
+    // final cluster barrier.
     __threadfence_system();
     tb::SignalBlock* mine = sig.block[self];
     if (atomicAdd(&mine->arrivals, 1u) == gridDim.x - 1) {

@@ -157,6 +157,58 @@ struct AllGatherPolicy : GemmPolicy {
   __device__ void finish() const { __threadfence_system(); }
 };
 
+// AllGatherPolicy's epilogue on the 2-SM pipeline. `enabled` is false after a failed
+// entry handshake: the CTA still runs the pipeline with its pair (both CTAs must reach
+// the pipeline's cluster barriers) but stores nothing.
+struct AllGather2Policy : Gemm2Policy {
+  const RankOutputs* outs;  // kernel parameter space
+  int ranks, self;
+  long long col0;
+  bool enabled;
+
+  struct Storer {
+    const RankOutputs* outs;
+    uint8_t* stage;  // this warp's [32 rows][256 B] staging block
+    int lane, row0, gc0, M, N, ranks, self;
+    long long ldc, col0;
+    bool enabled;
+    __device__ void store(int col, const uint32_t (&r)[32]) const {
+      const int first_seg = (col & 127) >> 3;  // 0, 4, 8, 12
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 v;
+        v.x = pack_bf16x2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
+        v.y = pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
+        v.z = pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
+        v.w = pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
+        *reinterpret_cast<uint4*>(stage + lane * 256 + (((first_seg + q) ^ (lane & 15)) << 4)) = v;
+      }
+      if ((col & 127) != 96) return;  // the 128-column half is complete after its fourth chunk
+      __syncwarp();
+      const int seg = lane & 15;                     // 16-byte segment (8 columns) of a row
+      const int gc = gc0 + (col & ~127) + seg * 8;  // this lane's local column
+      if (enabled) {
+        for (int it = 0; it < 16; ++it) {
+          const int rr = 2 * it + (lane >> 4);
+          const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 256 + ((seg ^ (rr & 15)) << 4));
+          const int gr = row0 + rr;
+          if (gr < M && gc < N) {
+            const long long off = (long long)gr * ldc + col0 + gc;
+            for (int i = 0, d = self; i < ranks; ++i, d = (d + 1 == ranks) ? 0 : d + 1)
+              *reinterpret_cast<uint4*>(outs->base[d] + off) = v;
+          }
+        }
+      }
+      __syncwarp();  // the next half overwrites the staging block
+    }
+  };
+  __device__ Storer storer(int row, int m_blk, int n_blk) const {
+    return Storer{outs, umma2::epilogue_smem() + (row >> 5) * (32 * 256), row & 31, m_blk * 128 + (row & ~31),
+                  n_blk * umma2::BN, M, N, ranks, self, ldc, col0, enabled};
+  }
+  __device__ void finish() const { __threadfence_system(); }
+};
+
 struct SplitKPolicy {
   const CUtensorMap* ta;
   const CUtensorMap* tb;

@@ -24,6 +24,7 @@
 #define TB_SIGNAL_BLOCK_BYTES 128
 #define TB_GEMM_AG_STAGE_BYTES (4 * 32 * 256)
 #define TB_GEMM_AG_SMEM_BYTES (TB_GEMM_SMEM_BYTES + TB_GEMM_AG_STAGE_BYTES)
+#define TB_GEMM2_AG_SMEM_BYTES (TB_GEMM2_SMEM_BYTES + TB_GEMM_AG_STAGE_BYTES)
 
 // Causal SDPA forward (sdpa_bf16.cu): 128-row query tiles, 128-key tiles, head dim 128.
 // Shared memory: Q 32 KB + K ring 2x32 KB + V ring 2x32 KB + P 2x32 KB + barriers.

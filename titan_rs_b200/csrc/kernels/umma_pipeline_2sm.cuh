@@ -53,6 +53,16 @@ __host__ __device__ constexpr int smem_bytes(int stages) { return stages * STAGE
 static_assert(sizeof(Barriers<8>) <= TB_GEMM2_BARRIER_BYTES, "barrier block overflows its reservation");
 static_assert(smem_bytes(STAGES) == TB_GEMM2_SMEM_BYTES, "smem layout");
 static_assert(TB_GEMM2_SMEM_BYTES <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
+static_assert(TB_GEMM2_AG_SMEM_BYTES <= 232448, "fused all-gather staging exceeds the 227 KB limit");
+
+// Dynamic shared memory past the ring and the barriers (from the 1 KB-aligned base) is
+// free for a policy's epilogue staging; its kernel is launched with the extra bytes.
+template <int Stages = STAGES>
+__device__ __forceinline__ uint8_t* epilogue_smem() {
+  extern __shared__ uint8_t smem_raw[];
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023)) +
+         Stages * STAGE_BYTES + TB_GEMM2_BARRIER_BYTES;
+}
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
