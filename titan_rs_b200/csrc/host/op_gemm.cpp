@@ -97,7 +97,7 @@ tb_status launch_gemm_bf16_tn_allgather(Session* s, Stream* st, CUdeviceptr a, C
   void* params[] = {&ta, &tbm, &rank_outputs, &rank_signals, &ranks, &self, &epoch, &M, &N, &K, &ldc, &col0, &status};
   if (pairs) {
     const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
-    return launch_builtin_pairs(s, st, fn, pair_tiles, TB_GEMM_THREADS, TB_GEMM2_AG_SMEM_BYTES, params, name);
+    return launch_builtin_pairs(s, st, fn, pair_tiles, TB_GEMM2_AG_THREADS, TB_GEMM2_AG_SMEM_BYTES, params, name);
   }
   const unsigned grid = (unsigned)(tiles < s->sm_count ? tiles : s->sm_count);
   return launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_AG_SMEM_BYTES, params, name);

@@ -97,7 +97,7 @@ struct ConvPolicy : ConvGeometry {
 // (128 output channels) of the 256-channel weight box; the weight map's box is
 // {64, 1, 128}. The odd CTA of a final pair past the last M block reads zeros and
 // stores nothing.
-struct Conv2Policy : ConvGeometry {
+struct Conv2Policy : ConvGeometry, umma2::PolicyBase {
   __device__ int m_blocks() const { return num_m(); }
   __device__ int n_blocks() const { return num_n; }
   __device__ int k_blocks() const { return R * S * c_blocks; }
@@ -136,7 +136,7 @@ struct Conv2Policy : ConvGeometry {
       umma::store_bf16_chunk(dst + col, cols - col, vec_ok, acc, bias ? bias + col : nullptr);
     }
   };
-  __device__ Storer storer(int row, int m_blk, int n_blk) const {
+  __device__ Storer storer(int row, int m_blk, int n_blk, int, uint32_t*) const {
     int n0, ho0, wo0;
     pixel_tile(m_blk, n0, ho0, wo0);
     const int n = n0 + (row >> 6), ho = ho0 + ((row >> 3) & 7), wo = wo0 + (row & 7);
@@ -145,7 +145,6 @@ struct Conv2Policy : ConvGeometry {
     return Storer{in ? y + (((long long)n * Ho + ho) * Wo + wo) * Cout + co : nullptr, bias ? bias + co : nullptr,
                   Cout - co, vec_ok};
   }
-  __device__ void finish() const {}
 };
 
 }  // namespace

@@ -163,9 +163,10 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
 }
 
 // The fused GEMM + all-gather on CTA pairs (clusters of 2 along x, 128-row boxes for A
-// and B). Same handshake as gemm_bf16_tn_allgather; a CTA whose entry wait fails still
-// runs the pair pipeline (its partner waits for it at cluster barriers) with stores off.
-extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
+// and B, TB_GEMM2_AG_THREADS threads: the pipeline's six warps and four push warps).
+// Same handshake as gemm_bf16_tn_allgather; a CTA whose entry wait fails still runs the
+// pair pipeline (its partner waits for it at cluster barriers) with stores off.
+extern "C" __global__ void __launch_bounds__(TB_GEMM2_AG_THREADS, 1)
     gemm_bf16_tn_allgather_2sm(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                                const __grid_constant__ tb::gemm::RankOutputs outs,
                                const __grid_constant__ tb::RankSignals sig, int ranks, int self, uint32_t epoch, int M,
@@ -191,9 +192,9 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
   p.self = self;
   p.col0 = col0;
   p.enabled = entry_ok != 0;
-  tb::umma2::run(p, status, kFailAllGather2);
+  tb::umma2::run<tb::gemm::AllGather2Policy, TB_GEMM2_AG_STAGES>(p, status, kFailAllGather2);
   if (threadIdx.x == 0) {
-    // Every epilogue thread fenced its stores (AllGather2Policy::finish) before run()'s
+    // Every push-warp thread fenced its stores (AllGather2Policy::side) before run()'s
     // final cluster barrier.
     __threadfence_system();
     tb::SignalBlock* mine = sig.block[self];

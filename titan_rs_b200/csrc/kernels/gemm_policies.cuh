@@ -56,7 +56,7 @@ struct GemmPolicy {
   __device__ void finish() const {}
 };
 
-struct Gemm2Policy {
+struct Gemm2Policy : umma2::PolicyBase {
   const CUtensorMap* ta;
   const CUtensorMap* tb;
   __nv_bfloat16* c;
@@ -96,12 +96,11 @@ struct Gemm2Policy {
       umma::store_bf16_chunk(dst + col, cols - col, vec_ok, r, bias ? bias + col : nullptr, act);
     }
   };
-  __device__ Storer storer(int row, int m_blk, int n_blk) const {
+  __device__ Storer storer(int row, int m_blk, int n_blk, int, uint32_t*) const {
     const int gr = m_blk * 128 + row;
     const int gc = n_blk * umma2::BN;
     return Storer{gr < M ? c + (long long)gr * ldc + gc : nullptr, bias ? bias + gc : nullptr, N - gc, act, vec_ok};
   }
-  __device__ void finish() const {}
 };
 
 // Output bases of every rank's C for the fused GEMM + all-gather (index = rank).
@@ -157,22 +156,53 @@ struct AllGatherPolicy : GemmPolicy {
   __device__ void finish() const { __threadfence_system(); }
 };
 
-// AllGatherPolicy's epilogue on the 2-SM pipeline. `enabled` is false after a failed
-// entry handshake: the CTA still runs the pipeline with its pair (both CTAs must reach
-// the pipeline's cluster barriers) but stores nothing.
+// AllGatherPolicy's product on the 2-SM pipeline, with the peer stores taken off the
+// epilogue. Writing a tile into every rank's C over NVLink takes about as long as
+// computing it, and an epilogue that did it would hold its TMEM accumulator (and so
+// the tensor cores) until the link had taken everything. Here the four epilogue warps
+// only pack their 32 rows into shared memory, one 32 x 128 slot per half tile (eight
+// slots = one whole 128 x 256 tile per CTA), and free the accumulator; four side
+// ("push") warps, one per epilogue warp, drain the slots to all ranks while the next
+// tile computes. Slot handshake: mbarriers slot_full / slot_empty (one arrival each),
+// phase = the CTA's tile ordinal.
+// `enabled` is false after a failed entry handshake: the CTA still runs the pipeline
+// with its pair (both CTAs must reach the pipeline's cluster barriers) but stores nothing.
 struct AllGather2Policy : Gemm2Policy {
+  static constexpr int kSideWarps = 4;
+  static constexpr int kStages = TB_GEMM2_AG_STAGES;  // 5 x 32 KB + 64 KB of slots fit in 227 KB
+  static constexpr int kSlotBytes = 32 * 256;
+  static constexpr int kStagingBytes = 128 + 8 * kSlotBytes;
   const RankOutputs* outs;  // kernel parameter space
   int ranks, self;
   long long col0;
   bool enabled;
 
+  struct Slots {
+    uint64_t full[8];
+    uint64_t empty[8];
+  };
+  __device__ static Slots* slots() { return reinterpret_cast<Slots*>(umma2::epilogue_smem<kStages>()); }
+  __device__ static uint8_t* slot(int i) { return umma2::epilogue_smem<kStages>() + 128 + i * kSlotBytes; }
+
+  __device__ void init() const {
+    for (int i = 0; i < 8; ++i) {
+      mbar_init(&slots()->full[i], 1);
+      mbar_init(&slots()->empty[i], 1);
+    }
+  }
+
   struct Storer {
-    const RankOutputs* outs;
-    uint8_t* stage;  // this warp's [32 rows][256 B] staging block
-    int lane, row0, gc0, M, N, ranks, self;
-    long long ldc, col0;
-    bool enabled;
+    int lane, quarter;
+    uint32_t parity;
+    uint32_t* status;
     __device__ void store(int col, const uint32_t (&r)[32]) const {
+      const int half = col >> 7, s = quarter * 2 + half;
+      uint8_t* stage = slot(s);
+      if ((col & 127) == 0) {
+        // The push warp has drained this slot's previous tile (first use passes at once).
+        if (!__all_sync(0xffffffffu, mbar_wait(&slots()->empty[s], parity ^ 1)) && lane == 0)
+          report_status(status, 0x47420601);
+      }
       const int first_seg = (col & 127) >> 3;  // 0, 4, 8, 12
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -183,30 +213,58 @@ struct AllGather2Policy : Gemm2Policy {
         v.w = pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
         *reinterpret_cast<uint4*>(stage + lane * 256 + (((first_seg + q) ^ (lane & 15)) << 4)) = v;
       }
-      if ((col & 127) != 96) return;  // the 128-column half is complete after its fourth chunk
-      __syncwarp();
-      const int seg = lane & 15;                     // 16-byte segment (8 columns) of a row
-      const int gc = gc0 + (col & ~127) + seg * 8;  // this lane's local column
-      if (enabled) {
-        for (int it = 0; it < 16; ++it) {
-          const int rr = 2 * it + (lane >> 4);
-          const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 256 + ((seg ^ (rr & 15)) << 4));
-          const int gr = row0 + rr;
-          if (gr < M && gc < N) {
-            const long long off = (long long)gr * ldc + col0 + gc;
-            for (int i = 0, d = self; i < ranks; ++i, d = (d + 1 == ranks) ? 0 : d + 1)
-              *reinterpret_cast<uint4*>(outs->base[d] + off) = v;
-          }
-        }
+      if ((col & 127) == 96) {  // the half is complete after its fourth chunk
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&slots()->full[s]);
       }
-      __syncwarp();  // the next half overwrites the staging block
     }
   };
-  __device__ Storer storer(int row, int m_blk, int n_blk) const {
-    return Storer{outs, umma2::epilogue_smem() + (row >> 5) * (32 * 256), row & 31, m_blk * 128 + (row & ~31),
-                  n_blk * umma2::BN, M, N, ranks, self, ldc, col0, enabled};
+  __device__ Storer storer(int row, int, int, int it, uint32_t* status) const {
+    return Storer{row & 31, row >> 5, (uint32_t)it & 1u, status};
   }
-  __device__ void finish() const { __threadfence_system(); }
+
+  // Push warp i drains epilogue warp i's slots: 32 rows x 128 columns per slot, 16 lanes
+  // per 256-byte row segment, into this rank's own C first, then its successors'.
+  __device__ void side(int i, int first, int stride, int tiles, int num_pm, int num_n, uint32_t* status,
+                       uint32_t fail_base) const {
+    const int lane = lane_id(), seg = lane & 15;
+    const int rank = (int)umma2::cluster_rank();
+    uint32_t parity = 0;
+    bool ok = true;
+    for (int t = first; t < tiles && ok; t += stride, parity ^= 1) {
+      int m_blk, n_blk;
+      umma::grouped_tile(t, num_pm, num_n, TB_GEMM2_GROUP, m_blk, n_blk);
+      m_blk = 2 * m_blk + rank;
+      const int row0 = m_blk * 128 + i * 32;
+      for (int half = 0; half < 2; ++half) {
+        const int s = i * 2 + half;
+        if (!__all_sync(0xffffffffu, mbar_wait(&slots()->full[s], parity))) {
+          if (lane == 0) report_status(status, fail_base | 0x0701);
+          ok = false;
+          break;
+        }
+        const uint8_t* stage = slot(s);
+        const int gc = n_blk * umma2::BN + half * 128 + seg * 8;
+        if (enabled) {
+          for (int it = 0; it < 16; ++it) {
+            const int rr = 2 * it + (lane >> 4);
+            const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 256 + ((seg ^ (rr & 15)) << 4));
+            const int gr = row0 + rr;
+            if (gr < M && gc < N) {
+              const long long off = (long long)gr * ldc + col0 + gc;
+              for (int k = 0, d = self; k < ranks; ++k, d = (d + 1 == ranks) ? 0 : d + 1)
+                *reinterpret_cast<uint4*>(outs->base[d] + off) = v;
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&slots()->empty[s]);
+      }
+    }
+    // These threads' peer stores are performed system-wide before the pipeline's final
+    // cluster barrier, hence before the kernel's exit handshake.
+    __threadfence_system();
+  }
 };
 
 struct SplitKPolicy {

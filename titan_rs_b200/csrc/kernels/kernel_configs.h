@@ -24,7 +24,11 @@
 #define TB_SIGNAL_BLOCK_BYTES 128
 #define TB_GEMM_AG_STAGE_BYTES (4 * 32 * 256)
 #define TB_GEMM_AG_SMEM_BYTES (TB_GEMM_SMEM_BYTES + TB_GEMM_AG_STAGE_BYTES)
-#define TB_GEMM2_AG_SMEM_BYTES (TB_GEMM2_SMEM_BYTES + TB_GEMM_AG_STAGE_BYTES)
+// Fused all-gather on CTA pairs: 5 ring stages + 128 B of slot barriers + eight
+// 8 KB staging slots, and four push warps beside the six pipeline warps.
+#define TB_GEMM2_AG_STAGES 5
+#define TB_GEMM2_AG_SMEM_BYTES (TB_GEMM2_AG_STAGES * 2 * 128 * TB_GEMM_BK * 2 + 1024 + TB_GEMM2_BARRIER_BYTES + 128 + 8 * 32 * 256)
+#define TB_GEMM2_AG_THREADS (TB_GEMM_THREADS + 4 * 32)
 
 // Causal SDPA forward (sdpa_bf16.cu): 128-row query tiles, 128-key tiles, head dim 128.
 // Shared memory: Q 32 KB + K ring 2x32 KB + V ring 2x32 KB + P 2x32 KB + barriers.

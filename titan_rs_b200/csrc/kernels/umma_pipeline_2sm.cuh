@@ -54,6 +54,7 @@ static_assert(sizeof(Barriers<8>) <= TB_GEMM2_BARRIER_BYTES, "barrier block over
 static_assert(smem_bytes(STAGES) == TB_GEMM2_SMEM_BYTES, "smem layout");
 static_assert(TB_GEMM2_SMEM_BYTES <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
 static_assert(TB_GEMM2_AG_SMEM_BYTES <= 232448, "fused all-gather staging exceeds the 227 KB limit");
+static_assert(TB_GEMM2_AG_SMEM_BYTES == smem_bytes(TB_GEMM2_AG_STAGES) + 128 + 8 * 32 * 256, "all-gather smem layout");
 
 // Dynamic shared memory past the ring and the barriers (from the 1 KB-aligned base) is
 // free for a policy's epilogue staging; its kernel is launched with the extra bytes.
@@ -158,9 +159,21 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t tmem, uint32_t cols) 
 //        A rows of 128-row block m_blk and B rows [256 n_blk + 128 half, +128), completing
 //        on `bar` (the even CTA's `full`, a shared::cluster address) with the *_pair
 //        tensor loads;
-//   storer(row, m_blk, n_blk) -> W;  W.store(col, acc) stores 32 fp32 accumulator
-//        columns [col, col + 32) of one row.
+//   storer(row, m_blk, n_blk, ordinal, status) -> W;  W.store(col, acc) stores 32 fp32
+//        accumulator columns [col, col + 32) of one row (ordinal = the CTA's tile count
+//        so far, for policies that hand tiles on through their own barriers).
 // Pair tile t covers 128-row blocks 2 pm and 2 pm + 1 (CTA rank 0 and 1).
+// A policy may add kSideWarps warps after the six pipeline warps (the block has
+// 192 + 32 kSideWarps threads): they run side(i, first_tile, tile_stride, tiles, num_pm,
+// num_n, status, fail_base) beside the pipeline, after init() has set up any barriers
+// they share with the epilogue. PolicyBase supplies the empty defaults.
+struct PolicyBase {
+  static constexpr int kSideWarps = 0;
+  __device__ void init() const {}
+  __device__ void side(int, int, int, int, int, int, uint32_t*, uint32_t) const {}
+  __device__ void finish() const {}
+};
+
 template <class Policy, int Stages = STAGES, int Group = TB_GEMM2_GROUP>
 __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t fail_base) {
   static_assert(smem_bytes(Stages) <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
@@ -186,6 +199,7 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
       mbar_init(&bars->acc_empty[a], 8);  // 4 epilogue warps in each CTA
     }
     mbar_init(&bars->drain, 1);
+    p.init();              // the policy's own barriers (side warps), if any
     fence_barrier_init();  // .release.cluster: visible to the peer CTA
   }
   cluster_sync();  // both CTAs' barriers exist before anything arrives remotely
@@ -281,6 +295,9 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
       umma_commit_pair_local(&bars->drain);
       if (!mbar_wait(&bars->drain, 0)) report_status(status, fail_base | 0x0203);
     }
+  } else if (warp >= 6) {
+    // ---------------- side warps (warps 6.., policies with kSideWarps > 0) ----------------
+    p.side(warp - 6, pair, pairs, tiles, num_pm, num_n, status, fail_base);
   } else {
     // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
     const int quarter = warp & 3;
@@ -288,7 +305,8 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
                                         map_to_rank(smem_addr(&bars->acc_empty[1]), 0)};
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = pair; t < tiles; t += pairs) {
+    int ordinal = 0;  // this CTA's tile count so far
+    for (int t = pair; t < tiles; t += pairs, ++ordinal) {
       int m_blk, n_blk;
       umma::grouped_tile(t, num_pm, num_n, Group, m_blk, n_blk);
       m_blk = 2 * m_blk + (int)rank;
@@ -299,7 +317,7 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
       }
       tc_fence_after_sync();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
-      const auto st = p.storer(quarter * 32 + lane, m_blk, n_blk);
+      const auto st = p.storer(quarter * 32 + lane, m_blk, n_blk, ordinal, status);
 #pragma unroll 1
       for (int col = 0; col < BN; col += 32) {
         uint32_t r[32];
