@@ -69,3 +69,42 @@ def test_validation_and_binding_errors():
     with pytest.raises(ExecutionError) as e:
         plan.execute(runtime=None, bindings={0: object()})
     assert e.value.phase == "bind" and "missing binding for input value 1" in e.value.message
+
+
+def attention_graph(tq=64, tk=96, d=128, dtype=DType.BF16, axis=1, p_is_output=False, s_users=1, v_shape=None,
+                    transpose_rhs=True):
+    # Q[tq,d] K[tk,d] V[tk,d] -> S = gemm(Q, K^T) -> P = softmax(S) -> O = gemm(P, V)
+    values = {0: spec(dtype, tq, d), 1: spec(dtype, tk, d), 2: spec(dtype, *(v_shape or (tk, d))),
+              3: spec(dtype, tq, tk), 4: spec(dtype, tq, tk), 5: spec(dtype, tq, d)}
+    attrs = {"axis": axis} if axis is not None else {}
+    nodes = [G.GraphNode(10, "gemm", [0, 1], [3], {"transpose_rhs": transpose_rhs}),
+             G.GraphNode(11, "softmax", [3], [4], attrs),
+             G.GraphNode(12, "gemm", [4, 2], [5])]
+    outputs = [5] + ([4] if p_is_output else [])
+    if s_users == 2:
+        values[6] = spec(dtype, tq, tk)
+        nodes.append(G.GraphNode(13, "softmax", [3], [6], {"axis": 1}))
+        outputs.append(6)
+    return G.Graph([0, 1, 2], outputs, values, nodes)
+
+
+def test_attention_fusion_replaces_the_chain():
+    plan = G.compile(attention_graph())
+    assert [(n.operator, n.inputs, n.outputs, n.attrs) for n in plan.graph.nodes] == \
+        [("attention.fused", [0, 1, 2], [5], {"scale": 1.0})]
+    assert 3 not in plan.graph.values and 4 not in plan.graph.values
+    rep = [r for r in plan.reports if r.name == "fusion.attention"][0]
+    assert rep.changed and "attention.fused [64x96, D=128]" in rep.notes[0]
+    # The default axis (none given) is the last one too.
+    assert G.compile(attention_graph(axis=None)).graph.nodes[0].operator == "attention.fused"
+
+
+def test_attention_fusion_leaves_other_chains_alone():
+    def ops(g):
+        return [n.operator for n in G.compile(g).graph.nodes]
+    unfused = ["gemm", "softmax", "gemm"]
+    assert ops(attention_graph(dtype=DType.F32)) == unfused          # f32 keeps the reference kernels
+    assert ops(attention_graph(axis=0)) == unfused                   # softmax over the query axis
+    assert ops(attention_graph(p_is_output=True)) == unfused         # P is visible
+    assert ops(attention_graph(s_users=2)) == ["gemm", "softmax", "gemm", "softmax"]  # S has another reader
+    assert ops(attention_graph(transpose_rhs=False, tk=128)) == unfused  # K not stored [Tk, D]

@@ -1,7 +1,8 @@
-"""A bf16 graph through the compiled plan on the B200: a two-layer MLP
+"""bf16 graphs through the compiled plan on the B200: a two-layer MLP
 (gemm -> broadcast.add -> gelu -> gemm -> broadcast.add) compiles to two
 gemm.bias_act nodes, runs without host waits between nodes, and matches the oracle
-(the reference's gemm, bias add and gelu in f32, with the bf16 hidden layer)."""
+(the reference's gemm, bias add and gelu in f32, with the bf16 hidden layer); an
+attention chain (gemm -> softmax -> gemm) compiles to one flash-attention launch."""
 import math
 
 import numpy as np
@@ -53,4 +54,37 @@ def test_bf16_mlp_graph_fuses_and_matches_oracle():
     ref = oracle.gemm_bf16_points(hid_bits, w2, True, m, d_out, d_hid, rows, cols).reshape(m, d_out) + b2
     assert np.isfinite(got).all()
     assert max_rel_err(got, ref) <= 1e-2, max_rel_err(got, ref)
+    s.close()
+
+
+def test_attention_chain_fuses_into_one_flash_attention_launch():
+    s = tb.Session(0)
+    rt = tb.Runtime(s)
+    tq, tk, d = 256, 384, 128
+    std = d ** -0.25  # scores of unit variance, as with pre-scaled queries
+    q = tb.fill_normal(tq * d, seed=311, std=std, dtype=DType.BF16).reshape(tq, d)
+    k = tb.fill_normal(tk * d, seed=312, std=std, dtype=DType.BF16).reshape(tk, d)
+    v = tb.fill_normal(tk * d, seed=313, dtype=DType.BF16).reshape(tk, d)
+    values = {0: TensorSpec(DType.BF16, (tq, d)), 1: TensorSpec(DType.BF16, (tk, d)),
+              2: TensorSpec(DType.BF16, (tk, d)), 3: TensorSpec(DType.BF16, (tq, tk)),
+              4: TensorSpec(DType.BF16, (tq, tk)), 5: TensorSpec(DType.BF16, (tq, d))}
+    nodes = [G.GraphNode(10, "gemm", [0, 1], [3], {"transpose_rhs": True}),
+             G.GraphNode(11, "softmax", [3], [4], {"axis": 1}),
+             G.GraphNode(12, "gemm", [4, 2], [5])]
+    graph = G.Graph([0, 1, 2], [5], values, nodes)
+    plan = G.compile(graph)
+    assert [n.operator for n in plan.graph.nodes] == ["attention.fused"]
+    binds = {i: tb.TensorHandle.from_numpy(s, a, DType.BF16, rt.stream) for i, a in enumerate((q, k, v))}
+    before = tb.launch_count()
+    fused = plan.execute(rt, binds).wait().outputs[0]
+    assert tb.launch_count() - before == 1 and tb.last_candidate() == "sdpa_fwd_bf16_d128_pair"
+    assert fused.shape == (tq, d)
+    # The same graph unfused: three kernels, S and P rounded to bf16 in memory.
+    before = tb.launch_count()
+    unfused = G.ExecutionPlan(graph, []).execute(rt, binds).wait().outputs[0]
+    assert tb.launch_count() - before == 3
+    ref = oracle.sdpa_bf16_rows(q.reshape(1, 1, tq, d), k.reshape(1, 1, tk, d), v.reshape(1, 1, tk, d), 1, 1, tq, tk,
+                                d, False, np.arange(tq), scale=1.0)
+    assert max_rel_err(fused.to_f32(), ref) <= 1e-2
+    assert max_rel_err(unfused.to_f32(), ref) <= 3e-2
     s.close()

@@ -163,3 +163,28 @@ def test_sdpa_contract_rejections(session, rt):
     assert "output shape" in err([q, k, v], (1, 1, 3, 2))
     assert "F32" in err([q, k, v], (1, 1, 2, 2), dtype=DType.I32)
     assert "contiguous" in err([q, k, v], (1, 1, 2, 2), layout="Strided")
+
+
+@pytest.mark.parametrize("candidate,d", [("sdpa_fwd_bf16_d128_pair", 128), ("sdpa_fwd_bf16_d128_bn64", 128),
+                                         ("sdpa_fwd_bf16_d128", 128), ("sdpa_bf16_generic", 64)])
+@pytest.mark.parametrize("scale", [1.0, 0.03])
+def test_sdpa_bf16_scale_attribute(session, rt, candidate, d, scale):
+    """`scale` (an extension; the reference fixes 1/sqrt(D)) multiplies Q K^T in every bf16 kernel."""
+    b, h, tq, tk = 1, 2, 256, 384
+    q, k, v = qkv_bf16(b, h, tq, tk, d, seed=41)
+    q = (tb.bf16_bits_to_f32(q) * 0.25).reshape(q.shape)  # keeps exp() of unscaled scores in range
+    q = (q.astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    ins = [upload(session, rt.stream, t, DType.BF16) for t in (q, k, v)]
+    res = run_op(rt, "scaled_dot_product_attention", ins, DType.BF16, q.shape,
+                 {"causal": True, "scale": scale, "candidate": candidate})
+    assert res.candidate == candidate
+    ref = oracle.sdpa_bf16_rows(q, k, v, b, h, tq, tk, d, True, np.arange(b * h * tq), scale=scale)
+    assert max_rel_err(res.outputs[0].to_f32(), ref.reshape(b, h, tq, d)) <= BF16_TOL
+
+
+def test_sdpa_bf16_scale_attribute_contract(session, rt):
+    q, k, v = qkv_bf16(1, 1, 128, 128, 128, seed=42)
+    ins = [upload(session, rt.stream, t, DType.BF16) for t in (q, k, v)]
+    for bad in ("0", "-1", "nan", "inf", "abc", "1.0x", 0.0):
+        with pytest.raises(tb.ExecutionError, match="scale must be a positive finite number"):
+            run_op(rt, "scaled_dot_product_attention", ins, DType.BF16, q.shape, {"scale": bad})

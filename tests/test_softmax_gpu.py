@@ -133,3 +133,30 @@ def test_reference_abi_launch_through_hal(session):
     y = np.empty_like(x)
     session.download(stream, bout, y)
     assert elementwise_rel_err(y, oracle.softmax(x)) <= REL_TOL
+
+
+@pytest.mark.parametrize("shape", [(3, 5), (7, 127), (4, 1000), (3, 4096), (2, 4097), (2, 3, 64), (1000, 12),
+                                   (64, 384)])
+def test_softmax_bf16_rows_matches_oracle(session, rt, shape):
+    """BF16 in and out (an extension for bf16 graphs): fp32 arithmetic, one rounding, so each
+    element is within one bf16 ulp (2^-8 relative) of the f32 oracle on the same inputs."""
+    n = int(np.prod(shape))
+    x = tb.fill_normal(n, seed=sum(shape) + 7, std=2.0, dtype=DType.BF16).reshape(shape)
+    h = run_op(rt, "softmax", [upload(session, rt.stream, x, DType.BF16)], DType.BF16, shape)
+    assert h.candidate == "softmax_bf16_rows"
+    y = h.outputs[0].to_f32()
+    ref = oracle.softmax(tb.bf16_bits_to_f32(x).reshape(shape), axis=-1)
+    assert np.all(np.abs(y - ref) <= 2.0 ** -8 * np.abs(ref) + 1e-38)
+    assert np.all(np.abs(y.reshape(-1, shape[-1]).sum(axis=-1, dtype=np.float64) - 1.0) <= 1e-2)
+
+
+def test_softmax_bf16_negative_infinity(session, rt):
+    """-inf scores (masked positions) come out as exact zeros; the rest still sums to 1."""
+    x = np.full((2, 16), 0.5, np.float32)
+    x[0, :5] = -np.inf
+    x[1, 7] = -np.inf
+    bits = (x.view(np.uint32) >> 16).astype(np.uint16)  # exact in bf16
+    y = run_op(rt, "softmax", [upload(session, rt.stream, bits, DType.BF16)], DType.BF16, x.shape).outputs[0].to_f32()
+    assert np.all(y[0, :5] == 0.0) and y[1, 7] == 0.0
+    np.testing.assert_allclose(y[0, 5:], 1.0 / 11, rtol=2.0 ** -8)
+    np.testing.assert_allclose(y[1, np.arange(16) != 7], 1.0 / 15, rtol=2.0 ** -8)

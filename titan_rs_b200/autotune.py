@@ -50,6 +50,7 @@ CANDIDATES = {
                           "softmax_f32_warp16", "softmax_f32_warp32", "softmax_f32_stream"], []),
     ("scaled_dot_product_attention", "BF16"): (["sdpa_fwd_bf16_d128_pair", "sdpa_fwd_bf16_d128_bn64",
                                                  "sdpa_fwd_bf16_d128"], ["sdpa_bf16_generic"]),
+    ("softmax", "BF16"): (["softmax_bf16_rows"], []),
     ("conv2d", "BF16"): (["conv2d_fprop_bf16_nhwc_2sm", "conv2d_fprop_bf16_nhwc"], ["conv2d_bf16_nhwc_generic"]),
     ("conv2d", "F32"): (["conv2d_f32"], []),
     ("gemm.bias_act", "BF16"): (["gemm_bf16_tn_bias_act_2sm", "gemm_bf16_tn_bias_act"], []),

@@ -9,7 +9,11 @@
 //   BF16, other head dims            -> sdpa_bf16_generic (CUDA cores)
 //   F32                              -> scaled_dot_product_attention_f32 (reference ABI kernel);
 //                                       mask/causal rejected as the reference does
+// BF16 also takes `scale` (a decimal string, > 0): the factor applied to Q K^T in place
+// of the reference's fixed 1/sqrt(D). The graph compiler's attention fusion uses it for
+// gemm -> softmax -> gemm chains, which carry no scale.
 #include <cmath>
+#include <cstdlib>
 
 #include "../kernels/kernel_configs.h"
 #include "ops_common.hpp"
@@ -30,7 +34,7 @@ tb_status tmap_bhtd(CUtensorMap* map, CUdeviceptr base, uint64_t bh, uint64_t t,
 }
 
 tb_status launch_sdpa_bf16_d128(Session* s, Stream* st, CUdeviceptr q, CUdeviceptr k, CUdeviceptr v, CUdeviceptr o,
-                                int bh, int tq, int tk, int causal) {
+                                int bh, int tq, int tk, int causal, float scale) {
   CUtensorMap mq, mk, mv;
   tb_status rc;
   if ((rc = tmap_bhtd(&mq, q, bh, tq, TB_SDPA_HD)) || (rc = tmap_bhtd(&mk, k, bh, tk, TB_SDPA_HD)) ||
@@ -39,7 +43,7 @@ tb_status launch_sdpa_bf16_d128(Session* s, Stream* st, CUdeviceptr q, CUdevicep
   CUfunction fn = nullptr;
   rc = builtin_function(s, "sdpa_bf16", "sdpa_fwd_bf16_d128", &fn);
   if (rc) return rc;
-  float scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)TB_SDPA_HD));
+  float scale_log2 = (float)(1.4426950408889634 * (double)scale);  // the kernels exponentiate base 2
   CUdeviceptr status = s->status.device;
   void* params[] = {&mq, &mk, &mv, &o, &tq, &tk, &causal, &scale_log2, &status};
   const unsigned long long qtiles = (unsigned long long)((tq + TB_SDPA_BM - 1) / TB_SDPA_BM);
@@ -49,7 +53,7 @@ tb_status launch_sdpa_bf16_d128(Session* s, Stream* st, CUdeviceptr q, CUdevicep
 }
 
 tb_status launch_sdpa_bf16_d128_pair(Session* s, Stream* st, CUdeviceptr q, CUdeviceptr k, CUdeviceptr v,
-                                     CUdeviceptr o, int bh, int tq, int tk, int causal) {
+                                     CUdeviceptr o, int bh, int tq, int tk, int causal, float scale) {
   CUtensorMap mq, mk, mv;
   tb_status rc;
   if ((rc = tmap_bhtd(&mq, q, bh, tq, TB_SDPA_HD)) || (rc = tmap_bhtd(&mk, k, bh, tk, TB_SDPA_HD)) ||
@@ -58,7 +62,7 @@ tb_status launch_sdpa_bf16_d128_pair(Session* s, Stream* st, CUdeviceptr q, CUde
   CUfunction fn = nullptr;
   rc = builtin_function(s, "sdpa_bf16_pair", "sdpa_fwd_bf16_d128_pair", &fn);
   if (rc) return rc;
-  float scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)TB_SDPA_HD));
+  float scale_log2 = (float)(1.4426950408889634 * (double)scale);  // the kernels exponentiate base 2
   CUdeviceptr status = s->status.device;
   void* params[] = {&mq, &mk, &mv, &o, &tq, &tk, &causal, &scale_log2, &status};
   const unsigned long long pairs = (unsigned long long)((tq + 2 * TB_SDPA_BM - 1) / (2 * TB_SDPA_BM));
@@ -68,7 +72,7 @@ tb_status launch_sdpa_bf16_d128_pair(Session* s, Stream* st, CUdeviceptr q, CUde
 }
 
 tb_status launch_sdpa_bf16_d128_bn64(Session* s, Stream* st, CUdeviceptr q, CUdeviceptr k, CUdeviceptr v,
-                                     CUdeviceptr o, int bh, int tq, int tk, int causal) {
+                                     CUdeviceptr o, int bh, int tq, int tk, int causal, float scale) {
   CUtensorMap mq, mk, mv;
   tb_status rc;
   if ((rc = tmap_bhtd(&mq, q, bh, tq, TB_SDPA_HD, 128)) || (rc = tmap_bhtd(&mk, k, bh, tk, TB_SDPA_HD, TB_SDPA3_BN)) ||
@@ -77,7 +81,7 @@ tb_status launch_sdpa_bf16_d128_bn64(Session* s, Stream* st, CUdeviceptr q, CUde
   CUfunction fn = nullptr;
   rc = builtin_function(s, "sdpa_bf16_bn64", "sdpa_fwd_bf16_d128_bn64", &fn);
   if (rc) return rc;
-  float scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)TB_SDPA_HD));
+  float scale_log2 = (float)(1.4426950408889634 * (double)scale);  // the kernels exponentiate base 2
   CUdeviceptr status = s->status.device;
   void* params[] = {&mq, &mk, &mv, &o, &tq, &tk, &causal, &scale_log2, &status};
   const unsigned long long qtiles = (unsigned long long)((tq + TB_SDPA_BM - 1) / TB_SDPA_BM);
@@ -100,6 +104,7 @@ extern "C" tb_status tb_op_sdpa(tb_session* session, tb_stream* stream, const tb
   const uint32_t dt = q->dtype;
   bool causal = false;
   const char* candidate = nullptr;  // optional: name of a registered kernel to run (autotuning / tests)
+  double scale = 0.0;               // optional score scale (a decimal string); 0 = the reference's 1/sqrt(D)
   if (dt == TB_F32) {
     if (num_attrs)
       return unsupported("CUDA scaled dot-product attention does not implement mask, causal, or other attributes");
@@ -114,7 +119,15 @@ extern "C" tb_status tb_op_sdpa(tb_session* session, tb_stream* stream, const tb
         candidate = attrs[i].str;
         continue;
       }
-      return unsupported("CUDA scaled dot-product attention does not implement mask or attributes other than causal");
+      if (attrs[i].key && strcmp(attrs[i].key, "scale") == 0) {
+        char* end = nullptr;
+        scale = attrs[i].str ? strtod(attrs[i].str, &end) : 0.0;
+        if (!attrs[i].str || end == attrs[i].str || *end != '\0' || !std::isfinite(scale) || !(scale > 0.0))
+          return contract("scaled dot-product attention scale must be a positive finite number (decimal string)");
+        continue;
+      }
+      return unsupported(
+          "CUDA scaled dot-product attention does not implement mask or attributes other than causal and scale");
     }
   }
   if (!(dt == TB_F32 || dt == TB_BF16) || k->dtype != dt || v->dtype != dt || output->dtype != dt)
@@ -149,6 +162,7 @@ extern "C" tb_status tb_op_sdpa(tb_session* session, tb_stream* stream, const tb
   if (rc) return rc;
   CUdeviceptr pq = bq->ptr, pk = bk->ptr, pv = bv->ptr, po = bo->ptr;
   int b = (int)B, h = (int)H, tq = (int)Tq, tk = (int)Tk, d = (int)D, c = causal ? 1 : 0;
+  float sc = (float)(scale > 0.0 ? scale : 1.0 / std::sqrt((double)D));
   const bool tc_ok = dt == TB_BF16 && D == TB_SDPA_HD && ((pq | pk | pv | po) & 15) == 0;
   if (candidate && strcmp(candidate, "sdpa_fwd_bf16_d128_pair") != 0 && strcmp(candidate, "sdpa_fwd_bf16_d128") != 0 &&
       strcmp(candidate, "sdpa_fwd_bf16_d128_bn64") != 0 && strcmp(candidate, "sdpa_bf16_generic") != 0)
@@ -156,11 +170,11 @@ extern "C" tb_status tb_op_sdpa(tb_session* session, tb_stream* stream, const tb
   if (candidate && !tc_ok && strcmp(candidate, "sdpa_bf16_generic") != 0)
     return unsupported(std::string("candidate ") + candidate + " does not take this shape or alignment");
   if (tc_ok && (!candidate || strcmp(candidate, "sdpa_fwd_bf16_d128_pair") == 0)) {
-    rc = launch_sdpa_bf16_d128_pair(s, st, pq, pk, pv, po, b * h, tq, tk, c);
+    rc = launch_sdpa_bf16_d128_pair(s, st, pq, pk, pv, po, b * h, tq, tk, c, sc);
   } else if (tc_ok && strcmp(candidate, "sdpa_fwd_bf16_d128_bn64") == 0) {
-    rc = launch_sdpa_bf16_d128_bn64(s, st, pq, pk, pv, po, b * h, tq, tk, c);
+    rc = launch_sdpa_bf16_d128_bn64(s, st, pq, pk, pv, po, b * h, tq, tk, c, sc);
   } else if (tc_ok && strcmp(candidate, "sdpa_fwd_bf16_d128") == 0) {
-    rc = launch_sdpa_bf16_d128(s, st, pq, pk, pv, po, b * h, tq, tk, c);
+    rc = launch_sdpa_bf16_d128(s, st, pq, pk, pv, po, b * h, tq, tk, c, sc);
   } else {
     const bool bf = dt == TB_BF16;
     CUfunction fn = nullptr;
@@ -170,7 +184,7 @@ extern "C" tb_status tb_op_sdpa(tb_session* session, tb_stream* stream, const tb
     uint64_t grid = (rows + 7) / 8;
     if (grid > (uint64_t)s->sm_count * 64) grid = (uint64_t)s->sm_count * 64;
     if (bf) {
-      void* params[] = {&pq, &pk, &pv, &po, &b, &h, &tq, &tk, &d, &c};
+      void* params[] = {&pq, &pk, &pv, &po, &b, &h, &tq, &tk, &d, &c, &sc};
       rc = launch_builtin(s, st, fn, (unsigned)grid, 1, 1, 256, 0, params, "sdpa_bf16_generic");
     } else {
       void* params[] = {&pq, &pk, &pv, &po, &b, &h, &tq, &tk, &d};

@@ -2,7 +2,8 @@
 // (titan-runtime/src/lib.rs:1504-1596), then the B200 kernel choice. Besides the
 // reference's `axis`, the operator takes `candidate` (a registered kernel name:
 // softmax_f32_warp{1,2,4,8,16,32} for rows of at most that many x 128 columns, or
-// softmax_f32_stream), which the autotuner uses.
+// softmax_f32_stream), which the autotuner uses. BF16 input and output (an extension
+// for bf16 graphs) take softmax_bf16_rows: fp32 arithmetic, one rounding.
 #include "ops_common.hpp"
 
 using namespace tb;
@@ -22,8 +23,9 @@ extern "C" tb_status tb_op_softmax(tb_session* session, tb_stream* stream, const
     if (!attrs[i].key || strcmp(attrs[i].key, "axis") != 0)
       return contract("CUDA softmax only accepts the axis attribute");
   }
-  if (input->dtype != TB_F32 || output->dtype != TB_F32)
-    return contract("CUDA softmax requires F32 input and output");
+  const bool bf16 = input->dtype == TB_BF16 && output->dtype == TB_BF16;
+  if (!bf16 && (input->dtype != TB_F32 || output->dtype != TB_F32))
+    return contract("CUDA softmax requires F32 input and output (or BF16 input and output)");
   if (input->rank == 0 || input->rank > TB_MAX_RANK) return contract("CUDA softmax requires a non-scalar input");
   if (!is_contiguous(input)) return contract("CUDA softmax requires a contiguous input");
   int64_t last = (int64_t)input->rank - 1, axis = 0;
@@ -54,6 +56,18 @@ extern "C" tb_status tb_op_softmax(tb_session* session, tb_stream* stream, const
   int r = (int)rows, c = (int)cols;
   CUdeviceptr pin = bin->ptr, pout = bout->ptr;
   void* params[] = {&pin, &pout, &r, &c};
+  if (bf16) {
+    if (candidate && strcmp(candidate, "softmax_bf16_rows") != 0)
+      return contract(std::string("unknown BF16 softmax candidate ") + candidate);
+    CUfunction fn = nullptr;
+    rc = builtin_function(s, "softmax", "softmax_bf16_rows", &fn);
+    if (rc) return rc;
+    uint64_t grid = (rows + 7) / 8;  // 8 rows (warps) per 256-thread CTA
+    if (grid > (uint64_t)s->sm_count * 32) grid = (uint64_t)s->sm_count * 32;
+    rc = launch_builtin(s, st, fn, (unsigned)grid, 1, 1, 256, 0, params, "softmax_bf16_rows");
+    if (rc) return rc;
+    return record_event(s, st, nullptr, out);
+  }
   const bool aligned = ((pin | pout) & 15u) == 0;
   const bool reg_ok = aligned && cols % 4 == 0 && cols <= 4096;
   // Register-path variants: one warp per row, up to `nv` x 128 columns.

@@ -221,14 +221,14 @@ extern "C" __global__ void conv2d_bf16_nhwc_generic(const __nv_bfloat16* __restr
 
 // bf16 attention for shapes the tensor-core kernel does not take (D != 128,
 // unaligned buffers): one warp per query row, online softmax in fp32, D <= 256.
-// causal != 0 masks keys j > i (top-left aligned).
+// causal != 0 masks keys j > i (top-left aligned). Scores are multiplied by `scale`
+// (1/sqrt(D) unless the operator's scale attribute says otherwise).
 extern "C" __global__ void sdpa_bf16_generic(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
                                              const __nv_bfloat16* __restrict__ v, __nv_bfloat16* __restrict__ o,
-                                             int B, int H, int Tq, int Tk, int D, int causal) {
+                                             int B, int H, int Tq, int Tk, int D, int causal, float scale) {
   const int lane = threadIdx.x & 31;
   const long long rows = (long long)B * H * Tq;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  const float scale = 1.0f / sqrtf((float)D);
   for (long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += warps) {
     const long long bh = row / Tq;
     const int i = (int)(row % Tq);

@@ -14,10 +14,13 @@
 //     element, the algorithmic minimum.
 //   * streaming path (any other shape): one CTA per row, online max/sum in a
 //     first read, normalised write in a second read.
+//   * bf16 rows (softmax_bf16_rows, an extension for bf16 graphs): one warp per
+//     row, fp32 arithmetic with expf, one bf16 rounding per output.
 //
 // exp(x - m) is evaluated as 2^((x - m) * log2 e) with the hardware ex2
 // instruction; (x - m) is formed first, as the reference does, so the argument
 // error stays relative to |x - m| and the result is within a few ulp of expf.
+#include <cuda_bf16.h>
 #include <math.h>
 #include <stdint.h>
 
@@ -195,5 +198,96 @@ extern "C" __global__ void softmax_f32(const float* __restrict__ in, float* __re
     else warp_rows<32>(in, out, rows, cols);
   } else {
     cta_rows(in, out, rows, cols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// bf16 rows (an extension: the reference's softmax is f32 only). One warp per row,
+// fp32 arithmetic, the row read twice: pass 1 keeps a running (max, sum of
+// exp(x - max)) per lane and merges the lanes; pass 2 writes exp(x - max) / sum,
+// rounded to bf16 once. -inf inputs contribute zero; a row of only -inf gives NaN,
+// as exp(x - max) / sum does in the reference. VEC = 8 reads 16-byte vectors (row
+// starts 16-byte aligned, cols % 8 == 0), VEC = 1 single elements.
+namespace {
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__device__ __forceinline__ void softmax_merge(float& m, float& s, float m2, float s2) {
+  const float mn = fmaxf(m, m2);
+  const float a = m == -INFINITY ? 0.0f : s * expf(m - mn);
+  const float b = m2 == -INFINITY ? 0.0f : s2 * expf(m2 - mn);
+  m = mn;
+  s = a + b;
+}
+
+template <int VEC>
+__device__ __forceinline__ void load_bf16(const __nv_bfloat16* p, float (&v)[VEC]) {
+  if constexpr (VEC == 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = __uint_as_float(w[j] << 16);
+      v[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+    }
+  } else {
+    v[0] = __bfloat162float(*p);
+  }
+}
+
+template <int VEC>
+__device__ void softmax_bf16_row(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int cols,
+                                 int lane) {
+  float m = -INFINITY, s = 0.0f;
+  for (int c = lane * VEC; c < cols; c += 32 * VEC) {
+    float v[VEC];
+    load_bf16<VEC>(x + c, v);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const float t = v[j];
+      if (t == -INFINITY) continue;
+      if (t > m) {
+        s = s * expf(m - t) + 1.0f;
+        m = t;
+      } else {
+        s += expf(t - m);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+    softmax_merge(m, s, __shfl_xor_sync(0xffffffffu, m, off), __shfl_xor_sync(0xffffffffu, s, off));
+  for (int c = lane * VEC; c < cols; c += 32 * VEC) {
+    float v[VEC];
+    load_bf16<VEC>(x + c, v);
+    if constexpr (VEC == 8) {
+      uint4 u;
+      u.x = pack_bf16(expf(v[0] - m) / s, expf(v[1] - m) / s);
+      u.y = pack_bf16(expf(v[2] - m) / s, expf(v[3] - m) / s);
+      u.z = pack_bf16(expf(v[4] - m) / s, expf(v[5] - m) / s);
+      u.w = pack_bf16(expf(v[6] - m) / s, expf(v[7] - m) / s);
+      *reinterpret_cast<uint4*>(y + c) = u;
+    } else {
+      y[c] = __float2bfloat16_rn(expf(v[0] - m) / s);
+    }
+  }
+}
+
+}  // namespace
+
+// rows x cols bf16, contiguous; grid-stride over rows, one warp per row.
+extern "C" __global__ void __launch_bounds__(256) softmax_bf16_rows(const __nv_bfloat16* __restrict__ in,
+                                                                   __nv_bfloat16* __restrict__ out, int rows,
+                                                                   int cols) {
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  const bool vec = cols % 8 == 0 && ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const long long base = (long long)r * cols;
+    if (vec) softmax_bf16_row<8>(in + base, out + base, cols, lane);
+    else softmax_bf16_row<1>(in + base, out + base, cols, lane);
   }
 }

@@ -38,6 +38,11 @@ def last_candidate() -> str:
     return (N.lib().tb_last_candidate() or b"").decode()
 
 
+def launch_count() -> int:
+    """Kernels this library has launched in the process so far (tb_launch_count)."""
+    return int(N.lib().tb_launch_count())
+
+
 def driver_available() -> bool:
     """True when libcuda loads and reports devices (the reference's no_cuda_environment inverse)."""
     try:

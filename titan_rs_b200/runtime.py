@@ -159,8 +159,9 @@ def _attrs(attrs: dict):
         kb = k.encode()
         keep.append(kb)
         arr[i].key = kb
-        if isinstance(v, str):
-            sb = v.encode()
+        if isinstance(v, (str, float)):
+            # Floats cross the C ABI as their shortest round-tripping decimal string.
+            sb = (v if isinstance(v, str) else repr(float(v))).encode()
             keep.append(sb)
             arr[i].str = sb
             arr[i].value = 0
