@@ -26,6 +26,19 @@ using namespace tb;
 constexpr uint32_t kFailConv = 0x43000000u;
 constexpr uint32_t kFailConv2 = 0x43320000u;
 
+// Output-pixel cursor shared by both forms: the pixel of row `row` of M block m_blk at
+// the tile's first channel, or null outside the output.
+struct ConvStorer {
+  __nv_bfloat16* dst;
+  const float* bias;
+  int cols;  // valid channels from the tile's first channel
+  bool vec_ok;
+  __device__ void store(int col, const uint32_t (&acc)[32]) const {
+    if (!dst || col >= cols) return;
+    umma::store_bf16_chunk(dst + col, cols - col, vec_ok, acc, bias ? bias + col : nullptr);
+  }
+};
+
 // Problem geometry shared by the 1-SM and 2-SM policies. A 128-row M block m_blk is
 // 2 images x 8 output rows x 8 output columns.
 struct ConvGeometry {
@@ -50,25 +63,42 @@ struct ConvGeometry {
     ho0 = hi * 8;
     wo0 = wi * 8;
   }
-  // Input-box coordinates {c, w, h, n} of k-block kb = (r, s, channel block) for M block m_blk.
-  __device__ void a_coords(int m_blk, int kb, int& x, int& w, int& h, int& n, int& rs) const {
-    rs = kb / c_blocks;
-    const int cb = kb - rs * c_blocks;
-    const int r = rs / S, s = rs - r * S;
-    int ho0, wo0;
-    pixel_tile(m_blk, n, ho0, wo0);
-    x = cb * 64;
-    w = wo0 * sw - pw + s * dw;
-    h = ho0 * sh - ph + r * dh;
-  }
-  // Row `row` of M block m_blk is output pixel (n, ho, wo); 32 channels from co.
-  __device__ void store_row(int row, int m_blk, int co, const uint32_t (&acc)[32]) const {
+  // Row `row` of M block m_blk is output pixel (n, ho, wo); channels from co.
+  __device__ ConvStorer conv_storer(int row, int m_blk, int co) const {
     int n0, ho0, wo0;
     pixel_tile(m_blk, n0, ho0, wo0);
     const int n = n0 + (row >> 6), ho = ho0 + ((row >> 3) & 7), wo = wo0 + (row & 7);
-    if (n >= batch || ho >= Ho || wo >= Wo || co >= Cout) return;
-    __nv_bfloat16* dst = y + (((long long)n * Ho + ho) * Wo + wo) * Cout + co;
-    umma::store_bf16_chunk(dst, Cout - co, vec_ok, acc, bias ? bias + co : nullptr);
+    const bool in = n < batch && ho < Ho && wo < Wo;
+    return ConvStorer{in ? y + (((long long)n * Ho + ho) * Wo + wo) * Cout + co : nullptr, bias ? bias + co : nullptr,
+                      Cout - co, vec_ok};
+  }
+};
+
+// Walks k-blocks in the order kb = (r * S + s) * c_blocks + cb with counters; Pair
+// selects the 2-SM tensor loads (completion on the even CTA's barrier).
+template <bool Pair>
+struct ConvLoader {
+  const CUtensorMap *tx, *tw;
+  int w0, h0, n0, co;  // input box origin for tap (0, 0); first output channel
+  int r, s, cb, rs;    // current tap and channel block
+  int S, c_blocks, dh, dw;
+  template <class Bar>
+  __device__ void load(uint8_t* a_dst, uint8_t* b_dst, Bar bar) {
+    if constexpr (Pair) {
+      umma2::tma_load_4d_pair(a_dst, tx, bar, cb * 64, w0 + s * dw, h0 + r * dh, n0);
+      umma2::tma_load_3d_pair(b_dst, tw, bar, cb * 64, rs, co);
+    } else {
+      tma_load_4d(a_dst, tx, bar, cb * 64, w0 + s * dw, h0 + r * dh, n0);
+      tma_load_3d(b_dst, tw, bar, cb * 64, rs, co);
+    }
+    if (++cb == c_blocks) {
+      cb = 0;
+      ++rs;
+      if (++s == S) {
+        s = 0;
+        ++r;
+      }
+    }
   }
 };
 
@@ -81,14 +111,14 @@ struct ConvPolicy : ConvGeometry {
   __device__ void tile(int t, int& m_blk, int& n_blk) const {
     umma::grouped_tile(t, num_m(), num_n, 16, m_blk, n_blk);
   }
-  __device__ void load(uint8_t* a_dst, uint8_t* b_dst, uint64_t* bar, int m_blk, int n_blk, int kb) const {
-    int x, w, h, n, rs;
-    a_coords(m_blk, kb, x, w, h, n, rs);
-    tma_load_4d(a_dst, tx, bar, x, w, h, n);
-    tma_load_3d(b_dst, tw, bar, x, rs, n_blk * umma::BN);
+  __device__ ConvLoader<false> loader(int, int m_blk, int n_blk, int) const {
+    int n0, ho0, wo0;
+    pixel_tile(m_blk, n0, ho0, wo0);
+    return ConvLoader<false>{tx, tw, wo0 * sw - pw, ho0 * sh - ph, n0, n_blk * umma::BN, 0, 0, 0, 0,
+                             S, c_blocks, dh, dw};
   }
-  __device__ void store(int row, int, int m_blk, int n_blk, int col, const uint32_t (&acc)[32]) const {
-    store_row(row, m_blk, n_blk * umma::BN + col, acc);
+  __device__ ConvStorer storer(int row, int, int m_blk, int n_blk) const {
+    return conv_storer(row, m_blk, n_blk * umma::BN);
   }
   __device__ void finish() const {}
 };
@@ -101,54 +131,18 @@ struct Conv2Policy : ConvGeometry, umma2::PolicyBase {
   __device__ int m_blocks() const { return num_m(); }
   __device__ int n_blocks() const { return num_n; }
   __device__ int k_blocks() const { return R * S * c_blocks; }
-  // Walks k-blocks in the order kb = (r * S + s) * c_blocks + cb with counters.
-  struct Loader {
-    const CUtensorMap *tx, *tw;
-    int w0, h0, n0, co;      // input box origin for tap (0, 0); first output channel
-    int r, s, cb, rs;        // current tap and channel block
-    int S, c_blocks, dh, dw;
-    __device__ void load(uint8_t* a_dst, uint8_t* b_dst, uint32_t bar) {
-      umma2::tma_load_4d_pair(a_dst, tx, bar, cb * 64, w0 + s * dw, h0 + r * dh, n0);
-      umma2::tma_load_3d_pair(b_dst, tw, bar, cb * 64, rs, co);
-      if (++cb == c_blocks) {
-        cb = 0;
-        ++rs;
-        if (++s == S) {
-          s = 0;
-          ++r;
-        }
-      }
-    }
-  };
-  __device__ Loader loader(int m_blk, int n_blk, int half) const {
+  __device__ ConvLoader<true> loader(int m_blk, int n_blk, int half) const {
     int n0, ho0, wo0;
     pixel_tile(m_blk, n0, ho0, wo0);
-    return Loader{tx, tw, wo0 * sw - pw, ho0 * sh - ph, n0, n_blk * umma2::BN + half * 128, 0, 0, 0, 0,
-                  S, c_blocks, dh, dw};
+    return ConvLoader<true>{tx, tw, wo0 * sw - pw, ho0 * sh - ph, n0, n_blk * umma2::BN + half * 128, 0, 0, 0, 0,
+                            S, c_blocks, dh, dw};
   }
-  struct Storer {
-    __nv_bfloat16* dst;  // output pixel at the tile's first channel; null outside the output
-    const float* bias;
-    int cols;            // valid channels from the tile's first channel
-    bool vec_ok;
-    __device__ void store(int col, const uint32_t (&acc)[32]) const {
-      if (!dst || col >= cols) return;
-      umma::store_bf16_chunk(dst + col, cols - col, vec_ok, acc, bias ? bias + col : nullptr);
-    }
-  };
-  __device__ Storer storer(int row, int m_blk, int n_blk, int, uint32_t*) const {
-    int n0, ho0, wo0;
-    pixel_tile(m_blk, n0, ho0, wo0);
-    const int n = n0 + (row >> 6), ho = ho0 + ((row >> 3) & 7), wo = wo0 + (row & 7);
-    const int co = n_blk * umma2::BN;
-    const bool in = n < batch && ho < Ho && wo < Wo;
-    return Storer{in ? y + (((long long)n * Ho + ho) * Wo + wo) * Cout + co : nullptr, bias ? bias + co : nullptr,
-                  Cout - co, vec_ok};
+  __device__ ConvStorer storer(int row, int m_blk, int n_blk, int, uint32_t*) const {
+    return conv_storer(row, m_blk, n_blk * umma2::BN);
   }
 };
 
 }  // namespace
-
 
 // Fills the geometry from the kernel arguments (identical for both forms).
 __device__ __forceinline__ void conv_geometry(ConvGeometry& p, const CUtensorMap* tx, const CUtensorMap* tw,

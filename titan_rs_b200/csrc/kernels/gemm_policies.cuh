@@ -43,15 +43,34 @@ struct GemmPolicy {
     tma_prefetch_desc(tb);
   }
   __device__ void tile(int t, int& m_blk, int& n_blk) const { umma::grouped_tile(t, num_m, num_n, 16, m_blk, n_blk); }
-  __device__ void load(uint8_t* a_dst, uint8_t* b_dst, uint64_t* bar, int m_blk, int n_blk, int kb) const {
-    tma_load_2d(a_dst, ta, bar, kb * umma::BK, m_blk * umma::BM);
-    tma_load_2d(b_dst, tb, bar, kb * umma::BK, n_blk * umma::BN);
+  // A rows m_blk*128.., B rows n_blk*256.., K from kb0*64 on, one k-block per load().
+  struct Loader {
+    const CUtensorMap *ta, *tb;
+    int row, col, k;
+    __device__ void load(uint8_t* a_dst, uint8_t* b_dst, uint64_t* bar) {
+      tma_load_2d(a_dst, ta, bar, k, row);
+      tma_load_2d(b_dst, tb, bar, k, col);
+      k += umma::BK;
+    }
+  };
+  __device__ Loader loader(int, int m_blk, int n_blk, int kb0) const {
+    return Loader{ta, tb, m_blk * umma::BM, n_blk * umma::BN, kb0 * umma::BK};
   }
-  __device__ void store(int row, int, int m_blk, int n_blk, int col, const uint32_t (&r)[32]) const {
+  struct Storer {
+    __nv_bfloat16* dst;  // row start at the tile's first column; null when the row is past M
+    const float* bias;   // at the tile's first column, or null
+    int cols;            // valid columns from the tile's first column
+    int act;
+    bool vec_ok;
+    __device__ void store(int col, const uint32_t (&r)[32]) const {
+      if (!dst || col >= cols) return;
+      umma::store_bf16_chunk(dst + col, cols - col, vec_ok, r, bias ? bias + col : nullptr, act);
+    }
+  };
+  __device__ Storer storer(int row, int, int m_blk, int n_blk) const {
     const int gr = m_blk * umma::BM + row;
-    const int gc = n_blk * umma::BN + col;
-    if (gr >= M || gc >= N) return;
-    umma::store_bf16_chunk(c + (long long)gr * ldc + gc, N - gc, vec_ok, r, bias ? bias + gc : nullptr, act);
+    const int gc = n_blk * umma::BN;
+    return Storer{gr < M ? c + (long long)gr * ldc + gc : nullptr, bias ? bias + gc : nullptr, N - gc, act, vec_ok};
   }
   __device__ void finish() const {}
 };
@@ -121,35 +140,42 @@ struct AllGatherPolicy : GemmPolicy {
   int ranks, self;
   long long col0;
 
-  __device__ void store(int row, int, int m_blk, int n_blk, int col, const uint32_t (&r)[32]) const {
-    const int lane = row & 31;
-    uint8_t* stage = umma::epilogue_smem() + (row >> 5) * (32 * 256);  // this warp's [32 rows][256 B]
-    const int first_seg = (col & 127) >> 3;                              // 0, 4, 8, 12
+  struct Storer {
+    const RankOutputs* outs;
+    uint8_t* stage;  // this warp's [32 rows][256 B] staging block
+    int lane, row0, gc0, M, N, ranks, self;
+    long long ldc, col0;
+    __device__ void store(int col, const uint32_t (&r)[32]) const {
+      const int first_seg = (col & 127) >> 3;  // 0, 4, 8, 12
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 v;
-      v.x = pack_bf16x2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
-      v.y = pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
-      v.z = pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
-      v.w = pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
-      *reinterpret_cast<uint4*>(stage + lane * 256 + (((first_seg + q) ^ (lane & 15)) << 4)) = v;
-    }
-    if ((col & 127) != 96) return;  // the 128-column half is complete after its fourth chunk
-    __syncwarp();
-    const int seg = lane & 15;                                // 16-byte segment (8 columns) of a row
-    const int gc = n_blk * umma::BN + (col & ~127) + seg * 8;  // this lane's local column
-    const int row0 = m_blk * umma::BM + (row & ~31);
-    for (int it = 0; it < 16; ++it) {
-      const int rr = 2 * it + (lane >> 4);
-      const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 256 + ((seg ^ (rr & 15)) << 4));
-      const int gr = row0 + rr;
-      if (gr < M && gc < N) {
-        const long long off = (long long)gr * ldc + col0 + gc;
-        for (int i = 0, d = self; i < ranks; ++i, d = (d + 1 == ranks) ? 0 : d + 1)
-          *reinterpret_cast<uint4*>(outs->base[d] + off) = v;
+      for (int q = 0; q < 4; ++q) {
+        uint4 v;
+        v.x = pack_bf16x2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
+        v.y = pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
+        v.z = pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
+        v.w = pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
+        *reinterpret_cast<uint4*>(stage + lane * 256 + (((first_seg + q) ^ (lane & 15)) << 4)) = v;
       }
+      if ((col & 127) != 96) return;  // the 128-column half is complete after its fourth chunk
+      __syncwarp();
+      const int seg = lane & 15;                     // 16-byte segment (8 columns) of a row
+      const int gc = gc0 + (col & ~127) + seg * 8;  // this lane's local column
+      for (int it = 0; it < 16; ++it) {
+        const int rr = 2 * it + (lane >> 4);
+        const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 256 + ((seg ^ (rr & 15)) << 4));
+        const int gr = row0 + rr;
+        if (gr < M && gc < N) {
+          const long long off = (long long)gr * ldc + col0 + gc;
+          for (int i = 0, d = self; i < ranks; ++i, d = (d + 1 == ranks) ? 0 : d + 1)
+            *reinterpret_cast<uint4*>(outs->base[d] + off) = v;
+        }
+      }
+      __syncwarp();  // the next half overwrites the staging block
     }
-    __syncwarp();  // the next half overwrites the staging block
+  };
+  __device__ Storer storer(int row, int, int m_blk, int n_blk) const {
+    return Storer{outs, umma::epilogue_smem() + (row >> 5) * (32 * 256), row & 31, m_blk * umma::BM + (row & ~31),
+                  n_blk * umma::BN, M, N, ranks, self, ldc, col0};
   }
   // The peer stores of this thread are performed system-wide before the kernel ends,
   // hence before the barrier that follows it on the stream signals any peer.
@@ -289,17 +315,26 @@ struct SplitKPolicy {
   __device__ void tile(int t, int& m_blk, int& n_blk) const {
     umma::grouped_tile(t % (num_m * num_n), num_m, num_n, 16, m_blk, n_blk);
   }
-  __device__ void load(uint8_t* a_dst, uint8_t* b_dst, uint64_t* bar, int m_blk, int n_blk, int kb) const {
-    tma_load_2d(a_dst, ta, bar, kb * umma::BK, m_blk * umma::BM);
-    tma_load_2d(b_dst, tb, bar, kb * umma::BK, n_blk * umma::BN);
+  __device__ GemmPolicy::Loader loader(int, int m_blk, int n_blk, int kb0) const {
+    return GemmPolicy::Loader{ta, tb, m_blk * umma::BM, n_blk * umma::BN, kb0 * umma::BK};
   }
-  __device__ void store(int row, int t, int m_blk, int n_blk, int col, const uint32_t (&r)[32]) const {
+  struct Storer {
+    float* dst;  // this row of split s's partial plane at the tile's first column; null past M
+    int cols;    // valid columns from the tile's first column
+    bool vec_ok;
+    __device__ void store(int col, const uint32_t (&r)[32]) const {
+      if (!dst || col >= cols) return;
+      SplitKPolicy::store_chunk(dst + col, cols - col, vec_ok, r);
+    }
+  };
+  __device__ Storer storer(int row, int t, int m_blk, int n_blk) const {
     const int s = t / (num_m * num_n);
     const int gr = m_blk * umma::BM + row;
-    const int gc = n_blk * umma::BN + col;
-    if (gr >= M || gc >= N) return;
-    float* dst = partial + ((long long)s * M + gr) * N + gc;
-    if (vec_ok && gc + 32 <= N) {
+    const int gc = n_blk * umma::BN;
+    return Storer{gr < M ? partial + ((long long)s * M + gr) * N + gc : nullptr, N - gc, vec_ok};
+  }
+  __device__ static void store_chunk(float* dst, int valid, bool vec_ok, const uint32_t (&r)[32]) {
+    if (vec_ok && valid >= 32) {
 #pragma unroll
       for (int q = 0; q < 8; ++q)
         reinterpret_cast<float4*>(dst)[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
@@ -307,7 +342,7 @@ struct SplitKPolicy {
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (gc + j < N) dst[j] = __uint_as_float(r[j]);
+        if (j < valid) dst[j] = __uint_as_float(r[j]);
     }
   }
   __device__ void finish() const {}

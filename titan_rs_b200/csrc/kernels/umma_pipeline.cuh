@@ -1,8 +1,11 @@
 // Persistent, warp-specialised tcgen05 GEMM pipeline shared by the GEMM and the
 // implicit-GEMM convolution. A problem policy supplies the tile space
-// (num_tiles, tile, k_blocks = the k-block range of a tile), the TMA loads of
-// one k-block and the epilogue addressing (store); this file owns the
-// shared-memory ring, the MMA issue and the TMEM accumulators.
+// (num_tiles, tile, k_blocks = the k-block range of a tile) and two per-tile cursors
+// that do their index arithmetic once per tile: loader(t, m_blk, n_blk, kb0) -> L,
+// L.load(a_dst, b_dst, bar) issuing the TMA loads of the next k-block, and
+// storer(row, t, m_blk, n_blk) -> W, W.store(col, acc) for 32 accumulator columns of
+// one row. This file owns the shared-memory ring, the MMA issue and the TMEM
+// accumulators.
 //
 //   D[128 x 256] (+)= A[128 x 64] * B[256 x 64]^T per k-block, bf16 in, fp32 in TMEM.
 //   warp 0      TMA producer (Policy::load), 4-stage ring of 48 KB stages.
@@ -130,7 +133,7 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       p.prefetch();
-      uint32_t issued[STAGES] = {0, 0, 0, 0};
+      uint32_t issued = 0;  // k-blocks loaded so far; stage s was filled (issued + STAGES - 1 - s) / STAGES times
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -139,6 +142,7 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
         p.tile(t, m_blk, n_blk);
         int kb0, kb1;
         p.k_blocks(t, kb0, kb1);
+        auto ld = p.loader(t, m_blk, n_blk, kb0);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&bars->empty[stage], phase ^ 1)) {
             report_status(status, fail_base | 0x0101);
@@ -147,8 +151,8 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
           }
           uint8_t* a_dst = smem + stage * STAGE_BYTES;
           mbar_arrive_expect_tx(&bars->full[stage], STAGE_BYTES);
-          p.load(a_dst, a_dst + A_BYTES, &bars->full[stage], m_blk, n_blk, kb);
-          ++issued[stage];
+          ld.load(a_dst, a_dst + A_BYTES, &bars->full[stage]);
+          ++issued;
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -156,8 +160,10 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
         }
       }
       if (!ok) {
-        for (int s = 0; s < STAGES; ++s)
-          if (issued[s] && !mbar_wait(&bars->full[s], (issued[s] - 1) & 1)) report_status(status, fail_base | 0x0102);
+        for (int s = 0; s < STAGES; ++s) {
+          const uint32_t fills = (issued + STAGES - 1 - s) / STAGES;
+          if (fills && !mbar_wait(&bars->full[s], (fills - 1) & 1)) report_status(status, fail_base | 0x0102);
+        }
       }
     }
   } else if (warp == 1) {
@@ -221,13 +227,13 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
       }
       tc_fence_after_sync();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
-      const int row = quarter * 32 + lane;
+      const auto st = p.storer(quarter * 32 + lane, t, m_blk, n_blk);
 #pragma unroll 1
       for (int col = 0; col < BN; col += 32) {
         uint32_t r[32];
         tmem_ld_x32(taddr + col, r);
         tmem_ld_wait();
-        p.store(row, t, m_blk, n_blk, col, r);
+        st.store(col, r);
       }
       tc_fence_before_sync();
       __syncwarp();
