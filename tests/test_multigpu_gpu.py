@@ -135,14 +135,19 @@ def _rank_main(rank, world, q_in, q_out, mode):
             coll.barrier(rt.stream)
             s.synchronize(rt.stream)
             q_out.put((rank, ok_gemm and ok_gather))
-        elif mode in ("gemm_p2p", "gemm_p2p_pairs"):
+        elif mode in ("gemm_p2p", "gemm_p2p_pairs", "gemm_p2p_pushers"):
             # Fused GEMM + all-gather into registered outputs, twice with different inputs.
             if mode == "gemm_p2p":
                 m, n, k = 520, 1536, 1024  # M is not a multiple of the 128-row tile
                 fused, plain = "gemm_bf16_tn_allgather", "gemm_bf16_tn"
-            else:
+            elif mode == "gemm_p2p_pairs":
                 m, n, k = 2056, 9712, 1024  # 323 tiles per shard, M and N tails: CTA pairs
                 fused, plain = "gemm_bf16_tn_allgather_2sm", "gemm_bf16_tn_2sm"
+            else:
+                # Dedicated pusher CTAs (the default from 4 ranks), forced here for 2.
+                os.environ["TITAN_B200_ALLGATHER_PUSHERS"] = "16"
+                m, n, k = 2056, 9712, 1024
+                fused, plain = "gemm_bf16_tn_allgather_2sm_push", "gemm_bf16_tn_2sm"
             lo, hi = Dm.even_shard(n, world, rank)
             c = tbm.TensorHandle.allocate(s, DType.BF16, (m, n))
             coll.register_buffer(rt.stream, c.buffer)
@@ -160,12 +165,16 @@ def _rank_main(rank, world, q_in, q_out, mode):
             s.synchronize(rt.stream)
             coll.deregister_buffer(c.buffer)
             q_out.put((rank, ok))
-        elif mode in ("p2p_absent", "p2p_absent_pairs"):
+        elif mode in ("p2p_absent", "p2p_absent_pairs", "p2p_absent_pushers"):
+            if mode == "p2p_absent_pushers":
+                os.environ["TITAN_B200_ALLGATHER_PUSHERS"] = "16"
             # Rank 1 registers its output but never makes the call: rank 0's fused kernel
             # gives up its entry wait after ~1 s (a flag nothing sets), reports the code, and
             # its context stays usable. With CTA pairs the CTAs still run the pair pipeline
             # (stores off), so every cluster barrier is reached.
             m, n, k = (256, 512, 256) if mode == "p2p_absent" else (2056, 9712, 512)
+            fused = {"p2p_absent": "gemm_bf16_tn_allgather", "p2p_absent_pairs": "gemm_bf16_tn_allgather_2sm",
+                     "p2p_absent_pushers": "gemm_bf16_tn_allgather_2sm_push"}[mode]
             c = tbm.TensorHandle.allocate(s, DType.BF16, (m, n))
             coll.register_buffer(rt.stream, c.buffer)
             if rank == 0:
@@ -179,6 +188,8 @@ def _rank_main(rank, world, q_in, q_out, mode):
                     outcome = "no error"
                 except tbm.HalError as e:
                     outcome = "timeout" if "47410501" in str(e) else repr(e)
+                if tbm.last_candidate() != fused:
+                    outcome = "ran " + tbm.last_candidate()
                 # The context still runs work.
                 probe = s.allocate(64)
                 s.wait(s.upload(rt.stream, probe, np.arange(16, dtype=np.float32)))
@@ -239,7 +250,12 @@ def test_two_rank_fused_sharded_gemm_on_cta_pairs():
 
 
 @pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("mode", ["p2p_absent", "p2p_absent_pairs"])
+def test_two_rank_fused_sharded_gemm_with_pusher_ctas():
+    assert _spawn(2, "gemm_p2p_pushers") == {0: True, 1: True}
+
+
+@pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("mode", ["p2p_absent", "p2p_absent_pairs", "p2p_absent_pushers"])
 def test_two_rank_fused_gemm_gives_up_when_a_peer_never_arrives(mode):
     assert _spawn(2, mode) == {0: ("timeout", True), 1: "absent"}
 

@@ -34,7 +34,7 @@ tb_status launch_gemm_bf16_default(Session* s, Stream* st, CUdeviceptr a, CUdevi
                                    int K, long long ldc);
 tb_status launch_gemm_bf16_tn_allgather(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, const CUdeviceptr* outs,
                                         const CUdeviceptr* signals, int ranks, int self, uint32_t epoch, int M, int N,
-                                        int K, long long ldc, long long col0);
+                                        int K, long long ldc, long long col0, CUdeviceptr ready, size_t ready_count);
 
 namespace {
 
@@ -99,6 +99,8 @@ struct PeerMapping {
   std::vector<CUdeviceptr> signal;     // per rank
   std::vector<CUdeviceptr> signal_opened;
   uint32_t epoch = 0;                  // fused calls made with this buffer (same on every rank)
+  CUdeviceptr ready = 0;               // per-tile counters of the pusher-CTA kernel (owned)
+  size_t ready_count = 0;
 };
 
 struct Comm {
@@ -205,6 +207,8 @@ void unmap(PeerMapping& m) {
   m.signal_opened.clear();
   if (m.signal_local && d) d->cuMemFree_v2(m.signal_local);
   m.signal_local = 0;
+  if (m.ready && d) d->cuMemFree_v2(m.ready);
+  m.ready = 0;
   if (m.local) tb_buffer_release(reinterpret_cast<tb_buffer*>(m.local));
   m.local = nullptr;
 }
@@ -371,6 +375,14 @@ tb_status tb_comm_register_buffer(tb_comm* comm, tb_stream* stream, tb_buffer* b
   m.signal_opened.assign(p, 0);
   TB_CU("allocate", d->cuMemAlloc_v2(&m.signal_local, TB_SIGNAL_BLOCK_BYTES));
   m.signal[c->rank] = m.signal_local;
+  // Tile counters for the pusher-CTA kernel (two per 256x256 tile of a rank's column
+  // block): one per 16 KB of the buffer, at least 1024. A call that needs more, or a
+  // failed allocation, runs the kernel with in-CTA push warps instead.
+  m.ready_count = b->bytes / 16384 > 1024 ? b->bytes / 16384 : 1024;
+  if (d->cuMemAlloc_v2(&m.ready, m.ready_count * sizeof(uint32_t)) != CUDA_SUCCESS) {
+    m.ready = 0;
+    m.ready_count = 0;
+  }
   CUresult zr = d->cuMemsetD32Async(m.signal_local, 0, TB_SIGNAL_BLOCK_BYTES / 4, st->raw);
   if (zr == CUDA_SUCCESS) zr = d->cuStreamSynchronize(st->raw);
   if (zr != CUDA_SUCCESS) {
@@ -497,7 +509,7 @@ tb_status tb_op_gemm_sharded(tb_comm* comm, tb_stream* stream, const tb_tensor* 
     if (rc) return rc;
     rc = launch_gemm_bf16_tn_allgather(s, st, ba->ptr, bb->ptr, mapping->base.data(), mapping->signal.data(), (int)p,
                                        c->rank, mapping->epoch + 1, (int)M, (int)Np, (int)K, (long long)(Np * p),
-                                       (long long)(Np * (uint64_t)c->rank));
+                                       (long long)(Np * (uint64_t)c->rank), mapping->ready, mapping->ready_count);
     if (rc) return rc;
     ++mapping->epoch;
     return record_event(s, st, nullptr, out);

@@ -95,6 +95,7 @@ struct Session : RefCounted {
   std::unordered_map<std::string, std::shared_ptr<Module>> module_cache;  // by artifact content hash
   std::unordered_map<std::string, CUfunction> builtin_functions;        // embedded cubin entries
   std::unordered_map<std::string, std::shared_ptr<Module>> builtin_modules;
+  std::unordered_map<CUfunction, int> pair_occupancy;  // resident CTA pairs of a built-in pair kernel
   std::unordered_set<void*> pinned;
   StatusWord status;
   int sm_count = 0;

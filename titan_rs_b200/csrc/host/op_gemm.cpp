@@ -64,9 +64,22 @@ tb_status launch_gemm_bf16_default(Session* s, Stream* st, CUdeviceptr a, CUdevi
 // Fused N-sharded GEMM + all-gather: this rank's [M, N] column block of the row-major
 // C[M, ldc] at column col0, stored into every rank's C (outs[i] = rank i's base); the
 // ranks synchronise through their signal blocks (signals[i] = rank i's) for call `epoch`.
+// Pusher CTAs for the fused all-gather: TITAN_B200_ALLGATHER_PUSHERS (an even count, 0 =
+// none) if set; else none below four ranks (the tensor work of the SMs they would take
+// outweighs the stores), 16 from four ranks (measured best of 0, 16, 32 at 4 ranks:
+// 3354, 3931, 3819 TFLOP/s for C3) and 32 from eight, where each rank receives 112 MB
+// against 0.1 ms of compute.
+static int allgather_pushers(int ranks) {
+  if (const char* e = getenv("TITAN_B200_ALLGATHER_PUSHERS")) {
+    const int v = atoi(e);
+    return v > 0 ? (v + 1) & ~1 : 0;
+  }
+  return ranks >= 8 ? 32 : ranks >= 4 ? 16 : 0;
+}
+
 tb_status launch_gemm_bf16_tn_allgather(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, const CUdeviceptr* outs,
                                         const CUdeviceptr* signals, int ranks, int self, uint32_t epoch, int M, int N,
-                                        int K, long long ldc, long long col0) {
+                                        int K, long long ldc, long long col0, CUdeviceptr ready, size_t ready_count) {
   if (ranks < 1 || ranks > TB_MAX_RANKS) return unsupported("fused all-gather supports 1 to 8 ranks");
   // The kernel stores whole 16-byte segments (8 columns) into every rank's C.
   if (ldc % 8 != 0 || col0 % 8 != 0 || N % 8 != 0) return unsupported("fused all-gather needs 8-column alignment");
@@ -94,9 +107,29 @@ tb_status launch_gemm_bf16_tn_allgather(Session* s, Stream* st, CUdeviceptr a, C
     rank_signals.base[i] = signals[i];
   }
   CUdeviceptr status = s->status.device;
+  const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+  const int pushers = pairs && ranks > 1 ? allgather_pushers(ranks) : 0;
+  if (pushers > 0 && ready && (size_t)(2 * pair_tiles) <= ready_count) {
+    // Dedicated pusher CTAs (gemm_bf16_tn_allgather_2sm_push); tile counters zeroed first.
+    CUfunction pfn = nullptr;
+    rc = builtin_function(s, "gemm_bf16", "gemm_bf16_tn_allgather_2sm_push", &pfn);
+    if (rc) return rc;
+    int clusters = 0;
+    rc = pair_occupancy(s, st, pfn, TB_GEMM2_PUSH_THREADS, TB_GEMM2_SMEM_BYTES, "gemm_bf16_tn_allgather_2sm_push",
+                        &clusters);
+    if (rc) return rc;
+    if (clusters > pushers / 2) {
+      int gemm_pairs = clusters - pushers / 2;
+      if (gemm_pairs > pair_tiles) gemm_pairs = (int)pair_tiles;
+      TB_CU("cuMemsetD32Async", driver()->cuMemsetD32Async(ready, 0, (size_t)(2 * pair_tiles), st->raw));
+      void* pp[] = {&ta, &tbm, &rank_outputs, &rank_signals, &ranks, &self, &epoch, &M, &N, &K, &ldc, &col0,
+                    &ready, &gemm_pairs, &status};
+      return launch_builtin(s, st, pfn, (unsigned)(2 * gemm_pairs + pushers), 1, 1, TB_GEMM2_PUSH_THREADS,
+                            TB_GEMM2_SMEM_BYTES, pp, "gemm_bf16_tn_allgather_2sm_push", 2);
+    }
+  }
   void* params[] = {&ta, &tbm, &rank_outputs, &rank_signals, &ranks, &self, &epoch, &M, &N, &K, &ldc, &col0, &status};
   if (pairs) {
-    const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
     return launch_builtin_pairs(s, st, fn, pair_tiles, TB_GEMM2_AG_THREADS, TB_GEMM2_AG_SMEM_BYTES, params, name);
   }
   const unsigned grid = (unsigned)(tiles < s->sm_count ? tiles : s->sm_count);

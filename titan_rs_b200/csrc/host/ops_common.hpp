@@ -117,30 +117,51 @@ inline tb_status launch_builtin(Session* s, Stream* st, CUfunction fn, unsigned 
   return TB_OK;
 }
 
-// Launches a persistent kernel built on the 2-SM pipeline (clusters of two CTAs along x):
-// as many pairs as the driver's cluster occupancy allows at once, at most `pair_tiles`.
+// CTA pairs (clusters of two along x) of a built-in pair kernel that can be resident at
+// once. The driver is asked once per kernel and session (each built-in pair kernel is
+// always launched with the same block and shared-memory size).
+inline tb_status pair_occupancy(Session* s, Stream* st, CUfunction fn, unsigned bx, unsigned shared_bytes,
+                                const char* candidate, int* out) {
+  int clusters = 0;
+  {
+    std::lock_guard<std::mutex> lock(s->mu);
+    auto it = s->pair_occupancy.find(fn);
+    if (it != s->pair_occupancy.end()) clusters = it->second;
+  }
+  if (clusters == 0) {
+    const DriverApi* d = driver();
+    TB_CU("cuFuncSetAttribute",
+          d->cuFuncSetAttribute(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)shared_bytes));
+    CUlaunchConfig cfg{};
+    cfg.gridDimX = (unsigned)s->sm_count & ~1u;
+    cfg.gridDimY = cfg.gridDimZ = 1;
+    cfg.blockDimX = bx;
+    cfg.blockDimY = cfg.blockDimZ = 1;
+    cfg.sharedMemBytes = shared_bytes;
+    cfg.hStream = st->raw;
+    CUlaunchAttribute attr{};
+    attr.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+    attr.value.clusterDim.x = 2;
+    attr.value.clusterDim.y = 1;
+    attr.value.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    TB_CU("cuOccupancyMaxActiveClusters", d->cuOccupancyMaxActiveClusters(&clusters, fn, &cfg));
+    if (clusters < 1) return unsupported(std::string("no CTA pair of ") + candidate + " fits on this device");
+    std::lock_guard<std::mutex> lock(s->mu);
+    s->pair_occupancy[fn] = clusters;
+  }
+  *out = clusters;
+  return TB_OK;
+}
+
+// Launches a persistent kernel built on the 2-SM pipeline: as many pairs as can be
+// resident at once, at most `pair_tiles`.
 inline tb_status launch_builtin_pairs(Session* s, Stream* st, CUfunction fn, long long pair_tiles, unsigned bx,
                                       unsigned shared_bytes, void** params, const char* candidate) {
-  const DriverApi* d = driver();
-  TB_CU("cuFuncSetAttribute",
-        d->cuFuncSetAttribute(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)shared_bytes));
-  CUlaunchConfig cfg{};
-  cfg.gridDimX = (unsigned)s->sm_count & ~1u;
-  cfg.gridDimY = cfg.gridDimZ = 1;
-  cfg.blockDimX = bx;
-  cfg.blockDimY = cfg.blockDimZ = 1;
-  cfg.sharedMemBytes = shared_bytes;
-  cfg.hStream = st->raw;
-  CUlaunchAttribute attr{};
-  attr.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
-  attr.value.clusterDim.x = 2;
-  attr.value.clusterDim.y = 1;
-  attr.value.clusterDim.z = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
   int clusters = 0;
-  TB_CU("cuOccupancyMaxActiveClusters", d->cuOccupancyMaxActiveClusters(&clusters, fn, &cfg));
-  if (clusters < 1) return unsupported(std::string("no CTA pair of ") + candidate + " fits on this device");
+  tb_status rc = pair_occupancy(s, st, fn, bx, shared_bytes, candidate, &clusters);
+  if (rc) return rc;
   const unsigned pairs = (unsigned)(pair_tiles < clusters ? pair_tiles : clusters);
   return launch_builtin(s, st, fn, 2 * pairs, 1, 1, bx, shared_bytes, params, candidate, 2);
 }

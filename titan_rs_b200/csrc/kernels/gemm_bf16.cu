@@ -208,6 +208,98 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM2_AG_THREADS, 1)
   }
 }
 
+// Pusher role of gemm_bf16_tn_allgather_2sm_push: the grid's pusher CTAs split the
+// CTA-tiles of this rank's column block into 32-row quarters (in tile order, which is
+// the order the pipeline finishes them), wait until the tile's four quarters are stored
+// in this rank's C (ready count 4), and copy each row (one 16-byte segment per lane,
+// read from L2) into every other rank's C.
+__device__ __forceinline__ void push_finished_tiles(const tb::gemm::RankOutputs* outs, int ranks, int self, int M,
+                                                    int N, long long ldc, long long col0, const uint32_t* ready,
+                                                    int tiles, int num_pm, int num_n, int first_pusher,
+                                                    uint32_t* status) {
+  const int warps_per_cta = blockDim.x >> 5, lane = tb::lane_id();
+  const int w = ((int)blockIdx.x - first_pusher) * warps_per_cta + (int)tb::warp_id();
+  const int stride = ((int)gridDim.x - first_pusher) * warps_per_cta;
+  const __nv_bfloat16* own = outs->base[self];
+  for (int c = w; c < tiles * 8; c += stride) {
+    const int t = c >> 3, r = (c >> 2) & 1, q = c & 3;
+    int m_blk, n_blk;
+    tb::umma::grouped_tile(t, num_pm, num_n, TB_GEMM2_GROUP, m_blk, n_blk);
+    const int row0 = (2 * m_blk + r) * 128 + q * 32;
+    if (row0 >= M) continue;
+    const uint64_t start = tb::global_timer_ns();  // each tile is waited for at most ~1 s
+    while (tb::ld_acquire_gpu(&ready[2 * t + r]) < 4u) {
+      if (tb::global_timer_ns() - start > tb::kWaitLimitNs) {
+        if (lane == 0) tb::report_status(status, kFailAllGather | 0x0801);
+        return;
+      }
+    }
+    const int gc = n_blk * 256 + lane * 8;
+    if (gc >= N) continue;
+    const int rows = min(32, M - row0);
+    for (int rr = 0; rr < rows; ++rr) {
+      const long long off = (long long)(row0 + rr) * ldc + col0 + gc;
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(own + off));
+      for (int k = 1, d = self + 1 == ranks ? 0 : self + 1; k < ranks; ++k, d = (d + 1 == ranks) ? 0 : d + 1)
+        *reinterpret_cast<uint4*>(outs->base[d] + off) = v;
+    }
+  }
+}
+
+// The fused GEMM + all-gather for many ranks: CTAs [0, 2 gemm_pairs) run the pair
+// pipeline into this rank's own C (AllGatherLocalPolicy); the rest push finished tiles
+// to the peers. Launched with clusters of 2, TB_GEMM2_PUSH_THREADS threads and
+// TB_GEMM2_SMEM_BYTES of shared memory for every CTA (one CTA per SM, so pushers have
+// SMs of their own); `ready` holds 2 x pair-tiles counters zeroed before the launch.
+// Same entry and exit handshake as the other fused kernels; a CTA whose entry wait
+// fails stores nothing (GEMM CTAs still run the pair pipeline with their partner).
+extern "C" __global__ void __launch_bounds__(TB_GEMM2_PUSH_THREADS, 1)
+    gemm_bf16_tn_allgather_2sm_push(const __grid_constant__ CUtensorMap tmap_a,
+                                    const __grid_constant__ CUtensorMap tmap_b,
+                                    const __grid_constant__ tb::gemm::RankOutputs outs,
+                                    const __grid_constant__ tb::RankSignals sig, int ranks, int self, uint32_t epoch,
+                                    int M, int N, int K, long long ldc, long long col0, uint32_t* ready,
+                                    int gemm_pairs, uint32_t* status) {
+  __shared__ int entry_ok;
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) tb::signal_peers(sig, ranks, self, epoch, false);
+    entry_ok = tb::wait_peers(sig, ranks, self, epoch, false) ? 1 : 0;
+    if (!entry_ok) tb::report_status(status, kFailAllGather | 0x0501);
+  }
+  __syncthreads();
+  const int num_pm = (M + 255) / 256, num_n = (N + 255) / 256;
+  if ((int)blockIdx.x < 2 * gemm_pairs) {
+    tb::gemm::AllGatherLocalPolicy p;
+    p.ta = &tmap_a;
+    p.tb = &tmap_b;
+    p.c = outs.base[self] + col0;
+    p.M = M;
+    p.enabled = entry_ok != 0;
+    p.N = N;
+    p.K = K;
+    p.ldc = ldc;
+    p.vec_ok = true;  // the host requires 16-byte aligned bases, ldc % 8 == 0, col0 % 8 == 0 and N % 8 == 0
+    p.ready = ready;
+    p.gemm_pairs = gemm_pairs;
+    tb::umma2::run(p, status, kFailAllGather2);
+  } else if (entry_ok && ranks > 1) {
+    push_finished_tiles(&outs, ranks, self, M, N, ldc, col0, ready, num_pm * num_n, num_pm, num_n, 2 * gemm_pairs,
+                        status);
+  }
+  __threadfence_system();  // this thread's peer stores, before the exit handshake
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    tb::SignalBlock* mine = sig.block[self];
+    if (atomicAdd(&mine->arrivals, 1u) == gridDim.x - 1) {
+      mine->arrivals = 0;  // the next call starts after this kernel (stream order)
+      if (entry_ok) {
+        tb::signal_peers(sig, ranks, self, epoch, true);
+        if (!tb::wait_peers(sig, ranks, self, epoch, true)) tb::report_status(status, kFailAllGather | 0x0502);
+      }
+    }
+  }
+}
+
 extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
     gemm_bf16_tn_splitk(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         float* __restrict__ partial, int M, int N, int K, int splits, int kb_per_split,

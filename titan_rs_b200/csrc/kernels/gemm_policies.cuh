@@ -293,6 +293,33 @@ struct AllGather2Policy : Gemm2Policy {
   }
 };
 
+// The GEMM half of the fused all-gather with dedicated pusher CTAs
+// (gemm_bf16_tn_allgather_2sm_push): the pipeline's CTAs write this rank's column block
+// into its own C only (c = own C at column col0) and count each CTA-tile's stored
+// quarters in ready[2 t + rank] (four per tile: one per epilogue warp); pusher CTAs on
+// other SMs copy finished tiles to the peers. Peer stores from the SMs that run the
+// tensor-core pipeline slow that pipeline far more than the stores take (the
+// stores wait in the same memory-instruction path as its TMA and MMA issue), so these
+// SMs keep to local memory.
+struct AllGatherLocalPolicy : Gemm2Policy {
+  uint32_t* ready;
+  int gemm_pairs;
+  bool enabled;  // false after a failed entry handshake: same tiles, nothing stored
+  __device__ int pair_count() const { return gemm_pairs; }
+  __device__ Storer storer(int row, int m_blk, int n_blk, int ordinal, uint32_t* status) const {
+    Storer w = Gemm2Policy::storer(row, m_blk, n_blk, ordinal, status);
+    if (!enabled) w.dst = nullptr;
+    return w;
+  }
+  __device__ void tile_stored(int t, int rank, int lane) const {
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence();  // this warp's stores (seen through the warp barrier) before the count
+      atomicAdd(&ready[2 * t + rank], 1u);
+    }
+  }
+};
+
 struct SplitKPolicy {
   const CUtensorMap* ta;
   const CUtensorMap* tb;

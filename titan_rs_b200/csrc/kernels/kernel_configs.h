@@ -29,6 +29,9 @@
 #define TB_GEMM2_AG_STAGES 5
 #define TB_GEMM2_AG_SMEM_BYTES (TB_GEMM2_AG_STAGES * 2 * 128 * TB_GEMM_BK * 2 + 1024 + TB_GEMM2_BARRIER_BYTES + 128 + 8 * 32 * 256)
 #define TB_GEMM2_AG_THREADS (TB_GEMM_THREADS + 4 * 32)
+// Fused all-gather with dedicated pusher CTAs: 16 warps per CTA (the pipeline uses
+// six of them in GEMM CTAs; pusher CTAs use all sixteen for peer stores).
+#define TB_GEMM2_PUSH_THREADS 512
 
 // Causal SDPA forward (sdpa_bf16.cu): 128-row query tiles, 128-key tiles, head dim 128.
 // Shared memory: Q 32 KB + K ring 2x32 KB + V ring 2x32 KB + P 2x32 KB + barriers.

@@ -39,6 +39,12 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Writes `epoch` into slot `self` of field `entry` (exit = false) or `exit` of every
 // other rank's block.
 __device__ __forceinline__ void signal_peers(const RankSignals& s, int ranks, int self, uint32_t epoch, bool exit) {

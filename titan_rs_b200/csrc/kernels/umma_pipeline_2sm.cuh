@@ -166,12 +166,17 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t tmem, uint32_t cols) 
 // A policy may add kSideWarps warps after the six pipeline warps (the block has
 // 192 + 32 kSideWarps threads): they run side(i, first_tile, tile_stride, tiles, num_pm,
 // num_n, status, fail_base) beside the pipeline, after init() has set up any barriers
-// they share with the epilogue. PolicyBase supplies the empty defaults.
+// they share with the epilogue. pair_count() is the number of CTA pairs running the
+// pipeline (the grid, unless the kernel gives other CTAs another job);
+// tile_stored(t, rank, lane) runs in each epilogue warp after it stored its rows of pair
+// tile t. PolicyBase supplies the defaults.
 struct PolicyBase {
   static constexpr int kSideWarps = 0;
   __device__ void init() const {}
   __device__ void side(int, int, int, int, int, int, uint32_t*, uint32_t) const {}
   __device__ void finish() const {}
+  __device__ int pair_count() const { return gridDim.x >> 1; }
+  __device__ void tile_stored(int, int, int) const {}
 };
 
 template <class Policy, int Stages = STAGES, int Group = TB_GEMM2_GROUP>
@@ -186,7 +191,7 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
   const int num_pm = (p.m_blocks() + 1) / 2;  // 256-row pair tiles
   const int num_n = p.n_blocks();
   const int tiles = num_pm * num_n;
-  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int pair = blockIdx.x >> 1, pairs = p.pair_count();
   const int num_k = p.k_blocks();
 
   if (threadIdx.x == 0) {
@@ -325,6 +330,7 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
         tmem_ld_wait();
         st.store(col, r);
       }
+      p.tile_stored(t, (int)rank, lane);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) {
