@@ -351,8 +351,8 @@ class GemmWorkload(Workload):
                "M": self.M, "N": self.N, "K": self.K, "parallelism": f"N-shard{self.world}" if self.world > 1
                else "single", "l2": "inputs 256 MiB > 126 MB L2"}
         if self.world > 1:
-            cfg["allgather"] = ("fused GEMM + all-gather kernel (gemm_bf16_tn_allgather, on CTA pairs when the shard "
-                                "fills the SMs): NVLink peer stores into registered C"
+            cfg["allgather"] = ("fused GEMM + all-gather kernel: NVLink peer stores into registered C (CTA pairs "
+                                "with push warps; from 4 ranks, dedicated pusher CTAs: gemm_bf16_tn_allgather_2sm_push)"
                                 if self.allgather == "p2p" else "NCCL all-gather + re-layout kernel")
         return cfg
 
