@@ -4,18 +4,21 @@
 //   where B is stored as [N,K] row-major, i.e. the column-major B of the
 //   titan.rs GEMM with transpose_rhs (projects/titan-runtime/src/lib.rs:955-989).
 //
-// The pipeline (umma_pipeline.cuh) is one persistent CTA per SM: TMA producer
-// warp, MMA warp with two 128x256 fp32 TMEM accumulators, four epilogue warps.
-// The policies (gemm_policies.cuh) map tiles and k-blocks to TMA coordinates:
-// A tile [128 x 64] at (k, m), B tile [256 x 64] at (k, n), 128-byte swizzle;
-// tiles are visited in groups of 16 M-blocks so the tiles in flight share A rows
+// Two pipelines: umma_pipeline.cuh, one persistent CTA per SM on 128x256 tiles (TMA
+// producer warp, MMA warp with two 128x256 fp32 TMEM accumulators, four epilogue
+// warps), and umma_pipeline_2sm.cuh, CTA pairs on 256x256 tiles with
+// tcgen05.mma.cta_group::2 (the default once the output fills the SMs). The policies
+// (gemm_policies.cuh) map tiles and k-blocks to TMA coordinates, 128-byte swizzle;
+// tiles are visited in groups of 2048 rows of A so the tiles in flight share A rows
 // and B columns in L2. K tails and M/N tails come back from TMA as zeros; the
 // epilogue masks them.
 //
-// Fused all-gather (gemm_bf16_tn_allgather): the N-sharded GEMM of one rank whose
-// epilogue stores every output chunk into all ranks' row-major C (NVLink peer stores
-// through CUDA IPC mappings), so the gather overlaps the remaining tiles' math; the
-// ranks synchronise through flags in each other's memory (peer_signal.cuh).
+// Fused all-gather (gemm_bf16_tn_allgather, _2sm, _2sm_push): the N-sharded GEMM of one
+// rank whose output tiles reach all ranks' row-major C through NVLink peer stores (CUDA
+// IPC mappings) while the remaining tiles compute; the ranks synchronise through flags
+// in each other's memory (peer_signal.cuh). The stores come from the epilogue (1-SM),
+// from push warps fed through shared memory (_2sm), or from dedicated pusher CTAs that
+// copy finished tiles out of this rank's C (_2sm_push, from four ranks).
 //
 // Split-K (gemm_bf16_tn_splitk + splitk_reduce_bf16): when the output has too
 // few 128x256 tiles to occupy the SMs, each tile's K range is cut into slices

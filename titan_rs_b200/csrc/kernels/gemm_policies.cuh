@@ -14,6 +14,10 @@
 //                  row-major C (peer copies through CUDA IPC mappings over NVLink).
 //   Gemm2Policy    GemmPolicy's product on the 2-SM pipeline (umma_pipeline_2sm.cuh):
 //                  tensor maps with 128-row boxes for A and B.
+//   AllGather2Policy      the fused all-gather on the 2-SM pipeline, its epilogue staging
+//                  tiles in shared memory for four push warps.
+//   AllGatherLocalPolicy  the GEMM CTAs of the fused all-gather with dedicated pusher
+//                  CTAs: own C only, plus per-tile ready counts.
 #pragma once
 
 #include "umma_pipeline.cuh"
