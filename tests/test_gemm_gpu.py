@@ -93,6 +93,43 @@ def test_gemm_bf16_tcgen05_matches_oracle(session, rt, m, n, k, candidate):
     assert np.isfinite(got).all()
 
 
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 128), (200, 304, 72), (1, 8, 8), (129, 264, 1032),
+                                   (1000, 1000, 1000), (2304, 4352, 520)])
+def test_gemm_bf16_row_major_b_on_tensor_cores(session, rt, m, n, k):
+    """B stored [K, N] (the reference's default layout): gemm_bf16_nn_2sm, B tiles N-contiguous."""
+    a, b = bf16_inputs(m, n, k, seed=m + n + k + 7, b_col_major=False)
+    h = run_op(rt, "gemm", [upload(session, rt.stream, a, DType.BF16), upload(session, rt.stream, b, DType.BF16)],
+               DType.BF16, (m, n))
+    assert h.candidate == "gemm_bf16_nn_2sm"
+    got = h.outputs[0].to_f32()
+    rows = np.repeat(np.arange(m), n)
+    cols = np.tile(np.arange(n), m)
+    ref = oracle.gemm_bf16_points(a, b, False, m, n, k, rows, cols).reshape(m, n)
+    assert max_rel_err(got, ref) <= BF16_TOL, max_rel_err(got, ref)
+    assert np.isfinite(got).all()
+
+
+def test_gemm_bf16_row_major_b_full_size(session, rt):
+    """8192^3 with B stored [K, N]: sampled points and the column-checksum identity."""
+    M = N = K = 8192
+    a = tb.fill_normal(M * K, seed=2 * 16 + 0, dtype=DType.BF16).reshape(M, K)
+    b = tb.fill_normal(K * N, seed=2 * 16 + 5, std=1.0 / math.sqrt(K), dtype=DType.BF16).reshape(K, N)
+    h = run_op(rt, "gemm", [upload(session, rt.stream, a, DType.BF16), upload(session, rt.stream, b, DType.BF16)],
+               DType.BF16, (M, N))
+    assert h.candidate == "gemm_bf16_nn_2sm"
+    got = h.outputs[0].to_f32()
+    rng = np.random.default_rng(3)
+    rows = np.concatenate([rng.integers(0, M, 4096), [0, M - 1, 255, 256]])
+    cols = np.concatenate([rng.integers(0, N, 4096), [N - 1, 0, 127, 128]])
+    ref = oracle.gemm_bf16_points(a, b, False, M, N, K, rows, cols)
+    assert max_rel_err(got[rows, cols], ref) <= BF16_TOL
+    af = tb.bf16_bits_to_f32(a).reshape(M, K).astype(np.float64)
+    bf = tb.bf16_bits_to_f32(b).reshape(K, N).astype(np.float64)
+    colsum_ref = af.sum(axis=0) @ bf
+    colsum = got.astype(np.float64).sum(axis=0)
+    assert np.max(np.abs(colsum - colsum_ref)) <= BF16_TOL * np.max(np.abs(colsum_ref))
+
+
 def test_gemm_bf16_row_major_b_and_transposed_a(session, rt):
     m, n, k = 70, 90, 40
     a, b = bf16_inputs(m, n, k, seed=5, b_col_major=False)

@@ -70,6 +70,23 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
   tb::umma2::run(p, status, kFailGemm2);
 }
 
+// C = A B with B stored [K, N] row-major, on CTA pairs (tensor map over B [K, N] with
+// {64, 64} boxes; A as for gemm_bf16_tn_2sm).
+extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
+    gemm_bf16_nn_2sm(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                     __nv_bfloat16* __restrict__ c, int M, int N, int K, long long ldc, uint32_t* status) {
+  tb::gemm::Gemm2NNPolicy p;
+  p.ta = &tmap_a;
+  p.tb = &tmap_b;
+  p.c = c;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = ldc;
+  p.vec_ok = (ldc % 8) == 0 && (reinterpret_cast<uintptr_t>(c) & 15) == 0;
+  tb::umma2::run(p, status, kFailGemm2);
+}
+
 // gemm_bf16_tn_bias_act on the 2-SM pipeline.
 extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
     gemm_bf16_tn_bias_act_2sm(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,

@@ -297,6 +297,26 @@ struct AllGather2Policy : Gemm2Policy {
   }
 };
 
+// Gemm2Policy's product with B stored [K, N] row-major (the reference's default layout):
+// B tiles are N-contiguous, two {64 N, 64 K} boxes per CTA and stage from a tensor map
+// over [K, N]; the MMA reads them MN-major.
+struct Gemm2NNPolicy : Gemm2Policy {
+  static constexpr bool kBMajorMN = true;
+  struct Loader {
+    const CUtensorMap *ta, *tb;
+    int row, col, k;
+    __device__ void load(uint8_t* a_dst, uint8_t* b_dst, uint32_t bar) {
+      umma2::tma_load_2d_pair(a_dst, ta, bar, k, row);
+      umma2::tma_load_2d_pair(b_dst, tb, bar, col, k);
+      umma2::tma_load_2d_pair(b_dst + 8192, tb, bar, col + 64, k);
+      k += umma2::BK;
+    }
+  };
+  __device__ Loader loader(int m_blk, int n_blk, int half) const {
+    return Loader{ta, tb, m_blk * 128, n_blk * umma2::BN + half * 128, 0};
+  }
+};
+
 // The GEMM half of the fused all-gather with dedicated pusher CTAs
 // (gemm_bf16_tn_allgather_2sm_push): the pipeline's CTAs write this rank's column block
 // into its own C only (c = own C at column col0) and count each CTA-tile's stored
