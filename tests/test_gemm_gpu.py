@@ -109,6 +109,22 @@ def test_gemm_bf16_row_major_b_on_tensor_cores(session, rt, m, n, k):
     assert np.isfinite(got).all()
 
 
+@pytest.mark.parametrize("tr,kernel", [(True, "gemm_bf16_ta_2sm"), (False, "gemm_bf16_ta_nn_2sm")])
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (200, 304, 72), (8, 8, 8), (1000, 1000, 1000), (2304, 4352, 520)])
+def test_gemm_bf16_transposed_a_on_tensor_cores(session, rt, m, n, k, tr, kernel):
+    """A stored [K, M] (transpose_lhs), B stored [N, K] or [K, N]: M-contiguous A tiles."""
+    a, b = bf16_inputs(m, n, k, seed=m + n + k + 11, b_col_major=tr)
+    at = np.ascontiguousarray(a.T)  # the stored [K, M] operand
+    h = run_op(rt, "gemm", [upload(session, rt.stream, at, DType.BF16), upload(session, rt.stream, b, DType.BF16)],
+               DType.BF16, (m, n), {"transpose_lhs": True, "transpose_rhs": tr})
+    assert h.candidate == kernel
+    got = h.outputs[0].to_f32()
+    rows = np.repeat(np.arange(m), n)
+    cols = np.tile(np.arange(n), m)
+    ref = oracle.gemm_bf16_points(a, b, tr, m, n, k, rows, cols).reshape(m, n)
+    assert max_rel_err(got, ref) <= BF16_TOL, max_rel_err(got, ref)
+
+
 def test_gemm_bf16_row_major_b_full_size(session, rt):
     """8192^3 with B stored [K, N]: sampled points and the column-checksum identity."""
     M = N = K = 8192

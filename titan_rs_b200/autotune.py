@@ -44,8 +44,8 @@ STRATEGY_VERSION = 1
 # tensor-core candidate takes the problem (they are slower by design, and timing them
 # on large problems would spend the tuning budget for nothing).
 CANDIDATES = {
-    ("gemm", "BF16"): (["gemm_bf16_tn_2sm", "gemm_bf16_tn", "gemm_bf16_tn_splitk", "gemm_bf16_nn_2sm"],
-                       ["gemm_bf16_generic"]),
+    ("gemm", "BF16"): (["gemm_bf16_tn_2sm", "gemm_bf16_tn", "gemm_bf16_tn_splitk", "gemm_bf16_nn_2sm",
+                        "gemm_bf16_ta_2sm", "gemm_bf16_ta_nn_2sm"], ["gemm_bf16_generic"]),
     ("gemm", "F32"): (["gemm_f32_tiled"], []),
     ("softmax", "F32"): (["softmax_f32_warp1", "softmax_f32_warp2", "softmax_f32_warp4", "softmax_f32_warp8",
                           "softmax_f32_warp16", "softmax_f32_warp32", "softmax_f32_stream"], []),

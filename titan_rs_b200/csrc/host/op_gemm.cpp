@@ -4,8 +4,10 @@
 //        aligned buffers        -> gemm_bf16_tn_2sm (tcgen05 on CTA pairs, TMA, TMEM) when the
 //                                  output fills the SMs, gemm_bf16_tn (one SM per tile) when it
 //                                  does not, gemm_bf16_tn_splitk when too few tiles exist
-//   BF16, A and B row-major (no transposes), K % 8 == 0, N % 8 == 0, aligned
-//                               -> gemm_bf16_nn_2sm (the same pairs reading B N-contiguous)
+//   BF16, other storage orders (B stored [K, N] and/or A stored [K, M] by transpose_lhs),
+//        contiguous extents % 8 == 0, aligned
+//                               -> gemm_bf16_nn_2sm / gemm_bf16_ta_2sm / gemm_bf16_ta_nn_2sm (the
+//                                  same pairs reading those operands M- or N-contiguous)
 //   BF16, any other layout      -> gemm_bf16_generic (CUDA cores)
 //   F32                         -> gemm_f32_tiled (CUDA cores, bit-exact with the CPU reference)
 #include "../kernels/kernel_configs.h"
@@ -52,23 +54,27 @@ tb_status launch_gemm_bf16_tn_2sm(Session* s, Stream* st, CUdeviceptr a, CUdevic
   return launch_builtin_pairs(s, st, fn, pair_tiles, TB_GEMM_THREADS, TB_GEMM2_SMEM_BYTES, params, "gemm_bf16_tn_2sm");
 }
 
-// B stored [K, N] row-major (no transpose_rhs): CTA pairs reading N-contiguous B tiles
-// (gemm_bf16_nn_2sm), at any size.
-tb_status launch_gemm_bf16_nn_2sm(Session* s, Stream* st, CUdeviceptr a, CUdeviceptr b, CUdeviceptr c, int M, int N,
-                                  int K, long long ldc) {
+// The storage orders other than A [M, K] x B [N, K] on CTA pairs, at any size: an
+// operand stored [K, rows] (A with transpose_lhs, B without transpose_rhs) is read
+// through a tensor map over that storage with {64, 64} boxes and fed to the MMA
+// M- or N-contiguous. `name` is gemm_bf16_nn_2sm, gemm_bf16_ta_2sm or gemm_bf16_ta_nn_2sm.
+tb_status launch_gemm_bf16_layout_2sm(Session* s, Stream* st, const char* name, bool a_km, bool b_kn, CUdeviceptr a,
+                                      CUdeviceptr b, CUdeviceptr c, int M, int N, int K, long long ldc) {
   CUtensorMap ta, tbm;
-  tb_status rc = tmap_bf16_2d(&ta, a, (uint64_t)M, (uint64_t)K, (uint64_t)K, 128, TB_GEMM_BK,
-                              CU_TENSOR_MAP_SWIZZLE_128B);
+  tb_status rc = a_km ? tmap_bf16_2d(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)M, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)
+                      : tmap_bf16_2d(&ta, a, (uint64_t)M, (uint64_t)K, (uint64_t)K, 128, TB_GEMM_BK,
+                                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = tmap_bf16_2d(&tbm, b, (uint64_t)K, (uint64_t)N, (uint64_t)N, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  rc = b_kn ? tmap_bf16_2d(&tbm, b, (uint64_t)K, (uint64_t)N, (uint64_t)N, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)
+            : tmap_bf16_2d(&tbm, b, (uint64_t)N, (uint64_t)K, (uint64_t)K, 128, TB_GEMM_BK, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   CUfunction fn = nullptr;
-  rc = builtin_function(s, "gemm_bf16", "gemm_bf16_nn_2sm", &fn);
+  rc = builtin_function(s, "gemm_bf16", name, &fn);
   if (rc) return rc;
   const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
   CUdeviceptr status = s->status.device;
   void* params[] = {&ta, &tbm, &c, &M, &N, &K, &ldc, &status};
-  return launch_builtin_pairs(s, st, fn, pair_tiles, TB_GEMM_THREADS, TB_GEMM2_SMEM_BYTES, params, "gemm_bf16_nn_2sm");
+  return launch_builtin_pairs(s, st, fn, pair_tiles, TB_GEMM_THREADS, TB_GEMM2_SMEM_BYTES, params, name);
 }
 
 // The unsplit tensor-core GEMM the operator runs by default: the 2-SM kernel once the
@@ -225,9 +231,12 @@ extern "C" tb_status tb_op_gemm(tb_session* session, tb_stream* stream, const tb
     if (!attrs[i].key || (strcmp(attrs[i].key, "transpose_lhs") != 0 && strcmp(attrs[i].key, "transpose_rhs") != 0))
       return contract("CUDA GEMM received unsupported attributes");
   }
-  if (candidate && strcmp(candidate, "gemm_bf16_tn") != 0 && strcmp(candidate, "gemm_bf16_tn_2sm") != 0 &&
-      strcmp(candidate, "gemm_bf16_nn_2sm") != 0 && strcmp(candidate, "gemm_bf16_tn_splitk") != 0 &&
-      strcmp(candidate, "gemm_bf16_generic") != 0 && strcmp(candidate, "gemm_f32_tiled") != 0)
+  static const char* kCandidates[] = {"gemm_bf16_tn",      "gemm_bf16_tn_2sm", "gemm_bf16_nn_2sm",
+                                      "gemm_bf16_ta_2sm",  "gemm_bf16_ta_nn_2sm", "gemm_bf16_tn_splitk",
+                                      "gemm_bf16_generic", "gemm_f32_tiled"};
+  bool known = !candidate;
+  for (const char* k : kCandidates) known = known || strcmp(candidate, k) == 0;
+  if (!known)
     return contract(std::string("unknown GEMM candidate ") + candidate);
   bool tl = false, tr = false;
   for (uint32_t i = 0; i < num_attrs; ++i) {
@@ -267,13 +276,20 @@ extern "C" tb_status tb_op_gemm(tb_session* session, tb_stream* stream, const tb
   CUdeviceptr pa = ba->ptr, pb = bb->ptr, pc = bc->ptr;
   CUfunction fn = nullptr;
   if (dt == TB_BF16) {
-    // B stored [K, N] (no transposes), rows 16-byte aligned: the N-contiguous tensor-core kernel.
-    const bool nn_ok = !tl && !tr && (K % 8) == 0 && (N % 8) == 0 && ((pa | pb | pc) & 15) == 0;
-    const bool want_nn = candidate && strcmp(candidate, "gemm_bf16_nn_2sm") == 0;
-    if (want_nn && !nn_ok)
-      return unsupported("candidate gemm_bf16_nn_2sm needs B stored [K, N], K % 8 == 0, N % 8 == 0, aligned");
-    if (nn_ok && (!candidate || want_nn)) {
-      rc = launch_gemm_bf16_nn_2sm(s, st, pa, pb, pc, M, N, K, (long long)N);
+    // Storage orders other than A [M, K] x B [N, K]: the layout kernels, when every row
+    // the TMA reads starts 16-byte aligned (the contiguous extent of each operand is a
+    // multiple of 8 elements).
+    const char* layout_kernel = !tl && !tr ? "gemm_bf16_nn_2sm" : tl && tr ? "gemm_bf16_ta_2sm"
+                                : tl ? "gemm_bf16_ta_nn_2sm" : nullptr;
+    const bool layout_ok = layout_kernel && ((tl ? M : K) % 8) == 0 && ((tr ? K : N) % 8) == 0 &&
+                           ((pa | pb | pc) & 15) == 0;
+    const bool want_layout = candidate && (strcmp(candidate, "gemm_bf16_nn_2sm") == 0 ||
+                                           strcmp(candidate, "gemm_bf16_ta_2sm") == 0 ||
+                                           strcmp(candidate, "gemm_bf16_ta_nn_2sm") == 0);
+    if (want_layout && (!layout_ok || strcmp(candidate, layout_kernel) != 0))
+      return unsupported(std::string("candidate ") + candidate + " does not take this layout or alignment");
+    if (layout_ok && (!candidate || want_layout)) {
+      rc = launch_gemm_bf16_layout_2sm(s, st, layout_kernel, tl, !tr, pa, pb, pc, M, N, K, (long long)N);
       if (rc) return rc;
       return record_event(s, st, nullptr, out);
     }

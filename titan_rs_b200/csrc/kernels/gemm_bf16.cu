@@ -70,22 +70,29 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
   tb::umma2::run(p, status, kFailGemm2);
 }
 
-// C = A B with B stored [K, N] row-major, on CTA pairs (tensor map over B [K, N] with
-// {64, 64} boxes; A as for gemm_bf16_tn_2sm).
-extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
-    gemm_bf16_nn_2sm(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                     __nv_bfloat16* __restrict__ c, int M, int N, int K, long long ldc, uint32_t* status) {
-  tb::gemm::Gemm2NNPolicy p;
-  p.ta = &tmap_a;
-  p.tb = &tmap_b;
-  p.c = c;
-  p.M = M;
-  p.N = N;
-  p.K = K;
-  p.ldc = ldc;
-  p.vec_ok = (ldc % 8) == 0 && (reinterpret_cast<uintptr_t>(c) & 15) == 0;
-  tb::umma2::run(p, status, kFailGemm2);
-}
+// The other storage orders on CTA pairs (Gemm2LayoutPolicy): an operand stored [K, rows]
+// comes through a tensor map over that storage with {64, 64} boxes.
+//   gemm_bf16_nn_2sm     A [M, K], B [K, N]
+//   gemm_bf16_ta_2sm     A [K, M] (transpose_lhs), B [N, K] (transpose_rhs)
+//   gemm_bf16_ta_nn_2sm  A [K, M] (transpose_lhs), B [K, N]
+#define TB_GEMM2_LAYOUT_ENTRY(name, at, bn)                                                                       \
+  extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)                                                \
+      name(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,                \
+           __nv_bfloat16* __restrict__ c, int M, int N, int K, long long ldc, uint32_t* status) {                 \
+    tb::gemm::Gemm2LayoutPolicy<at, bn> p;                                                                       \
+    p.ta = &tmap_a;                                                                                               \
+    p.tb = &tmap_b;                                                                                               \
+    p.c = c;                                                                                                      \
+    p.M = M;                                                                                                      \
+    p.N = N;                                                                                                      \
+    p.K = K;                                                                                                      \
+    p.ldc = ldc;                                                                                                  \
+    p.vec_ok = (ldc % 8) == 0 && (reinterpret_cast<uintptr_t>(c) & 15) == 0;                                      \
+    tb::umma2::run(p, status, kFailGemm2);                                                                        \
+  }
+TB_GEMM2_LAYOUT_ENTRY(gemm_bf16_nn_2sm, false, true)
+TB_GEMM2_LAYOUT_ENTRY(gemm_bf16_ta_2sm, true, false)
+TB_GEMM2_LAYOUT_ENTRY(gemm_bf16_ta_nn_2sm, true, true)
 
 // gemm_bf16_tn_bias_act on the 2-SM pipeline.
 extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)

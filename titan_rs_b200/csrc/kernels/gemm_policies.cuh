@@ -297,18 +297,30 @@ struct AllGather2Policy : Gemm2Policy {
   }
 };
 
-// Gemm2Policy's product with B stored [K, N] row-major (the reference's default layout):
-// B tiles are N-contiguous, two {64 N, 64 K} boxes per CTA and stage from a tensor map
-// over [K, N]; the MMA reads them MN-major.
-struct Gemm2NNPolicy : Gemm2Policy {
-  static constexpr bool kBMajorMN = true;
+// Gemm2Policy's product for the other storage orders: A stored [K, M] (transpose_lhs,
+// AT) and/or B stored [K, N] (the reference's default, no transpose_rhs, BN). An
+// M- or N-contiguous operand comes as two {64, 64 K} boxes per CTA and stage from a
+// tensor map over its [K, rows] storage; the MMA reads it MN-major.
+template <bool AT, bool BN_>
+struct Gemm2LayoutPolicy : Gemm2Policy {
+  static constexpr bool kAMajorMN = AT;
+  static constexpr bool kBMajorMN = BN_;
   struct Loader {
     const CUtensorMap *ta, *tb;
     int row, col, k;
     __device__ void load(uint8_t* a_dst, uint8_t* b_dst, uint32_t bar) {
-      umma2::tma_load_2d_pair(a_dst, ta, bar, k, row);
-      umma2::tma_load_2d_pair(b_dst, tb, bar, col, k);
-      umma2::tma_load_2d_pair(b_dst + 8192, tb, bar, col + 64, k);
+      if constexpr (AT) {
+        umma2::tma_load_2d_pair(a_dst, ta, bar, row, k);
+        umma2::tma_load_2d_pair(a_dst + 8192, ta, bar, row + 64, k);
+      } else {
+        umma2::tma_load_2d_pair(a_dst, ta, bar, k, row);
+      }
+      if constexpr (BN_) {
+        umma2::tma_load_2d_pair(b_dst, tb, bar, col, k);
+        umma2::tma_load_2d_pair(b_dst + 8192, tb, bar, col + 64, k);
+      } else {
+        umma2::tma_load_2d_pair(b_dst, tb, bar, k, col);
+      }
       k += umma2::BK;
     }
   };

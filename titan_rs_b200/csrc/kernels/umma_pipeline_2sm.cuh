@@ -166,13 +166,14 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t tmem, uint32_t cols) 
 // A policy may add kSideWarps warps after the six pipeline warps (the block has
 // 192 + 32 kSideWarps threads): they run side(i, first_tile, tile_stride, tiles, num_pm,
 // num_n, status, fail_base) beside the pipeline, after init() has set up any barriers
-// they share with the epilogue. kBMajorMN selects N-contiguous B tiles (two 64-column
-// boxes of 64 K-rows per CTA and stage). pair_count() is the number of CTA pairs running the
+// they share with the epilogue. kAMajorMN / kBMajorMN select M- / N-contiguous tiles
+// (two 64-element boxes of 64 K-rows per operand, CTA and stage). pair_count() is the number of CTA pairs running the
 // pipeline (the grid, unless the kernel gives other CTAs another job);
 // tile_stored(t, rank, lane) runs in each epilogue warp after it stored its rows of pair
 // tile t. PolicyBase supplies the defaults.
 struct PolicyBase {
   static constexpr int kSideWarps = 0;
+  static constexpr bool kAMajorMN = false;  // A tiles M-contiguous (A stored [K, M]) instead of K-contiguous
   static constexpr bool kBMajorMN = false;  // B tiles N-contiguous (B stored [K, N]) instead of K-contiguous
   __device__ void init() const {}
   __device__ void side(int, int, int, int, int, int, uint32_t*, uint32_t) const {}
@@ -280,16 +281,17 @@ __device__ __forceinline__ void run(const Policy& p, uint32_t* status, uint32_t 
           }
           tc_fence_after_sync();
           const uint32_t a_addr = stage0 + stage * STAGE_BYTES;
-          const uint64_t a_desc = sdesc_sw128(a_addr, 16, 1024);
-          // B K-major: rows of 64 K, 16 K = 32 bytes; B MN-major: 64-column boxes of 64
-          // K-rows (8 KB apart), 16 K = 16 rows = 2 KB.
+          // K-major operand: rows of 64 K, 16 K = 32 bytes. MN-major operand: 64-element
+          // boxes of 64 K-rows (8 KB apart), 16 K = 16 rows = 2 KB.
+          const uint64_t a_desc = Policy::kAMajorMN ? sdesc_sw128(a_addr, 8192, 1024) : sdesc_sw128(a_addr, 16, 1024);
           const uint64_t b_desc = Policy::kBMajorMN ? sdesc_sw128(a_addr + A_BYTES, 8192, 1024)
                                                     : sdesc_sw128(a_addr + A_BYTES, 16, 1024);
+          constexpr uint32_t a_step = Policy::kAMajorMN ? (2048 >> 4) : 2;
           constexpr uint32_t b_step = Policy::kBMajorMN ? (2048 >> 4) : 2;
-          constexpr uint32_t idesc = Policy::kBMajorMN ? idesc_bf16_f32(2 * BM, BN, true) : IDESC;
+          constexpr uint32_t idesc = idesc_bf16_f32(2 * BM, BN, Policy::kBMajorMN, Policy::kAMajorMN);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)  // 32 bytes of K per 16-element step inside A's 128-byte rows
-            umma_bf16_ss_pair(d_tmem, a_desc + (uint64_t)(k * 2), b_desc + (uint64_t)(k * b_step), idesc,
+          for (int k = 0; k < BK / 16; ++k)
+            umma_bf16_ss_pair(d_tmem, a_desc + (uint64_t)(k * a_step), b_desc + (uint64_t)(k * b_step), idesc,
                               (kb > 0) || (k > 0));
           umma_commit_pair(&bars->empty[stage], 0x3);
           if (++stage == Stages) {
