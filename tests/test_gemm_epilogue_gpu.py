@@ -89,6 +89,25 @@ def test_no_bias_no_activation_equals_plain_gemm_bitwise(session, rt, fused_cand
     np.testing.assert_array_equal(fused.outputs[0].to_numpy(), plain.outputs[0].to_numpy())
 
 
+@pytest.mark.parametrize("tl,tr,kernel", [(False, False, "gemm_bf16_nn_2sm"), (True, True, "gemm_bf16_ta_2sm"),
+                                          (True, False, "gemm_bf16_ta_nn_2sm")])
+@pytest.mark.parametrize("act", ["none", "gelu", "silu"])
+def test_gemm_bias_act_other_storage_orders(session, rt, tl, tr, kernel, act):
+    """A stored [K, M] and/or B stored [K, N]: the layout kernels with the same epilogue."""
+    m, n, k = 264, 520, 1032
+    a, b, bias = _inputs(m, n, k, seed=13)
+    a2, b2 = a.reshape(m, k), b.reshape(n, k)  # the logical A [M, K] and B^T [N, K]
+    a_stored = np.ascontiguousarray(a2.T) if tl else a2
+    b_stored = b2 if tr else np.ascontiguousarray(b2.T)
+    ins = [upload(session, rt.stream, a_stored, DType.BF16), upload(session, rt.stream, b_stored, DType.BF16),
+           upload(session, rt.stream, bias)]
+    h = run_op(rt, "gemm.bias_act", ins, DType.BF16, (m, n),
+               {"transpose_lhs": tl, "transpose_rhs": tr, "activation": act})
+    assert h.candidate == kernel
+    ref = _reference(a, b, bias, m, n, k, act)
+    assert max_rel_err(h.outputs[0].to_f32(), ref) <= BF16_TOL
+
+
 def test_gemm_bias_act_contract(session, rt):
     m, n, k = 64, 128, 64
     a, b, bias = _inputs(m, n, k, seed=9)
@@ -103,6 +122,8 @@ def test_gemm_bias_act_contract(session, rt):
     assert e.phase == "contract" and "F32 [N]" in e.message
     assert "activation" in err([ta, tbb], {"transpose_rhs": True, "activation": "relu"}).message
     assert "unsupported attributes" in err([ta, tbb], {"transpose_rhs": True, "axis": 1}).message
-    e = err([ta, upload(session, rt.stream, b.reshape(k, n), DType.BF16)], {"activation": "gelu"})
-    assert e.status == N.TB_ERR_UNSUPPORTED and "transpose_rhs" in e.message
+    # B stored [K, N] with N % 8 != 0: no tensor-core kernel takes it.
+    b_kn = np.ascontiguousarray(b.reshape(n, k).T[:, :124])
+    e = err([ta, upload(session, rt.stream, b_kn, DType.BF16)], {"activation": "gelu"}, shape=(m, 124))
+    assert e.status == N.TB_ERR_UNSUPPORTED and "multiples of 8" in e.message
     assert "output shape" in err([ta, tbb], {"transpose_rhs": True}, shape=(m, n + 8)).message

@@ -43,8 +43,23 @@ def test_fusion_keeps_what_it_cannot_absorb():
     # A bf16 bias or an untransposed B is left alone.
     assert [n.operator for n in G.compile(mlp_graph(bias_dtype=DType.BF16)).graph.nodes][:3] == \
         ["gemm", "broadcast.add", "gelu"]
-    assert G.compile(mlp_graph(transpose_rhs=False)).graph.nodes[0].operator == "gemm"
     assert G.compile(mlp_graph(act="silu")).graph.nodes[0].attrs["activation"] == "silu"
+
+
+def test_fusion_covers_other_storage_orders_with_aligned_extents():
+    def chain(k, n, attrs):
+        # x[8, k] times W (stored [k, n], or [n, k] with transpose_rhs) -> + b[n] -> gelu
+        w_shape = (n, k) if attrs.get("transpose_rhs") else (k, n)
+        values = {0: spec(DType.BF16, 8, k), 1: spec(DType.BF16, *w_shape), 2: spec(DType.F32, n),
+                  3: spec(DType.BF16, 8, n), 4: spec(DType.BF16, 8, n), 5: spec(DType.BF16, 8, n)}
+        nodes = [G.GraphNode(10, "gemm", [0, 1], [3], attrs), G.GraphNode(11, "broadcast.add", [3, 2], [4]),
+                 G.GraphNode(12, "gelu", [4], [5])]
+        return G.compile(G.Graph([0, 1, 2], [5], values, nodes)).graph.nodes
+    fused = chain(16, 24, {})  # B stored [K, N]: the N-contiguous kernel takes it
+    assert [n.operator for n in fused] == ["gemm.bias_act"] and fused[0].attrs == {"activation": "gelu"}
+    assert [n.operator for n in chain(12, 24, {})] == ["gemm", "broadcast.add", "gelu"]  # K % 8 != 0
+    assert [n.operator for n in chain(16, 20, {})] == ["gemm", "broadcast.add", "gelu"]  # N % 8 != 0 with B [K, N]
+    assert [n.operator for n in chain(16, 20, {"transpose_rhs": True})] == ["gemm.bias_act"]  # B [N, K]: K only
 
 
 def test_dead_code_and_empty_graph():

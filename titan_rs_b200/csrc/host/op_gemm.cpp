@@ -59,7 +59,8 @@ tb_status launch_gemm_bf16_tn_2sm(Session* s, Stream* st, CUdeviceptr a, CUdevic
 // through a tensor map over that storage with {64, 64} boxes and fed to the MMA
 // M- or N-contiguous. `name` is gemm_bf16_nn_2sm, gemm_bf16_ta_2sm or gemm_bf16_ta_nn_2sm.
 tb_status launch_gemm_bf16_layout_2sm(Session* s, Stream* st, const char* name, bool a_km, bool b_kn, CUdeviceptr a,
-                                      CUdeviceptr b, CUdeviceptr c, int M, int N, int K, long long ldc) {
+                                      CUdeviceptr b, CUdeviceptr c, int M, int N, int K, long long ldc,
+                                      CUdeviceptr bias = 0, int act = TB_ACT_NONE) {
   CUtensorMap ta, tbm;
   tb_status rc = a_km ? tmap_bf16_2d(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)M, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)
                       : tmap_bf16_2d(&ta, a, (uint64_t)M, (uint64_t)K, (uint64_t)K, 128, TB_GEMM_BK,
@@ -73,8 +74,17 @@ tb_status launch_gemm_bf16_layout_2sm(Session* s, Stream* st, const char* name, 
   if (rc) return rc;
   const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
   CUdeviceptr status = s->status.device;
-  void* params[] = {&ta, &tbm, &c, &M, &N, &K, &ldc, &status};
+  void* params[] = {&ta, &tbm, &c, &bias, &act, &M, &N, &K, &ldc, &status};
   return launch_builtin_pairs(s, st, fn, pair_tiles, TB_GEMM_THREADS, TB_GEMM2_SMEM_BYTES, params, name);
+}
+
+// The layout kernel for an A/B storage order other than A [M, K] x B [N, K], or null
+// when the order is that one or a TMA row would not start 16-byte aligned.
+static const char* layout_kernel_for(bool tl, bool tr, uint64_t M, uint64_t N, uint64_t K, CUdeviceptr any_ptrs) {
+  const char* name = !tl && !tr ? "gemm_bf16_nn_2sm" : tl && tr ? "gemm_bf16_ta_2sm" : tl ? "gemm_bf16_ta_nn_2sm"
+                                                                                        : nullptr;
+  const bool ok = name && ((tl ? M : K) % 8) == 0 && ((tr ? K : N) % 8) == 0 && (any_ptrs & 15) == 0;
+  return ok ? name : nullptr;
 }
 
 // The unsplit tensor-core GEMM the operator runs by default: the 2-SM kernel once the
@@ -279,10 +289,8 @@ extern "C" tb_status tb_op_gemm(tb_session* session, tb_stream* stream, const tb
     // Storage orders other than A [M, K] x B [N, K]: the layout kernels, when every row
     // the TMA reads starts 16-byte aligned (the contiguous extent of each operand is a
     // multiple of 8 elements).
-    const char* layout_kernel = !tl && !tr ? "gemm_bf16_nn_2sm" : tl && tr ? "gemm_bf16_ta_2sm"
-                                : tl ? "gemm_bf16_ta_nn_2sm" : nullptr;
-    const bool layout_ok = layout_kernel && ((tl ? M : K) % 8) == 0 && ((tr ? K : N) % 8) == 0 &&
-                           ((pa | pb | pc) & 15) == 0;
+    const char* layout_kernel = layout_kernel_for(tl, tr, (uint64_t)M, (uint64_t)N, (uint64_t)K, pa | pb | pc);
+    const bool layout_ok = layout_kernel != nullptr;
     const bool want_layout = candidate && (strcmp(candidate, "gemm_bf16_nn_2sm") == 0 ||
                                            strcmp(candidate, "gemm_bf16_ta_2sm") == 0 ||
                                            strcmp(candidate, "gemm_bf16_ta_nn_2sm") == 0);
@@ -355,7 +363,9 @@ extern "C" tb_status tb_op_gemm_bias_act(tb_session* session, tb_stream* stream,
     if (!key) return contract("gemm.bias_act received an unnamed attribute");
     if (strcmp(key, "candidate") == 0) {
       if (!attrs[i].str || (strcmp(attrs[i].str, "gemm_bf16_tn_bias_act") != 0 &&
-                            strcmp(attrs[i].str, "gemm_bf16_tn_bias_act_2sm") != 0))
+                            strcmp(attrs[i].str, "gemm_bf16_tn_bias_act_2sm") != 0 &&
+                            strcmp(attrs[i].str, "gemm_bf16_nn_2sm") != 0 && strcmp(attrs[i].str, "gemm_bf16_ta_2sm") != 0 &&
+                            strcmp(attrs[i].str, "gemm_bf16_ta_nn_2sm") != 0))
         return contract(std::string("unknown gemm.bias_act candidate ") + (attrs[i].str ? attrs[i].str : "(null)"));
       candidate = attrs[i].str;
     } else if (strcmp(key, "activation") == 0) {
@@ -394,12 +404,27 @@ extern "C" tb_status tb_op_gemm_bias_act(tb_session* session, tb_stream* stream,
       (rc = tensor_buffer(s, output, "gemm output", &bc)) || (bias && (rc = tensor_buffer(s, bias, "gemm bias", &bbias))))
     return rc;
   const CUdeviceptr pa = ba->ptr, pb = bb->ptr, pc = bc->ptr;
-  if (tl || !tr || k % 8 != 0 || ((pa | pb | pc) & 15) != 0)
+  int M = (int)m, N = (int)n, K = (int)k;
+  if (tl || !tr) {
+    // Other storage orders: the layout kernels, whose epilogue takes the bias and activation.
+    const char* lk = layout_kernel_for(tl, tr, m, n, k, pa | pb | pc);
+    if (!lk || (candidate && strcmp(candidate, lk) != 0))
+      return unsupported("gemm.bias_act needs operand rows whose contiguous extents are multiples of 8 and 16-byte "
+                         "aligned tensors");
+    rc = activate(s);
+    if (rc) return rc;
+    rc = launch_gemm_bf16_layout_2sm(s, st, lk, tl, !tr, pa, pb, pc, M, N, K, (long long)N, bbias ? bbias->ptr : 0,
+                                     act);
+    if (rc) return rc;
+    return record_event(s, st, nullptr, out);
+  }
+  if (k % 8 != 0 || ((pa | pb | pc) & 15) != 0)
     return unsupported("gemm.bias_act needs A [M,K] row-major, B stored [N,K] (transpose_rhs), K % 8 == 0 and "
                        "16-byte aligned tensors");
+  if (candidate && strcmp(candidate, "gemm_bf16_tn_bias_act") != 0 && strcmp(candidate, "gemm_bf16_tn_bias_act_2sm") != 0)
+    return unsupported(std::string("candidate ") + candidate + " does not take this layout");
   rc = activate(s);
   if (rc) return rc;
-  int M = (int)m, N = (int)n, K = (int)k;
   // Same choice as the plain GEMM: CTA pairs once the output fills the SMs.
   const long long tiles = (long long)((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN);
   const bool pairs = candidate ? strcmp(candidate, "gemm_bf16_tn_bias_act_2sm") == 0

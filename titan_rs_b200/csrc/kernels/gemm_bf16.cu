@@ -71,15 +71,19 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
 }
 
 // The other storage orders on CTA pairs (Gemm2LayoutPolicy): an operand stored [K, rows]
-// comes through a tensor map over that storage with {64, 64} boxes.
+// comes through a tensor map over that storage with {64, 64} boxes. C = act(A B + bias)
+// as in gemm_bf16_tn_bias_act (bias null and act none for the plain product).
 //   gemm_bf16_nn_2sm     A [M, K], B [K, N]
 //   gemm_bf16_ta_2sm     A [K, M] (transpose_lhs), B [N, K] (transpose_rhs)
 //   gemm_bf16_ta_nn_2sm  A [K, M] (transpose_lhs), B [K, N]
 #define TB_GEMM2_LAYOUT_ENTRY(name, at, bn)                                                                       \
   extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)                                                \
       name(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,                \
-           __nv_bfloat16* __restrict__ c, int M, int N, int K, long long ldc, uint32_t* status) {                 \
+           __nv_bfloat16* __restrict__ c, const float* __restrict__ bias, int act, int M, int N, int K,           \
+           long long ldc, uint32_t* status) {                                                                     \
     tb::gemm::Gemm2LayoutPolicy<at, bn> p;                                                                       \
+    p.bias = bias;                                                                                                \
+    p.act = act;                                                                                                  \
     p.ta = &tmap_a;                                                                                               \
     p.tb = &tmap_b;                                                                                               \
     p.c = c;                                                                                                      \
