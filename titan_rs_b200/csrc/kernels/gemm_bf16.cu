@@ -153,13 +153,7 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
                            const __grid_constant__ tb::gemm::RankOutputs outs,
                            const __grid_constant__ tb::RankSignals sig, int ranks, int self, uint32_t epoch, int M,
                            int N, int K, long long ldc, long long col0, uint32_t* status) {
-  __shared__ int entry_ok;
-  if (threadIdx.x == 0) {
-    if (blockIdx.x == 0) tb::signal_peers(sig, ranks, self, epoch, false);
-    entry_ok = tb::wait_peers(sig, ranks, self, epoch, false) ? 1 : 0;
-    if (!entry_ok) tb::report_status(status, kFailAllGather | 0x0501);
-  }
-  __syncthreads();
+  const bool entry_ok = tb::call_entry(sig, ranks, self, epoch, status, kFailAllGather | 0x0501);
   if (entry_ok) {
     tb::gemm::AllGatherPolicy p;
     p.ta = &tmap_a;
@@ -178,19 +172,9 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)
     p.col0 = col0;
     tb::umma::run(p, status, kFailAllGather);
   }
-  if (threadIdx.x == 0) {
-    // Every epilogue thread fenced its stores (AllGatherPolicy::finish) before run()'s
-    // final __syncthreads.
-    __threadfence_system();
-    tb::SignalBlock* mine = sig.block[self];
-    if (atomicAdd(&mine->arrivals, 1u) == gridDim.x - 1) {
-      mine->arrivals = 0;  // the next call starts after this kernel (stream order)
-      if (entry_ok) {
-        tb::signal_peers(sig, ranks, self, epoch, true);
-        if (!tb::wait_peers(sig, ranks, self, epoch, true)) tb::report_status(status, kFailAllGather | 0x0502);
-      }
-    }
-  }
+  // Every epilogue thread fenced its stores (AllGatherPolicy::finish) before run()'s
+  // final __syncthreads (a CTA whose entry failed stored nothing).
+  tb::call_exit(sig, ranks, self, epoch, entry_ok, status, kFailAllGather | 0x0502);
 }
 
 // The fused GEMM + all-gather on CTA pairs (clusters of 2 along x, 128-row boxes for A
@@ -202,13 +186,7 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM2_AG_THREADS, 1)
                                const __grid_constant__ tb::gemm::RankOutputs outs,
                                const __grid_constant__ tb::RankSignals sig, int ranks, int self, uint32_t epoch, int M,
                                int N, int K, long long ldc, long long col0, uint32_t* status) {
-  __shared__ int entry_ok;
-  if (threadIdx.x == 0) {
-    if (blockIdx.x == 0) tb::signal_peers(sig, ranks, self, epoch, false);
-    entry_ok = tb::wait_peers(sig, ranks, self, epoch, false) ? 1 : 0;
-    if (!entry_ok) tb::report_status(status, kFailAllGather | 0x0501);
-  }
-  __syncthreads();
+  const bool entry_ok = tb::call_entry(sig, ranks, self, epoch, status, kFailAllGather | 0x0501);
   tb::gemm::AllGather2Policy p;
   p.ta = &tmap_a;
   p.tb = &tmap_b;
@@ -224,19 +202,9 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM2_AG_THREADS, 1)
   p.col0 = col0;
   p.enabled = entry_ok != 0;
   tb::umma2::run<tb::gemm::AllGather2Policy, TB_GEMM2_AG_STAGES>(p, status, kFailAllGather2);
-  if (threadIdx.x == 0) {
-    // Every push-warp thread fenced its stores (AllGather2Policy::side) before run()'s
-    // final cluster barrier.
-    __threadfence_system();
-    tb::SignalBlock* mine = sig.block[self];
-    if (atomicAdd(&mine->arrivals, 1u) == gridDim.x - 1) {
-      mine->arrivals = 0;  // the next call starts after this kernel (stream order)
-      if (entry_ok) {
-        tb::signal_peers(sig, ranks, self, epoch, true);
-        if (!tb::wait_peers(sig, ranks, self, epoch, true)) tb::report_status(status, kFailAllGather | 0x0502);
-      }
-    }
-  }
+  // Every push-warp thread fenced its stores (AllGather2Policy::side) before run()'s
+  // final cluster barrier.
+  tb::call_exit(sig, ranks, self, epoch, entry_ok, status, kFailAllGather | 0x0502);
 }
 
 // Pusher role of gemm_bf16_tn_allgather_2sm_push: the grid's pusher CTAs split the
@@ -291,13 +259,7 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM2_PUSH_THREADS, 1)
                                     const __grid_constant__ tb::RankSignals sig, int ranks, int self, uint32_t epoch,
                                     int M, int N, int K, long long ldc, long long col0, uint32_t* ready,
                                     int gemm_pairs, uint32_t* status) {
-  __shared__ int entry_ok;
-  if (threadIdx.x == 0) {
-    if (blockIdx.x == 0) tb::signal_peers(sig, ranks, self, epoch, false);
-    entry_ok = tb::wait_peers(sig, ranks, self, epoch, false) ? 1 : 0;
-    if (!entry_ok) tb::report_status(status, kFailAllGather | 0x0501);
-  }
-  __syncthreads();
+  const bool entry_ok = tb::call_entry(sig, ranks, self, epoch, status, kFailAllGather | 0x0501);
   const int num_pm = (M + 255) / 256, num_n = (N + 255) / 256;
   if ((int)blockIdx.x < 2 * gemm_pairs) {
     tb::gemm::AllGatherLocalPolicy p;
@@ -319,16 +281,7 @@ extern "C" __global__ void __launch_bounds__(TB_GEMM2_PUSH_THREADS, 1)
   }
   __threadfence_system();  // this thread's peer stores, before the exit handshake
   __syncthreads();
-  if (threadIdx.x == 0) {
-    tb::SignalBlock* mine = sig.block[self];
-    if (atomicAdd(&mine->arrivals, 1u) == gridDim.x - 1) {
-      mine->arrivals = 0;  // the next call starts after this kernel (stream order)
-      if (entry_ok) {
-        tb::signal_peers(sig, ranks, self, epoch, true);
-        if (!tb::wait_peers(sig, ranks, self, epoch, true)) tb::report_status(status, kFailAllGather | 0x0502);
-      }
-    }
-  }
+  tb::call_exit(sig, ranks, self, epoch, entry_ok, status, kFailAllGather | 0x0502);
 }
 
 extern "C" __global__ void __launch_bounds__(TB_GEMM_THREADS, 1)

@@ -70,4 +70,40 @@ __device__ __forceinline__ bool wait_peers(const RankSignals& s, int ranks, int 
   return true;
 }
 
+// Entry of call `epoch` of a fused kernel, for every CTA: CTA 0 announces the epoch in
+// every peer's signal block; each CTA's thread 0 waits until every peer has announced
+// it (so every peer is done with its previous output). Returns, to all threads of the
+// CTA, whether the wait succeeded (a failure records `fail_code`). Contains a
+// __syncthreads.
+__device__ __forceinline__ bool call_entry(const RankSignals& sig, int ranks, int self, uint32_t epoch,
+                                           uint32_t* status, uint32_t fail_code) {
+  __shared__ int entered;
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) signal_peers(sig, ranks, self, epoch, false);
+    entered = wait_peers(sig, ranks, self, epoch, false) ? 1 : 0;
+    if (!entered) report_status(status, fail_code);
+  }
+  __syncthreads();
+  return entered != 0;
+}
+
+// Exit, called by every thread of every CTA after all of the CTA's threads have fenced
+// their peer stores system-wide and met at a barrier: thread 0 counts the CTA in, and
+// the last CTA of the grid tells every peer that this rank's stores have landed and
+// waits until every peer has said the same (a failure records `fail_code`), so the
+// kernel ends only when this rank's output is whole.
+__device__ __forceinline__ void call_exit(const RankSignals& sig, int ranks, int self, uint32_t epoch, bool entered,
+                                          uint32_t* status, uint32_t fail_code) {
+  if (threadIdx.x != 0) return;
+  __threadfence_system();
+  SignalBlock* mine = sig.block[self];
+  if (atomicAdd(&mine->arrivals, 1u) == gridDim.x - 1) {
+    mine->arrivals = 0;  // the next call starts after this kernel (stream order)
+    if (entered) {
+      signal_peers(sig, ranks, self, epoch, true);
+      if (!wait_peers(sig, ranks, self, epoch, true)) report_status(status, fail_code);
+    }
+  }
+}
+
 }  // namespace tb
