@@ -408,9 +408,11 @@ extern "C" tb_status tb_op_gemm_bias_act(tb_session* session, tb_stream* stream,
   if (tl || !tr) {
     // Other storage orders: the layout kernels, whose epilogue takes the bias and activation.
     const char* lk = layout_kernel_for(tl, tr, m, n, k, pa | pb | pc);
-    if (!lk || (candidate && strcmp(candidate, lk) != 0))
+    if (!lk)
       return unsupported("gemm.bias_act needs operand rows whose contiguous extents are multiples of 8 and 16-byte "
                          "aligned tensors");
+    if (candidate && strcmp(candidate, lk) != 0)
+      return unsupported(std::string("candidate ") + candidate + " does not take this layout");
     rc = activate(s);
     if (rc) return rc;
     rc = launch_gemm_bf16_layout_2sm(s, st, lk, tl, !tr, pa, pb, pc, M, N, K, (long long)N, bbias ? bbias->ptr : 0,
