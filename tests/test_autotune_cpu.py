@@ -151,3 +151,24 @@ def test_non_finite_output_is_a_correctness_rejection(tmp_path):
     res = A.Autotuner(tmp_path / "t").tune(key(), ["a", "b"], [], fp.run, fp.read, fp.time_ns, 1e-2)
     assert res.entry.candidate == "a"
     assert [(r.candidate, r.stage) for r in res.rejections] == [("b", "correctness")]
+
+
+def test_every_registered_candidate_is_a_native_kernel_its_operator_accepts():
+    """The registry names only kernels that exist in the sm_100a sources and that the
+    operator's C entry recognises as a candidate (a typo would surface as a rejection
+    at tuning time, never as a wrong kernel)."""
+    import pathlib
+    import re
+    root = pathlib.Path(A.__file__).resolve().parent / "csrc"
+    kernels = "\n".join(f.read_text() for f in (root / "kernels").glob("*.cu"))
+    # Entries a macro builds by token pasting (e.g. softmax_f32_warp##NV), by invocation.
+    pasted = set()
+    for macro, param, prefix in re.findall(r"#define (\w+)\((\w+)\)[^\n]*\\\n[^\n]*?(\w+)##\2", kernels):
+        pasted.update(prefix + arg for arg in re.findall(rf"^{macro}\((\w+)\)", kernels, re.M))
+    host = {"gemm": "op_gemm.cpp", "gemm.bias_act": "op_gemm.cpp", "softmax": "op_softmax.cpp",
+            "scaled_dot_product_attention": "op_sdpa.cpp", "conv2d": "op_conv2d.cpp"}
+    for (op, _dtype), (primary, fallback) in A.CANDIDATES.items():
+        source = (root / "host" / host[op]).read_text()
+        for name in primary + fallback:
+            assert f'"{name}"' in source, (op, name)
+            assert name in pasted or re.search(rf"\b{re.escape(name)}\s*[(,]", kernels), (op, name)
