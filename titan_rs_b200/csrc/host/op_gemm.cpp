@@ -103,9 +103,9 @@ tb_status launch_gemm_bf16_default(Session* s, Stream* st, CUdeviceptr a, CUdevi
 // ranks synchronise through their signal blocks (signals[i] = rank i's) for call `epoch`.
 // Pusher CTAs for the fused all-gather: TITAN_B200_ALLGATHER_PUSHERS (an even count, 0 =
 // none) if set; else none below four ranks (the tensor work of the SMs they would take
-// outweighs the stores), 16 from four ranks (measured best of 0, 16, 32 at 4 ranks:
-// 3354, 3931, 3819 TFLOP/s for C3) and 32 from eight, where each rank receives 112 MB
-// against 0.1 ms of compute.
+// outweighs the stores: 2428 against 2281 TFLOP/s with 16 at 2 ranks for C3), 16 from
+// four ranks (best of 0, 16, 32 at 4 ranks: 3354, 3931, 3819) and 32 from eight (3917
+// against 3860 with 16), where each rank receives 112 MB against 0.1 ms of compute.
 static int allgather_pushers(int ranks) {
   if (const char* e = getenv("TITAN_B200_ALLGATHER_PUSHERS")) {
     const int v = atoi(e);
