@@ -19,6 +19,11 @@
 //               `acc_full` barriers.
 //   warps 2..5  epilogue of each CTA's 128 rows; after draining an accumulator they
 //               arrive on the even CTA's `acc_empty` (4 local + 4 remote arrivals).
+//   warps 6..   optional side warps of a policy (the fused all-gather's push warps).
+// Problems plug in as policies (run() below): the tile space, per-tile load and store
+// cursors (index arithmetic once per tile, never per k-block: the single producer lane
+// is on the critical path), M- or N-contiguous operand tiles (A stored [K, M], B
+// stored [K, N]), and a pair count for kernels whose other CTAs do another job.
 // Every mbarrier wait is bounded; both CTAs always reach the two cluster barriers
 // (after barrier initialisation, and before TMEM is freed), so a failure in one role
 // ends as a status code, not a hang.
