@@ -96,3 +96,15 @@ def test_embedded_cubins_are_sm100a_elf():
         assert blob[:4] == b"\x7fELF"
     with pytest.raises(KeyError):
         N.builtin_cubin("no_such_module")
+
+
+def test_attributes_cross_the_abi_as_ints_and_strings():
+    """OpRequest attributes become TbAttr: bools and ints in `value`, strings in `str`, and
+    floats (the attention `scale`) as their shortest round-tripping decimal string."""
+    from titan_rs_b200.runtime import _attrs
+    arr, n, keep = _attrs({"transpose_rhs": True, "axis": -1, "layout": "NHWC", "scale": 0.08838834764831845})
+    assert n == 4
+    got = {arr[i].key.decode(): (arr[i].value, arr[i].str) for i in range(n)}
+    assert got["transpose_rhs"] == (1, None) and got["axis"] == (-1, None)
+    assert got["layout"] == (0, b"NHWC")
+    assert got["scale"][1] == b"0.08838834764831845" and float(got["scale"][1]) == 0.08838834764831845
