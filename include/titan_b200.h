@@ -52,7 +52,8 @@ typedef enum tb_status {
   TB_ERR_UNSUPPORTED = 5,        /* valid request this backend does not implement */
   TB_ERR_TIMEOUT = 6,            /* a bounded device-side wait gave up; context stays usable */
   TB_ERR_NCCL = 7,               /* an NCCL call failed or the communicator was aborted */
-  TB_ERR_OUT_OF_MEMORY = 8
+  TB_ERR_OUT_OF_MEMORY = 8,
+  TB_ERR_IO = 9                  /* a file-system call failed; the detail names the path and errno */
 } tb_status;
 
 /* titan_types::DType order (projects/titan-types/src/lib.rs:42-49). */
@@ -349,6 +350,46 @@ tb_status tb_fill_normal(void* dst, uint32_t dtype, size_t count, uint64_t seed,
                          int threads);
 tb_status tb_fill_uniform(void* dst, uint32_t dtype, size_t count, uint64_t seed, double low, double high,
                           int threads);
+
+/* ---------------- Tuning store (`.tune` version 2) ---------------- */
+
+/* The autotuner's persistent cache (projects/titan-autotune/src/lib.rs:46-82, Autotuner::
+ * open/get/insert/flush) with the persistence rules of docs/architecture/autotune-v2.md:9.
+ * The file is `# titan.tune version=2` followed by one canonical JSON line per record,
+ * {"checksum": C, "entry": E, "key": K}: K and E are JSON objects, C is the lowercase hex
+ * SHA-256 of the canonical {"entry": E, "key": K}. Canonical JSON is byte-identical to
+ * Python's json.dumps(obj, sort_keys=True, separators=(",", ":")). Keys are exact: two
+ * keys are the same decision when their canonical texts are equal. Lines that are not
+ * JSON, lack a field or fail their checksum are skipped and counted; a file without the
+ * version-2 header contributes no records. The store does not interpret key or entry
+ * fields, so records written by hosts with other fields survive a flush.
+ *
+ * Text outputs: *len receives the length without the terminating NUL; the text and a
+ * NUL are copied when cap > *len, otherwise the call fails with TB_ERR_INVALID and the
+ * caller retries with a larger buffer. A store handle may be used from several threads. */
+typedef struct tb_tune_store tb_tune_store;
+
+/* Opens the store at `path` (the full file name, e.g. "kernels.tune") and reads it
+ * without locking; a missing or unreadable file gives an empty store. */
+tb_status tb_tune_open(const char* path, tb_tune_store** out);
+void tb_tune_release(tb_tune_store* store);
+/* Records `entry_json` for `key_json` in memory (both JSON objects, any formatting). */
+tb_status tb_tune_insert(tb_tune_store* store, const char* key_json, const char* entry_json);
+/* Canonical entry for `key_json`; *len = 0 when the key has no record. */
+tb_status tb_tune_get(const tb_tune_store* store, const char* key_json, char* entry, size_t cap, size_t* len);
+/* Takes an exclusive flock on `<path>.lock`, merges with the records on disk (the
+ * store's own records win), writes `<path>.tmp`, fsyncs it, renames it over `path` and
+ * fsyncs the directory. The store then holds the merged records. TB_ERR_IO on failure. */
+tb_status tb_tune_flush(tb_tune_store* store);
+/* Number of records, and lines the last read of the file (open or flush) skipped. */
+tb_status tb_tune_stats(const tb_tune_store* store, size_t* records, size_t* ignored_lines);
+/* Record `index` (0 <= index < records) in canonical key order. */
+tb_status tb_tune_record(const tb_tune_store* store, size_t index, char* key, size_t key_cap, size_t* key_len,
+                         char* entry, size_t entry_cap, size_t* entry_len);
+/* Canonical form of any JSON text (the form records are keyed and checksummed in). */
+tb_status tb_tune_canonical_json(const char* json, char* out, size_t cap, size_t* len);
+/* SHA-256 (FIPS 180-4) of `len` bytes as 64 lowercase hex digits and a NUL in out[65]. */
+tb_status tb_sha256_hex(const void* data, size_t len, char* out);
 
 #ifdef __cplusplus
 }

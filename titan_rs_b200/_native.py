@@ -20,6 +20,7 @@ TB_ERR_UNSUPPORTED = 5
 TB_ERR_TIMEOUT = 6
 TB_ERR_NCCL = 7
 TB_ERR_OUT_OF_MEMORY = 8
+TB_ERR_IO = 9
 
 TB_F32, TB_F16, TB_BF16, TB_I32, TB_I64 = 0, 1, 2, 3, 4
 TB_ARG_BUFFER, TB_ARG_SCALAR, TB_ARG_SHAPE = 0, 1, 2
@@ -137,6 +138,16 @@ _SIGNATURES = {
     "tb_gemm_bf16_splitk_noalloc": (_S, [_U64, _P, _P, _P, _S, _S, _S, _S]),
     "tb_fill_normal": (_S, [_P, _U32, _SZ, _U64, ctypes.c_double, ctypes.c_double, _S]),
     "tb_fill_uniform": (_S, [_P, _U32, _SZ, _U64, ctypes.c_double, ctypes.c_double, _S]),
+    "tb_tune_open": (_S, [ctypes.c_char_p, _PP]),
+    "tb_tune_release": (None, [_P]),
+    "tb_tune_insert": (_S, [_P, ctypes.c_char_p, ctypes.c_char_p]),
+    "tb_tune_get": (_S, [_P, ctypes.c_char_p, ctypes.c_char_p, _SZ, ctypes.POINTER(_SZ)]),
+    "tb_tune_flush": (_S, [_P]),
+    "tb_tune_stats": (_S, [_P, ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]),
+    "tb_tune_record": (_S, [_P, _SZ, ctypes.c_char_p, _SZ, ctypes.POINTER(_SZ), ctypes.c_char_p, _SZ,
+                            ctypes.POINTER(_SZ)]),
+    "tb_tune_canonical_json": (_S, [ctypes.c_char_p, ctypes.c_char_p, _SZ, ctypes.POINTER(_SZ)]),
+    "tb_sha256_hex": (_S, [ctypes.c_char_p, _SZ, ctypes.c_char_p]),
 }
 
 EXPORTED = tuple(_SIGNATURES)
@@ -178,3 +189,81 @@ def builtin_cubin(module: str) -> bytes:
 def last_error() -> tuple[str, str]:
     L = lib()
     return L.tb_last_error_operation().decode(), L.tb_last_error_detail().decode()
+
+
+def _text_out(call, *args):
+    """Runs a tb_* call whose last three arguments are (out, cap, len); grows the buffer
+    until the text fits. Returns the text, or None when *len is 0."""
+    cap = 512
+    n = ctypes.c_size_t(0)
+    while True:
+        buf = ctypes.create_string_buffer(cap)
+        status = call(*args, buf, cap, ctypes.byref(n))
+        if status == TB_OK:
+            return buf.raw[:n.value].decode() if n.value else None
+        if n.value < cap:
+            raise ValueError(last_error()[1])
+        cap = n.value + 1
+
+
+def sha256_hex(data: bytes) -> str:
+    out = ctypes.create_string_buffer(65)
+    if lib().tb_sha256_hex(data, len(data), out) != TB_OK:
+        raise ValueError(last_error()[1])
+    return out.value.decode()
+
+
+def canonical_json(text: str) -> str:
+    return _text_out(lib().tb_tune_canonical_json, text.encode())
+
+
+class TuneStore:
+    """Owner of a native `.tune` version 2 store (tb_tune_*); records are canonical JSON text."""
+
+    def __init__(self, path):
+        self._lib = lib()
+        h = ctypes.c_void_p(0)
+        if self._lib.tb_tune_open(str(path).encode(), ctypes.byref(h)) != TB_OK:
+            raise ValueError(last_error()[1])
+        self._h = h
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            self._lib.tb_tune_release(h)
+            self._h = None
+
+    def insert(self, key_json: str, entry_json: str) -> None:
+        if self._lib.tb_tune_insert(self._h, key_json.encode(), entry_json.encode()) != TB_OK:
+            raise ValueError(last_error()[1])
+
+    def get(self, key_json: str):
+        return _text_out(self._lib.tb_tune_get, self._h, key_json.encode())
+
+    def flush(self) -> None:
+        status = self._lib.tb_tune_flush(self._h)
+        if status == TB_ERR_IO:
+            raise OSError(last_error()[1])
+        if status != TB_OK:
+            raise ValueError(last_error()[1])
+
+    def stats(self) -> tuple[int, int]:
+        records, ignored = ctypes.c_size_t(0), ctypes.c_size_t(0)
+        self._lib.tb_tune_stats(self._h, ctypes.byref(records), ctypes.byref(ignored))
+        return records.value, ignored.value
+
+    def records(self) -> list[tuple[str, str]]:
+        out = []
+        kcap = ecap = 512
+        kn, en = ctypes.c_size_t(0), ctypes.c_size_t(0)
+        for i in range(self.stats()[0]):
+            while True:
+                kb, eb = ctypes.create_string_buffer(kcap), ctypes.create_string_buffer(ecap)
+                status = self._lib.tb_tune_record(self._h, i, kb, kcap, ctypes.byref(kn), eb, ecap, ctypes.byref(en))
+                if status == TB_OK:
+                    out.append((kb.raw[:kn.value].decode(), eb.raw[:en.value].decode()))
+                    break
+                if kn.value < kcap and en.value < ecap:
+                    raise ValueError(last_error()[1])
+                kcap, ecap = max(kcap, kn.value + 1), max(ecap, en.value + 1)
+        return out

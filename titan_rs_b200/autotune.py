@@ -19,22 +19,22 @@ docs/architecture/autotune-v2.md that the reference specifies but does not imple
   a SHA-256 checksum of its record; writes take an exclusive lock, merge with the
   records on disk, go to a temporary file that is fsynced, are renamed atomically,
   and fsync the directory. Malformed, tampered or old-version lines are ignored.
-  A cache hit neither compiles nor benchmarks.
+  A cache hit neither compiles nor benchmarks. The store itself is native
+  (tb_tune_* in libtitan_b200.so), so Rust and C hosts share the same file.
 """
 from __future__ import annotations
 
-import errno
-import fcntl
 import hashlib
 import json
 import math
-import os
 import pathlib
 import time
 from dataclasses import asdict, dataclass, field
 from typing import Callable, Iterable, Optional, Sequence
 
 import numpy as np
+
+from . import _native
 
 HEADER = "# titan.tune version=2"
 STRATEGY_VERSION = 1
@@ -131,10 +131,6 @@ def _canonical(obj) -> str:
     return json.dumps(obj, sort_keys=True, separators=(",", ":"))
 
 
-def _checksum(record: dict) -> str:
-    return hashlib.sha256(_canonical(record).encode()).hexdigest()
-
-
 def _percentile(sorted_vals: Sequence[float], q: float) -> float:
     """Nearest-rank percentile of an ascending sequence."""
     k = max(0, min(len(sorted_vals) - 1, math.ceil(q * len(sorted_vals)) - 1))
@@ -149,91 +145,54 @@ def select(measured: Sequence[Measured]) -> Measured:
 
 
 class Autotuner:
-    """Version 2 `.tune` store (Autotuner, lib.rs:47-82)."""
+    """Version 2 `.tune` store (Autotuner, lib.rs:46-82) over the native store (tb_tune_*).
+
+    The native library owns the file: parsing, checksums, canonical JSON, the lock, the
+    merge and the atomic write. This class maps its canonical records to `TuneKey` and
+    `TuneEntry`; a record that passed the native checks but whose fields these classes do
+    not take is counted in `ignored_lines` and left in the file for the host that wrote it."""
 
     def __init__(self, path):
         p = pathlib.Path(path)
         self.path = p.with_suffix(".tune")
-        self.entries: dict[TuneKey, TuneEntry] = {}
-        self.ignored_lines = 0
         self.tunings = 0  # candidate searches run by this object (a cache hit runs none)
-        self._load()
+        self._store = _native.TuneStore(self.path)
+        self._foreign = 0
+        self.entries: dict[TuneKey, TuneEntry] = self._decode()
 
     @classmethod
     def open(cls, path) -> "Autotuner":
         return cls(path)
 
     # ---- persistence ----
-    def _parse(self, text: str) -> dict:
+    @property
+    def ignored_lines(self) -> int:
+        """Lines the last read of the file skipped, plus records of another schema."""
+        return self._store.stats()[1] + self._foreign
+
+    def _decode(self) -> dict:
         entries: dict[TuneKey, TuneEntry] = {}
-        lines = text.splitlines()
-        if not lines or lines[0].strip() != HEADER:
-            self.ignored_lines += len(lines)
-            return entries
-        for line in lines[1:]:
-            if not line.strip():
-                continue
+        self._foreign = 0
+        for k, e in self._store.records():
             try:
-                rec = json.loads(line)
-                body = {"key": rec["key"], "entry": rec["entry"]}
-                if rec.get("checksum") != _checksum(body):
-                    raise ValueError("checksum mismatch")
-                entries[TuneKey(**rec["key"])] = TuneEntry(**rec["entry"])
-            except (ValueError, KeyError, TypeError):
-                self.ignored_lines += 1
+                entries[TuneKey(**json.loads(k))] = TuneEntry(**json.loads(e))
+            except TypeError:
+                self._foreign += 1
         return entries
-
-    def _read_disk(self) -> dict:
-        try:
-            return self._parse(self.path.read_text())
-        except FileNotFoundError:
-            return {}
-        except (OSError, UnicodeDecodeError):
-            return {}
-
-    def _load(self) -> None:
-        self.entries = self._read_disk()
 
     def get(self, key: TuneKey) -> Optional[TuneEntry]:
         return self.entries.get(key)
 
     def insert(self, key: TuneKey, entry: TuneEntry) -> None:
         self.entries[key] = entry
+        self._store.insert(_canonical(asdict(key)), _canonical(asdict(entry)))
 
     def flush(self) -> None:
         """Merges with the file under an exclusive lock and replaces it atomically."""
-        self.path.parent.mkdir(parents=True, exist_ok=True)
-        lock_path = self.path.with_suffix(".tune.lock")
-        with open(lock_path, "a+") as lock:
-            fcntl.flock(lock.fileno(), fcntl.LOCK_EX)
-            try:
-                merged = self._read_disk()
-                merged.update(self.entries)  # this process's decisions win
-                self.entries = merged
-                rows = []
-                for k, e in merged.items():
-                    body = {"key": asdict(k), "entry": asdict(e)}
-                    rows.append(_canonical({**body, "checksum": _checksum(body)}))
-                rows.sort()
-                tmp = self.path.with_suffix(".tune.tmp")
-                with open(tmp, "w") as f:
-                    f.write(HEADER + "\n")
-                    for r in rows:
-                        f.write(r + "\n")
-                    f.flush()
-                    os.fsync(f.fileno())
-                os.replace(tmp, self.path)
-                try:
-                    dfd = os.open(self.path.parent, os.O_RDONLY)
-                    try:
-                        os.fsync(dfd)
-                    finally:
-                        os.close(dfd)
-                except OSError as e:  # some filesystems refuse fsync on directories
-                    if e.errno not in (errno.EINVAL, errno.EBADF):
-                        raise
-            finally:
-                fcntl.flock(lock.fileno(), fcntl.LOCK_UN)
+        for k, e in self.entries.items():
+            self._store.insert(_canonical(asdict(k)), _canonical(asdict(e)))
+        self._store.flush()
+        self.entries = self._decode()
 
     # ---- search ----
     def tune(self, key: TuneKey, primary: Sequence[str], fallback: Sequence[str],
