@@ -106,6 +106,9 @@ extern "C" tb_status tb_op_conv2d(tb_session* session, tb_stream* stream, const 
   if (!is_contiguous(input) || !is_contiguous(weight) || (bias && !is_contiguous(bias)))
     return contract("CUDA Conv2D requires contiguous NCHW input, OIHW weight, and optional rank-1 bias");
   if (output->rank != 4 || !is_contiguous(output)) return contract("CUDA Conv2D requires a contiguous rank-4 output");
+  // Conv2dF32Descriptor::validate (titan-backend-cuda/src/lib.rs:815-825): every input and weight extent first.
+  for (int i = 0; i < 4; ++i)
+    if (input->shape[i] == 0 || weight->shape[i] == 0) return contract("CUDA Conv2D dimensions must be non-zero");
   int64_t sh, sw, ph, pw, dh, dw, groups;
   tb_status rc;
   if ((rc = int_attr(attrs, num_attrs, "stride_h", nullptr, &sh)) ||

@@ -397,6 +397,8 @@ tb_status tb_session_fingerprint(const tb_session* session, tb_fingerprint* out)
 tb_status tb_allocate(tb_session* session, size_t bytes, size_t alignment, tb_buffer** out) {
   Session* s = reinterpret_cast<Session*>(session);
   if (!s || !out) return set_error(TB_ERR_INVALID, "allocate", "null argument");
+  // As CudaContext::allocate (titan-backend-cuda/src/lib.rs:122-125).
+  if (bytes == 0) return set_error(TB_ERR_INVALID, "allocate", "zero-byte CUDA allocations are unsupported");
   // cuMemAlloc returns 256-byte aligned memory; larger alignments are not offered.
   if (alignment > 256 || (alignment & (alignment - 1)) != 0)
     return set_error(TB_ERR_INVALID, "allocate", "alignment must be a power of two no larger than 256");
@@ -404,7 +406,7 @@ tb_status tb_allocate(tb_session* session, size_t bytes, size_t alignment, tb_bu
   if (st) return st;
   const DriverApi* d = driver();
   CUdeviceptr p = 0;
-  if (bytes > 0) TB_CU("allocate", d->cuMemAlloc_v2(&p, bytes));
+  TB_CU("allocate", d->cuMemAlloc_v2(&p, bytes));
   Buffer* b = new Buffer();
   b->session = s;
   b->identity = g_next_identity.fetch_add(1);
