@@ -97,7 +97,8 @@ tb_status tb_session_fingerprint(const tb_session* session, tb_fingerprint* out)
 
 /* ---------------- DeviceSession (titan-hal/src/lib.rs:200-230) ---------------- */
 
-/* DeviceSession::allocate (titan-backend-cuda/src/lib.rs:1255-1262). */
+/* DeviceSession::allocate (titan-backend-cuda/src/lib.rs:1255-1262); zero bytes are refused
+ * ("zero-byte CUDA allocations are unsupported", :122-125). */
 tb_status tb_allocate(tb_session* session, size_t bytes, size_t alignment, tb_buffer** out);
 /* Registers device memory owned by someone else (e.g. a torch tensor) as a
  * non-owning buffer of this session. No reference counterpart; it lets callers
@@ -232,7 +233,8 @@ typedef struct tb_attr {
 } tb_attr;
 
 /* "softmax" — execute_cuda_softmax (titan-runtime/src/lib.rs:1504-1596):
- * last axis only, F32, contiguous, output the same shape. */
+ * last axis only, F32 (or BF16 in and out, fp32 arithmetic), contiguous, output the
+ * same shape. */
 tb_status tb_op_softmax(tb_session* session, tb_stream* stream, const tb_tensor* input, const tb_tensor* output,
                         const tb_attr* attrs, uint32_t num_attrs, tb_event** out);
 
@@ -260,6 +262,17 @@ tb_status tb_op_sdpa(tb_session* session, tb_stream* stream, const tb_tensor* q,
 tb_status tb_op_conv2d(tb_session* session, tb_stream* stream, const tb_tensor* input, const tb_tensor* weight,
                        const tb_tensor* bias, const tb_tensor* output, const tb_attr* attrs, uint32_t num_attrs,
                        tb_event** out);
+
+/* Runtime::execute (titan-runtime/src/lib.rs:1171-1256) by operator name, for a host
+ * that routes OpRequests without naming each entry: "softmax" (1 input),
+ * "gemm" (2), "scaled_dot_product_attention" (3), "conv2d" (2 or 3: input, weight,
+ * optional bias) and "gemm.bias_act" (2 or 3: A, B, optional bias) go to the entries
+ * above with the same checks. Another name is TB_ERR_UNSUPPORTED ("does not
+ * implement"); a wrong input count is TB_ERR_INVALID with the operator's arity message.
+ * Both report operation "contract", as ExecutionError{phase: "contract"} does. */
+tb_status tb_execute(tb_session* session, tb_stream* stream, const char* op, const tb_tensor* inputs,
+                     uint32_t num_inputs, const tb_tensor* output, const tb_attr* attrs, uint32_t num_attrs,
+                     tb_event** out);
 
 /* Which kernel the last successful op on this thread launched (the candidate id
  * the runtime reports in ExecutionHandle, titan-runtime/src/lib.rs:2403). */
@@ -317,10 +330,13 @@ tb_status tb_op_gemm_sharded(tb_comm* comm, tb_stream* stream, const tb_tensor* 
  * (titan-runtime/src/lib.rs:955-989) with broadcast.add of a per-column bias and its
  * gelu (:625-640, erf by Abramowitz & Stegun 7.1.26) or silu (:3064) operators:
  * the bias is added and the activation applied to the fp32 accumulator, which is
- * rounded to bf16 once. A BF16 [M,K] row-major, B BF16 stored [N,K] (attribute
- * transpose_rhs = 1), C BF16 [M,N]; bias F32 [N] or NULL; attributes activation
- * ("none" | "gelu" | "silu"), transpose_lhs (0), transpose_rhs, candidate
- * ("gemm_bf16_tn_bias_act"). Other layouts are TB_ERR_UNSUPPORTED. */
+ * rounded to bf16 once. A BF16 [M,K] (or stored [K,M] with transpose_lhs = 1), B BF16
+ * [K,N] (or stored [N,K] with transpose_rhs = 1), C BF16 [M,N]; bias F32 [N] or NULL;
+ * attributes activation ("none" | "gelu" | "silu"), transpose_lhs, transpose_rhs,
+ * candidate ("gemm_bf16_tn_bias_act[_2sm]" for A row-major and B stored [N,K];
+ * "gemm_bf16_nn_2sm", "gemm_bf16_ta_2sm", "gemm_bf16_ta_nn_2sm" for the other storage
+ * orders). The contiguous extents of A and B must be multiples of 8 and the tensors
+ * 16-byte aligned, else TB_ERR_UNSUPPORTED. */
 tb_status tb_op_gemm_bias_act(tb_session* session, tb_stream* stream, const tb_tensor* lhs, const tb_tensor* rhs,
                               const tb_tensor* bias, const tb_tensor* output, const tb_attr* attrs,
                               uint32_t num_attrs, tb_event** out);

@@ -108,3 +108,24 @@ def test_attributes_cross_the_abi_as_ints_and_strings():
     assert got["transpose_rhs"] == (1, None) and got["axis"] == (-1, None)
     assert got["layout"] == (0, b"NHWC")
     assert got["scale"][1] == b"0.08838834764831845" and float(got["scale"][1]) == 0.08838834764831845
+
+
+def test_execute_routes_by_operator_name_before_touching_a_session():
+    """tb_execute mirrors Runtime::execute (projects/titan-runtime/src/lib.rs:1171-1256): an
+    operator without a route and a wrong input count fail in the contract phase."""
+    L = N.lib()
+    t = (N.Tensor * 4)()
+    out = N.Tensor()
+    ev = ctypes.c_void_p(0)
+
+    def call(op, n):
+        return L.tb_execute(None, None, op, t, n, ctypes.byref(out), None, 0, ctypes.byref(ev))
+
+    assert call(b"layer_norm", 1) == N.TB_ERR_UNSUPPORTED
+    assert N.last_error() == ("contract", "operator layer_norm is not on the B200 hot path (does not implement)")
+    for op, bad, keyword in [(b"softmax", 2, "exactly one input"), (b"gemm", 3, "exactly two"),
+                             (b"scaled_dot_product_attention", 2, "exactly three"), (b"conv2d", 1, "optional bias"),
+                             (b"conv2d", 4, "optional bias"), (b"gemm.bias_act", 4, "optional bias")]:
+        assert call(op, bad) == N.TB_ERR_INVALID, op
+        operation, detail = N.last_error()
+        assert operation == "contract" and keyword in detail, (op, detail)

@@ -231,30 +231,14 @@ class Runtime:
                                Event(self.session, ev))
 
     def _launch(self, name: str, request: OpRequest, output: TensorHandle, attrs_dict: dict) -> int:
+        """One request through tb_execute, the native Runtime::execute router."""
         spec = request.outputs[0]
         out_c = c_tensor(output.buffer, spec.dtype, spec.shape, spec.resolved_strides())
-        ins = [t.c_tensor() for t in request.inputs]
+        ins = (N.Tensor * len(request.inputs))(*[t.c_tensor() for t in request.inputs])
         attrs, nattrs, _keep = _attrs(attrs_dict)
         ev = ctypes.c_void_p(0)
-        L = N.lib()
-        fn = getattr(L, _OPS[name])
-        if name == "softmax":
-            st = fn(self.session.ptr, self.stream.ptr, ctypes.byref(ins[0]), ctypes.byref(out_c), attrs, nattrs,
-                    ctypes.byref(ev))
-        elif name == "gemm":
-            st = fn(self.session.ptr, self.stream.ptr, ctypes.byref(ins[0]), ctypes.byref(ins[1]), ctypes.byref(out_c),
-                    attrs, nattrs, ctypes.byref(ev))
-        elif name == "scaled_dot_product_attention":
-            st = fn(self.session.ptr, self.stream.ptr, ctypes.byref(ins[0]), ctypes.byref(ins[1]),
-                    ctypes.byref(ins[2]), ctypes.byref(out_c), attrs, nattrs, ctypes.byref(ev))
-        elif name == "gemm.bias_act":
-            bias = ctypes.byref(ins[2]) if len(ins) > 2 else None
-            st = fn(self.session.ptr, self.stream.ptr, ctypes.byref(ins[0]), ctypes.byref(ins[1]), bias,
-                    ctypes.byref(out_c), attrs, nattrs, ctypes.byref(ev))
-        else:
-            bias = ctypes.byref(ins[2]) if len(ins) > 2 else None
-            st = fn(self.session.ptr, self.stream.ptr, ctypes.byref(ins[0]), ctypes.byref(ins[1]), bias,
-                    ctypes.byref(out_c), attrs, nattrs, ctypes.byref(ev))
+        st = N.lib().tb_execute(self.session.ptr, self.stream.ptr, name.encode(), ins, len(request.inputs),
+                                ctypes.byref(out_c), attrs, nattrs, ctypes.byref(ev))
         if st != N.TB_OK:
             op, detail = N.last_error()
             raise ExecutionError(name, op or "launch", detail, st)
