@@ -171,4 +171,5 @@ def test_every_registered_candidate_is_a_native_kernel_its_operator_accepts():
         source = (root / "host" / host[op]).read_text()
         for name in primary + fallback:
             assert f'"{name}"' in source, (op, name)
-            assert name in pasted or re.search(rf"\b{re.escape(name)}\s*[(,]", kernels), (op, name)
+            for kernel in A.COMPOSED.get(name, (name,)):
+                assert kernel in pasted or re.search(rf"\b{re.escape(kernel)}\s*[(,]", kernels), (op, name, kernel)

@@ -14,6 +14,7 @@ import pytest
 
 import oracle
 import titan_rs_b200 as tb
+from titan_rs_b200 import _native as N
 from titan_rs_b200.kernel_abi import DType
 
 from gpu_util import max_rel_err, run_op, upload
@@ -159,6 +160,28 @@ def test_gemm_bf16_row_major_b_and_transposed_a(session, rt):
     assert max_rel_err(h.outputs[0].to_f32(), ref) <= BF16_TOL
 
 
+@pytest.mark.parametrize("tl,tr,m,n,k", [
+    (False, True, 300, 500, 1001),   # K % 8 != 0: no operand row starts 16-byte aligned
+    (False, False, 257, 333, 515),   # B row-major [K, N] with N % 8 != 0
+    (True, True, 333, 520, 777),     # A stored [K, M] with M % 8 != 0
+    (True, False, 129, 130, 1023),   # both stored transposed, all extents ragged
+])
+def test_gemm_bf16_staged_for_storage_the_tma_cannot_describe(session, rt, tl, tr, m, n, k):
+    """Operands are copied K-major with K rounded up to 8 (zero columns), then the
+    tensor-core GEMM runs; the CUDA-core kernel is the cross-check."""
+    a = tb.fill_normal(m * k, seed=m + k, dtype=DType.BF16).reshape((k, m) if tl else (m, k))
+    b = tb.fill_normal(n * k, seed=n + k, std=1.0 / math.sqrt(k), dtype=DType.BF16).reshape((n, k) if tr else (k, n))
+    ta, tbb = upload(session, rt.stream, a, DType.BF16), upload(session, rt.stream, b, DType.BF16)
+    attrs = {"transpose_lhs": tl, "transpose_rhs": tr}
+    h = run_op(rt, "gemm", [ta, tbb], DType.BF16, (m, n), attrs)
+    assert h.candidate == "gemm_bf16_staged"
+    got = h.outputs[0].to_f32()
+    ref = oracle.gemm(tb.bf16_bits_to_f32(a).reshape(a.shape), tb.bf16_bits_to_f32(b).reshape(b.shape), tl, tr)
+    assert max_rel_err(got, ref) <= BF16_TOL
+    generic = run_op(rt, "gemm", [ta, tbb], DType.BF16, (m, n), {**attrs, "candidate": "gemm_bf16_generic"})
+    assert max_rel_err(got, generic.outputs[0].to_f32()) <= BF16_TOL
+
+
 @pytest.mark.parametrize("candidate", [None, "gemm_bf16_tn_2sm"])
 def test_gemm_bf16_full_c3_config(session, rt, candidate):
     """C3: 8192^3, A N(0,1), B column-major N(0,1/8192), seed 2. Sampled points against the
@@ -252,5 +275,13 @@ def test_gemm_candidate_attribute(session, rt):
                                                                      "candidate": "gemm_bf16_generic"})
     assert generic.candidate == "gemm_bf16_generic"
     assert max_rel_err(forced.outputs[0].to_f32(), generic.outputs[0].to_f32()) <= BF16_TOL
+    staged = run_op(rt, "gemm", [ta, tbb], DType.BF16, (256, 512), {"transpose_rhs": True,
+                                                                    "candidate": "gemm_bf16_staged"})
+    assert staged.candidate == "gemm_bf16_staged"
+    assert max_rel_err(forced.outputs[0].to_f32(), staged.outputs[0].to_f32()) <= BF16_TOL
     with pytest.raises(tb.ExecutionError, match="unknown GEMM candidate"):
         run_op(rt, "gemm", [ta, tbb], DType.BF16, (256, 512), {"transpose_rhs": True, "candidate": "nope"})
+    x = upload(session, rt.stream, np.ones((8, 8), np.float32))
+    with pytest.raises(tb.ExecutionError, match="does not take F32") as e:
+        run_op(rt, "gemm", [x, x], DType.F32, (8, 8), {"candidate": "gemm_bf16_tn"})
+    assert e.value.status == N.TB_ERR_UNSUPPORTED

@@ -40,12 +40,13 @@ HEADER = "# titan.tune version=2"
 STRATEGY_VERSION = 1
 
 # Registered kernels per operator and input dtype, in preference order: the first
-# capable one is the correctness baseline. CUDA-core fallbacks are only tried when no
+# capable one is the correctness baseline. Fallbacks are only tried when no direct
 # tensor-core candidate takes the problem (they are slower by design, and timing them
-# on large problems would spend the tuning budget for nothing).
+# on large problems would spend the tuning budget for nothing): the staged GEMM (operands
+# copied K-major, then the tensor cores) and the CUDA-core kernels.
 CANDIDATES = {
     ("gemm", "BF16"): (["gemm_bf16_tn_2sm", "gemm_bf16_tn", "gemm_bf16_tn_splitk", "gemm_bf16_nn_2sm",
-                        "gemm_bf16_ta_2sm", "gemm_bf16_ta_nn_2sm"], ["gemm_bf16_generic"]),
+                        "gemm_bf16_ta_2sm", "gemm_bf16_ta_nn_2sm"], ["gemm_bf16_staged", "gemm_bf16_generic"]),
     ("gemm", "F32"): (["gemm_f32_tiled"], []),
     ("softmax", "F32"): (["softmax_f32_warp1", "softmax_f32_warp2", "softmax_f32_warp4", "softmax_f32_warp8",
                           "softmax_f32_warp16", "softmax_f32_warp32", "softmax_f32_stream"], []),
@@ -56,6 +57,11 @@ CANDIDATES = {
     ("conv2d", "F32"): (["conv2d_f32"], []),
     ("gemm.bias_act", "BF16"): (["gemm_bf16_tn_bias_act_2sm", "gemm_bf16_tn_bias_act", "gemm_bf16_nn_2sm",
                                  "gemm_bf16_ta_2sm", "gemm_bf16_ta_nn_2sm"], []),
+}
+
+# Candidates that are a sequence of launches rather than one kernel, with their kernels.
+COMPOSED = {
+    "gemm_bf16_staged": ("stage_bf16_k_major_rows", "stage_bf16_k_major_cols", "gemm_bf16_tn_2sm", "gemm_bf16_tn"),
 }
 
 # Correctness bar against the baseline candidate: |got - ref| <= tol * max|ref|.

@@ -125,6 +125,8 @@ tb_status consume_device_status(Session* s);
 
 // Counts kernel launches made by this thread (the bench's gpu_launches figure).
 void note_launch(const char* candidate);
+// Names the candidate an operator ran when it took several launches (no launch counted).
+void note_candidate(const char* candidate);
 
 // Embedded cubins (generated at build time).
 struct EmbeddedCubin {

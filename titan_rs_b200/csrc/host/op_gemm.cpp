@@ -8,9 +8,13 @@
 //        contiguous extents % 8 == 0, aligned
 //                               -> gemm_bf16_nn_2sm / gemm_bf16_ta_2sm / gemm_bf16_ta_nn_2sm (the
 //                                  same pairs reading those operands M- or N-contiguous)
-//   BF16, any other layout      -> gemm_bf16_generic (CUDA cores)
+//   BF16, any other layout      -> gemm_bf16_staged (the operands the TMA cannot read copied
+//                                  K-major with K rounded up to 8, then the kernels above) from
+//                                  2^24 multiply-adds, gemm_bf16_generic (CUDA cores) below
 //   F32                         -> gemm_f32_tiled (CUDA cores, bit-exact with the CPU reference)
 #include "../kernels/kernel_configs.h"
+#include <algorithm>
+
 #include "ops_common.hpp"
 
 namespace tb {
@@ -96,6 +100,55 @@ tb_status launch_gemm_bf16_default(Session* s, Stream* st, CUdeviceptr a, CUdevi
   const long long tiles = (long long)((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN);
   if (M >= 256 && tiles >= s->sm_count) return launch_gemm_bf16_tn_2sm(s, st, a, b, c, M, N, K, ldc);
   return launch_gemm_bf16_tn(s, st, a, b, c, M, N, K, ldc);
+}
+
+// K-major [rows, kp] copy of a [rows, k] bf16 operand whose element (r, c) is at
+// src[r * s_r + c * s_c] (one of the strides is 1), zero in columns k..kp-1.
+static tb_status launch_stage_bf16(Session* s, Stream* st, CUdeviceptr src, CUdeviceptr dst, int rows, int k, int kp,
+                                   long long s_r, long long s_c) {
+  CUfunction fn = nullptr;
+  tb_status rc;
+  if (s_c == 1) {
+    rc = builtin_function(s, "layout", "stage_bf16_k_major_rows", &fn);
+    if (rc) return rc;
+    const unsigned gx = (unsigned)std::min((kp + 255) / 256, 16);
+    const unsigned gy = (unsigned)std::min<long long>({(long long)rows, std::max(1LL, s->sm_count * 16LL / gx), 65535LL});
+    void* params[] = {&src, &dst, &rows, &k, &kp, &s_r};
+    return launch_builtin(s, st, fn, gx, gy, 1, 256, 0, params, "stage_bf16_k_major_rows");
+  }
+  if (s_r != 1) return contract("staged GEMM operand has no unit stride");
+  rc = builtin_function(s, "layout", "stage_bf16_k_major_cols", &fn);
+  if (rc) return rc;
+  const long long tiles = (long long)((kp + 31) / 32) * ((rows + 31) / 32);
+  const unsigned grid = (unsigned)std::min<long long>(tiles, s->sm_count * 8LL);
+  void* params[] = {&src, &dst, &rows, &k, &kp, &s_c};
+  return launch_builtin(s, st, fn, grid, 1, 1, 256, 0, params, "stage_bf16_k_major_cols");
+}
+
+// op(A) (M x K, strides as0/as1) times op(B) (K x N, strides bs0/bs1) for storage the TMA
+// cannot describe: each operand that is not already K-major with 16-byte aligned rows
+// is staged K-major, K rounded up to 8, in the stream's scratch; the tensor-core GEMM
+// then runs on the copies (an operand that needs no copy is read in place, which
+// happens only when K % 8 == 0, so both agree on the padded K).
+static tb_status launch_gemm_bf16_staged(Session* s, Stream* st, CUdeviceptr a, long long as0, long long as1,
+                                         CUdeviceptr b, long long bs0, long long bs1, CUdeviceptr c, int M, int N,
+                                         int K) {
+  const int kp = (K + 7) / 8 * 8;
+  const bool stage_a = !(as1 == 1 && K % 8 == 0 && (a & 15) == 0);
+  const bool stage_b = !(bs0 == 1 && K % 8 == 0 && (b & 15) == 0);
+  const size_t a_span = stage_a ? ((size_t)M * kp * 2 + 255) & ~(size_t)255 : 0;
+  const size_t b_span = stage_b ? (size_t)N * kp * 2 : 0;
+  CUdeviceptr ws = 0;
+  tb_status rc = TB_OK;
+  if (a_span + b_span) rc = stream_scratch(s, st, a_span + b_span, &ws);
+  if (rc) return rc;
+  const CUdeviceptr ka = stage_a ? ws : a, kb = stage_b ? ws + a_span : b;
+  if ((stage_a && (rc = launch_stage_bf16(s, st, a, ka, M, K, kp, as0, as1))) ||
+      (stage_b && (rc = launch_stage_bf16(s, st, b, kb, N, K, kp, bs1, bs0))) ||
+      (rc = launch_gemm_bf16_default(s, st, ka, kb, c, M, N, kp, (long long)N)))
+    return rc;
+  note_candidate("gemm_bf16_staged");
+  return TB_OK;
 }
 
 // Fused N-sharded GEMM + all-gather: this rank's [M, N] column block of the row-major
@@ -243,7 +296,7 @@ extern "C" tb_status tb_op_gemm(tb_session* session, tb_stream* stream, const tb
   }
   static const char* kCandidates[] = {"gemm_bf16_tn",      "gemm_bf16_tn_2sm", "gemm_bf16_nn_2sm",
                                       "gemm_bf16_ta_2sm",  "gemm_bf16_ta_nn_2sm", "gemm_bf16_tn_splitk",
-                                      "gemm_bf16_generic", "gemm_f32_tiled"};
+                                      "gemm_bf16_staged",  "gemm_bf16_generic", "gemm_f32_tiled"};
   bool known = !candidate;
   for (const char* k : kCandidates) known = known || strcmp(candidate, k) == 0;
   if (!known)
@@ -302,6 +355,16 @@ extern "C" tb_status tb_op_gemm(tb_session* session, tb_stream* stream, const tb
       return record_event(s, st, nullptr, out);
     }
     const bool tma_ok = !tl && tr && (K % 8) == 0 && ((pa | pb | pc) & 15) == 0;
+    // Any other storage goes through staged K-major copies once the product is large
+    // enough for the tensor cores to repay the two copies (2^24 multiply-adds).
+    const bool want_staged = candidate && strcmp(candidate, "gemm_bf16_staged") == 0;
+    const bool staged_ok = (pc & 15) == 0;
+    if (want_staged && !staged_ok) return unsupported("candidate gemm_bf16_staged needs a 16-byte aligned output");
+    if (want_staged || (!candidate && !tma_ok && staged_ok && (uint64_t)M * N * K >= (1ull << 24))) {
+      rc = launch_gemm_bf16_staged(s, st, pa, as0, as1, pb, bs0, bs1, pc, M, N, K);
+      if (rc) return rc;
+      return record_event(s, st, nullptr, out);
+    }
     const bool want_generic = candidate && strcmp(candidate, "gemm_bf16_generic") == 0;
     if (candidate && !tma_ok && !want_generic)
       return unsupported(std::string("candidate ") + candidate + " does not take this layout or alignment");
@@ -335,6 +398,8 @@ extern "C" tb_status tb_op_gemm(tb_session* session, tb_stream* stream, const tb
       rc = launch_builtin(s, st, fn, (unsigned)grid, 1, 1, 256, 0, params, "gemm_bf16_generic");
     }
   } else {
+    if (candidate && strcmp(candidate, "gemm_f32_tiled") != 0)
+      return unsupported(std::string("candidate ") + candidate + " does not take F32");
     rc = builtin_function(s, "compat", "gemm_f32_tiled", &fn);
     if (rc) return rc;
     void* params[] = {&pa, &pb, &pc, &M, &N, &K, &as0, &as1, &bs0, &bs1};

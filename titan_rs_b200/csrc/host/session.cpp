@@ -51,6 +51,8 @@ void note_launch(const char* candidate) {
   ++g_launches;
 }
 
+void note_candidate(const char* candidate) { g_candidate = candidate ? candidate : ""; }
+
 // ---------------------------------------------------------------- driver
 namespace {
 std::once_flag g_driver_once;
