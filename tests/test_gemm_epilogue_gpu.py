@@ -9,7 +9,6 @@ import pytest
 
 import oracle
 import titan_rs_b200 as tb
-from titan_rs_b200 import _native as N
 from titan_rs_b200.kernel_abi import DType
 
 from gpu_util import max_rel_err, run_op, upload
@@ -122,8 +121,23 @@ def test_gemm_bias_act_contract(session, rt):
     assert e.phase == "contract" and "F32 [N]" in e.message
     assert "activation" in err([ta, tbb], {"transpose_rhs": True, "activation": "relu"}).message
     assert "unsupported attributes" in err([ta, tbb], {"transpose_rhs": True, "axis": 1}).message
-    # B stored [K, N] with N % 8 != 0: no tensor-core kernel takes it.
-    b_kn = np.ascontiguousarray(b.reshape(n, k).T[:, :124])
-    e = err([ta, upload(session, rt.stream, b_kn, DType.BF16)], {"activation": "gelu"}, shape=(m, 124))
-    assert e.status == N.TB_ERR_UNSUPPORTED and "multiples of 8" in e.message
     assert "output shape" in err([ta, tbb], {"transpose_rhs": True}, shape=(m, n + 8)).message
+
+
+@pytest.mark.parametrize("tl,tr,m,n,k", [(False, False, 264, 124, 1032),   # B stored [K, N], N % 8 != 0
+                                         (False, True, 300, 520, 1001),    # K % 8 != 0
+                                         (True, False, 261, 136, 520)])    # A stored [K, M], M % 8 != 0
+@pytest.mark.parametrize("act", ["gelu", "silu"])
+def test_gemm_bias_act_staged_for_storage_the_tma_cannot_describe(session, rt, tl, tr, m, n, k, act):
+    """Operands copied K-major with K rounded up to 8, then the tn bias/activation epilogue."""
+    a, b, bias = _inputs(m, n, k, seed=m + n + k + 1)
+    a2, b2 = a.reshape(m, k), b.reshape(n, k)
+    a_stored = np.ascontiguousarray(a2.T) if tl else a2
+    b_stored = b2 if tr else np.ascontiguousarray(b2.T)
+    ins = [upload(session, rt.stream, a_stored, DType.BF16), upload(session, rt.stream, b_stored, DType.BF16),
+           upload(session, rt.stream, bias)]
+    h = run_op(rt, "gemm.bias_act", ins, DType.BF16, (m, n),
+               {"transpose_lhs": tl, "transpose_rhs": tr, "activation": act})
+    assert h.candidate == "gemm_bf16_staged"
+    ref = _reference(a, b, bias, m, n, k, act)
+    assert max_rel_err(h.outputs[0].to_f32(), ref) <= BF16_TOL

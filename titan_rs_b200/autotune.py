@@ -56,12 +56,13 @@ CANDIDATES = {
     ("conv2d", "BF16"): (["conv2d_fprop_bf16_nhwc_2sm", "conv2d_fprop_bf16_nhwc"], ["conv2d_bf16_nhwc_generic"]),
     ("conv2d", "F32"): (["conv2d_f32"], []),
     ("gemm.bias_act", "BF16"): (["gemm_bf16_tn_bias_act_2sm", "gemm_bf16_tn_bias_act", "gemm_bf16_nn_2sm",
-                                 "gemm_bf16_ta_2sm", "gemm_bf16_ta_nn_2sm"], []),
+                                 "gemm_bf16_ta_2sm", "gemm_bf16_ta_nn_2sm"], ["gemm_bf16_staged"]),
 }
 
 # Candidates that are a sequence of launches rather than one kernel, with their kernels.
 COMPOSED = {
-    "gemm_bf16_staged": ("stage_bf16_k_major_rows", "stage_bf16_k_major_cols", "gemm_bf16_tn_2sm", "gemm_bf16_tn"),
+    "gemm_bf16_staged": ("stage_bf16_k_major_rows", "stage_bf16_k_major_cols", "gemm_bf16_tn_2sm", "gemm_bf16_tn",
+                         "gemm_bf16_tn_bias_act_2sm", "gemm_bf16_tn_bias_act"),
 }
 
 # Correctness bar against the baseline candidate: |got - ref| <= tol * max|ref|.

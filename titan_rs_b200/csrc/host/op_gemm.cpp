@@ -130,9 +130,40 @@ static tb_status launch_stage_bf16(Session* s, Stream* st, CUdeviceptr src, CUde
 // is staged K-major, K rounded up to 8, in the stream's scratch; the tensor-core GEMM
 // then runs on the copies (an operand that needs no copy is read in place, which
 // happens only when K % 8 == 0, so both agree on the padded K).
+// C = act(A B^T + bias) on the K-major operands A [M, K] and B [N, K] (gemm_bf16_tn_bias_act
+// and its CTA-pair form, chosen as for the plain GEMM unless `candidate` names one).
+static tb_status launch_gemm_bf16_tn_bias_act(Session* s, Stream* st, CUdeviceptr pa, CUdeviceptr pb, CUdeviceptr pc,
+                                              int M, int N, int K, CUdeviceptr pbias, int act, const char* candidate) {
+  const long long tiles = (long long)((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN);
+  const bool pairs = candidate ? strcmp(candidate, "gemm_bf16_tn_bias_act_2sm") == 0
+                               : (M >= 256 && tiles >= s->sm_count);
+  const uint32_t box_rows_b = pairs ? 128 : TB_GEMM_BN;
+  CUtensorMap ta, tbm;
+  tb_status rc;
+  if ((rc = tmap_bf16_2d(&ta, pa, (uint64_t)M, (uint64_t)K, (uint64_t)K, TB_GEMM_BM, TB_GEMM_BK,
+                         CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = tmap_bf16_2d(&tbm, pb, (uint64_t)N, (uint64_t)K, (uint64_t)K, box_rows_b, TB_GEMM_BK,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  CUfunction fn = nullptr;
+  const char* name = pairs ? "gemm_bf16_tn_bias_act_2sm" : "gemm_bf16_tn_bias_act";
+  rc = builtin_function(s, "gemm_bf16", name, &fn);
+  if (rc) return rc;
+  CUdeviceptr c = pc, status = s->status.device;
+  long long ldc = N;
+  void* params[] = {&ta, &tbm, &c, &pbias, &act, &M, &N, &K, &ldc, &status};
+  if (pairs) {
+    const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+    return launch_builtin_pairs(s, st, fn, pair_tiles, TB_GEMM_THREADS, TB_GEMM2_SMEM_BYTES, params, name);
+  }
+  const unsigned grid = (unsigned)(tiles < s->sm_count ? tiles : s->sm_count);
+  return launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_SMEM_BYTES, params, name);
+}
+
 static tb_status launch_gemm_bf16_staged(Session* s, Stream* st, CUdeviceptr a, long long as0, long long as1,
                                          CUdeviceptr b, long long bs0, long long bs1, CUdeviceptr c, int M, int N,
-                                         int K) {
+                                         int K, bool epilogue = false, CUdeviceptr bias = 0,
+                                         int act = TB_ACT_NONE) {
   const int kp = (K + 7) / 8 * 8;
   const bool stage_a = !(as1 == 1 && K % 8 == 0 && (a & 15) == 0);
   const bool stage_b = !(bs0 == 1 && K % 8 == 0 && (b & 15) == 0);
@@ -145,7 +176,8 @@ static tb_status launch_gemm_bf16_staged(Session* s, Stream* st, CUdeviceptr a, 
   const CUdeviceptr ka = stage_a ? ws : a, kb = stage_b ? ws + a_span : b;
   if ((stage_a && (rc = launch_stage_bf16(s, st, a, ka, M, K, kp, as0, as1))) ||
       (stage_b && (rc = launch_stage_bf16(s, st, b, kb, N, K, kp, bs1, bs0))) ||
-      (rc = launch_gemm_bf16_default(s, st, ka, kb, c, M, N, kp, (long long)N)))
+      (rc = epilogue ? launch_gemm_bf16_tn_bias_act(s, st, ka, kb, c, M, N, kp, bias, act, nullptr)
+                     : launch_gemm_bf16_default(s, st, ka, kb, c, M, N, kp, (long long)N)))
     return rc;
   note_candidate("gemm_bf16_staged");
   return TB_OK;
@@ -430,7 +462,8 @@ extern "C" tb_status tb_op_gemm_bias_act(tb_session* session, tb_stream* stream,
       if (!attrs[i].str || (strcmp(attrs[i].str, "gemm_bf16_tn_bias_act") != 0 &&
                             strcmp(attrs[i].str, "gemm_bf16_tn_bias_act_2sm") != 0 &&
                             strcmp(attrs[i].str, "gemm_bf16_nn_2sm") != 0 && strcmp(attrs[i].str, "gemm_bf16_ta_2sm") != 0 &&
-                            strcmp(attrs[i].str, "gemm_bf16_ta_nn_2sm") != 0))
+                            strcmp(attrs[i].str, "gemm_bf16_ta_nn_2sm") != 0 &&
+                            strcmp(attrs[i].str, "gemm_bf16_staged") != 0))
         return contract(std::string("unknown gemm.bias_act candidate ") + (attrs[i].str ? attrs[i].str : "(null)"));
       candidate = attrs[i].str;
     } else if (strcmp(key, "activation") == 0) {
@@ -468,53 +501,40 @@ extern "C" tb_status tb_op_gemm_bias_act(tb_session* session, tb_stream* stream,
   if ((rc = tensor_buffer(s, lhs, "gemm lhs", &ba)) || (rc = tensor_buffer(s, rhs, "gemm rhs", &bb)) ||
       (rc = tensor_buffer(s, output, "gemm output", &bc)) || (bias && (rc = tensor_buffer(s, bias, "gemm bias", &bbias))))
     return rc;
-  const CUdeviceptr pa = ba->ptr, pb = bb->ptr, pc = bc->ptr;
+  const CUdeviceptr pa = ba->ptr, pb = bb->ptr, pc = bc->ptr, pbias = bbias ? bbias->ptr : 0;
   int M = (int)m, N = (int)n, K = (int)k;
+  // Strides of op(A) (m, k) and op(B) (k, n) in elements, for the staged path.
+  const long long as0 = tl ? 1 : (long long)lhs->shape[1], as1 = tl ? (long long)lhs->shape[1] : 1;
+  const long long bs0 = tr ? 1 : (long long)rhs->shape[1], bs1 = tr ? (long long)rhs->shape[1] : 1;
+  const bool want_staged = candidate && strcmp(candidate, "gemm_bf16_staged") == 0;
+  const bool staged_ok = (pc & 15) == 0;
+  rc = activate(s);
+  if (rc) return rc;
   if (tl || !tr) {
-    // Other storage orders: the layout kernels, whose epilogue takes the bias and activation.
+    // Other storage orders: the layout kernels, whose epilogue takes the bias and activation;
+    // storage they cannot read goes through the staged copies.
     const char* lk = layout_kernel_for(tl, tr, m, n, k, pa | pb | pc);
-    if (!lk)
-      return unsupported("gemm.bias_act needs operand rows whose contiguous extents are multiples of 8 and 16-byte "
-                         "aligned tensors");
+    if (!lk || want_staged) {
+      if (!staged_ok) return unsupported("gemm.bias_act needs a 16-byte aligned output");
+      rc = launch_gemm_bf16_staged(s, st, pa, as0, as1, pb, bs0, bs1, pc, M, N, K, true, pbias, act);
+      if (rc) return rc;
+      return record_event(s, st, nullptr, out);
+    }
     if (candidate && strcmp(candidate, lk) != 0)
       return unsupported(std::string("candidate ") + candidate + " does not take this layout");
-    rc = activate(s);
-    if (rc) return rc;
-    rc = launch_gemm_bf16_layout_2sm(s, st, lk, tl, !tr, pa, pb, pc, M, N, K, (long long)N, bbias ? bbias->ptr : 0,
-                                     act);
+    rc = launch_gemm_bf16_layout_2sm(s, st, lk, tl, !tr, pa, pb, pc, M, N, K, (long long)N, pbias, act);
     if (rc) return rc;
     return record_event(s, st, nullptr, out);
   }
-  if (k % 8 != 0 || ((pa | pb | pc) & 15) != 0)
-    return unsupported("gemm.bias_act needs A [M,K] row-major, B stored [N,K] (transpose_rhs), K % 8 == 0 and "
-                       "16-byte aligned tensors");
+  if (want_staged || k % 8 != 0 || ((pa | pb | pc) & 15) != 0) {
+    if (!staged_ok) return unsupported("gemm.bias_act needs a 16-byte aligned output");
+    rc = launch_gemm_bf16_staged(s, st, pa, as0, as1, pb, bs0, bs1, pc, M, N, K, true, pbias, act);
+    if (rc) return rc;
+    return record_event(s, st, nullptr, out);
+  }
   if (candidate && strcmp(candidate, "gemm_bf16_tn_bias_act") != 0 && strcmp(candidate, "gemm_bf16_tn_bias_act_2sm") != 0)
     return unsupported(std::string("candidate ") + candidate + " does not take this layout");
-  rc = activate(s);
-  if (rc) return rc;
-  // Same choice as the plain GEMM: CTA pairs once the output fills the SMs.
-  const long long tiles = (long long)((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN);
-  const bool pairs = candidate ? strcmp(candidate, "gemm_bf16_tn_bias_act_2sm") == 0
-                               : (M >= 256 && tiles >= s->sm_count);
-  const uint32_t box_rows_b = pairs ? 128 : TB_GEMM_BN;
-  CUtensorMap ta, tbm;
-  if ((rc = tmap_bf16_2d(&ta, pa, m, k, k, TB_GEMM_BM, TB_GEMM_BK, CU_TENSOR_MAP_SWIZZLE_128B)) ||
-      (rc = tmap_bf16_2d(&tbm, pb, n, k, k, box_rows_b, TB_GEMM_BK, CU_TENSOR_MAP_SWIZZLE_128B)))
-    return rc;
-  CUfunction fn = nullptr;
-  const char* name = pairs ? "gemm_bf16_tn_bias_act_2sm" : "gemm_bf16_tn_bias_act";
-  rc = builtin_function(s, "gemm_bf16", name, &fn);
-  if (rc) return rc;
-  CUdeviceptr c = pc, pbias = bbias ? bbias->ptr : 0, status = s->status.device;
-  long long ldc = N;
-  void* params[] = {&ta, &tbm, &c, &pbias, &act, &M, &N, &K, &ldc, &status};
-  if (pairs) {
-    const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
-    rc = launch_builtin_pairs(s, st, fn, pair_tiles, TB_GEMM_THREADS, TB_GEMM2_SMEM_BYTES, params, name);
-  } else {
-    const unsigned grid = (unsigned)(tiles < s->sm_count ? tiles : s->sm_count);
-    rc = launch_builtin(s, st, fn, grid, 1, 1, TB_GEMM_THREADS, TB_GEMM_SMEM_BYTES, params, name);
-  }
+  rc = launch_gemm_bf16_tn_bias_act(s, st, pa, pb, pc, M, N, K, pbias, act, candidate);
   if (rc) return rc;
   return record_event(s, st, nullptr, out);
 }

@@ -13,7 +13,8 @@ Two differences, both for the B200:
   last node's event. The reference waits after every node (`handle.wait()`, :235).
 * `compile` runs fusion passes beside validation and dead-code elimination (the
   reference's core pipeline, projects/titan-graph/src/optimize.rs:23-60):
-  - a bf16 `gemm` (any storage order the tensor-core kernels take) whose only consumer
+  - a bf16 `gemm` (any storage order and extents; storage the tensor maps cannot read
+    is staged K-major inside the fused node) whose only consumer
     is `broadcast.add` of an fp32 [N] bias and/or `gelu` / `silu` becomes one
     `gemm.bias_act` node, i.e. one
     tensor-core kernel whose epilogue applies the bias and the activation to the
@@ -94,19 +95,6 @@ def _consumers(graph: Graph, value: int) -> list:
     return [n for n in graph.nodes if value in n.inputs]
 
 
-def _tensor_core_gemm(node: GraphNode, values: dict) -> bool:
-    """Whether gemm.bias_act takes this gemm's storage order and extents: every operand row
-    the tensor maps read must be a multiple of 8 bf16 elements (A stored [K, M] needs
-    M % 8, B stored [K, N] needs N % 8, K-contiguous operands need K % 8)."""
-    tl, tr = bool(node.attrs.get("transpose_lhs")), bool(node.attrs.get("transpose_rhs"))
-    a, b = (values.get(v) for v in node.inputs)
-    if a is None or b is None or len(a.shape) != 2 or len(b.shape) != 2:
-        return False
-    m, k = (a.shape[1], a.shape[0]) if tl else tuple(a.shape)
-    n = b.shape[0] if tr else b.shape[1]
-    return all(x % 8 == 0 for x in (m if tl else k, k if tr else n))
-
-
 def fuse_gemm_epilogues(graph: Graph) -> tuple[Graph, list]:
     """gemm -> [broadcast.add(bias fp32 [N])] -> [gelu | silu]  =>  gemm.bias_act."""
     notes = []
@@ -122,7 +110,7 @@ def fuse_gemm_epilogues(graph: Graph) -> tuple[Graph, list]:
                 continue
             out = g.outputs[0]
             spec = values[out]
-            if spec.dtype != DType.BF16 or len(spec.shape) != 2 or not _tensor_core_gemm(g, values):
+            if spec.dtype != DType.BF16 or len(spec.shape) != 2:
                 continue
             absorbed, bias, act, tail = [], None, "none", out
             users = _consumers(current, tail)
