@@ -859,6 +859,7 @@ tb_status tb_tune_flush(tb_tune_store* store) {
   std::sort(rows.begin(), rows.end());
   std::string content = std::string(kHeader) + "\n";
   for (const auto& row : rows) content += row + "\n";
+  bool renamed = false;
   int fd = open(tmp_path.c_str(), O_WRONLY | O_CREAT | O_TRUNC | O_CLOEXEC, 0666);
   if (fd < 0) {
     st = io_error("open", tmp_path);
@@ -873,6 +874,7 @@ tb_status tb_tune_flush(tb_tune_store* store) {
   } else if (rename(tmp_path.c_str(), path.c_str()) != 0) {
     st = io_error("rename", tmp_path);
   } else {
+    renamed = true;
     int dfd = open(dir.c_str(), O_RDONLY | O_CLOEXEC);
     if (dfd >= 0) {
       // Some file systems refuse fsync on a directory; the rename is still in place.
@@ -880,9 +882,11 @@ tb_status tb_tune_flush(tb_tune_store* store) {
       close(dfd);
     }
   }
-  if (st == TB_OK) {
+  if (renamed) {  // the merged records are the file now, even if the directory fsync failed
     store->records = std::move(merged);
     store->ignored = ignored;
+  } else if (fd >= 0) {
+    unlink(tmp_path.c_str());  // the file on disk is untouched; leave no partial copy beside it
   }
   flock(lock, LOCK_UN);
   close(lock);
