@@ -274,6 +274,24 @@ tb_status tb_execute(tb_session* session, tb_stream* stream, const char* op, con
                      uint32_t num_inputs, const tb_tensor* output, const tb_attr* attrs, uint32_t num_attrs,
                      tb_event** out);
 
+/* Runtime::compile (titan-runtime/src/lib.rs:3472-3483) over the Graph IR
+ * (titan-graph/src/graph.rs:72-105), shaped like the core pipeline
+ * (titan-graph/src/optimize.rs:23-60): validate, dead-code elimination, the GEMM-epilogue
+ * fusion (bf16 gemm -> broadcast.add of an F32 [N] bias -> gelu/silu becomes
+ * "gemm.bias_act") and the attention fusion (gemm(Q, K; transpose_rhs) -> softmax(last
+ * axis) -> gemm(P, V) on bf16 [T, D] values becomes "attention.fused" with scale 1.0),
+ * validate, and a non-empty check. The graph is JSON:
+ *   {"inputs": [ids], "outputs": [ids], "values": {"<id>": {"dtype": "BF16", "shape": [..]}},
+ *    "nodes": [{"id": n, "operator": "...", "inputs": [ids], "outputs": [ids], "attrs": {..}}]}
+ * `passes` is "compile" (or NULL) for the whole pipeline, or a comma-separated list of
+ * "validate", "check" (validate without a report), "dce", "fusion.gemm_epilogue",
+ * "fusion.attention", "nonempty". On success `out` holds {"graph": {inputs, outputs,
+ * values: [ids kept], nodes}, "reports": [{"name", "changed", "notes"}]}; a failing graph
+ * returns TB_ERR_INVALID with {"error": {"operator", "phase": "compile", "message"}} in
+ * `out`. Text output follows the tune store's convention (*len always set; retry with
+ * cap > *len). */
+tb_status tb_graph_compile(const char* graph_json, const char* passes, char* out, size_t cap, size_t* len);
+
 /* Which kernel the last successful op on this thread launched (the candidate id
  * the runtime reports in ExecutionHandle, titan-runtime/src/lib.rs:2403). */
 const char* tb_last_candidate(void);

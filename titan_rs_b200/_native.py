@@ -140,6 +140,7 @@ _SIGNATURES = {
     "tb_fill_uniform": (_S, [_P, _U32, _SZ, _U64, ctypes.c_double, ctypes.c_double, _S]),
     "tb_execute": (_S, [_P, _P, ctypes.c_char_p, ctypes.POINTER(Tensor), _U32, ctypes.POINTER(Tensor),
                         ctypes.POINTER(Attr), _U32, _PP]),
+    "tb_graph_compile": (_S, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, _SZ, ctypes.POINTER(_SZ)]),
     "tb_tune_open": (_S, [ctypes.c_char_p, _PP]),
     "tb_tune_release": (None, [_P]),
     "tb_tune_insert": (_S, [_P, ctypes.c_char_p, ctypes.c_char_p]),

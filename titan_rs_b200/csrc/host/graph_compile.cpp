@@ -1,0 +1,477 @@
+// Graph compilation for the hot-path operators: Runtime::compile
+// (projects/titan-runtime/src/lib.rs:3472-3483) over the Graph IR
+// (projects/titan-graph/src/graph.rs:72-105), with the core pipeline's shape
+// (projects/titan-graph/src/optimize.rs:23-60: validate, dead-code elimination, fusion,
+// validate) and two fusions for the B200 kernels in place of the reference's
+// elementwise -> relu annotation:
+//
+//   fusion.gemm_epilogue  a bf16 rank-2 `gemm` whose only consumer is `broadcast.add` of
+//                         an F32 [N] bias and/or `gelu` / `silu` (each intermediate used
+//                         once and not a graph output) becomes one `gemm.bias_act` node
+//                         with the gemm's id, attributes transpose_lhs / transpose_rhs
+//                         (as bools, when given) and `activation`;
+//   fusion.attention      S = gemm(Q, K; transpose_rhs), P = softmax(S; last axis),
+//                         O = gemm(P, V) on bf16 [T, D] values, S and P used only in the
+//                         chain and not outputs, becomes `attention.fused(Q, K, V)` with
+//                         the id of the P V gemm and attribute scale = 1.0.
+//
+// Each fusion applies one rewrite at a time and rescans, so chains are found in node
+// order. The graph crosses the C ABI as JSON:
+//   {"inputs": [ids], "outputs": [ids], "values": {"<id>": {"dtype": "BF16", "shape": [..]}},
+//    "nodes": [{"id": n, "operator": "gemm", "inputs": [ids], "outputs": [ids], "attrs": {..}}]}
+// and comes back as {"graph": {... "values": [ids still present] ...}, "reports":
+// [{"name", "changed", "notes"}]}, or {"error": {"operator", "phase", "message"}}.
+#include <algorithm>
+#include <set>
+
+#include "internal.hpp"
+#include "json.hpp"
+
+namespace {
+
+using tb::json::Json;
+
+struct Spec {
+  std::string dtype;
+  std::vector<long long> shape;
+};
+
+struct Node {
+  long long id = 0;
+  std::string op;
+  std::vector<long long> in, out;
+  Json attrs;  // an object
+};
+
+struct Graph {
+  std::vector<long long> inputs, outputs;
+  std::map<long long, Spec> values;
+  std::vector<Node> nodes;
+};
+
+struct Report {
+  std::string name;
+  bool changed = false;
+  std::vector<std::string> notes;
+};
+
+// A compile failure: ExecutionError{operator, phase: "compile", message}.
+struct Failure {
+  std::string op, message;
+};
+
+bool to_int(const Json& v, long long& out) {
+  if (v.kind != Json::Int) return false;
+  char* end = nullptr;
+  errno = 0;
+  out = strtoll(v.text.c_str(), &end, 10);
+  return errno == 0 && end && *end == '\0';
+}
+
+bool int_list(const Json& v, std::vector<long long>& out) {
+  if (v.kind != Json::Array) return false;
+  out.clear();
+  for (const Json& x : v.items) {
+    long long i;
+    if (!to_int(x, i)) return false;
+    out.push_back(i);
+  }
+  return true;
+}
+
+const Json* member(const Json& obj, const char* key) {
+  auto it = obj.members.find(key);
+  return it == obj.members.end() ? nullptr : &it->second;
+}
+
+// Python truthiness of an attribute value (absent is false).
+bool truthy(const Json* v) {
+  if (!v) return false;
+  switch (v->kind) {
+    case Json::Null: return false;
+    case Json::Bool: return v->flag;
+    case Json::Int: return v->text != "0";
+    case Json::Float: return v->number != 0.0;
+    case Json::String: return !v->text.empty();
+    case Json::Array: return !v->items.empty();
+    case Json::Object: return !v->members.empty();
+  }
+  return false;
+}
+
+bool parse_graph(const Json& j, Graph& g, std::string& err) {
+  if (j.kind != Json::Object) return err = "graph must be an object", false;
+  const Json *in = member(j, "inputs"), *out = member(j, "outputs"), *vals = member(j, "values"),
+             *nodes = member(j, "nodes");
+  if (!in || !int_list(*in, g.inputs)) return err = "inputs must be a list of integer value ids", false;
+  if (!out || !int_list(*out, g.outputs)) return err = "outputs must be a list of integer value ids", false;
+  if (!vals || vals->kind != Json::Object) return err = "values must map value ids to specs", false;
+  for (const auto& kv : vals->members) {
+    char* end = nullptr;
+    long long id = strtoll(kv.first.c_str(), &end, 10);
+    if (kv.first.empty() || *end != '\0') return err = "value id " + kv.first + " is not an integer", false;
+    const Json *dt = member(kv.second, "dtype"), *shape = member(kv.second, "shape");
+    Spec sp;
+    if (kv.second.kind != Json::Object || !dt || dt->kind != Json::String || !shape || !int_list(*shape, sp.shape))
+      return err = "value " + kv.first + " needs a dtype string and an integer shape", false;
+    sp.dtype = dt->text;
+    g.values[id] = sp;
+  }
+  if (!nodes || nodes->kind != Json::Array) return err = "nodes must be a list", false;
+  for (const Json& n : nodes->items) {
+    Node node;
+    const Json *id = member(n, "id"), *op = member(n, "operator"), *ni = member(n, "inputs"),
+               *no = member(n, "outputs"), *at = member(n, "attrs");
+    if (n.kind != Json::Object || !id || !to_int(*id, node.id) || !op || op->kind != Json::String || !ni ||
+        !int_list(*ni, node.in) || !no || !int_list(*no, node.out))
+      return err = "every node needs an integer id, an operator string and integer input/output lists", false;
+    node.op = op->text;
+    if (at && at->kind != Json::Object) return err = "node attrs must be an object", false;
+    node.attrs.kind = Json::Object;
+    if (at) node.attrs = *at;
+    g.nodes.push_back(std::move(node));
+  }
+  return true;
+}
+
+bool contains(const std::vector<long long>& v, long long x) { return std::find(v.begin(), v.end(), x) != v.end(); }
+
+bool validate(const Graph& g, Failure& f) {
+  for (const auto* list : {&g.inputs, &g.outputs})
+    for (long long v : *list)
+      if (!g.values.count(v)) return f = {"graph.validate", "value " + std::to_string(v) + " has no TensorSpec"}, false;
+  std::set<long long> produced(g.inputs.begin(), g.inputs.end());
+  for (const Node& n : g.nodes) {
+    for (long long v : n.in)
+      if (!produced.count(v))
+        return f = {n.op, "node " + std::to_string(n.id) + " reads value " + std::to_string(v) +
+                              " before it is produced"},
+               false;
+    for (long long v : n.out) {
+      if (!g.values.count(v)) return f = {n.op, "missing TensorSpec for value " + std::to_string(v)}, false;
+      produced.insert(v);
+    }
+  }
+  return true;
+}
+
+bool dead_code_eliminate(Graph& g) {
+  std::set<long long> live(g.outputs.begin(), g.outputs.end());
+  std::vector<Node> kept;
+  for (auto it = g.nodes.rbegin(); it != g.nodes.rend(); ++it) {
+    bool used = false;
+    for (long long o : it->out) used = used || live.count(o);
+    if (used) {
+      kept.push_back(*it);
+      live.insert(it->in.begin(), it->in.end());
+    }
+  }
+  std::reverse(kept.begin(), kept.end());
+  const bool changed = kept.size() != g.nodes.size();
+  g.nodes = std::move(kept);
+  return changed;
+}
+
+std::vector<size_t> consumers(const Graph& g, long long value) {
+  std::vector<size_t> out;
+  for (size_t i = 0; i < g.nodes.size(); ++i)
+    if (contains(g.nodes[i].in, value)) out.push_back(i);
+  return out;
+}
+
+const Spec* spec_of(const Graph& g, long long v) {
+  auto it = g.values.find(v);
+  return it == g.values.end() ? nullptr : &it->second;
+}
+
+bool is_output(const Graph& g, long long v) { return contains(g.outputs, v); }
+
+// gemm -> [broadcast.add(bias F32 [N])] -> [gelu | silu]  =>  gemm.bias_act
+std::vector<std::string> fuse_gemm_epilogues(Graph& g) {
+  std::vector<std::string> notes;
+  for (bool changed = true; changed;) {
+    changed = false;
+    for (size_t gi = 0; gi < g.nodes.size() && !changed; ++gi) {
+      const Node& gm = g.nodes[gi];
+      if (gm.op != "gemm" || gm.out.size() != 1 || gm.in.size() != 2) continue;
+      const Spec* spec = spec_of(g, gm.out[0]);
+      if (!spec || spec->dtype != "BF16" || spec->shape.size() != 2) continue;
+      std::vector<size_t> absorbed;
+      long long tail = gm.out[0], bias = 0;
+      bool has_bias = false;
+      std::string act = "none";
+      std::vector<size_t> users = consumers(g, tail);
+      if (!is_output(g, tail) && users.size() == 1 && g.nodes[users[0]].op == "broadcast.add" &&
+          g.nodes[users[0]].in.size() == 2 && g.nodes[users[0]].out.size() == 1) {
+        const Node& add = g.nodes[users[0]];
+        const long long other = add.in[0] == tail ? add.in[1] : add.in[0];
+        const Spec *bspec = spec_of(g, other), *aspec = spec_of(g, add.out[0]);
+        if (bspec && aspec && bspec->dtype == "F32" && bspec->shape == std::vector<long long>{spec->shape[1]} &&
+            aspec->dtype == "BF16") {
+          absorbed.push_back(users[0]);
+          bias = other;
+          has_bias = true;
+          tail = add.out[0];
+          users = consumers(g, tail);
+        }
+      }
+      if (!is_output(g, tail) && users.size() == 1 &&
+          (g.nodes[users[0]].op == "gelu" || g.nodes[users[0]].op == "silu") && g.nodes[users[0]].out.size() == 1) {
+        const Spec* ospec = spec_of(g, g.nodes[users[0]].out[0]);
+        if (ospec && ospec->dtype == "BF16") {
+          absorbed.push_back(users[0]);
+          act = g.nodes[users[0]].op;
+          tail = g.nodes[users[0]].out[0];
+        }
+      }
+      if (absorbed.empty()) continue;
+      Node fused;
+      fused.id = gm.id;
+      fused.op = "gemm.bias_act";
+      fused.in = gm.in;
+      if (has_bias) fused.in.push_back(bias);
+      fused.out = {tail};
+      fused.attrs.kind = Json::Object;
+      for (const char* key : {"transpose_lhs", "transpose_rhs"}) {
+        const Json* v = member(gm.attrs, key);
+        if (!v) continue;
+        Json b;
+        b.kind = Json::Bool;
+        b.flag = truthy(v);
+        fused.attrs.members[key] = b;
+      }
+      Json a;
+      a.kind = Json::String;
+      a.text = act;
+      fused.attrs.members["activation"] = a;
+      std::string note = "fused node " + std::to_string(gm.id) + " (gemm) with ";
+      std::set<long long> gone;
+      for (size_t i = 0; i < absorbed.size(); ++i) {
+        const Node& n = g.nodes[absorbed[i]];
+        note += (i ? ", " : "") + std::string("node ") + std::to_string(n.id) + " (" + n.op + ")";
+        gone.insert(n.id);
+      }
+      notes.push_back(note + " into gemm.bias_act");
+      // Values that only lived inside the chain: the gemm's output and every absorbed
+      // node's output but the last.
+      std::vector<long long> dropped = {gm.out[0]};
+      for (size_t i = 0; i + 1 < absorbed.size(); ++i) dropped.push_back(g.nodes[absorbed[i]].out[0]);
+      std::vector<Node> nodes;
+      for (size_t i = 0; i < g.nodes.size(); ++i) {
+        if (i == gi) nodes.push_back(fused);
+        else if (!gone.count(g.nodes[i].id)) nodes.push_back(g.nodes[i]);
+      }
+      g.nodes = std::move(nodes);
+      for (long long v : dropped) g.values.erase(v);
+      changed = true;
+    }
+  }
+  return notes;
+}
+
+bool last_axis_softmax(const Node& n, long long rank) {
+  for (const auto& kv : n.attrs.members)
+    if (kv.first != "axis") return false;
+  const Json* axis = member(n.attrs, "axis");
+  if (!axis) return true;
+  long long a;
+  return to_int(*axis, a) && a == rank - 1;
+}
+
+// gemm(Q, K; transpose_rhs) -> softmax(last axis) -> gemm(P, V)  =>  attention.fused(Q, K, V)
+std::vector<std::string> fuse_attention(Graph& g) {
+  std::vector<std::string> notes;
+  auto bf16_2d = [&](long long v) {
+    const Spec* s = spec_of(g, v);
+    return s && s->dtype == "BF16" && s->shape.size() == 2 ? s : nullptr;
+  };
+  for (bool changed = true; changed;) {
+    changed = false;
+    for (size_t gi = 0; gi < g.nodes.size() && !changed; ++gi) {
+      const Node& gm = g.nodes[gi];
+      if (gm.op != "gemm" || gm.in.size() != 2 || gm.out.size() != 1 || !truthy(member(gm.attrs, "transpose_rhs")) ||
+          truthy(member(gm.attrs, "transpose_lhs")))
+        continue;
+      const long long q = gm.in[0], k = gm.in[1], s_val = gm.out[0];
+      const Spec *qs = bf16_2d(q), *ks = bf16_2d(k), *ss = bf16_2d(s_val);
+      if (!qs || !ks || !ss) continue;
+      const long long tq = qs->shape[0], d = qs->shape[1], tk = ks->shape[0], dk = ks->shape[1];
+      std::vector<size_t> users = consumers(g, s_val);
+      if (is_output(g, s_val) || users.size() != 1 || g.nodes[users[0]].op != "softmax" ||
+          !last_axis_softmax(g.nodes[users[0]], 2) || g.nodes[users[0]].out.empty())
+        continue;
+      const size_t si = users[0];
+      const long long p_val = g.nodes[si].out[0];
+      const Spec* ps = spec_of(g, p_val);
+      if (!ps || ps->dtype != "BF16" || ps->shape != std::vector<long long>{tq, tk}) continue;
+      users = consumers(g, p_val);
+      if (is_output(g, p_val) || users.size() != 1) continue;
+      const size_t pi = users[0];
+      const Node& pv = g.nodes[pi];
+      if (pv.op != "gemm" || pv.in[0] != p_val || pv.in.size() != 2 || truthy(member(pv.attrs, "transpose_lhs")) ||
+          truthy(member(pv.attrs, "transpose_rhs")) || pv.out.empty())
+        continue;
+      const long long v = pv.in[1];
+      const Spec *vs = spec_of(g, v), *os = spec_of(g, pv.out[0]);
+      if (!vs || !os || vs->dtype != "BF16" || os->dtype != "BF16" || vs->shape != std::vector<long long>{tk, d} ||
+          os->shape != std::vector<long long>{tq, d} || dk != d)
+        continue;
+      // The fused node sits where P V was: Q, K and V are all produced by then.
+      Node fused;
+      fused.id = pv.id;
+      fused.op = "attention.fused";
+      fused.in = {q, k, v};
+      fused.out = {pv.out[0]};
+      fused.attrs.kind = Json::Object;
+      Json scale;
+      scale.kind = Json::Float;
+      scale.number = 1.0;
+      fused.attrs.members["scale"] = scale;
+      notes.push_back("fused node " + std::to_string(gm.id) + " (gemm), node " + std::to_string(g.nodes[si].id) +
+                      " (softmax) and node " + std::to_string(pv.id) + " (gemm) into attention.fused [" +
+                      std::to_string(tq) + "x" + std::to_string(tk) + ", D=" + std::to_string(d) + "]");
+      std::vector<Node> nodes;
+      for (size_t i = 0; i < g.nodes.size(); ++i) {
+        if (i == pi) nodes.push_back(fused);
+        else if (i != gi && i != si) nodes.push_back(g.nodes[i]);
+      }
+      g.nodes = std::move(nodes);
+      g.values.erase(s_val);
+      g.values.erase(p_val);
+      changed = true;
+    }
+  }
+  return notes;
+}
+
+Json int_array(const std::vector<long long>& v) {
+  Json a;
+  a.kind = Json::Array;
+  for (long long x : v) {
+    Json i;
+    i.kind = Json::Int;
+    i.text = std::to_string(x);
+    a.items.push_back(i);
+  }
+  return a;
+}
+
+Json str(const std::string& s) {
+  Json j;
+  j.kind = Json::String;
+  j.text = s;
+  return j;
+}
+
+std::string result_json(const Graph& g, const std::vector<Report>& reports) {
+  Json graph, out, reps;
+  graph.kind = out.kind = Json::Object;
+  reps.kind = Json::Array;
+  graph.members["inputs"] = int_array(g.inputs);
+  graph.members["outputs"] = int_array(g.outputs);
+  std::vector<long long> ids;
+  for (const auto& kv : g.values) ids.push_back(kv.first);
+  graph.members["values"] = int_array(ids);
+  Json nodes;
+  nodes.kind = Json::Array;
+  for (const Node& n : g.nodes) {
+    Json j;
+    j.kind = Json::Object;
+    Json id;
+    id.kind = Json::Int;
+    id.text = std::to_string(n.id);
+    j.members["id"] = id;
+    j.members["operator"] = str(n.op);
+    j.members["inputs"] = int_array(n.in);
+    j.members["outputs"] = int_array(n.out);
+    j.members["attrs"] = n.attrs;
+    nodes.items.push_back(j);
+  }
+  graph.members["nodes"] = nodes;
+  for (const Report& r : reports) {
+    Json j, notes, changed;
+    j.kind = Json::Object;
+    notes.kind = Json::Array;
+    for (const auto& s : r.notes) notes.items.push_back(str(s));
+    changed.kind = Json::Bool;
+    changed.flag = r.changed;
+    j.members["name"] = str(r.name);
+    j.members["changed"] = changed;
+    j.members["notes"] = notes;
+    reps.items.push_back(j);
+  }
+  out.members["graph"] = graph;
+  out.members["reports"] = reps;
+  std::string text;
+  tb::json::emit(text, out);
+  return text;
+}
+
+std::string error_json(const Failure& f) {
+  Json e, o;
+  e.kind = o.kind = Json::Object;
+  e.members["operator"] = str(f.op);
+  e.members["phase"] = str("compile");
+  e.members["message"] = str(f.message);
+  o.members["error"] = e;
+  std::string text;
+  tb::json::emit(text, o);
+  return text;
+}
+
+tb_status give(const std::string& text, char* out, size_t cap, size_t* len, tb_status status) {
+  if (len) *len = text.size();
+  if (!out || cap <= text.size())
+    return tb::set_error(TB_ERR_INVALID, "compile",
+                         "output buffer too small: " + std::to_string(text.size() + 1) + " bytes needed");
+  memcpy(out, text.data(), text.size());
+  out[text.size()] = '\0';
+  return status;
+}
+
+}  // namespace
+
+extern "C" tb_status tb_graph_compile(const char* graph_json, const char* passes, char* out, size_t cap,
+                                      size_t* len) {
+  Failure f;
+  auto fail = [&](const Failure& failure) {
+    std::string text = error_json(failure);
+    tb_status st = give(text, out, cap, len, TB_ERR_INVALID);
+    if (st == TB_ERR_INVALID && len && *len < cap)  // the error object fits: report the compile failure itself
+      tb::set_error(TB_ERR_INVALID, "compile", failure.op + ": " + failure.message);
+    return st;
+  };
+  if (!graph_json) return fail({"graph", "graph JSON is null"});
+  Json j;
+  std::string canon, err;
+  if (!tb::json::canonical(graph_json, canon, err, &j)) return fail({"graph", "graph JSON: " + err});
+  Graph g;
+  if (!parse_graph(j, g, err)) return fail({"graph", err});
+  const std::string list = passes && *passes ? passes : "compile";
+  std::vector<std::string> steps;
+  for (size_t b = 0; b <= list.size();) {
+    size_t e = list.find(',', b);
+    if (e == std::string::npos) e = list.size();
+    steps.push_back(list.substr(b, e - b));
+    b = e + 1;
+  }
+  if (steps.size() == 1 && steps[0] == "compile")
+    steps = {"validate", "dce", "fusion.gemm_epilogue", "fusion.attention", "check", "nonempty"};
+  std::vector<Report> reports;
+  for (const std::string& step : steps) {
+    if (step == "validate" || step == "check") {
+      if (!validate(g, f)) return fail(f);
+      if (step == "validate") reports.push_back({"validate", false, {"schema and constraints ok"}});
+    } else if (step == "dce") {
+      reports.push_back({"dce", dead_code_eliminate(g), {"removed unreachable pure nodes"}});
+    } else if (step == "fusion.gemm_epilogue" || step == "fusion.attention") {
+      std::vector<std::string> notes = step == "fusion.attention" ? fuse_attention(g) : fuse_gemm_epilogues(g);
+      reports.push_back({step, !notes.empty(), notes});
+    } else if (step == "nonempty") {
+      if (g.nodes.empty()) return fail({"graph.empty", "graph has no nodes after passes"});
+    } else {
+      return fail({"graph", "unknown pass " + step});
+    }
+  }
+  return give(result_json(g, reports), out, cap, len, TB_OK);
+}

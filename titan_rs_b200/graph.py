@@ -29,6 +29,8 @@ Two differences, both for the B200:
 """
 from __future__ import annotations
 
+import ctypes
+import json
 from dataclasses import dataclass, field
 from typing import Optional
 
@@ -65,141 +67,60 @@ class PassReport:
     notes: list
 
 
+def _graph_json(graph: Graph) -> str:
+    values = {str(k): {"dtype": v.dtype.name, "shape": [int(x) for x in v.shape]} for k, v in graph.values.items()}
+    nodes = [{"id": n.id, "operator": n.operator, "inputs": list(n.inputs), "outputs": list(n.outputs),
+              "attrs": dict(n.attrs)} for n in graph.nodes]
+    return json.dumps({"inputs": list(graph.inputs), "outputs": list(graph.outputs), "values": values,
+                       "nodes": nodes})
+
+
+def _run_passes(graph: Graph, passes: str) -> tuple[Graph, list]:
+    """Runs passes of the native compiler (tb_graph_compile) and maps the result back:
+    unchanged nodes keep their objects, value specs come from this graph."""
+    L = N.lib()
+    text = _graph_json(graph).encode()
+    cap = 1 << 16
+    n = ctypes.c_size_t(0)
+    while True:
+        buf = ctypes.create_string_buffer(cap)
+        L.tb_graph_compile(text, passes.encode(), buf, cap, ctypes.byref(n))
+        if n.value < cap:
+            break
+        cap = n.value + 1
+    res = json.loads(buf.raw[:n.value].decode())
+    if "error" in res:
+        e = res["error"]
+        raise ExecutionError(e["operator"], e["phase"], e["message"], N.TB_ERR_INVALID)
+    out = res["graph"]
+    originals = {(n.id, n.operator, tuple(n.inputs), tuple(n.outputs)): n for n in graph.nodes}
+    nodes = [originals.get((j["id"], j["operator"], tuple(j["inputs"]), tuple(j["outputs"])))
+             or GraphNode(j["id"], j["operator"], j["inputs"], j["outputs"], j["attrs"]) for j in out["nodes"]]
+    values = {v: graph.values[v] for v in out["values"]}
+    reports = [PassReport(r["name"], r["changed"], r["notes"]) for r in res["reports"]]
+    return Graph(list(graph.inputs), list(graph.outputs), values, nodes), reports
+
+
 def validate(graph: Graph) -> None:
-    for v in list(graph.inputs) + list(graph.outputs):
-        if v not in graph.values:
-            raise ExecutionError("graph.validate", "compile", f"value {v} has no TensorSpec")
-    produced = set(graph.inputs)
-    for node in graph.nodes:
-        for v in node.inputs:
-            if v not in produced:
-                raise ExecutionError(node.operator, "compile", f"node {node.id} reads value {v} before it is produced")
-        for v in node.outputs:
-            if v not in graph.values:
-                raise ExecutionError(node.operator, "compile", f"missing TensorSpec for value {v}")
-            produced.add(v)
+    """Every graph input/output has a spec; every node reads only produced values."""
+    _run_passes(graph, "check")
 
 
 def dead_code_eliminate(graph: Graph) -> tuple[Graph, bool]:
-    live = set(graph.outputs)
-    kept = []
-    for node in reversed(graph.nodes):
-        if any(o in live for o in node.outputs):
-            kept.append(node)
-            live.update(node.inputs)
-    kept.reverse()
-    return Graph(list(graph.inputs), list(graph.outputs), dict(graph.values), kept), len(kept) != len(graph.nodes)
-
-
-def _consumers(graph: Graph, value: int) -> list:
-    return [n for n in graph.nodes if value in n.inputs]
+    g, reports = _run_passes(graph, "dce")
+    return g, reports[0].changed
 
 
 def fuse_gemm_epilogues(graph: Graph) -> tuple[Graph, list]:
     """gemm -> [broadcast.add(bias fp32 [N])] -> [gelu | silu]  =>  gemm.bias_act."""
-    notes = []
-    nodes = list(graph.nodes)
-    values = dict(graph.values)
-    outputs = set(graph.outputs)
-    changed = True
-    while changed:
-        changed = False
-        current = Graph(graph.inputs, graph.outputs, values, nodes)
-        for g in nodes:
-            if g.operator != "gemm" or len(g.outputs) != 1 or len(g.inputs) != 2:
-                continue
-            out = g.outputs[0]
-            spec = values[out]
-            if spec.dtype != DType.BF16 or len(spec.shape) != 2:
-                continue
-            absorbed, bias, act, tail = [], None, "none", out
-            users = _consumers(current, tail)
-            if tail not in outputs and len(users) == 1 and users[0].operator == "broadcast.add" and \
-                    len(users[0].inputs) == 2:
-                add = users[0]
-                other = add.inputs[1] if add.inputs[0] == tail else add.inputs[0]
-                bspec = values.get(other)
-                if bspec is not None and bspec.dtype == DType.F32 and tuple(bspec.shape) == (spec.shape[1],) and \
-                        values[add.outputs[0]].dtype == DType.BF16:
-                    absorbed.append(add)
-                    bias, tail = other, add.outputs[0]
-                    users = _consumers(current, tail)
-            if tail not in outputs and len(users) == 1 and users[0].operator in ("gelu", "silu") and \
-                    values[users[0].outputs[0]].dtype == DType.BF16:
-                absorbed.append(users[0])
-                act, tail = users[0].operator, users[0].outputs[0]
-            if not absorbed:
-                continue
-            layout = {key: bool(g.attrs[key]) for key in ("transpose_lhs", "transpose_rhs") if key in g.attrs}
-            fused = GraphNode(g.id, "gemm.bias_act", list(g.inputs) + ([bias] if bias is not None else []), [tail],
-                              {**layout, "activation": act})
-            gone = {n.id for n in absorbed}
-            nodes = [fused if n is g else n for n in nodes if n.id not in gone]
-            for n in [g] + absorbed[:-1]:
-                values.pop(n.outputs[0], None)
-            notes.append(f"fused node {g.id} (gemm) with " + ", ".join(f"node {n.id} ({n.operator})" for n in absorbed)
-                         + " into gemm.bias_act")
-            changed = True
-            break
-    return Graph(list(graph.inputs), list(graph.outputs), values, nodes), notes
-
-
-def _is_last_axis_softmax(node: GraphNode, rank: int) -> bool:
-    axis = node.attrs.get("axis", rank - 1)
-    return isinstance(axis, int) and not isinstance(axis, bool) and axis == rank - 1 and \
-        set(node.attrs) <= {"axis"}
+    g, reports = _run_passes(graph, "fusion.gemm_epilogue")
+    return g, reports[0].notes
 
 
 def fuse_attention(graph: Graph) -> tuple[Graph, list]:
     """gemm(Q, K; transpose_rhs) -> softmax(last axis) -> gemm(P, V)  =>  attention.fused(Q, K, V)."""
-    notes = []
-    nodes = list(graph.nodes)
-    values = dict(graph.values)
-    outputs = set(graph.outputs)
-    changed = True
-    while changed:
-        changed = False
-        current = Graph(graph.inputs, graph.outputs, values, nodes)
-        for g in nodes:
-            if g.operator != "gemm" or len(g.inputs) != 2 or len(g.outputs) != 1 or \
-                    not g.attrs.get("transpose_rhs") or g.attrs.get("transpose_lhs"):
-                continue
-            q, k = g.inputs
-            s_val = g.outputs[0]
-            specs = [values.get(v) for v in (q, k, s_val)]
-            if any(sp is None or sp.dtype != DType.BF16 or len(sp.shape) != 2 for sp in specs):
-                continue
-            (tq, d), (tk, dk), _ = (tuple(sp.shape) for sp in specs)
-            users = _consumers(current, s_val)
-            if s_val in outputs or len(users) != 1 or users[0].operator != "softmax" or \
-                    not _is_last_axis_softmax(users[0], 2):
-                continue
-            sm = users[0]
-            p_val = sm.outputs[0]
-            p_spec = values.get(p_val)
-            if p_spec is None or p_spec.dtype != DType.BF16 or tuple(p_spec.shape) != (tq, tk):
-                continue
-            users = _consumers(current, p_val)
-            if p_val in outputs or len(users) != 1 or users[0].operator != "gemm" or \
-                    users[0].inputs[0] != p_val or len(users[0].inputs) != 2 or \
-                    users[0].attrs.get("transpose_lhs") or users[0].attrs.get("transpose_rhs"):
-                continue
-            pv = users[0]
-            v = pv.inputs[1]
-            v_spec, o_spec = values.get(v), values.get(pv.outputs[0])
-            if v_spec is None or o_spec is None or v_spec.dtype != DType.BF16 or o_spec.dtype != DType.BF16 or \
-                    tuple(v_spec.shape) != (tk, d) or tuple(o_spec.shape) != (tq, d) or dk != d:
-                continue
-            # The fused node sits where P V was: Q, K and V are all produced by then.
-            fused = GraphNode(pv.id, "attention.fused", [q, k, v], [pv.outputs[0]], {"scale": 1.0})
-            nodes = [fused if n is pv else n for n in nodes if n is not g and n is not sm]
-            values.pop(s_val, None)
-            values.pop(p_val, None)
-            notes.append(f"fused node {g.id} (gemm), node {sm.id} (softmax) and node {pv.id} (gemm) into "
-                         f"attention.fused [{tq}x{tk}, D={d}]")
-            changed = True
-            break
-    return Graph(list(graph.inputs), list(graph.outputs), values, nodes), notes
+    g, reports = _run_passes(graph, "fusion.attention")
+    return g, reports[0].notes
 
 
 def _view(t: TensorHandle, shape: tuple) -> TensorHandle:
@@ -265,20 +186,10 @@ class ExecutionPlan:
 
 
 def compile(graph: Graph) -> ExecutionPlan:
-    """Runtime::compile (lib.rs:3472-3483): validate, DCE, fusion; an empty result is an error."""
-    reports = []
-    validate(graph)
-    reports.append(PassReport("validate", False, ["schema and constraints ok"]))
-    graph, changed = dead_code_eliminate(graph)
-    reports.append(PassReport("dce", changed, ["removed unreachable pure nodes"]))
-    graph, notes = fuse_gemm_epilogues(graph)
-    reports.append(PassReport("fusion.gemm_epilogue", bool(notes), notes))
-    graph, notes = fuse_attention(graph)
-    reports.append(PassReport("fusion.attention", bool(notes), notes))
-    validate(graph)
-    if not graph.nodes:
-        raise ExecutionError("graph.empty", "compile", "graph has no nodes after passes", N.TB_ERR_INVALID)
-    return ExecutionPlan(graph, reports)
+    """Runtime::compile (lib.rs:3472-3483): validate, DCE, fusion; an empty result is an error.
+    The passes run in the native library (tb_graph_compile)."""
+    g, reports = _run_passes(graph, "compile")
+    return ExecutionPlan(g, reports)
 
 
 __all__ = ["GraphNode", "Graph", "PassReport", "ExecutionPlan", "compile", "validate", "dead_code_eliminate",
