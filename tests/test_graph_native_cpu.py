@@ -288,3 +288,43 @@ def test_individual_passes_match():
     assert [n.operator for n in fused.nodes] == ["gemm.bias_act"] and fused.nodes[0].attrs == {
         "transpose_rhs": True, "activation": "silu"}
     assert notes == ["fused node 10 (gemm) with node 11 (broadcast.add), node 12 (silu) into gemm.bias_act"]
+
+
+def test_serde_shaped_graph_with_tagged_attributes():
+    """A graph as serde_json writes the reference's Graph (graph.rs:72-105, AttrValue
+    externally tagged, titan-types/src/lib.rs:140-147): extra fields are ignored, tagged
+    attributes are read, and the fused nodes carry tagged attributes back."""
+    import ctypes
+    import json
+    import struct
+    from titan_rs_b200 import _native as N
+
+    def spec(dtype, *shape):
+        return {"dtype": dtype, "shape": list(shape), "strides": [], "layout": "Contiguous", "alias": "NoAlias"}
+
+    def node(i, op, ins, outs, attrs):
+        return {"id": i, "operator": op, "inputs": ins, "outputs": outs, "attrs": attrs,
+                "effects": {"kind": "pure"}, "source": {"file": "g", "line": 1, "column": 1}}
+
+    graph = {"schema": 1, "inputs": [0, 1, 2, 6, 7, 8], "outputs": [5, 11], "constraints": [],
+             "values": {"0": spec("BF16", 8, 16), "1": spec("BF16", 32, 16), "2": spec("F32", 32),
+                        "3": spec("BF16", 8, 32), "4": spec("BF16", 8, 32), "5": spec("BF16", 8, 32),
+                        "6": spec("BF16", 4, 16), "7": spec("BF16", 4, 16), "8": spec("BF16", 4, 16),
+                        "9": spec("BF16", 4, 4), "10": spec("BF16", 4, 4), "11": spec("BF16", 4, 16)},
+             "nodes": [node(20, "gemm", [0, 1], [3], {"transpose_rhs": {"Bool": True}}),
+                       node(21, "broadcast.add", [3, 2], [4], {}),
+                       node(22, "gelu", [4], [5], {}),
+                       node(23, "gemm", [6, 7], [9], {"transpose_rhs": {"Int": 1}}),
+                       node(24, "softmax", [9], [10], {"axis": {"Int": 1}}),
+                       node(25, "gemm", [10, 8], [11], {})]}
+    buf = ctypes.create_string_buffer(1 << 16)
+    n = ctypes.c_size_t(0)
+    assert N.lib().tb_graph_compile(json.dumps(graph).encode(), b"compile", buf, len(buf), ctypes.byref(n)) == N.TB_OK
+    out = json.loads(buf.raw[:n.value])
+    nodes = {x["id"]: x for x in out["graph"]["nodes"]}
+    assert nodes[20]["operator"] == "gemm.bias_act" and nodes[20]["inputs"] == [0, 1, 2] and nodes[20]["outputs"] == [5]
+    assert nodes[20]["attrs"] == {"transpose_rhs": {"Bool": True}, "activation": {"String": "gelu"}}
+    one = struct.unpack("<Q", struct.pack("<d", 1.0))[0]
+    assert nodes[25]["operator"] == "attention.fused" and nodes[25]["inputs"] == [6, 7, 8]
+    assert nodes[25]["attrs"] == {"scale": {"Float": one}}
+    assert sorted(nodes) == [20, 25]

@@ -19,7 +19,10 @@
 // order. The graph crosses the C ABI as JSON:
 //   {"inputs": [ids], "outputs": [ids], "values": {"<id>": {"dtype": "BF16", "shape": [..]}},
 //    "nodes": [{"id": n, "operator": "gemm", "inputs": [ids], "outputs": [ids], "attrs": {..}}]}
-// and comes back as {"graph": {... "values": [ids still present] ...}, "reports":
+// Attribute values may be plain JSON or serde's externally tagged AttrValue (a serde_json
+// dump of the reference's Graph); nodes the passes create are written in the same form,
+// kept nodes exactly as given. The result comes back as
+// {"graph": {... "values": [ids still present] ...}, "reports":
 // [{"name", "changed", "notes"}]}, or {"error": {"operator", "phase", "message"}}.
 #include <algorithm>
 #include <set>
@@ -40,13 +43,16 @@ struct Node {
   long long id = 0;
   std::string op;
   std::vector<long long> in, out;
-  Json attrs;  // an object
+  Json attrs;      // an object of plain values, what the passes read
+  Json raw_attrs;  // the attributes as given, written back for nodes the passes keep
+  bool rewritten = false;
 };
 
 struct Graph {
   std::vector<long long> inputs, outputs;
   std::map<long long, Spec> values;
   std::vector<Node> nodes;
+  bool tagged = false;  // attributes arrive as serde's externally tagged AttrValue
 };
 
 struct Report {
@@ -99,6 +105,48 @@ bool truthy(const Json* v) {
   return false;
 }
 
+// titan_types::AttrValue (titan-types/src/lib.rs:140-147) as serde_json writes it:
+// {"Bool": b}, {"Int": i}, {"Float": f64 bits as u64}, {"String": s}, {"Ints": [..]},
+// {"Strings": [..]}. Such a value becomes the plain JSON value; anything else is kept.
+bool untag(const Json& v, Json& plain) {
+  if (v.kind != Json::Object || v.members.size() != 1) return false;
+  const std::string& tag = v.members.begin()->first;
+  const Json& x = v.members.begin()->second;
+  if ((tag == "Bool" && x.kind == Json::Bool) || (tag == "Int" && x.kind == Json::Int) ||
+      (tag == "String" && x.kind == Json::String) || ((tag == "Ints" || tag == "Strings") && x.kind == Json::Array)) {
+    plain = x;
+    return true;
+  }
+  if (tag == "Float" && x.kind == Json::Int) {
+    unsigned long long bits = strtoull(x.text.c_str(), nullptr, 10);
+    double d;
+    memcpy(&d, &bits, sizeof d);
+    plain = Json();
+    plain.kind = Json::Float;
+    plain.number = d;
+    return true;
+  }
+  return false;
+}
+
+// A plain attribute value in the form the input used.
+Json attr_out(const Json& plain, bool tagged) {
+  if (!tagged) return plain;
+  Json x = plain, w;
+  w.kind = Json::Object;
+  const char* tag = plain.kind == Json::Bool ? "Bool" : plain.kind == Json::Int ? "Int" : "String";
+  if (plain.kind == Json::Float) {
+    unsigned long long bits;
+    memcpy(&bits, &plain.number, sizeof bits);
+    x = Json();
+    x.kind = Json::Int;
+    x.text = std::to_string(bits);
+    tag = "Float";
+  }
+  w.members[tag] = x;
+  return w;
+}
+
 bool parse_graph(const Json& j, Graph& g, std::string& err) {
   if (j.kind != Json::Object) return err = "graph must be an object", false;
   const Json *in = member(j, "inputs"), *out = member(j, "outputs"), *vals = member(j, "values"),
@@ -128,7 +176,16 @@ bool parse_graph(const Json& j, Graph& g, std::string& err) {
     node.op = op->text;
     if (at && at->kind != Json::Object) return err = "node attrs must be an object", false;
     node.attrs.kind = Json::Object;
-    if (at) node.attrs = *at;
+    node.raw_attrs.kind = Json::Object;
+    if (at) {
+      node.raw_attrs = *at;
+      for (const auto& kv : at->members) {
+        Json plain;
+        const bool t = untag(kv.second, plain);
+        g.tagged = g.tagged || t;
+        node.attrs.members[kv.first] = t ? plain : kv.second;
+      }
+    }
     g.nodes.push_back(std::move(node));
   }
   return true;
@@ -228,6 +285,7 @@ std::vector<std::string> fuse_gemm_epilogues(Graph& g) {
       Node fused;
       fused.id = gm.id;
       fused.op = "gemm.bias_act";
+      fused.rewritten = true;
       fused.in = gm.in;
       if (has_bias) fused.in.push_back(bias);
       fused.out = {tail};
@@ -320,6 +378,7 @@ std::vector<std::string> fuse_attention(Graph& g) {
       Node fused;
       fused.id = pv.id;
       fused.op = "attention.fused";
+      fused.rewritten = true;
       fused.in = {q, k, v};
       fused.out = {pv.out[0]};
       fused.attrs.kind = Json::Object;
@@ -384,7 +443,14 @@ std::string result_json(const Graph& g, const std::vector<Report>& reports) {
     j.members["operator"] = str(n.op);
     j.members["inputs"] = int_array(n.in);
     j.members["outputs"] = int_array(n.out);
-    j.members["attrs"] = n.attrs;
+    if (n.rewritten) {
+      Json attrs;
+      attrs.kind = Json::Object;
+      for (const auto& kv : n.attrs.members) attrs.members[kv.first] = attr_out(kv.second, g.tagged);
+      j.members["attrs"] = attrs;
+    } else {
+      j.members["attrs"] = n.raw_attrs;
+    }
     nodes.items.push_back(j);
   }
   graph.members["nodes"] = nodes;
