@@ -422,6 +422,17 @@ tb_status tb_tune_record(const tb_tune_store* store, size_t index, char* key, si
                          char* entry, size_t entry_cap, size_t* entry_len);
 /* Canonical form of any JSON text (the form records are keyed and checksummed in). */
 tb_status tb_tune_canonical_json(const char* json, char* out, size_t cap, size_t* len);
+/* One timed candidate for the selection rule. */
+typedef struct tb_tune_measurement {
+  const char* candidate;
+  uint64_t median_ns;
+  uint64_t p95_ns;
+  uint64_t workspace_bytes;
+} tb_tune_measurement;
+/* The v2 selection rule (docs/architecture/autotune-v2.md): the lowest median wins;
+ * among candidates whose median is within 2% of it, the lower p95, then the smaller
+ * workspace, then the smaller name (byte order) decide. *winner is an index into ms. */
+tb_status tb_tune_select(const tb_tune_measurement* ms, size_t n, size_t* winner);
 /* SHA-256 (FIPS 180-4) of `len` bytes as 64 lowercase hex digits and a NUL in out[65]. */
 tb_status tb_sha256_hex(const void* data, size_t len, char* out);
 

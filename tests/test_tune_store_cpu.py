@@ -167,3 +167,18 @@ def test_arguments_must_be_json_objects(tmp_path):
         store.insert("[1]", "{}")
     with pytest.raises(ValueError, match="entry is not a JSON object"):
         store.insert("{}", "{oops")
+
+
+@settings(max_examples=300, deadline=None)
+@given(st.lists(st.tuples(st.sampled_from(["a", "b", "c", "gemm_bf16_tn", "gemm_bf16_tn_2sm"]),
+                          st.integers(1, 200), st.integers(1, 300), st.sampled_from([0, 64, 4096])),
+                min_size=1, max_size=8))
+def test_native_selection_rule_matches_its_statement(rows):
+    """tb_tune_select against the rule written out: lowest median; within 2% of it the
+    lower p95, then the smaller workspace, then the name."""
+    ms = [A.Measured(c, med, p95, "h", ws) for c, med, p95, ws in rows]
+    best = min(m.median_ns for m in ms)
+    want = min((m for m in ms if m.median_ns <= best * 1.02), key=lambda m: (m.p95_ns, m.workspace_bytes, m.candidate))
+    got = A.select(ms)
+    assert (got.candidate, got.median_ns, got.p95_ns, got.workspace_bytes) == \
+        (want.candidate, want.median_ns, want.p95_ns, want.workspace_bytes)

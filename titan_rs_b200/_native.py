@@ -28,6 +28,11 @@ TB_MAX_RANK = 6
 TB_COMM_ID_BYTES = 128
 
 
+class TuneMeasurement(ctypes.Structure):
+    _fields_ = [("candidate", ctypes.c_char_p), ("median_ns", ctypes.c_uint64), ("p95_ns", ctypes.c_uint64),
+                ("workspace_bytes", ctypes.c_uint64)]
+
+
 class Fingerprint(ctypes.Structure):
     _fields_ = [("ordinal", ctypes.c_uint32), ("model", ctypes.c_char * 128), ("driver", ctypes.c_char * 32),
                 ("capability_revision", ctypes.c_char * 16), ("sm_count", ctypes.c_uint32),
@@ -150,6 +155,7 @@ _SIGNATURES = {
     "tb_tune_record": (_S, [_P, _SZ, ctypes.c_char_p, _SZ, ctypes.POINTER(_SZ), ctypes.c_char_p, _SZ,
                             ctypes.POINTER(_SZ)]),
     "tb_tune_canonical_json": (_S, [ctypes.c_char_p, ctypes.c_char_p, _SZ, ctypes.POINTER(_SZ)]),
+    "tb_tune_select": (_S, [ctypes.POINTER(TuneMeasurement), _SZ, ctypes.POINTER(_SZ)]),
     "tb_sha256_hex": (_S, [ctypes.c_char_p, _SZ, ctypes.c_char_p]),
 }
 

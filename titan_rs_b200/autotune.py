@@ -24,6 +24,7 @@ docs/architecture/autotune-v2.md that the reference specifies but does not imple
 """
 from __future__ import annotations
 
+import ctypes
 import hashlib
 import json
 import math
@@ -145,10 +146,16 @@ def _percentile(sorted_vals: Sequence[float], q: float) -> float:
 
 
 def select(measured: Sequence[Measured]) -> Measured:
-    """Lowest median; within 2% of it: lower p95, then smaller workspace, then name."""
-    best = min(m.median_ns for m in measured)
-    close = [m for m in measured if m.median_ns <= best * 1.02]
-    return min(close, key=lambda m: (m.p95_ns, m.workspace_bytes, m.candidate))
+    """Lowest median; within 2% of it: lower p95, then smaller workspace, then name
+    (the native rule, tb_tune_select)."""
+    names = [m.candidate.encode() for m in measured]
+    arr = (_native.TuneMeasurement * len(measured))(
+        *[_native.TuneMeasurement(nm, int(m.median_ns), int(m.p95_ns), int(m.workspace_bytes))
+          for nm, m in zip(names, measured)])
+    w = ctypes.c_size_t(0)
+    if _native.lib().tb_tune_select(arr, len(measured), ctypes.byref(w)) != _native.TB_OK:
+        raise ValueError(_native.last_error()[1])
+    return measured[w.value]
 
 
 class Autotuner:

@@ -333,6 +333,28 @@ struct tb_tune_store {
 
 extern "C" {
 
+tb_status tb_tune_select(const tb_tune_measurement* ms, size_t n, size_t* winner) {
+  if (!ms || !n || !winner) return tb::set_error(TB_ERR_INVALID, "tune", "select needs at least one measurement");
+  uint64_t best = ms[0].median_ns;
+  for (size_t i = 1; i < n; ++i) best = std::min(best, ms[i].median_ns);
+  size_t w = n;
+  for (size_t i = 0; i < n; ++i) {
+    if ((double)ms[i].median_ns > (double)best * 1.02) continue;
+    if (w == n) {
+      w = i;
+      continue;
+    }
+    const tb_tune_measurement &a = ms[i], &b = ms[w];
+    const int names = strcmp(a.candidate ? a.candidate : "", b.candidate ? b.candidate : "");
+    if (a.p95_ns != b.p95_ns ? a.p95_ns < b.p95_ns
+                             : a.workspace_bytes != b.workspace_bytes ? a.workspace_bytes < b.workspace_bytes
+                                                                      : names < 0)
+      w = i;
+  }
+  *winner = w;
+  return TB_OK;
+}
+
 tb_status tb_sha256_hex(const void* data, size_t len, char* out) {
   if (!out || (!data && len)) return tb::set_error(TB_ERR_INVALID, "tune", "null pointer");
   std::string h = sha256_hex((const uint8_t*)data, len);
