@@ -27,3 +27,34 @@ def test_c_host_uses_the_library_through_the_header(tmp_path):
                       "tune_get", "tune_stats", "tune_record", "tune_miss", "short_buffer", "graph_compile",
                       "graph_error", "execute_route"]
     assert (tmp_path / "kernels.tune").read_text().startswith("# titan.tune version=2\n")
+
+
+STRUCTS = {"tb_fingerprint": "Fingerprint", "tb_launch_arg": "LaunchArg", "tb_launch_metadata": "LaunchMetadata",
+           "tb_binding": "Binding", "tb_encoded_args": "EncodedArgs", "tb_launch_geometry": "LaunchGeometry",
+           "tb_tensor": "Tensor", "tb_attr": "Attr", "tb_tune_measurement": "TuneMeasurement"}
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="no C compiler on this machine")
+def test_ctypes_structures_match_the_header_layout(tmp_path):
+    """Every struct of the header has the size and field offsets of its ctypes mirror."""
+    import ctypes
+    import re
+    header = (ROOT / "include" / "titan_b200.h").read_text()
+    assert set(re.findall(r"typedef struct (tb_\w+) \{", header)) == set(STRUCTS)
+    lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "titan_b200.h"', "int main(void) {"]
+    expected = []
+    for c_name, py_name in STRUCTS.items():
+        cls = getattr(N, py_name)
+        lines.append(f'  printf("{c_name} %zu\\n", sizeof({c_name}));')
+        expected.append(f"{c_name} {ctypes.sizeof(cls)}")
+        for field, *_ in cls._fields_:
+            lines.append(f'  printf("{c_name}.{field} %zu\\n", offsetof({c_name}, {field}));')
+            expected.append(f"{c_name}.{field} {getattr(cls, field).offset}")
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", str(ROOT / "include"), str(src), "-o", str(exe)],
+                   check=True, capture_output=True, text=True)
+    got = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.splitlines()
+    assert got == expected
