@@ -328,3 +328,14 @@ def test_serde_shaped_graph_with_tagged_attributes():
     assert nodes[25]["operator"] == "attention.fused" and nodes[25]["inputs"] == [6, 7, 8]
     assert nodes[25]["attrs"] == {"scale": {"Float": one}}
     assert sorted(nodes) == [20, 25]
+
+
+def test_numpy_attribute_values_compile_like_python_ones():
+    import numpy as np
+    values = {0: TensorSpec(BF, (8, 16)), 1: TensorSpec(BF, (32, 16)), 3: TensorSpec(BF, (8, 32)),
+              5: TensorSpec(BF, (8, 32))}
+    nodes = [GraphNode(10, "gemm", [0, 1], [3], {"transpose_rhs": np.bool_(True), "tag": object()}),
+             GraphNode(12, "gelu", [3], [5], {"weight": np.float32(0.5), "dims": np.arange(2)})]
+    plan = G.compile(Graph([0, 1], [5], values, nodes))
+    assert [(n.operator, n.attrs) for n in plan.graph.nodes] == [
+        ("gemm.bias_act", {"transpose_rhs": True, "activation": "gelu"})]

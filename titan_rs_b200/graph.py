@@ -34,6 +34,8 @@ import json
 from dataclasses import dataclass, field
 from typing import Optional
 
+import numpy as np
+
 from . import _native as N
 from .kernel_abi import DType
 from .runtime import (ExecutionError, ExecutionHandle, OpRequest, Runtime, TensorHandle, TensorSpec,
@@ -67,12 +69,27 @@ class PassReport:
     notes: list
 
 
+def _json_attr(value):
+    """Attribute values json does not know: numpy scalars by kind, anything else by repr
+    (the compiler only reads bools, ints, floats and strings; other values pass through on
+    the Python side untouched)."""
+    if isinstance(value, np.bool_):
+        return bool(value)
+    if isinstance(value, np.integer):
+        return int(value)
+    if isinstance(value, np.floating):
+        return float(value)
+    if isinstance(value, (tuple, np.ndarray)):
+        return list(value.tolist() if isinstance(value, np.ndarray) else value)
+    return repr(value)
+
+
 def _graph_json(graph: Graph) -> str:
     values = {str(k): {"dtype": v.dtype.name, "shape": [int(x) for x in v.shape]} for k, v in graph.values.items()}
     nodes = [{"id": n.id, "operator": n.operator, "inputs": list(n.inputs), "outputs": list(n.outputs),
               "attrs": dict(n.attrs)} for n in graph.nodes]
-    return json.dumps({"inputs": list(graph.inputs), "outputs": list(graph.outputs), "values": values,
-                       "nodes": nodes})
+    return json.dumps({"inputs": [int(v) for v in graph.inputs], "outputs": [int(v) for v in graph.outputs],
+                       "values": values, "nodes": nodes}, default=_json_attr)
 
 
 def _run_passes(graph: Graph, passes: str) -> tuple[Graph, list]:
