@@ -15,8 +15,9 @@
 //                         chain and not outputs, becomes `attention.fused(Q, K, V)` with
 //                         the id of the P V gemm and attribute scale = 1.0.
 //
-// Each fusion applies one rewrite at a time and rescans, so chains are found in node
-// order. The graph crosses the C ABI as JSON:
+// Each fusion scans the nodes once in order and rewrites in place, which finds the same
+// chains as rewriting one at a time and rescanning (see Index below); a graph of a few
+// thousand nodes compiles in milliseconds. The graph crosses the C ABI as JSON:
 //   {"inputs": [ids], "outputs": [ids], "values": {"<id>": {"dtype": "BF16", "shape": [..]}},
 //    "nodes": [{"id": n, "operator": "gemm", "inputs": [ids], "outputs": [ids], "attrs": {..}}]}
 // Attribute values may be plain JSON or serde's externally tagged AttrValue (a serde_json
@@ -26,6 +27,8 @@
 // [{"name", "changed", "notes"}]}, or {"error": {"operator", "phase", "message"}}.
 #include <algorithm>
 #include <set>
+#include <unordered_map>
+#include <unordered_set>
 
 #include "internal.hpp"
 #include "json.hpp"
@@ -229,101 +232,132 @@ bool dead_code_eliminate(Graph& g) {
   return changed;
 }
 
-std::vector<size_t> consumers(const Graph& g, long long value) {
-  std::vector<size_t> out;
-  for (size_t i = 0; i < g.nodes.size(); ++i)
-    if (contains(g.nodes[i].in, value)) out.push_back(i);
-  return out;
-}
+// The fusions rewrite in place: a fused node takes the position of the node it replaces
+// and the other nodes of its chain are marked dead, so positions stay valid. The index
+// holds the consumers of each value (live positions; a node once however often it reads
+// the value) and is updated with each rewrite.
+//
+// Both fusions scan the nodes once, in order. Rescanning from the first node after each
+// rewrite (the plain statement of "one rewrite, then rescan") finds nothing more: a
+// rewrite keeps every surviving value's consumer count (the fused node reads what the
+// chain read from outside it, at one position), and the only consumers that change
+// operator name are chain nodes, which no earlier chain could have matched (they are
+// gemm / broadcast.add / gelu / silu / softmax nodes whose inputs an earlier gemm would
+// have needed as its own single consumer).
+struct Index {
+  std::unordered_map<long long, std::vector<size_t>> users;
+  std::unordered_set<long long> outputs;
+  std::vector<bool> dead;
+  explicit Index(const Graph& g) : outputs(g.outputs.begin(), g.outputs.end()), dead(g.nodes.size(), false) {
+    for (size_t i = 0; i < g.nodes.size(); ++i)
+      for (long long v : g.nodes[i].in) add(v, i);
+  }
+  void add(long long v, size_t i) {
+    std::vector<size_t>& u = users[v];
+    if (std::find(u.begin(), u.end(), i) == u.end()) u.push_back(i);
+  }
+  std::vector<size_t> consumers(long long v) const {
+    std::vector<size_t> out;
+    auto it = users.find(v);
+    if (it != users.end())
+      for (size_t i : it->second)
+        if (!dead[i]) out.push_back(i);
+    std::sort(out.begin(), out.end());
+    return out;
+  }
+};
 
 const Spec* spec_of(const Graph& g, long long v) {
   auto it = g.values.find(v);
   return it == g.values.end() ? nullptr : &it->second;
 }
 
-bool is_output(const Graph& g, long long v) { return contains(g.outputs, v); }
+void drop_dead(Graph& g, const Index& ix) {
+  std::vector<Node> nodes;
+  nodes.reserve(g.nodes.size());
+  for (size_t i = 0; i < g.nodes.size(); ++i)
+    if (!ix.dead[i]) nodes.push_back(std::move(g.nodes[i]));
+  g.nodes = std::move(nodes);
+}
 
 // gemm -> [broadcast.add(bias F32 [N])] -> [gelu | silu]  =>  gemm.bias_act
 std::vector<std::string> fuse_gemm_epilogues(Graph& g) {
   std::vector<std::string> notes;
-  for (bool changed = true; changed;) {
-    changed = false;
-    for (size_t gi = 0; gi < g.nodes.size() && !changed; ++gi) {
-      const Node& gm = g.nodes[gi];
-      if (gm.op != "gemm" || gm.out.size() != 1 || gm.in.size() != 2) continue;
-      const Spec* spec = spec_of(g, gm.out[0]);
-      if (!spec || spec->dtype != "BF16" || spec->shape.size() != 2) continue;
-      std::vector<size_t> absorbed;
-      long long tail = gm.out[0], bias = 0;
-      bool has_bias = false;
-      std::string act = "none";
-      std::vector<size_t> users = consumers(g, tail);
-      if (!is_output(g, tail) && users.size() == 1 && g.nodes[users[0]].op == "broadcast.add" &&
-          g.nodes[users[0]].in.size() == 2 && g.nodes[users[0]].out.size() == 1) {
-        const Node& add = g.nodes[users[0]];
-        const long long other = add.in[0] == tail ? add.in[1] : add.in[0];
-        const Spec *bspec = spec_of(g, other), *aspec = spec_of(g, add.out[0]);
-        if (bspec && aspec && bspec->dtype == "F32" && bspec->shape == std::vector<long long>{spec->shape[1]} &&
-            aspec->dtype == "BF16") {
-          absorbed.push_back(users[0]);
-          bias = other;
-          has_bias = true;
-          tail = add.out[0];
-          users = consumers(g, tail);
-        }
+  Index ix(g);
+  for (size_t gi = 0; gi < g.nodes.size(); ++gi) {
+    if (ix.dead[gi]) continue;
+    const Node& gm = g.nodes[gi];
+    if (gm.op != "gemm" || gm.out.size() != 1 || gm.in.size() != 2) continue;
+    const Spec* spec = spec_of(g, gm.out[0]);
+    if (!spec || spec->dtype != "BF16" || spec->shape.size() != 2) continue;
+    std::vector<size_t> absorbed;
+    long long tail = gm.out[0], bias = 0;
+    bool has_bias = false;
+    std::string act = "none";
+    std::vector<size_t> users = ix.consumers(tail);
+    if (!ix.outputs.count(tail) && users.size() == 1 && g.nodes[users[0]].op == "broadcast.add" &&
+        g.nodes[users[0]].in.size() == 2 && g.nodes[users[0]].out.size() == 1) {
+      const Node& add = g.nodes[users[0]];
+      const long long other = add.in[0] == tail ? add.in[1] : add.in[0];
+      const Spec *bspec = spec_of(g, other), *aspec = spec_of(g, add.out[0]);
+      if (bspec && aspec && bspec->dtype == "F32" && bspec->shape == std::vector<long long>{spec->shape[1]} &&
+          aspec->dtype == "BF16") {
+        absorbed.push_back(users[0]);
+        bias = other;
+        has_bias = true;
+        tail = add.out[0];
+        users = ix.consumers(tail);
       }
-      if (!is_output(g, tail) && users.size() == 1 &&
-          (g.nodes[users[0]].op == "gelu" || g.nodes[users[0]].op == "silu") && g.nodes[users[0]].out.size() == 1) {
-        const Spec* ospec = spec_of(g, g.nodes[users[0]].out[0]);
-        if (ospec && ospec->dtype == "BF16") {
-          absorbed.push_back(users[0]);
-          act = g.nodes[users[0]].op;
-          tail = g.nodes[users[0]].out[0];
-        }
-      }
-      if (absorbed.empty()) continue;
-      Node fused;
-      fused.id = gm.id;
-      fused.op = "gemm.bias_act";
-      fused.rewritten = true;
-      fused.in = gm.in;
-      if (has_bias) fused.in.push_back(bias);
-      fused.out = {tail};
-      fused.attrs.kind = Json::Object;
-      for (const char* key : {"transpose_lhs", "transpose_rhs"}) {
-        const Json* v = member(gm.attrs, key);
-        if (!v) continue;
-        Json b;
-        b.kind = Json::Bool;
-        b.flag = truthy(v);
-        fused.attrs.members[key] = b;
-      }
-      Json a;
-      a.kind = Json::String;
-      a.text = act;
-      fused.attrs.members["activation"] = a;
-      std::string note = "fused node " + std::to_string(gm.id) + " (gemm) with ";
-      std::set<long long> gone;
-      for (size_t i = 0; i < absorbed.size(); ++i) {
-        const Node& n = g.nodes[absorbed[i]];
-        note += (i ? ", " : "") + std::string("node ") + std::to_string(n.id) + " (" + n.op + ")";
-        gone.insert(n.id);
-      }
-      notes.push_back(note + " into gemm.bias_act");
-      // Values that only lived inside the chain: the gemm's output and every absorbed
-      // node's output but the last.
-      std::vector<long long> dropped = {gm.out[0]};
-      for (size_t i = 0; i + 1 < absorbed.size(); ++i) dropped.push_back(g.nodes[absorbed[i]].out[0]);
-      std::vector<Node> nodes;
-      for (size_t i = 0; i < g.nodes.size(); ++i) {
-        if (i == gi) nodes.push_back(fused);
-        else if (!gone.count(g.nodes[i].id)) nodes.push_back(g.nodes[i]);
-      }
-      g.nodes = std::move(nodes);
-      for (long long v : dropped) g.values.erase(v);
-      changed = true;
     }
+    if (!ix.outputs.count(tail) && users.size() == 1 &&
+        (g.nodes[users[0]].op == "gelu" || g.nodes[users[0]].op == "silu") && g.nodes[users[0]].out.size() == 1) {
+      const Spec* ospec = spec_of(g, g.nodes[users[0]].out[0]);
+      if (ospec && ospec->dtype == "BF16") {
+        absorbed.push_back(users[0]);
+        act = g.nodes[users[0]].op;
+        tail = g.nodes[users[0]].out[0];
+      }
+    }
+    if (absorbed.empty()) continue;
+    Node fused;
+    fused.id = gm.id;
+    fused.op = "gemm.bias_act";
+    fused.rewritten = true;
+    fused.in = gm.in;
+    if (has_bias) fused.in.push_back(bias);
+    fused.out = {tail};
+    fused.attrs.kind = Json::Object;
+    for (const char* key : {"transpose_lhs", "transpose_rhs"}) {
+      const Json* v = member(gm.attrs, key);
+      if (!v) continue;
+      Json b;
+      b.kind = Json::Bool;
+      b.flag = truthy(v);
+      fused.attrs.members[key] = b;
+    }
+    Json a;
+    a.kind = Json::String;
+    a.text = act;
+    fused.attrs.members["activation"] = a;
+    std::string note = "fused node " + std::to_string(gm.id) + " (gemm) with ";
+    for (size_t i = 0; i < absorbed.size(); ++i) {
+      const Node& n = g.nodes[absorbed[i]];
+      note += (i ? ", " : "") + std::string("node ") + std::to_string(n.id) + " (" + n.op + ")";
+    }
+    notes.push_back(note + " into gemm.bias_act");
+    // Values that only lived inside the chain: the gemm's output and every absorbed
+    // node's output but the last.
+    g.values.erase(gm.out[0]);
+    for (size_t i = 0; i + 1 < absorbed.size(); ++i) g.values.erase(g.nodes[absorbed[i]].out[0]);
+    // Absorbed nodes go, and so does every other node with one of their ids.
+    std::set<long long> gone;
+    for (size_t i : absorbed) gone.insert(g.nodes[i].id);
+    for (size_t i = 0; i < g.nodes.size(); ++i)
+      if (i != gi && gone.count(g.nodes[i].id)) ix.dead[i] = true;
+    if (has_bias) ix.add(bias, gi);
+    g.nodes[gi] = std::move(fused);
   }
+  drop_dead(g, ix);
   return notes;
 }
 
@@ -343,63 +377,60 @@ std::vector<std::string> fuse_attention(Graph& g) {
     const Spec* s = spec_of(g, v);
     return s && s->dtype == "BF16" && s->shape.size() == 2 ? s : nullptr;
   };
-  for (bool changed = true; changed;) {
-    changed = false;
-    for (size_t gi = 0; gi < g.nodes.size() && !changed; ++gi) {
-      const Node& gm = g.nodes[gi];
-      if (gm.op != "gemm" || gm.in.size() != 2 || gm.out.size() != 1 || !truthy(member(gm.attrs, "transpose_rhs")) ||
-          truthy(member(gm.attrs, "transpose_lhs")))
-        continue;
-      const long long q = gm.in[0], k = gm.in[1], s_val = gm.out[0];
-      const Spec *qs = bf16_2d(q), *ks = bf16_2d(k), *ss = bf16_2d(s_val);
-      if (!qs || !ks || !ss) continue;
-      const long long tq = qs->shape[0], d = qs->shape[1], tk = ks->shape[0], dk = ks->shape[1];
-      std::vector<size_t> users = consumers(g, s_val);
-      if (is_output(g, s_val) || users.size() != 1 || g.nodes[users[0]].op != "softmax" ||
-          !last_axis_softmax(g.nodes[users[0]], 2) || g.nodes[users[0]].out.empty())
-        continue;
-      const size_t si = users[0];
-      const long long p_val = g.nodes[si].out[0];
-      const Spec* ps = spec_of(g, p_val);
-      if (!ps || ps->dtype != "BF16" || ps->shape != std::vector<long long>{tq, tk}) continue;
-      users = consumers(g, p_val);
-      if (is_output(g, p_val) || users.size() != 1) continue;
-      const size_t pi = users[0];
-      const Node& pv = g.nodes[pi];
-      if (pv.op != "gemm" || pv.in[0] != p_val || pv.in.size() != 2 || truthy(member(pv.attrs, "transpose_lhs")) ||
-          truthy(member(pv.attrs, "transpose_rhs")) || pv.out.empty())
-        continue;
-      const long long v = pv.in[1];
-      const Spec *vs = spec_of(g, v), *os = spec_of(g, pv.out[0]);
-      if (!vs || !os || vs->dtype != "BF16" || os->dtype != "BF16" || vs->shape != std::vector<long long>{tk, d} ||
-          os->shape != std::vector<long long>{tq, d} || dk != d)
-        continue;
-      // The fused node sits where P V was: Q, K and V are all produced by then.
-      Node fused;
-      fused.id = pv.id;
-      fused.op = "attention.fused";
-      fused.rewritten = true;
-      fused.in = {q, k, v};
-      fused.out = {pv.out[0]};
-      fused.attrs.kind = Json::Object;
-      Json scale;
-      scale.kind = Json::Float;
-      scale.number = 1.0;
-      fused.attrs.members["scale"] = scale;
-      notes.push_back("fused node " + std::to_string(gm.id) + " (gemm), node " + std::to_string(g.nodes[si].id) +
-                      " (softmax) and node " + std::to_string(pv.id) + " (gemm) into attention.fused [" +
-                      std::to_string(tq) + "x" + std::to_string(tk) + ", D=" + std::to_string(d) + "]");
-      std::vector<Node> nodes;
-      for (size_t i = 0; i < g.nodes.size(); ++i) {
-        if (i == pi) nodes.push_back(fused);
-        else if (i != gi && i != si) nodes.push_back(g.nodes[i]);
-      }
-      g.nodes = std::move(nodes);
-      g.values.erase(s_val);
-      g.values.erase(p_val);
-      changed = true;
-    }
+  Index ix(g);
+  for (size_t gi = 0; gi < g.nodes.size(); ++gi) {
+    if (ix.dead[gi]) continue;
+    const Node& gm = g.nodes[gi];
+    if (gm.op != "gemm" || gm.in.size() != 2 || gm.out.size() != 1 || !truthy(member(gm.attrs, "transpose_rhs")) ||
+        truthy(member(gm.attrs, "transpose_lhs")))
+      continue;
+    const long long q = gm.in[0], k = gm.in[1], s_val = gm.out[0];
+    const Spec *qs = bf16_2d(q), *ks = bf16_2d(k), *ss = bf16_2d(s_val);
+    if (!qs || !ks || !ss) continue;
+    const long long tq = qs->shape[0], d = qs->shape[1], tk = ks->shape[0], dk = ks->shape[1];
+    std::vector<size_t> users = ix.consumers(s_val);
+    if (ix.outputs.count(s_val) || users.size() != 1 || g.nodes[users[0]].op != "softmax" ||
+        !last_axis_softmax(g.nodes[users[0]], 2) || g.nodes[users[0]].out.empty())
+      continue;
+    const size_t si = users[0];
+    const long long p_val = g.nodes[si].out[0];
+    const Spec* ps = spec_of(g, p_val);
+    if (!ps || ps->dtype != "BF16" || ps->shape != std::vector<long long>{tq, tk}) continue;
+    users = ix.consumers(p_val);
+    if (ix.outputs.count(p_val) || users.size() != 1) continue;
+    const size_t pi = users[0];
+    const Node& pv = g.nodes[pi];
+    if (pv.op != "gemm" || pv.in[0] != p_val || pv.in.size() != 2 || truthy(member(pv.attrs, "transpose_lhs")) ||
+        truthy(member(pv.attrs, "transpose_rhs")) || pv.out.empty())
+      continue;
+    const long long v = pv.in[1];
+    const Spec *vs = spec_of(g, v), *os = spec_of(g, pv.out[0]);
+    if (!vs || !os || vs->dtype != "BF16" || os->dtype != "BF16" || vs->shape != std::vector<long long>{tk, d} ||
+        os->shape != std::vector<long long>{tq, d} || dk != d)
+      continue;
+    // The fused node sits where P V was: Q, K and V are all produced by then.
+    Node fused;
+    fused.id = pv.id;
+    fused.op = "attention.fused";
+    fused.rewritten = true;
+    fused.in = {q, k, v};
+    fused.out = {pv.out[0]};
+    fused.attrs.kind = Json::Object;
+    Json scale;
+    scale.kind = Json::Float;
+    scale.number = 1.0;
+    fused.attrs.members["scale"] = scale;
+    notes.push_back("fused node " + std::to_string(gm.id) + " (gemm), node " + std::to_string(g.nodes[si].id) +
+                    " (softmax) and node " + std::to_string(pv.id) + " (gemm) into attention.fused [" +
+                    std::to_string(tq) + "x" + std::to_string(tk) + ", D=" + std::to_string(d) + "]");
+    g.values.erase(s_val);
+    g.values.erase(p_val);
+    ix.dead[gi] = ix.dead[si] = true;
+    ix.add(q, pi);
+    ix.add(k, pi);
+    g.nodes[pi] = std::move(fused);
   }
+  drop_dead(g, ix);
   return notes;
 }
 
