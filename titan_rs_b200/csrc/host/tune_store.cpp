@@ -329,6 +329,9 @@ struct tb_tune_store {
   mutable std::mutex mu;
   Records records;
   size_t ignored = 0;
+  // Records by position for tb_tune_record, rebuilt after a change (under mu).
+  mutable std::vector<Records::const_iterator> order;
+  mutable bool order_stale = true;
 };
 
 extern "C" {
@@ -388,6 +391,7 @@ tb_status tb_tune_insert(tb_tune_store* store, const char* key_json, const char*
   if (!object_json(key_json, "key", key, st) || !object_json(entry_json, "entry", entry, st)) return st;
   std::lock_guard<std::mutex> g(store->mu);
   store->records[key] = entry;
+  store->order_stale = true;
   return TB_OK;
 }
 
@@ -427,10 +431,13 @@ tb_status tb_tune_record(const tb_tune_store* store, size_t index, char* key, si
     if (index >= store->records.size())
       return tb::set_error(TB_ERR_INVALID, "tune",
                            "record " + std::to_string(index) + " of " + std::to_string(store->records.size()));
-    auto it = store->records.begin();
-    std::advance(it, (long)index);
-    k = it->first;
-    e = it->second;
+    if (store->order_stale) {
+      store->order.clear();
+      for (auto it = store->records.begin(); it != store->records.end(); ++it) store->order.push_back(it);
+      store->order_stale = false;
+    }
+    k = store->order[index]->first;
+    e = store->order[index]->second;
   }
   tb_status a = give_text(k, key, key_cap, key_len);
   tb_status b = give_text(e, entry, entry_cap, entry_len);
@@ -494,6 +501,7 @@ tb_status tb_tune_flush(tb_tune_store* store) {
   if (renamed) {  // the merged records are the file now, even if the directory fsync failed
     store->records = std::move(merged);
     store->ignored = ignored;
+    store->order_stale = true;
   } else if (fd >= 0) {
     unlink(tmp_path.c_str());  // the file on disk is untouched; leave no partial copy beside it
   }
