@@ -540,8 +540,10 @@ extern "C" tb_status tb_graph_compile(const char* graph_json, const char* passes
   };
   if (!graph_json) return fail({"graph", "graph JSON is null"});
   Json j;
-  std::string canon, err;
-  if (!tb::json::canonical(graph_json, canon, err, &j)) return fail({"graph", "graph JSON: " + err});
+  std::string err;
+  const std::string text = graph_json;
+  if (!tb::json::valid_utf8(text)) return fail({"graph", "graph JSON: not valid UTF-8"});
+  if (!tb::json::Parser(text).parse(j, err)) return fail({"graph", "graph JSON: " + err});
   Graph g;
   if (!parse_graph(j, g, err)) return fail({"graph", err});
   const std::string list = passes && *passes ? passes : "compile";
