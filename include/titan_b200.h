@@ -267,7 +267,9 @@ tb_status tb_op_conv2d(tb_session* session, tb_stream* stream, const tb_tensor* 
  * that routes OpRequests without naming each entry: "softmax" (1 input),
  * "gemm" (2), "scaled_dot_product_attention" (3), "conv2d" (2 or 3: input, weight,
  * optional bias) and "gemm.bias_act" (2 or 3: A, B, optional bias) go to the entries
- * above with the same checks. Another name is TB_ERR_UNSUPPORTED ("does not
+ * above with the same checks; "attention.fused" (3: contiguous [Tq, D] Q, [Tk, D] K and
+ * V, [Tq, D] output, the graph compiler's gemm -> softmax -> gemm node) runs tb_op_sdpa
+ * on [1, 1, T, D] views of the same buffers. Another name is TB_ERR_UNSUPPORTED ("does not
  * implement"); a wrong input count is TB_ERR_INVALID with the operator's arity message.
  * Both report operation "contract", as ExecutionError{phase: "contract"} does. */
 tb_status tb_execute(tb_session* session, tb_stream* stream, const char* op, const tb_tensor* inputs,

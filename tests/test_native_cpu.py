@@ -129,3 +129,30 @@ def test_execute_routes_by_operator_name_before_touching_a_session():
         assert call(op, bad) == N.TB_ERR_INVALID, op
         operation, detail = N.last_error()
         assert operation == "contract" and keyword in detail, (op, detail)
+
+
+def test_execute_takes_the_fused_graph_nodes():
+    """tb_execute routes the graph compiler's fused nodes; attention.fused wants contiguous
+    rank-2 [T, D] tensors (viewed as [1, 1, T, D]) before any session is touched."""
+    L = N.lib()
+
+    def t2(rows, cols, strides=None):
+        t = N.Tensor()
+        t.dtype, t.rank = N.TB_BF16, 2
+        t.shape[0], t.shape[1] = rows, cols
+        t.strides[0], t.strides[1] = strides or (cols, 1)
+        return t
+
+    ev = ctypes.c_void_p(0)
+    ins = (N.Tensor * 3)(t2(4, 8), t2(6, 8, (1, 6)), t2(6, 8))
+    assert L.tb_execute(None, None, b"attention.fused", ins, 3, ctypes.byref(t2(4, 8)), None, 0,
+                        ctypes.byref(ev)) == N.TB_ERR_INVALID
+    assert N.last_error() == ("contract", "attention.fused requires contiguous rank-2 [T, D] Q, K, V and output")
+    assert L.tb_execute(None, None, b"attention.fused", ins, 2, ctypes.byref(t2(4, 8)), None, 0,
+                        ctypes.byref(ev)) == N.TB_ERR_INVALID
+    assert N.last_error()[1] == "attention.fused requires Q, K and V"
+    # Contiguous views pass the router and reach the attention operator's own checks.
+    ins = (N.Tensor * 3)(t2(4, 8), t2(6, 8), t2(6, 8))
+    assert L.tb_execute(None, None, b"attention.fused", ins, 3, ctypes.byref(t2(4, 8)), None, 0,
+                        ctypes.byref(ev)) != N.TB_OK
+    assert "attention.fused" not in N.last_error()[1]

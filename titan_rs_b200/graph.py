@@ -37,9 +37,7 @@ from typing import Optional
 import numpy as np
 
 from . import _native as N
-from .kernel_abi import DType
-from .runtime import (ExecutionError, ExecutionHandle, OpRequest, Runtime, TensorHandle, TensorSpec,
-                      contiguous_strides)
+from .runtime import ExecutionError, ExecutionHandle, OpRequest, Runtime
 
 
 @dataclass
@@ -140,13 +138,6 @@ def fuse_attention(graph: Graph) -> tuple[Graph, list]:
     return g, reports[0].notes
 
 
-def _view(t: TensorHandle, shape: tuple) -> TensorHandle:
-    """The same contiguous buffer under another shape (a reshape without a copy)."""
-    if tuple(t.strides) != contiguous_strides(t.shape):
-        raise ExecutionError("attention.fused", "bind", "fused attention requires contiguous Q, K and V")
-    return TensorHandle(t.session, t.buffer, t.dtype, tuple(shape), contiguous_strides(shape))
-
-
 class ExecutionPlan:
     """ExecutionPlan (lib.rs:176-276): the optimised graph and its pass reports."""
 
@@ -174,17 +165,8 @@ class ExecutionPlan:
                 if v not in self.graph.values:
                     raise ExecutionError(node.operator, "bind", f"missing TensorSpec for value {v}")
                 specs.append(self.graph.values[v])
-            if node.operator == "attention.fused":
-                # [T, D] values as [1, 1, T, D] views for the BHTD attention operator.
-                (tq, d), (tk, _) = inputs[0].shape, inputs[1].shape
-                views = [_view(inputs[0], (1, 1, tq, d)), _view(inputs[1], (1, 1, tk, d)),
-                         _view(inputs[2], (1, 1, tk, d))]
-                handle = runtime.execute(OpRequest("scaled_dot_product_attention", views,
-                                                   [TensorSpec(DType.BF16, (1, 1, tq, d))], dict(node.attrs)))
-                handle = ExecutionHandle([_view(handle.outputs[0], (tq, d))], handle.candidate, handle.kernel,
-                                         handle.event)
-            else:
-                handle = runtime.execute(OpRequest(node.operator, inputs, specs, dict(node.attrs)))
+            # Fused nodes ("gemm.bias_act", "attention.fused") are operators of the router too.
+            handle = runtime.execute(OpRequest(node.operator, inputs, specs, dict(node.attrs)))
             if len(handle.outputs) != len(node.outputs):
                 raise ExecutionError(node.operator, "execute", f"node {node.id} produced {len(handle.outputs)} "
                                                                f"outputs, expected {len(node.outputs)}")

@@ -172,14 +172,15 @@ def _attrs(attrs: dict):
 
 
 _OPS = {"softmax": "tb_op_softmax", "gemm": "tb_op_gemm", "scaled_dot_product_attention": "tb_op_sdpa",
-        "conv2d": "tb_op_conv2d", "gemm.bias_act": "tb_op_gemm_bias_act"}
+        "conv2d": "tb_op_conv2d", "gemm.bias_act": "tb_op_gemm_bias_act", "attention.fused": "tb_op_sdpa"}
 _ARITY = {"softmax": (1, 1), "gemm": (2, 2), "scaled_dot_product_attention": (3, 3), "conv2d": (2, 3),
-          "gemm.bias_act": (2, 3)}
+          "gemm.bias_act": (2, 3), "attention.fused": (3, 3)}
 _ARITY_MSG = {"softmax": "CUDA softmax requires exactly one input and one output",
               "gemm": "gemm requires exactly two rank-2 inputs",
               "scaled_dot_product_attention": "scaled dot-product attention requires exactly three rank-4 BHTD inputs",
               "conv2d": "conv2d requires rank-4 NCHW input, rank-4 OIHW weight, and optional bias",
-              "gemm.bias_act": "gemm.bias_act requires two rank-2 inputs, an optional bias and one output"}
+              "gemm.bias_act": "gemm.bias_act requires two rank-2 inputs, an optional bias and one output",
+              "attention.fused": "attention.fused requires Q, K and V"}
 
 
 class Runtime:
