@@ -22,9 +22,16 @@ from titan_rs_b200.runtime import ExecutionError, TensorSpec
 class Oracle:
     @staticmethod
     def validate(graph: Graph) -> None:
+        if not graph.outputs:
+            raise ExecutionError("graph.validate", "compile", "graph must declare at least one output")
         for v in list(graph.inputs) + list(graph.outputs):
             if v not in graph.values:
                 raise ExecutionError("graph.validate", "compile", f"value {v} has no TensorSpec")
+        seen = set()
+        for node in graph.nodes:
+            if node.id in seen:
+                raise ExecutionError("graph.validate", "compile", f"duplicate node id {node.id}")
+            seen.add(node.id)
         produced = set(graph.inputs)
         for node in graph.nodes:
             for v in node.inputs:
@@ -92,8 +99,9 @@ class Oracle:
                 layout = {key: bool(g.attrs[key]) for key in ("transpose_lhs", "transpose_rhs") if key in g.attrs}
                 fused = GraphNode(g.id, "gemm.bias_act", list(g.inputs) + ([bias] if bias is not None else []), [tail],
                                   {**layout, "activation": act})
-                gone = {n.id for n in absorbed}
-                nodes = [fused if n is g else n for n in nodes if n.id not in gone]
+                # The fused node sits where the chain's last node was.
+                gone = [g] + absorbed[:-1]
+                nodes = [fused if n is absorbed[-1] else n for n in nodes if not any(n is x for x in gone)]
                 for n in [g] + absorbed[:-1]:
                     values.pop(n.outputs[0], None)
                 notes.append(f"fused node {g.id} (gemm) with " + ", ".join(f"node {n.id} ({n.operator})" for n in absorbed)
@@ -221,7 +229,12 @@ def graphs(draw):
             nodes.append(GraphNode(next(ids), "gemm", [x, w], [y], attrs))
             produced.append(y)
             if not maybe(0.3):
-                b = value(flip(F32), n if not maybe(0.1) else n + 1, graph_input=True)
+                if maybe(0.2):  # a bias produced by a node between the gemm and the add
+                    b0 = value(F32, n, graph_input=True)
+                    b = value(flip(F32), n if not maybe(0.1) else n + 1)
+                    nodes.append(GraphNode(next(ids), "silu", [b0], [b]))
+                else:
+                    b = value(flip(F32), n if not maybe(0.1) else n + 1, graph_input=True)
                 z = value(flip(BF), m, n)
                 nodes.append(GraphNode(next(ids), "broadcast.add", [y, b] if maybe(0.7) else [b, y], [z]))
                 produced.append(z)
@@ -251,6 +264,10 @@ def graphs(draw):
         outputs.append(max(values) + 1)  # an output without a spec
     if maybe(0.05) and len(nodes) > 1:
         nodes.insert(0, nodes.pop())  # a node that reads values before they exist
+    if maybe(0.04) and len(nodes) > 1:
+        nodes[-1].id = nodes[0].id  # two nodes with one id
+    if maybe(0.02):
+        outputs = []
     return Graph(inputs, outputs, values, nodes)
 
 
@@ -339,3 +356,31 @@ def test_numpy_attribute_values_compile_like_python_ones():
     plan = G.compile(Graph([0, 1], [5], values, nodes))
     assert [(n.operator, n.attrs) for n in plan.graph.nodes] == [
         ("gemm.bias_act", {"transpose_rhs": True, "activation": "gelu"})]
+
+
+def test_bias_produced_after_the_gemm_fuses_at_the_add():
+    """gemm (10) -> silu making the bias (11) -> broadcast.add (12): the fused node takes the
+    add's position, after the bias exists, and the compiled graph validates."""
+    values = {0: TensorSpec(BF, (8, 16)), 1: TensorSpec(BF, (32, 16)), 2: TensorSpec(F32, (32,)),
+              3: TensorSpec(BF, (8, 32)), 4: TensorSpec(F32, (32,)), 5: TensorSpec(BF, (8, 32))}
+    nodes = [GraphNode(10, "gemm", [0, 1], [3], {"transpose_rhs": True}), GraphNode(11, "silu", [2], [4]),
+             GraphNode(12, "broadcast.add", [3, 4], [5])]
+    g = Graph([0, 1, 2], [5], values, nodes)
+    plan = G.compile(g)
+    assert [(n.id, n.operator, n.inputs, n.outputs) for n in plan.graph.nodes] == [
+        (11, "silu", [2], [4]), (10, "gemm.bias_act", [0, 1, 4], [5])]
+    want, _ = Oracle.compile(g)
+    assert shape_of(plan.graph) == shape_of(want)
+
+
+def test_validate_rejects_duplicate_node_ids_and_graphs_without_outputs():
+    values = {0: TensorSpec(F32, (4,)), 1: TensorSpec(F32, (4,)), 2: TensorSpec(F32, (4,))}
+    dup = Graph([0], [2], values, [GraphNode(7, "softmax", [0], [1]), GraphNode(7, "softmax", [1], [2])])
+    with pytest.raises(ExecutionError) as e:
+        G.compile(dup)
+    assert (e.value.operator, e.value.message) == ("graph.validate", "duplicate node id 7")
+    none = Graph([0], [], values, [GraphNode(7, "softmax", [0], [1])])
+    with pytest.raises(ExecutionError) as e:
+        G.compile(none)
+    assert (e.value.operator, e.value.message) == ("graph.validate", "graph must declare at least one output")
+

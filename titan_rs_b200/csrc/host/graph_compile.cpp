@@ -196,10 +196,17 @@ bool parse_graph(const Json& j, Graph& g, std::string& err) {
 
 bool contains(const std::vector<long long>& v, long long x) { return std::find(v.begin(), v.end(), x) != v.end(); }
 
+// Graph::validate (titan-graph/src/graph.rs:185-214): at least one output, a spec for
+// every graph input and output, unique node ids; then every node reads only values
+// produced before it and writes values that have a spec.
 bool validate(const Graph& g, Failure& f) {
+  if (g.outputs.empty()) return f = {"graph.validate", "graph must declare at least one output"}, false;
   for (const auto* list : {&g.inputs, &g.outputs})
     for (long long v : *list)
       if (!g.values.count(v)) return f = {"graph.validate", "value " + std::to_string(v) + " has no TensorSpec"}, false;
+  std::set<long long> ids;
+  for (const Node& n : g.nodes)
+    if (!ids.insert(n.id).second) return f = {"graph.validate", "duplicate node id " + std::to_string(n.id)}, false;
   std::set<long long> produced(g.inputs.begin(), g.inputs.end());
   for (const Node& n : g.nodes) {
     for (long long v : n.in)
@@ -232,8 +239,10 @@ bool dead_code_eliminate(Graph& g) {
   return changed;
 }
 
-// The fusions rewrite in place: a fused node takes the position of the node it replaces
-// and the other nodes of its chain are marked dead, so positions stay valid. The index
+// The fusions rewrite in place: a fused node takes the position of the last node of its
+// chain (where every value it reads has been produced, a bias made between the gemm and
+// the add included) and the other nodes of the chain are marked dead, so positions stay
+// valid. The index
 // holds the consumers of each value (live positions; a node once however often it reads
 // the value) and is updated with each rewrite.
 //
@@ -349,13 +358,13 @@ std::vector<std::string> fuse_gemm_epilogues(Graph& g) {
     // node's output but the last.
     g.values.erase(gm.out[0]);
     for (size_t i = 0; i + 1 < absorbed.size(); ++i) g.values.erase(g.nodes[absorbed[i]].out[0]);
-    // Absorbed nodes go, and so does every other node with one of their ids.
-    std::set<long long> gone;
-    for (size_t i : absorbed) gone.insert(g.nodes[i].id);
-    for (size_t i = 0; i < g.nodes.size(); ++i)
-      if (i != gi && gone.count(g.nodes[i].id)) ix.dead[i] = true;
-    if (has_bias) ix.add(bias, gi);
-    g.nodes[gi] = std::move(fused);
+    // The fused node replaces the chain's last node; the gemm and the other absorbed
+    // nodes go.
+    const size_t last = absorbed.back();
+    ix.dead[gi] = true;
+    for (size_t i = 0; i + 1 < absorbed.size(); ++i) ix.dead[absorbed[i]] = true;
+    for (long long v : fused.in) ix.add(v, last);
+    g.nodes[last] = std::move(fused);
   }
   drop_dead(g, ix);
   return notes;
