@@ -377,6 +377,15 @@ tb_status tb_op_gemm_bias_act(tb_session* session, tb_stream* stream, const tb_t
 tb_status tb_gemm_bf16_splitk_noalloc(uint64_t stream, const void* a, const void* b, void* c, int m, int n, int k,
                                       int splits);
 
+/* No counterpart in the reference. The device-side result of the calls above:
+ * synchronises `stream` (a CUstream of the current device), then reads and clears
+ * the device's status word, which a split-K kernel sets when one of its bounded
+ * waits (~1 s each) runs out and it returns early, leaving that call's C invalid.
+ * The word is sticky until read, so TB_ERR_TIMEOUT (operation "wait", the code in
+ * `*code` and in the error detail) means some call on this device since the
+ * previous query failed; TB_OK with *code == 0 means none did. Allocates nothing. */
+tb_status tb_gemm_bf16_splitk_noalloc_status(uint64_t stream, uint32_t* code);
+
 /* ---------------- Seeded synthetic inputs (host side) ---------------- */
 
 /* Counter-based generator: element i depends only on (seed, i), so any slice is

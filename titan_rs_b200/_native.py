@@ -141,6 +141,7 @@ _SIGNATURES = {
     "tb_op_gemm_sharded": (_S, [_P, _P, ctypes.POINTER(Tensor), ctypes.POINTER(Tensor), ctypes.POINTER(Tensor), _P,
                                 _PP]),
     "tb_gemm_bf16_splitk_noalloc": (_S, [_U64, _P, _P, _P, _S, _S, _S, _S]),
+    "tb_gemm_bf16_splitk_noalloc_status": (_S, [_U64, ctypes.POINTER(_U32)]),
     "tb_fill_normal": (_S, [_P, _U32, _SZ, _U64, ctypes.c_double, ctypes.c_double, _S]),
     "tb_fill_uniform": (_S, [_P, _U32, _SZ, _U64, ctypes.c_double, ctypes.c_double, _S]),
     "tb_execute": (_S, [_P, _P, ctypes.c_char_p, ctypes.POINTER(Tensor), _U32, ctypes.POINTER(Tensor),

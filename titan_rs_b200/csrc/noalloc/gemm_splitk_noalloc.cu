@@ -18,10 +18,18 @@
 // overlap on the GPU (different streams, or different host threads on one
 // device) race on it and must be serialised by the caller. Nothing in the array
 // needs clearing: every partial the reduction reads is written earlier in the
-// same call. The small status word that the kernels' bounded waits write on a
-// timeout is cleared at the start of each call.
+// same call.
+//
+// The kernels run asynchronously, so the call itself cannot report a device-side
+// failure. Each bounded wait inside the split-K kernel that runs out writes a code
+// into a per-device status word (zero when the module loads) and the kernel then
+// returns early, which leaves C wrong. The word is sticky: later calls do not clear
+// it. tb_gemm_bf16_splitk_noalloc_status synchronises a stream, reads the word and
+// clears it, and returns TB_ERR_TIMEOUT with the code when any call on the device
+// since the previous query timed out. It allocates nothing either.
 #include <cuda_runtime.h>
 
+#include <cstdio>
 #include <mutex>
 
 #include "../../../include/titan_b200.h"
@@ -139,7 +147,6 @@ extern "C" tb_status tb_gemm_bf16_splitk_noalloc(uint64_t stream, const void* a,
   rc = encode(&tbm, b, (uint64_t)n, (uint64_t)k, TB_GEMM_BN);
   if (rc) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(static_cast<uintptr_t>(stream));
-  if ((e = cudaMemsetAsync(d.status, 0, sizeof(uint32_t), st)) != cudaSuccess) return rt_error("cudaMemsetAsync", e);
   const long long units = (long long)tiles * used;
   const unsigned grid = (unsigned)(units < d.sm_count ? units : d.sm_count);
   gemm_bf16_tn_splitk_noalloc<<<grid, TB_GEMM_THREADS, TB_GEMM_SMEM_BYTES, st>>>(ta, tbm, d.partial, m, n, k, used,
@@ -152,5 +159,33 @@ extern "C" tb_status tb_gemm_bf16_splitk_noalloc(uint64_t stream, const void* a,
                                                              (long long)n);
   if ((e = cudaGetLastError()) != cudaSuccess) return rt_error("splitk_reduce_bf16_noalloc", e);
   tb::note_launch("gemm_bf16_tn_splitk_noalloc");
+  return TB_OK;
+}
+
+extern "C" tb_status tb_gemm_bf16_splitk_noalloc_status(uint64_t stream, uint32_t* code) {
+  if (code) *code = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return rt_error("cudaGetDevice", e);
+  if (dev < 0 || dev >= kMaxDevices) return tb::set_error(TB_ERR_INVALID, "contract", "device ordinal out of range");
+  DeviceSetup& d = g_setup[dev];
+  std::call_once(d.once, setup_device, dev);
+  if (d.error != cudaSuccess) return rt_error(d.step, d.error);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(static_cast<uintptr_t>(stream));
+  // Stream order: the copy sees every earlier call on this stream; the clear follows it.
+  uint32_t word = 0;
+  if ((e = cudaMemcpyAsync(&word, d.status, sizeof(word), cudaMemcpyDeviceToHost, st)) != cudaSuccess)
+    return rt_error("cudaMemcpyAsync(status)", e);
+  if ((e = cudaMemsetAsync(d.status, 0, sizeof(uint32_t), st)) != cudaSuccess)
+    return rt_error("cudaMemsetAsync(status)", e);
+  if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return rt_error("cudaStreamSynchronize", e);
+  if (code) *code = word;
+  if (word != 0) {
+    char buf[160];
+    snprintf(buf, sizeof buf,
+             "a split-K no-alloc kernel gave up a bounded device-side wait (code 0x%08x); its output is invalid",
+             word);
+    return tb::set_error(TB_ERR_TIMEOUT, "wait", buf);
+  }
   return TB_OK;
 }
