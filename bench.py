@@ -14,7 +14,14 @@ Inputs are seeded synthetic data (no dataset exists for this path).
 `e2e` is the same metric through the C ABI with pinned-host inputs copied in and
 the result copied out inside every timed step (steps pipelined over two streams, so one
 step's upload overlaps the previous step's download). `--impl reference` times the CPU
-restatement of the reference's scalar operator (oracle/) on the host cores.
+restatement of the reference's scalar operator (oracle/) on the host cores; it never
+loads the product library (its inputs come from the oracle's copy of the generator).
+
+The headline line is `--op` (default gemm, C3). With `--ops` (default: the other three
+configs when `--op` is gemm) the same run measures C2, C4 and C5 the same way and
+reports them under "ops", each with value, ms_per_step, roofline, e2e and, at N=1,
+cpu_baseline; "ops" also holds C1, the reference's own CPU configuration (f32 256^3),
+timed on the host at one thread and at all threads beside the f32 kernel on the GPU.
 """
 from __future__ import annotations
 
@@ -108,6 +115,41 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- workloads
+def workload_config(op: str, world: int, small: bool = False) -> dict:
+    """The `config` object of a bench line; both arms print the same dict for the same run."""
+    if op == "softmax":
+        rows = 16384 if small else 32768
+        return {"workload": "C2 row softmax fp32 [32768,4096], x~N(0,2^2) seed 1", "rows": rows, "cols": 4096,
+                "parallelism": f"replicas{world}", "l2": f"inputs {rows * 4096 * 4 // 2**20} MiB > 126 MB L2"}
+    if op == "gemm":
+        m = 4096 if small else 8192
+        cfg = {"workload": f"C3 bf16 GEMM M=N=K={m}, A row-major N(0,1), B column-major N(0,1/K), seed 2",
+               "M": m, "N": m, "K": m, "parallelism": f"N-shard{world}" if world > 1 else "single",
+               "l2": f"inputs {2 * m * m * 2 // 2**20} MiB > 126 MB L2"}
+        if world > 1:
+            p2p = os.environ.get("TITAN_B200_ALLGATHER", "p2p") == "p2p"
+            cfg["allgather"] = ("fused GEMM + all-gather kernel: NVLink peer stores into registered C (CTA pairs "
+                                "with push warps; from 4 ranks, dedicated pusher CTAs: gemm_bf16_tn_allgather_2sm_push)"
+                                if p2p else "NCCL all-gather + re-layout kernel")
+        return cfg
+    if op == "sdpa":
+        b = 2 if small else 8
+        return {"workload": f"C4 causal SDPA fwd bf16 B{b} H32 S4096 D128, N(0,1) seed 3, "
+                            "scale 1/sqrt(128), FLOPs = 4*B*H*S^2*D/2",
+                "B": b, "H": 32, "S": 4096, "D": 128,
+                "parallelism": f"bh-shard{world}" if world > 1 else "single",
+                "l2": f"inputs {3 * b * 32 * 4096 * 128 * 2 // world // 2**20} MiB per GPU vs 126 MB L2"}
+    if op == "conv2d":
+        n = 16 if small else 64
+        return {"workload": f"C5 conv2d fwd bf16 NHWC N{n} 56x56 Cin256 Cout256 3x3 s1 p1, "
+                            "x N(0,1), w N(0,2/2304), seed 4",
+                "N": n, "H": 56, "W": 56, "Cin": 256, "Cout": 256, "R": 3, "S": 3,
+                "parallelism": f"batch-shard{world}" if world > 1 else "single",
+                "l2": f"3 rotating input/output pairs ({3 * 2 * n * 56 * 56 * 256 * 2 // world // 2**20} MiB "
+                      "working set per GPU > 126 MB L2)"}
+    raise ValueError(op)
+
+
 class Workload:
     """One hot-path op at one configuration, on one rank."""
     name = ""
@@ -210,12 +252,11 @@ class SoftmaxWorkload(Workload):
         return self.nbytes
 
     def config(self):
-        return {"workload": "C2 row softmax fp32 [32768,4096], x~N(0,2^2) seed 1", "rows": self.rows,
-                "cols": self.cols, "parallelism": f"replicas{self.world}", "l2": "inputs 512 MiB > 126 MB L2"}
+        return workload_config(self.name, self.world, self.small)
 
-    def cpu_sample(self, budget_s):
+    def cpu_sample(self, budget_s, threads=0):
         import oracle
-        threads = oracle.num_threads()
+        threads = threads or oracle.num_threads()
         rows = 256
         t0 = time.perf_counter()
         done = 0
@@ -347,18 +388,11 @@ class GemmWorkload(Workload):
         return self.c_bytes
 
     def config(self):
-        cfg = {"workload": f"C3 bf16 GEMM M=N=K={self.M}, A row-major N(0,1), B column-major N(0,1/K), seed 2",
-               "M": self.M, "N": self.N, "K": self.K, "parallelism": f"N-shard{self.world}" if self.world > 1
-               else "single", "l2": "inputs 256 MiB > 126 MB L2"}
-        if self.world > 1:
-            cfg["allgather"] = ("fused GEMM + all-gather kernel: NVLink peer stores into registered C (CTA pairs "
-                                "with push warps; from 4 ranks, dedicated pusher CTAs: gemm_bf16_tn_allgather_2sm_push)"
-                                if self.allgather == "p2p" else "NCCL all-gather + re-layout kernel")
-        return cfg
+        return workload_config(self.name, self.world, self.small)
 
-    def cpu_sample(self, budget_s):
+    def cpu_sample(self, budget_s, threads=0):
         import oracle
-        threads = oracle.num_threads()
+        threads = threads or oracle.num_threads()
         rng = np.random.default_rng(0)
         pts = 0
         t0 = time.perf_counter()
@@ -447,15 +481,11 @@ class SdpaWorkload(Workload):
         return self.nbytes
 
     def config(self):
-        return {"workload": f"C4 causal SDPA fwd bf16 B{self.B} H{self.H} S{self.S} D{self.D}, N(0,1) seed 3, "
-                            "scale 1/sqrt(128), FLOPs = 4*B*H*S^2*D/2",
-                "B": self.B, "H": self.H, "S": self.S, "D": self.D,
-                "parallelism": f"bh-shard{self.world}" if self.world > 1 else "single",
-                "l2": f"inputs {3 * self.nbytes / 2**20:.0f} MiB per GPU vs 126 MB L2"}
+        return workload_config(self.name, self.world, self.small)
 
-    def cpu_sample(self, budget_s):
+    def cpu_sample(self, budget_s, threads=0):
         import oracle
-        threads = oracle.num_threads()
+        threads = threads or oracle.num_threads()
         S, D = self.S, self.D
         rng = np.random.default_rng(0)
         macs = 0.0
@@ -567,15 +597,11 @@ class ConvWorkload(Workload):
         return self.y_bytes
 
     def config(self):
-        return {"workload": f"C5 conv2d fwd bf16 NHWC N{self.N} {self.H}x{self.W} Cin{self.C} Cout{self.K} 3x3 s1 p1, "
-                            "x N(0,1), w N(0,2/2304), seed 4",
-                "N": self.N, "H": self.H, "W": self.W, "Cin": self.C, "Cout": self.K, "R": self.R, "S": self.S,
-                "parallelism": f"batch-shard{self.world}" if self.world > 1 else "single",
-                "l2": f"{self.ROTATE} rotating input/output pairs (588 MB working set > 126 MB L2)"}
+        return workload_config(self.name, self.world, self.small)
 
-    def cpu_sample(self, budget_s):
+    def cpu_sample(self, budget_s, threads=0):
         import oracle
-        threads = oracle.num_threads()
+        threads = threads or oracle.num_threads()
         rng = np.random.default_rng(0)
         pts = 0
         t0 = time.perf_counter()
@@ -631,165 +657,219 @@ def reduce_max(dist, value: float) -> float:
 
 
 def run_reference_arm(args, world, rank):
-    """CPU restatement of the reference's scalar operator, all host threads, bounded samples."""
+    """The reference's scalar CPU operators (the oracle's restatement) on all host threads.
+
+    Each step is one bounded sample of the configuration's work (args.ref_step_seconds of
+    CPU time); the rate is extrapolated per output element or row. The product library is
+    not loaded: the inputs come from the oracle's copy of the seeded generator."""
     if rank != 0:
         return 0
-    sys.path.insert(0, str(ROOT))
-    import titan_rs_b200 as tb
     import oracle
     wl_cls = WORKLOADS[args.op]
     sampler = REFERENCE_SAMPLERS[args.op]
+    threads = oracle.num_threads()
+    inputs = sampler(oracle, None, 0, 0)  # the sample's inputs, made once before the steps
     times = []
     info = None
     for i in range(args.warmup + args.steps):
         t0 = time.perf_counter()
-        info = sampler(tb, oracle, budget_s=args.ref_step_seconds)
+        info = sampler(oracle, inputs, args.ref_step_seconds, threads)
         if i >= args.warmup:
             times.append(time.perf_counter() - t0)
+    single = sampler(oracle, inputs, max(args.ref_step_seconds / 2, 0.5), 1)
+    cpu = {"value": info["value"], "unit": info["unit"], "cores": threads, "kind": "port",
+           "sample": info["sample"] + "; ms_per_step is the wall time of one such bounded sample",
+           "single_thread": {"value": single["value"], "cores": 1, "sample": single["sample"]}}
     line = {"impl": "reference", "metric": wl_cls.metric, "value": info["value"], "unit": info["unit"],
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000.0 * statistics.mean(times), "higher_is_better": True, "scaling": wl_cls.scaling,
-            "vs_baseline": None, "dtype": wl_cls.dtype, "data": "synthetic",
-            "config": info["config"],
-            "cpu_baseline": {"value": info["value"], "unit": info["unit"], "cores": info["cores"], "kind": "port",
-                             "sample": info["sample"]},
+            "vs_baseline": None, "dtype": wl_cls.dtype, "data": "synthetic (seeded, BASELINE.json shapes)",
+            "config": workload_config(args.op, world), "op": wl_cls.name, "cpu_baseline": cpu,
             "e2e": {"value": info["value"], "unit": info["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    ops = {}
+    for op in parse_ops(args):
+        samp = REFERENCE_SAMPLERS[op]
+        ins = samp(oracle, None, 0, 0)
+        r = samp(oracle, ins, args.ref_step_seconds, threads)
+        r1 = samp(oracle, ins, max(args.ref_step_seconds / 2, 0.5), 1)
+        ops[OP_LABEL[op]] = {"metric": WORKLOADS[op].metric, "value": r["value"], "unit": r["unit"],
+                             "config": workload_config(op, world),
+                             "cpu_baseline": {"value": r["value"], "unit": r["unit"], "cores": threads,
+                                              "kind": "port", "sample": r["sample"],
+                                              "single_thread": {"value": r1["value"], "cores": 1,
+                                                                "sample": r1["sample"]}}}
+    if parse_ops(args) or args.op == DEFAULT_OP:
+        ops["C1"] = c1_cpu(oracle, threads)
+    if ops:
+        line["ops"] = ops
+    if any(m == "titan_rs_b200" or m.startswith("titan_rs_b200.") for m in sys.modules):
+        raise SystemExit("the reference arm loaded the product library")
     print(json.dumps(line), flush=True)
     return 0
 
 
-def _ref_softmax(tb, oracle, budget_s):
+def _timed(budget_s, fn):
+    """Calls fn() until budget_s has passed (at least once); returns (calls, seconds)."""
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        fn()
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    return n, time.perf_counter() - t0
+
+
+def _ref_softmax(oracle, inputs, budget_s, threads):
     rows, cols = SoftmaxWorkload.rows, SoftmaxWorkload.cols
     chunk = 512
-    x = tb.fill_normal(chunk * cols, seed=1, std=2.0).reshape(chunk, cols)  # the first rows of the C2 tensor
-    threads = oracle.num_threads()
-    t0 = time.perf_counter()
-    n = 0
-    while time.perf_counter() - t0 < budget_s or n == 0:
-        oracle.softmax_rows_mt(x, threads)
-        n += 1
-    dt = time.perf_counter() - t0
-    return {"value": n * chunk * cols * 8 / dt / 1e9, "unit": "GB/s", "cores": threads,
-            "sample": f"{n * chunk} of {rows} rows of C2 in {dt:.1f} s",
-            "config": {"workload": "C2 row softmax fp32 [32768,4096], x~N(0,2^2) seed 1", "rows": rows, "cols": cols}}
+    if inputs is None:  # the first rows of the C2 tensor
+        return oracle.fill_normal(chunk * cols, 1, 0.0, 2.0).reshape(chunk, cols)
+    n, dt = _timed(budget_s, lambda: oracle.softmax_rows_mt(inputs, threads))
+    return {"value": n * chunk * cols * 8 / dt / 1e9, "unit": "GB/s",
+            "sample": f"{n} passes over the first {chunk} of the {rows} rows of C2 ({n * chunk} rows) in {dt:.1f} s "
+                      f"on {threads} threads; bytes = 8 per element (read x, write y)"}
 
 
-def _ref_gemm(tb, oracle, budget_s):
-    from titan_rs_b200.kernel_abi import DType
-    M = N = K = GemmWorkload.M
+def _ref_gemm(oracle, inputs, budget_s, threads):
+    K = GemmWorkload.K
     rows_needed = 512
-    # The first 512 rows of A and of B's [N,K] storage: the sample draws only from those.
-    a = tb.fill_normal(rows_needed * K, seed=tensor_seed(2, 0), dtype=DType.BF16).reshape(rows_needed, K)
-    b = tb.fill_normal(rows_needed * K, seed=tensor_seed(2, 1), std=1.0 / math.sqrt(K),
-                       dtype=DType.BF16).reshape(rows_needed, K)
-    threads = oracle.num_threads()
+    if inputs is None:  # the first 512 rows of A and of B's [N,K] storage: the sample draws only from those
+        return (oracle.fill_normal(rows_needed * K, tensor_seed(2, 0), bf16=True).reshape(rows_needed, K),
+                oracle.fill_normal(rows_needed * K, tensor_seed(2, 1), 0.0, 1.0 / math.sqrt(K),
+                                   bf16=True).reshape(rows_needed, K))
+    a, b = inputs
     rng = np.random.default_rng(0)
-    pts = 0
-    t0 = time.perf_counter()
-    while time.perf_counter() - t0 < budget_s or pts == 0:
-        rows = rng.integers(0, rows_needed, 2048)
-        cols = rng.integers(0, rows_needed, 2048)
-        oracle.gemm_bf16_points(a, b, True, rows_needed, rows_needed, K, rows, cols, threads)
-        pts += 2048
-    dt = time.perf_counter() - t0
-    return {"value": 2.0 * K * pts / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
-            "sample": f"{pts} C elements of C3 ({K}-long dot products in the reference loop order) in {dt:.1f} s; "
-                      f"rate extrapolated per element",
-            "config": {"workload": f"C3 bf16 GEMM M=N=K={M}, A row-major N(0,1), B column-major N(0,1/K), seed 2",
-                       "M": M, "N": N, "K": K}}
+
+    def one():
+        oracle.gemm_bf16_points(a, b, True, rows_needed, rows_needed, K, rng.integers(0, rows_needed, 2048),
+                                rng.integers(0, rows_needed, 2048), threads)
+
+    n, dt = _timed(budget_s, one)
+    pts = n * 2048
+    return {"value": 2.0 * K * pts / dt / 1e12, "unit": "TFLOP/s",
+            "sample": f"{pts} C elements of C3 ({K}-long dot products in the reference loop order) in {dt:.1f} s "
+                      f"on {threads} threads; rate extrapolated per element"}
 
 
-def _ref_sdpa(tb, oracle, budget_s):
-    from titan_rs_b200.kernel_abi import DType
-    B, H, S, D = SdpaWorkload.B, SdpaWorkload.H, SdpaWorkload.S, SdpaWorkload.D
+def _ref_sdpa(oracle, inputs, budget_s, threads):
+    S, D = SdpaWorkload.S, SdpaWorkload.D
     heads = 2  # the first two (b, h) pairs of C4
-    n = heads * S * D
-    q, k, v = (tb.fill_normal(n, seed=tensor_seed(3, i), dtype=DType.BF16) for i in range(3))
-    threads = oracle.num_threads()
+    if inputs is None:
+        return [oracle.fill_normal(heads * S * D, tensor_seed(3, i), bf16=True) for i in range(3)]
+    q, k, v = inputs
     rng = np.random.default_rng(0)
-    macs, rows_done = 0.0, 0
-    t0 = time.perf_counter()
-    while time.perf_counter() - t0 < budget_s or rows_done == 0:
+    acc = {"macs": 0.0, "rows": 0}
+
+    def one():
         ids = np.sort(rng.integers(0, heads * S, 256))
         oracle.sdpa_bf16_rows(q, k, v, 1, heads, S, S, D, True, ids, threads=threads)
-        macs += float(np.sum((ids % S) + 1)) * 2 * D
-        rows_done += ids.size
-    dt = time.perf_counter() - t0
-    return {"value": 2.0 * macs / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
-            "sample": f"{rows_done} causal query rows of the first 2 heads of C4 in {dt:.1f} s",
-            "config": {"workload": f"C4 causal SDPA fwd bf16 B{B} H{H} S{S} D{D}, N(0,1) seed 3", "B": B, "H": H,
-                       "S": S, "D": D}}
+        acc["macs"] += float(np.sum((ids % S) + 1)) * 2 * D
+        acc["rows"] += ids.size
+
+    n, dt = _timed(budget_s, one)
+    return {"value": 2.0 * acc["macs"] / dt / 1e12, "unit": "TFLOP/s",
+            "sample": f"{acc['rows']} causal query rows of the first 2 heads of C4 in {dt:.1f} s on {threads} "
+                      "threads; FLOP/s of the rows computed"}
 
 
-def _ref_conv2d(tb, oracle, budget_s):
-    from titan_rs_b200.kernel_abi import DType
+def _ref_conv2d(oracle, inputs, budget_s, threads):
     wl = ConvWorkload
     imgs = 2  # the first two images of C5
-    x = tb.fill_normal(imgs * wl.H * wl.W * wl.C, seed=tensor_seed(4, 0), dtype=DType.BF16)
-    w = tb.fill_normal(wl.K * wl.R * wl.S * wl.C, seed=tensor_seed(4, 1), std=math.sqrt(2.0 / (wl.R * wl.S * wl.C)),
-                       dtype=DType.BF16)
-    threads = oracle.num_threads()
+    if inputs is None:
+        return (oracle.fill_normal(imgs * wl.H * wl.W * wl.C, tensor_seed(4, 0), bf16=True),
+                oracle.fill_normal(wl.K * wl.R * wl.S * wl.C, tensor_seed(4, 1), 0.0,
+                                   math.sqrt(2.0 / (wl.R * wl.S * wl.C)), bf16=True))
+    x, w = inputs
     rng = np.random.default_rng(0)
-    pts = 0
-    t0 = time.perf_counter()
-    while time.perf_counter() - t0 < budget_s or pts == 0:
+
+    def one():
         idx = rng.integers(0, imgs * wl.H * wl.W * wl.K, 2048)
         oracle.conv2d_nhwc_bf16_points(x, w, None, imgs, wl.H, wl.W, wl.C, wl.K, wl.R, wl.S, (1, 1), (1, 1), (1, 1),
                                        wl.H, wl.W, idx, threads)
-        pts += 2048
-    dt = time.perf_counter() - t0
-    return {"value": 2.0 * wl.C * wl.R * wl.S * pts / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
-            "sample": f"{pts} output elements of the first 2 images of C5 in {dt:.1f} s",
-            "config": {"workload": f"C5 conv2d fwd bf16 NHWC N{wl.N} {wl.H}x{wl.W} Cin{wl.C} Cout{wl.K} 3x3 s1 p1",
-                       "N": wl.N, "H": wl.H, "W": wl.W, "Cin": wl.C, "Cout": wl.K}}
+
+    n, dt = _timed(budget_s, one)
+    pts = n * 2048
+    return {"value": 2.0 * wl.C * wl.R * wl.S * pts / dt / 1e12, "unit": "TFLOP/s",
+            "sample": f"{pts} output elements of the first 2 images of C5 in {dt:.1f} s on {threads} threads; "
+                      "rate extrapolated per element (border taps counted)"}
 
 
 REFERENCE_SAMPLERS = {"softmax": _ref_softmax, "gemm": _ref_gemm, "sdpa": _ref_sdpa, "conv2d": _ref_conv2d}
+OP_LABEL = {"softmax": "C2", "gemm": "C3", "sdpa": "C4", "conv2d": "C5"}
+C1_FLOP = 2.0 * 256 ** 3
 
 
-def main(argv=None) -> int:
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--op", default=DEFAULT_OP, choices=sorted(WORKLOADS))
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU baseline sample budget (rank 0, N=1)")
-    ap.add_argument("--ref-step-seconds", type=float, default=4.0)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--small", action="store_true",
-                    help="reduced problem (still larger than L2) for profiler captures; not a bench line")
-    args = ap.parse_args(argv)
-    if args.warmup < 3:
-        args.warmup = 3
-    world, rank, local = dist_env()
-    if args.impl == "reference":
-        return run_reference_arm(args, world, rank)
+def c1_inputs(oracle):
+    """C1: A, B f32 [256, 256] row-major, U[-1, 1), seed 0 (A = seed 0, B = seed 1)."""
+    a = oracle.fill_uniform(256 * 256, tensor_seed(0, 0), -1.0, 1.0).reshape(256, 256)
+    b = oracle.fill_uniform(256 * 256, tensor_seed(0, 1), -1.0, 1.0).reshape(256, 256)
+    return a, b
 
-    import titan_rs_b200 as tb
-    from titan_rs_b200 import _native as N
-    dist = init_dist(world, local)
-    session = tb.Session(local)
-    stream = session.create_stream()
-    comm = None
-    if world > 1 and args.op == "gemm":
-        from titan_rs_b200 import distributed as D
-        comm = D.NcclCollective(session, D.broadcast_comm_id(rank), world, rank, timeout_ms=60000)
-    wl = WORKLOADS[args.op](tb, session, stream, rank, world, comm=comm, small=args.small)
-    peaks, peak_src = load_peaks()
 
+def c1_cpu(oracle, threads, budget_s=1.0):
+    """The reference's scalar gemm (rt:955-989) on the whole of C1, one thread and all threads."""
+    a, b = c1_inputs(oracle)
+    n1, dt1 = _timed(budget_s, lambda: oracle.gemm(a, b))
+    nt, dtt = _timed(budget_s, lambda: oracle.gemm_mt(a, b, threads))
+    return {"metric": "CPU scalar-reference MatMul f32 C[256,256] = A[256,256] B[256,256] GFLOP/s",
+            "unit": "GFLOP/s",
+            "config": {"workload": "C1 f32 GEMM M=N=K=256 row-major, A,B ~ U[-1,1) seed 0", "M": 256, "N": 256,
+                       "K": 256},
+            "cpu_baseline": {"value": nt * C1_FLOP / dtt / 1e9, "unit": "GFLOP/s", "cores": threads, "kind": "port",
+                             "sample": f"{nt} full 256^3 products in {dtt:.2f} s on {threads} threads (rows split)",
+                             "single_thread": {"value": n1 * C1_FLOP / dt1 / 1e9, "cores": 1,
+                                               "sample": f"{n1} full 256^3 products in {dt1:.2f} s, one thread, "
+                                                         "the reference's loop order"}}}
+
+
+def parse_ops(args) -> list:
+    """The extra configurations measured in the same run (never the headline op itself)."""
+    if args.ops == "default":
+        names = ["softmax", "sdpa", "conv2d"] if args.op == DEFAULT_OP else []
+    elif args.ops in ("", "none"):
+        names = []
+    else:
+        names = [o.strip() for o in args.ops.split(",") if o.strip()]
+        for o in names:
+            if o not in WORKLOADS:
+                raise SystemExit(f"--ops: unknown op {o}")
+    return [o for o in names if o != args.op]
+
+
+def roofline_of(wl, per_launch_ms, peaks, peak_src, small):
+    scale = 1e9 if wl.unit == "GB/s" else 1e12
+    achieved = wl.units_per_step() / (per_launch_ms / 1e3) / scale
+    if wl.bound == "hbm":
+        peak, r_unit = float(peaks.get("hbm_gbs", PEAK_FALLBACK["hbm_gbs"])), "GB/s"
+    else:
+        peak, r_unit = float(peaks.get("bf16_tflops", PEAK_FALLBACK["bf16_tflops"])), "TFLOP/s"
+    line = {"bound": wl.bound, "kernel": wl.kernel, "achieved": achieved, "peak": peak, "unit": r_unit,
+            "frac": achieved / peak, "peak_source": "measured burst figure (MEASURED_PEAKS.json)"
+            if peak_src == "measured" else "fallback", "ms_per_launch": per_launch_ms,
+            "algorithmic_units_per_launch": wl.units_per_step()}
+    line.update(traffic_of(wl.kernel, wl.world == 1 and not small))
+    return line
+
+
+def measure(wl, args, session, stream, dist, peaks, peak_src, tb, N) -> dict:
+    """Warm-up, a clock soak, K device-timed steps (max over ranks), the kernel's roofline and
+    the end-to-end figure through the C ABI with host buffers, for one workload."""
     w0 = session.record(stream)
     for _ in range(args.warmup):
         wl.step()
     w1 = session.record(stream)
     session.synchronize(stream)
+    # The kernel the operator actually launched for this workload (the roofline names it).
+    wl.kernel = N.lib().tb_last_candidate().decode()
     est_ms = max(session.elapsed_ms(w0, w1) / args.warmup, 1e-3)
 
     # nvidia-smi samples every 50 ms: keep the GPU busy with untimed steps for
     # ~0.3 s first so the clock record covers the load the timed steps run under.
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
     clocks.start()
-    soak = 0 if args.small else int(reduce_max(dist, float(min(max(300.0 / est_ms, 1), 20000))))
+    soak = 0 if args.small or args.soak_ms <= 0 else int(
+        reduce_max(dist, float(min(max(args.soak_ms / est_ms, 1), 20000))))
     for _ in range(soak):
         wl.step()
 
@@ -814,33 +894,29 @@ def main(argv=None) -> int:
     scale = 1e9 if wl.unit == "GB/s" else 1e12
     value = units_step / (ms_step / 1e3) / scale
 
-    # Roofline of the dominant kernel: its algorithmic units per launch / its
-    # average launch duration, timed alone on the launching stream.
-    # With a collective in the step (sharded GEMM), the kernel is also timed
-    # alone: that is the compute phase, reported beside the end-to-end value.
+    # Roofline of the dominant kernel: its algorithmic units per launch / its average
+    # launch duration on the launching stream. With a collective in the step (sharded
+    # GEMM) the GEMM kernel is also timed alone: that is the compute phase, reported
+    # beside the end-to-end value.
     kernel_ms = wl.dominant_kernel_ms(session, stream, args.steps) if hasattr(wl, "dominant_kernel_ms") else None
     compute_phase = None
     if kernel_ms is not None:
+        step_kernel = wl.kernel
+        wl.kernel = N.lib().tb_last_candidate().decode()
         kernel_ms_max = reduce_max(dist, kernel_ms)
         compute_phase = {"ms_per_step": kernel_ms_max, "value": units_step / (kernel_ms_max / 1e3) / scale,
-                         "note": "GEMM kernel alone on this rank's shard, max over ranks (no all-gather, no re-layout)"}
+                         "kernel": wl.kernel, "step_kernel": step_kernel,
+                         "note": "GEMM kernel alone on this rank's shard, max over ranks (no all-gather); the step "
+                                 "itself is bound by the all-gather's NVLink traffic"}
     per_launch_ms = kernel_ms if kernel_ms is not None else local_ms / args.steps
-    achieved = wl.units_per_step() / (per_launch_ms / 1e3) / scale
-    if wl.bound == "hbm":
-        peak = float(peaks.get("hbm_gbs", PEAK_FALLBACK["hbm_gbs"]))
-        r_unit = "GB/s"
-    else:
-        peak = float(peaks.get("bf16_tflops", PEAK_FALLBACK["bf16_tflops"]))
-        r_unit = "TFLOP/s"
-    # Captured on the 1-GPU configuration of each kernel; a shard has other traffic.
-    traffic = TRAFFIC_PER_LAUNCH.get(wl.kernel) if wl.world == 1 and not args.small else None
+    roofline = roofline_of(wl, per_launch_ms, peaks, peak_src, args.small)
 
     # End to end through the C ABI with pinned host buffers: every step copies its inputs
     # in and its result out. Steps are pipelined as a server would run them: uploads and
     # the operator on the main stream, downloads on a second stream, so step i+1's upload
     # overlaps step i's download (PCIe is full duplex); the operator of step i+1 waits
     # for step i's download, since it overwrites the result buffer.
-    e2e_ms = e2e_value = None
+    e2e = None
     if not args.small:
         out_stream = session.create_stream()
 
@@ -867,29 +943,128 @@ def main(argv=None) -> int:
         session.synchronize(out_stream)
         session.synchronize(stream)
         e2e_ms = reduce_max(dist, session.elapsed_ms(e0, e1)) / e2e_steps
-        e2e_value = units_step / (e2e_ms / 1e3) / scale
+        e2e = {"value": units_step / (e2e_ms / 1e3) / scale, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d_bytes(),
+               "d2h_bytes_per_step": wl.d2h_bytes(), "ms_per_step": e2e_ms}
+    out = {"metric": wl.metric, "value": value, "unit": wl.unit, "ms_per_step": ms_step, "scaling": wl.scaling,
+           "dtype": wl.dtype, "config": wl.config(), "op": wl.name, "roofline": roofline, "e2e": e2e,
+           "gpu_launches": launches, "clocks": clock_info}
+    if compute_phase is not None:
+        out["compute_phase"] = compute_phase
+    return out
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.small:
-        cpu = wl.cpu_sample(args.cpu_seconds)
+
+def cpu_baseline_of(wl, budget_s):
+    """All host threads on a bounded sample, then one thread on a shorter one."""
+    cpu = wl.cpu_sample(budget_s)
+    one = wl.cpu_sample(max(budget_s / 4, 0.5), threads=1)
+    cpu["single_thread"] = {"value": one["value"], "cores": 1, "sample": one["sample"]}
+    return cpu
+
+
+def c1_gpu(tb, N, session, stream, steps):
+    """The f32 reference-ABI GEMM on the GPU over C1's inputs (device-timed, launch-bound)."""
+    import ctypes
+    from titan_rs_b200.kernel_abi import DType
+    a = tb.fill_uniform(256 * 256, seed=tensor_seed(0, 0), low=-1.0, high=1.0).reshape(256, 256)
+    b = tb.fill_uniform(256 * 256, seed=tensor_seed(0, 1), low=-1.0, high=1.0).reshape(256, 256)
+    bufs = [session.allocate(256 * 256 * 4) for _ in range(3)]
+    session.upload(stream, bufs[0], a)
+    session.upload(stream, bufs[1], b)
+    ta, tbm, tc = (_tensor(tb, buf, DType.F32, (256, 256)) for buf in bufs)
+
+    def step():
+        rc = N.lib().tb_op_gemm(session.ptr, stream.ptr, ctypes.byref(ta), ctypes.byref(tbm), ctypes.byref(tc), None,
+                                0, None)
+        if rc:
+            raise RuntimeError(N.last_error())
+
+    for _ in range(3):
+        step()
+    session.synchronize(stream)
+    kernel = N.lib().tb_last_candidate().decode()
+    e0 = session.record(stream)
+    for _ in range(steps):
+        step()
+    e1 = session.record(stream)
+    session.synchronize(stream)
+    ms = session.elapsed_ms(e0, e1) / steps
+    return {"value": C1_FLOP / (ms / 1e3) / 1e9, "unit": "GFLOP/s", "ms_per_step": ms, "kernel": kernel,
+            "note": "f32 reference ABI on CUDA cores (bit-identical to the scalar reference); launch-bound at this size"}
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--op", default=DEFAULT_OP, choices=sorted(WORKLOADS))
+    ap.add_argument("--ops", default="default",
+                    help="extra configs measured in the same run: comma list of ops, 'none', or 'default' "
+                         "(softmax,sdpa,conv2d when --op is gemm)")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU baseline sample budget (rank 0, N=1)")
+    ap.add_argument("--ops-cpu-seconds", type=float, default=4.0, help="CPU baseline budget of each extra config")
+    ap.add_argument("--ref-step-seconds", type=float, default=2.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--soak-ms", type=float, default=300.0,
+                    help="untimed steps run before the timed ones so the clocks settle under load (0: none)")
+    ap.add_argument("--small", action="store_true",
+                    help="reduced problem (still larger than L2) for profiler captures; not a bench line")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        return run_reference_arm(args, world, rank)
+
+    import gc
+
+    import titan_rs_b200 as tb
+    from titan_rs_b200 import _native as N
+    dist = init_dist(world, local)
+    session = tb.Session(local)
+    stream = session.create_stream()
+    comm = None
+    if world > 1 and args.op == "gemm":
+        from titan_rs_b200 import distributed as D
+        comm = D.NcclCollective(session, D.broadcast_comm_id(rank), world, rank, timeout_ms=60000)
+    peaks, peak_src = load_peaks()
+    cpu_leg = rank == 0 and world == 1 and not args.no_cpu_baseline and not args.small
+
+    wl = WORKLOADS[args.op](tb, session, stream, rank, world, comm=comm, small=args.small)
+    head = measure(wl, args, session, stream, dist, peaks, peak_src, tb, N)
+    cpu = cpu_baseline_of(wl, args.cpu_seconds) if cpu_leg else None
+    del wl
+    gc.collect()
+
+    ops = {}
+    for op in parse_ops(args):
+        w = WORKLOADS[op](tb, session, stream, rank, world, small=args.small)
+        r = measure(w, args, session, stream, dist, peaks, peak_src, tb, N)
+        r["cpu_baseline"] = cpu_baseline_of(w, args.ops_cpu_seconds) if cpu_leg else None
+        ops[OP_LABEL[op]] = r
+        del w
+        gc.collect()
+    if ops and not args.small:
+        c1 = {"gpu": c1_gpu(tb, N, session, stream, args.steps)}
+        if cpu_leg:
+            import oracle
+            c1.update(c1_cpu(oracle, oracle.num_threads()))
+        ops["C1"] = c1
 
     if rank == 0:
         line = {
-            "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": wl.scaling,
-            "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded, BASELINE.json shapes)",
-            "config": wl.config(), "op": wl.name,
-            "roofline": {"bound": wl.bound, "kernel": wl.kernel, "achieved": achieved, "peak": peak, "unit": r_unit,
-                         "frac": achieved / peak, "peak_source": f"{peak_src} (MEASURED_PEAKS.json)"
-                         if peak_src == "measured" else "fallback", "traffic": traffic},
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d_bytes(),
-                    "d2h_bytes_per_step": wl.d2h_bytes(), "ms_per_step": e2e_ms},
-            "gpu_launches": launches,
-            "clocks": clock_info,
+            "metric": head["metric"], "value": head["value"], "unit": head["unit"], "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+            "scaling": head["scaling"], "vs_baseline": None, "dtype": head["dtype"],
+            "data": "synthetic (seeded, BASELINE.json shapes)", "config": head["config"], "op": head["op"],
+            "roofline": head["roofline"], "cpu_baseline": cpu, "e2e": head["e2e"],
+            "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
         }
-        if compute_phase is not None:
-            line["compute_phase"] = compute_phase
+        if "compute_phase" in head:
+            line["compute_phase"] = head["compute_phase"]
+        if ops:
+            line["ops"] = ops
         print(json.dumps(line), flush=True)
     if dist is not None:
         session.synchronize(stream)
@@ -901,16 +1076,40 @@ def main(argv=None) -> int:
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one full-size launch of
-# each default kernel at N=1, from the 1-pass ncu captures summarised in
-# profiles/dram_traffic_full_size.md. Kernels not listed report null.
-TRAFFIC_PER_LAUNCH: dict = {
-    "softmax_f32_warp32": 536.99e6 + 480.30e6,
-    "gemm_bf16_tn": 997.83e6 + 127.29e6,
-    "gemm_bf16_tn_2sm": 1088.31e6 + 127.76e6,
-    "sdpa_fwd_bf16_d128_pair": 806.43e6 + 253.34e6,
-    "conv2d_fprop_bf16_nhwc": 104.21e6 + 53.92e6,
-    "conv2d_fprop_bf16_nhwc_2sm": 104.09e6 + 55.92e6,
-}
+# each kernel at N=1, from 1-pass ncu captures of bench.py. Each figure carries the
+# SHA-256 prefix of the kernel's sources (its .cu file, every shared .cuh and the tile
+# configuration header) at capture time; when the sources differ now, the figure
+# belongs to another build of the kernel and the bench prints null instead.
+TRAFFIC_PER_LAUNCH: dict = {}
+
+KERNEL_SOURCE = {"softmax_f32_warp": "softmax.cu", "gemm_bf16_tn": "gemm_bf16.cu", "gemm_bf16_nn": "gemm_bf16.cu",
+                 "gemm_bf16_ta": "gemm_bf16.cu", "sdpa_fwd_bf16_d128_pair": "sdpa_bf16_pair.cu",
+                 "sdpa_fwd_bf16_d128_bn64": "sdpa_bf16_bn64.cu", "sdpa_fwd_bf16_d128": "sdpa_bf16.cu",
+                 "conv2d_fprop_bf16_nhwc": "conv2d_bf16.cu"}
+
+
+def kernel_source_digest(kernel: str):
+    import hashlib
+    kdir = ROOT / "titan_rs_b200" / "csrc" / "kernels"
+    src = next((f for prefix, f in sorted(KERNEL_SOURCE.items(), key=lambda kv: -len(kv[0]))
+                if kernel.startswith(prefix)), None)
+    if src is None:
+        return None
+    h = hashlib.sha256()
+    for path in [kdir / src] + sorted(kdir.glob("*.cuh")) + [kdir / "kernel_configs.h"]:
+        h.update(path.name.encode())
+        h.update(path.read_bytes())
+    return h.hexdigest()[:16]
+
+
+def traffic_of(kernel: str, full_size_single_gpu: bool) -> dict:
+    entry = TRAFFIC_PER_LAUNCH.get(kernel)
+    if not full_size_single_gpu or entry is None:
+        return {"traffic": None, "traffic_note": "no ncu capture of this kernel at this configuration"}
+    if entry["source_sha16"] != kernel_source_digest(kernel):
+        return {"traffic": None, "traffic_note": "the ncu capture was of another build of this kernel"}
+    return {"traffic": entry["read"] + entry["write"], "traffic_read": entry["read"], "traffic_write": entry["write"],
+            "traffic_note": f"ncu dram__bytes_read.sum + dram__bytes_write.sum per launch ({entry['capture']})"}
 
 
 if __name__ == "__main__":

@@ -57,6 +57,9 @@ def lib():
                                         _i64p, _sz, _f32p, ctypes.c_int]
     L.oracle_conv2d_nhwc_bf16_points.argtypes = [_u16p, _u16p, ctypes.c_void_p] + [_sz] * 15 + [_i64p, _sz, _f32p,
                                                                                               ctypes.c_int]
+    for name in ("oracle_fill_uniform", "oracle_fill_normal"):
+        getattr(L, name).argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_uint64, _sz, ctypes.c_uint64,
+                                     ctypes.c_double, ctypes.c_double, ctypes.c_int]
     _lib = L
     return L
 
@@ -225,3 +228,23 @@ def conv2d_nhwc_bf16_points(x_bits, w_bits, bias, n, h, w, cin, cout, r, s, stri
 
 def cpu_count() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+# ---- seeded synthetic inputs (the benchmark's generator, without the product library) ----
+
+def _fill(fn, count, seed, a, b, bf16, first, threads):
+    out = np.empty(int(count), dtype=np.uint16 if bf16 else np.float32)
+    _check(fn(out.ctypes.data_as(ctypes.c_void_p), int(bool(bf16)), int(first), int(count), int(seed), float(a),
+              float(b), int(threads)))
+    return out
+
+
+def fill_normal(count, seed, mean=0.0, std=1.0, bf16=False, first=0, threads=0) -> np.ndarray:
+    """Elements [first, first + count) of the seeded normal fill (f32, or bf16 bit patterns)."""
+    return _fill(lib().oracle_fill_normal, count, seed, mean, std, bf16, first, threads)
+
+
+def fill_uniform(count, seed, low=0.0, high=1.0, bf16=False, first=0, threads=0) -> np.ndarray:
+    """Elements [first, first + count) of the seeded uniform fill in [low, high)."""
+    return _fill(lib().oracle_fill_uniform, count, seed, low, high, bf16, first, threads)
+

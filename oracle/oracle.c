@@ -326,3 +326,59 @@ int oracle_conv2d_nhwc_bf16_points(const uint16_t* x, const uint16_t* w, const f
   }
   return bad ? fail("conv2d point out of range") : 0;
 }
+
+/* ---- seeded synthetic inputs ----
+ * The counter-based generator of the benchmark inputs, restated so the CPU-side
+ * legs (the reference arm, the checker) can make the same tensors without the
+ * product library. Element i depends only on (seed, i): SplitMix64's finaliser
+ * (Steele, Lea and Flood, "Fast splittable pseudorandom number generators",
+ * OOPSLA 2014) of key + (i + 1) * golden-ratio increment gives 64 bits; a uniform
+ * takes the top 53 bits; normals are the Box-Muller pair (Box and Muller 1958) of
+ * elements (2j, 2j + 1), cos for the even element and sin for the odd one. */
+static uint64_t sm64_mix(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+static double sm64_unit(uint64_t key, uint64_t i) {
+  const uint64_t bits = sm64_mix(key + (i + 1) * 0x9E3779B97F4A7C15ull);
+  return (double)(bits >> 11) * (1.0 / 9007199254740992.0);
+}
+
+static void fill_store(void* dst, int bf16, size_t j, double v) {
+  const float f = (float)v;
+  if (bf16)
+    ((uint16_t*)dst)[j] = oracle_f32_to_bf16(f);
+  else
+    ((float*)dst)[j] = f;
+}
+
+int oracle_fill_uniform(void* dst, int bf16, uint64_t first, size_t count, uint64_t seed, double low, double high,
+                        int threads) {
+  if (!dst && count) return fail("null destination");
+  const uint64_t key = sm64_mix(seed ^ 0x5851F42D4C957F2Dull);
+  const int t = resolve_threads(threads);
+#pragma omp parallel for num_threads(t) schedule(static)
+  for (size_t j = 0; j < count; ++j) fill_store(dst, bf16, j, low + (high - low) * sm64_unit(key, first + j));
+  return 0;
+}
+
+int oracle_fill_normal(void* dst, int bf16, uint64_t first, size_t count, uint64_t seed, double mean,
+                       double stddev, int threads) {
+  if (!dst && count) return fail("null destination");
+  const uint64_t key = sm64_mix(seed ^ 0x2545F4914F6CDD1Dull);
+  const double two_pi = 6.283185307179586476925286766559;
+  const int t = resolve_threads(threads);
+#pragma omp parallel for num_threads(t) schedule(static)
+  for (size_t j = 0; j < count; ++j) {
+    const uint64_t i = first + j, pair = i & ~(uint64_t)1;
+    const double u1 = 1.0 - sm64_unit(key, pair); /* (0, 1] */
+    const double u2 = sm64_unit(key, pair + 1);
+    const double r = sqrt(-2.0 * log(u1));
+    const double z = (i & 1) ? r * sin(two_pi * u2) : r * cos(two_pi * u2);
+    fill_store(dst, bf16, j, mean + stddev * z);
+  }
+  return 0;
+}
+

@@ -94,6 +94,14 @@ int oracle_conv2d_nhwc_bf16_points(const uint16_t* x, const uint16_t* w, const f
                                    size_t dil_h, size_t dil_w, size_t out_h, size_t out_w,
                                    const int64_t* idx, size_t npoints, float* out, int threads);
 
+/* Seeded synthetic inputs: elements [first, first + count) of the fill with `seed`
+ * (SplitMix64 bits, 53-bit uniforms, Box-Muller normals), as f32 (bf16 = 0) or as
+ * bf16 bit patterns rounded to nearest even (bf16 = 1). Any slice can be made alone. */
+int oracle_fill_uniform(void* dst, int bf16, uint64_t first, size_t count, uint64_t seed, double low, double high,
+                        int threads);
+int oracle_fill_normal(void* dst, int bf16, uint64_t first, size_t count, uint64_t seed, double mean,
+                       double stddev, int threads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -170,3 +170,23 @@ def test_gelu_and_silu_match_the_reference_known_answers():
     xs = np.linspace(-8, 8, 4001, dtype=np.float32)
     exact = np.array([0.5 * v * (1 + erf(v / 2 ** 0.5)) for v in xs.astype(np.float64)])
     assert np.max(np.abs(oracle.gelu(xs) - exact)) < 2e-6
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+@pytest.mark.parametrize("seed,count", [(0, 1), (1, 4097), (33, 1 << 17), (48, 3 * (1 << 16) + 5)])
+def test_oracle_generator_is_bit_identical_to_the_library(seed, count, bf16):
+    """The reference arm of bench.py makes its inputs with the oracle's generator so it never
+    loads the product library; both must produce the same bits for every seed and slice."""
+    import titan_rs_b200 as tb
+    from titan_rs_b200.kernel_abi import DType
+    dt = DType.BF16 if bf16 else DType.F32
+    for mean, std in [(0.0, 1.0), (0.0, 2.0), (0.5, 1.0 / 90.5)]:
+        want = tb.fill_normal(count, seed=seed, mean=mean, std=std, dtype=dt)
+        got = oracle.fill_normal(count, seed, mean, std, bf16=bf16, threads=3)
+        assert want.dtype == got.dtype and want.tobytes() == got.tobytes()
+    want = tb.fill_uniform(count, seed=seed, low=-1.0, high=1.0, dtype=dt)
+    assert want.tobytes() == oracle.fill_uniform(count, seed, -1.0, 1.0, bf16=bf16).tobytes()
+    # A slice made on its own equals the same slice of the whole fill (odd start included).
+    lo = count // 3 | 1 if count > 2 else 0
+    part = oracle.fill_normal(count - lo, seed, 0.0, 1.0, bf16=bf16, first=lo)
+    assert part.tobytes() == tb.fill_normal(count, seed=seed, dtype=dt)[lo:].tobytes()
