@@ -8,6 +8,7 @@ native call fails.
 from __future__ import annotations
 
 import ctypes
+import threading
 from dataclasses import dataclass
 from typing import Optional
 
@@ -67,6 +68,9 @@ def _fp_dict(fp: N.Fingerprint) -> dict:
             "total_memory": fp.total_memory}
 
 
+_RELEASE_LOCK = threading.Lock()
+
+
 class _Handle:
     _release = None
 
@@ -75,9 +79,12 @@ class _Handle:
         self.ptr = ptr
 
     def release(self) -> None:
-        if self.ptr:
-            getattr(N.lib(), self._release)(self.ptr)
-            self.ptr = 0
+        # Handles may be dropped from any thread (the session is Send + Sync): take the
+        # pointer under a lock so two threads never release the same handle.
+        with _RELEASE_LOCK:
+            ptr, self.ptr = self.ptr, 0
+        if ptr:
+            getattr(N.lib(), self._release)(ptr)
 
     def __del__(self):
         try:
