@@ -1,6 +1,6 @@
-"""Distributed host logic on CPU (no GPU): the reference collective contracts
-(projects/titan-distributed/tests/collective.rs:6-49) and world_size-2 gloo runs
-of the sharded-GEMM gather path and of failure detection.
+"""Distributed host logic on CPU (no GPU): the even shards and the re-layout of the
+sharded GEMM's gather, and world_size-2 gloo runs of the gather path and of failure
+detection (the Collective trait, projects/titan-distributed/src/lib.rs:95-99).
 """
 import datetime
 import multiprocessing as mp
@@ -10,42 +10,6 @@ import numpy as np
 import pytest
 
 from titan_rs_b200 import distributed as D
-
-
-def test_local_ring_matches_reference_tests():
-    assert D.LocalRing().all_reduce_sum([[1.0, 2.0], [3.0, 4.0]]) == [4.0, 6.0]
-    assert D.LocalRing().reduce_scatter_sum([[1.0, 2.0, 3.0, 4.0], [1.0, 1.0, 1.0, 1.0]]) == [[2.0, 3.0], [4.0, 5.0]]
-    assert D.LocalRing().all_gather([[1.0, 2.0], [3.0]]) == [1.0, 2.0, 3.0]
-    with pytest.raises(D.CollectiveError) as e:
-        D.LocalRing().all_gather([])
-    assert e.value.kind == "EmptyWorld"
-    with pytest.raises(D.CollectiveError) as e:
-        D.LocalRing().all_reduce_sum([[1.0], [1.0, 2.0]])
-    assert e.value.kind == "InconsistentLengths"
-
-
-def test_local_transport_checks_run_epoch_sequence_timeout_and_checksum():
-    t = datetime.timedelta(milliseconds=1)
-    sender, receiver = D.LocalTransport("run-a", 7, t), D.LocalTransport("run-a", 7, t)
-    frame = sender.send(b"payload", t)
-    assert receiver.receive(frame, t) == b"payload"
-    for other, kind in ((D.LocalTransport("run-b", 7, t), "RunMismatch"), (D.LocalTransport("run-a", 8, t),
-                                                                            "EpochMismatch"),
-                        (receiver, "SequenceMismatch")):
-        with pytest.raises(D.CollectiveError) as e:
-            other.receive(frame, t)
-        assert e.value.kind == kind
-    with pytest.raises(D.CollectiveError) as e:
-        sender.send(b"x", datetime.timedelta(0))
-    assert e.value.kind == "Timeout"
-    corrupt = sender.send(b"payload", t)
-    corrupt.checksum = "broken"
-    verifier = D.LocalTransport("run-a", 7, t)
-    verifier.receive(frame, t)
-    with pytest.raises(D.CollectiveError) as e:
-        verifier.receive(corrupt, t)
-    assert e.value.kind == "ChecksumMismatch"
-    assert D.checksum(b"") == "cbf29ce484222325"
 
 
 def test_even_shard_and_reassembly():
@@ -131,3 +95,16 @@ def test_lost_rank_surfaces_as_an_error_not_a_hang():
     results = _run(_failure_rank)
     assert results[1] == "left"
     assert results[0].startswith("error:"), results
+
+
+@pytest.mark.parametrize("units,world", [(256, 8), (256, 3), (6, 4), (2, 4), (64, 8), (1, 1)])
+def test_shard_units_cover_every_unit_once(units, world):
+    spans = [D.shard_units(units, world, r) for r in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == units
+    assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+    sizes = [hi - lo for lo, hi in spans]
+    assert max(sizes) - min(sizes) <= 1
+    if units % world == 0:
+        assert spans == [D.even_shard(units, world, r) for r in range(world)]
+    with pytest.raises(ValueError):
+        D.shard_units(units, world, world)

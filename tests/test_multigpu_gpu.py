@@ -1,7 +1,9 @@
-"""Multi-GPU path: NCCL all-gather (Collective::all_gather on device buffers) and
-the N-sharded GEMM. The one-rank cases run on any single B200; the two-rank
-cases run as child processes when at least two GPUs are visible (NVLS off, as
-this pool requires for multi-process GPU tests)."""
+"""Multi-GPU path: NCCL all-gather (Collective::all_gather on device buffers), the
+N-sharded GEMM, and attention / conv2d sharded over batch x heads / batch. The
+one-rank cases run on any single B200; the two-rank cases run as child processes
+when at least two GPUs are visible (NVLS off, as this pool requires for
+multi-process GPU tests). Sharded results are compared with the unsharded kernel
+of the same family bit for bit and with the CPU oracle on sampled points."""
 import math
 import multiprocessing as mp
 import os
@@ -93,6 +95,19 @@ def test_one_rank_fused_sharded_gemm_equals_single_gpu_gemm(m, n, k, fused, plai
     s.close()
 
 
+def _oracle_ok(a, b, c_bits, samples=2048, seed=0):
+    """Sampled points of C = A B^T (B stored [N, K]) against the CPU oracle."""
+    import oracle
+    m, k = a.shape
+    n = b.shape[0]
+    rng = np.random.default_rng(seed)
+    rows = np.concatenate([rng.integers(0, m, samples), [0, m - 1, 0, m - 1]])
+    cols = np.concatenate([rng.integers(0, n, samples), [0, 0, n - 1, n - 1]])
+    ref = oracle.gemm_bf16_points(a, b, True, m, n, k, rows, cols)
+    got = tb.bf16_bits_to_f32(c_bits[rows, cols])
+    return bool(np.isfinite(got).all() and np.max(np.abs(got - ref)) <= 1e-2 * np.max(np.abs(ref)))
+
+
 def _device_count() -> int:
     try:
         return len(tb.enumerate_devices())
@@ -125,7 +140,8 @@ def _rank_main(rank, world, q_in, q_out, mode):
             ws = s.allocate(m * n * 2)
             coll.sharded_gemm(rt.stream, ta, tbs, c, ws)
             s.synchronize(rt.stream)
-            ok_gemm = bool(np.array_equal(c.to_numpy(), ref))
+            got = c.to_numpy()
+            ok_gemm = bool(np.array_equal(got, ref)) and _oracle_ok(a, b, got)
             src, dst = s.allocate(1024 * 4), s.allocate(1024 * 4 * world)
             s.wait(s.upload(rt.stream, src, np.full(1024, rank, np.float32)))
             coll.all_gather(rt.stream, src, dst, 1024 * 4)
@@ -160,11 +176,69 @@ def _rank_main(rank, world, q_in, q_out, mode):
                 coll.sharded_gemm(rt.stream, ta, tbs, c, None)
                 s.synchronize(rt.stream)
                 ok = ok and tbm.last_candidate() == fused
-                ok = ok and bool(np.array_equal(c.to_numpy(), ref))
+                got = c.to_numpy()
+                ok = ok and bool(np.array_equal(got, ref)) and _oracle_ok(a, b, got, seed=seed)
             coll.barrier(rt.stream)
             s.synchronize(rt.stream)
             coll.deregister_buffer(c.buffer)
             q_out.put((rank, ok))
+        elif mode == "gemm_c3":
+            # C3 itself: 8192^3, B column-major N-sharded over the ranks, fused all-gather
+            # into registered outputs; checked against the oracle on sampled points and by
+            # the column-checksum identity 1^T C = (1^T A) B over every column.
+            m = n = k = 8192
+            a = tbm.fill_normal(m * k, seed=32, dtype=DType.BF16).reshape(m, k)
+            b = tbm.fill_normal(n * k, seed=33, std=1.0 / math.sqrt(k), dtype=DType.BF16).reshape(n, k)
+            lo, hi = Dm.even_shard(n, world, rank)
+            c = tbm.TensorHandle.allocate(s, DType.BF16, (m, n))
+            coll.register_buffer(rt.stream, c.buffer)
+            ta = tbm.TensorHandle.from_numpy(s, a, DType.BF16, rt.stream)
+            tbs = tbm.TensorHandle.from_numpy(s, np.ascontiguousarray(b[lo:hi]), DType.BF16, rt.stream)
+            coll.sharded_gemm(rt.stream, ta, tbs, c, None)
+            s.synchronize(rt.stream)
+            got = c.to_numpy()
+            ok = tbm.last_candidate().startswith("gemm_bf16_tn_allgather") and _oracle_ok(a, b, got, 4096, rank)
+            af = tbm.bf16_bits_to_f32(a).astype(np.float64)
+            colsum_ref = af.sum(axis=0) @ tbm.bf16_bits_to_f32(b).astype(np.float64).T
+            colsum = tbm.bf16_bits_to_f32(got).astype(np.float64).sum(axis=0)
+            ok = ok and bool(np.max(np.abs(colsum - colsum_ref)) <= 1e-2 * np.max(np.abs(colsum_ref)))
+            coll.barrier(rt.stream)
+            s.synchronize(rt.stream)
+            coll.deregister_buffer(c.buffer)
+            q_out.put((rank, ok))
+        elif mode in ("sdpa_shard", "conv_shard"):
+            # No communication: every rank holds the whole seeded inputs, runs only its
+            # units and checks them against the oracle.
+            import oracle
+            if mode == "sdpa_shard":
+                bb, hh, t, d = 2, 4, 512, 128
+                q, k, v = (tbm.fill_normal(bb * hh * t * d, seed=340 + i, dtype=DType.BF16).reshape(bb, hh, t, d)
+                           for i in range(3))
+                ins = [tbm.TensorHandle.from_numpy(s, x, DType.BF16, rt.stream) for x in (q, k, v)]
+                req = tbm.OpRequest("scaled_dot_product_attention", ins, [tbm.TensorSpec(DType.BF16, q.shape)],
+                                    {"causal": True})
+                hdl, (lo, hi) = Dm.execute_local(rt, req, world, rank)
+                hdl.wait()
+                got = hdl.outputs[0].to_f32().reshape(-1, d)
+                ref = oracle.sdpa_bf16_rows(q, k, v, bb, hh, t, t, d, True, np.arange(lo * t, hi * t))
+            else:
+                n, hw, cin, cout = 6, 28, 64, 256
+                x = tbm.fill_normal(n * hw * hw * cin, seed=350, dtype=DType.BF16).reshape(n, hw, hw, cin)
+                w = tbm.fill_normal(cout * 9 * cin, seed=351, std=math.sqrt(2.0 / (9 * cin)),
+                                    dtype=DType.BF16).reshape(cout, 3, 3, cin)
+                attrs = {"stride_h": 1, "stride_w": 1, "pad_h": 1, "pad_w": 1, "dilation_h": 1, "dilation_w": 1,
+                         "groups": 1, "layout": "NHWC"}
+                ins = [tbm.TensorHandle.from_numpy(s, x, DType.BF16, rt.stream),
+                       tbm.TensorHandle.from_numpy(s, w, DType.BF16, rt.stream)]
+                req = tbm.OpRequest("conv2d", ins, [tbm.TensorSpec(DType.BF16, (n, hw, hw, cout))], attrs)
+                hdl, (lo, hi) = Dm.execute_local(rt, req, world, rank)
+                hdl.wait()
+                got = hdl.outputs[0].to_f32().ravel()
+                per = hw * hw * cout
+                ref = oracle.conv2d_nhwc_bf16_points(x, w, None, n, hw, hw, cin, cout, 3, 3, (1, 1), (1, 1), (1, 1),
+                                                     hw, hw, np.arange(lo * per, hi * per))
+            err = float(np.max(np.abs(got.ravel() - ref.ravel())) / np.max(np.abs(ref)))
+            q_out.put((rank, (hi - lo > 0) and err <= 1e-2))
         elif mode in ("p2p_absent", "p2p_absent_pairs", "p2p_absent_pushers"):
             if mode == "p2p_absent_pushers":
                 os.environ["TITAN_B200_ALLGATHER_PUSHERS"] = "16"
@@ -258,6 +332,17 @@ def test_two_rank_fused_sharded_gemm_with_pusher_ctas():
 @pytest.mark.parametrize("mode", ["p2p_absent", "p2p_absent_pairs", "p2p_absent_pushers"])
 def test_two_rank_fused_gemm_gives_up_when_a_peer_never_arrives(mode):
     assert _spawn(2, mode) == {0: ("timeout", True), 1: "absent"}
+
+
+@pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")
+def test_two_rank_fused_sharded_gemm_at_c3_against_the_oracle():
+    assert _spawn(2, "gemm_c3") == {0: True, 1: True}
+
+
+@pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("mode", ["sdpa_shard", "conv_shard"])
+def test_two_rank_communication_free_shards_against_the_oracle(mode):
+    assert _spawn(2, mode) == {0: True, 1: True}
 
 
 @pytest.mark.skipif(_device_count() < 2, reason="needs two GPUs")

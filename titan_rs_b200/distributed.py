@@ -1,7 +1,7 @@
-"""Distributed contracts for the hot path: the titan.rs `Collective` trait and
-its in-process transport (projects/titan-distributed/src/lib.rs:4-135), plus the
-B200 implementation that runs the trait's all_gather over NCCL/NVLink on device
-buffers and the N-sharded GEMM built on it.
+"""Distributed contracts for the hot path: the titan.rs `Collective` trait
+(projects/titan-distributed/src/lib.rs:95-99) and the B200 implementation that runs
+its all_gather over NCCL/NVLink on device buffers, in place of the reference's
+in-process transport, plus the N-sharded GEMM built on it.
 
 Sharding of the north-star configurations (one process per GPU):
   GEMM    rank r owns output columns [r*N/p, (r+1)*N/p); B (column-major, stored
@@ -13,8 +13,6 @@ Sharding of the north-star configurations (one process per GPU):
 from __future__ import annotations
 
 import ctypes
-import datetime
-from dataclasses import dataclass
 from typing import Optional, Sequence
 
 import numpy as np
@@ -32,52 +30,6 @@ class CollectiveError(RuntimeError):
         self.kind = kind
 
 
-def checksum(data: bytes) -> str:
-    """FNV-1a 64 rendered as 16 hex digits (projects/titan-distributed/src/lib.rs:24-32)."""
-    h = 0xCBF29CE484222325
-    for b in data:
-        h ^= b
-        h = (h * 0x100000001B3) & 0xFFFFFFFFFFFFFFFF
-    return f"{h:016x}"
-
-
-@dataclass
-class LocalFrame:
-    run_id: str
-    epoch: int
-    sequence: int
-    payload: bytes
-    checksum: str
-
-
-class LocalTransport:
-    """Run/epoch/sequence/checksum/timeout framing (projects/titan-distributed/src/lib.rs:44-93)."""
-
-    def __init__(self, run_id: str, epoch: int, timeout: datetime.timedelta):
-        self.run_id, self.epoch, self.next_sequence, self.timeout = run_id, epoch, 0, timeout
-
-    def send(self, payload: bytes, timeout: datetime.timedelta) -> LocalFrame:
-        if timeout.total_seconds() <= 0 or self.timeout.total_seconds() <= 0:
-            raise CollectiveError("Timeout")
-        frame = LocalFrame(self.run_id, self.epoch, self.next_sequence, bytes(payload), checksum(bytes(payload)))
-        self.next_sequence += 1
-        return frame
-
-    def receive(self, frame: LocalFrame, timeout: datetime.timedelta) -> bytes:
-        if timeout.total_seconds() <= 0 or self.timeout.total_seconds() <= 0:
-            raise CollectiveError("Timeout")
-        if frame.run_id != self.run_id:
-            raise CollectiveError("RunMismatch")
-        if frame.epoch != self.epoch:
-            raise CollectiveError("EpochMismatch")
-        if frame.sequence != self.next_sequence:
-            raise CollectiveError("SequenceMismatch")
-        if checksum(frame.payload) != frame.checksum:
-            raise CollectiveError("ChecksumMismatch")
-        self.next_sequence += 1
-        return frame.payload
-
-
 class Collective:
     """The `Collective` trait (projects/titan-distributed/src/lib.rs:95-99) over host shards."""
 
@@ -91,33 +43,6 @@ class Collective:
         raise NotImplementedError
 
 
-class LocalRing(Collective):
-    """In-process reference implementation (projects/titan-distributed/src/lib.rs:101-135)."""
-
-    def all_reduce_sum(self, shards):
-        if not shards:
-            raise CollectiveError("EmptyWorld")
-        n = len(shards[0])
-        if any(len(s) != n for s in shards):
-            raise CollectiveError("InconsistentLengths")
-        total = np.zeros(n, dtype=np.float32)
-        for s in shards:
-            total += np.asarray(s, dtype=np.float32)
-        return total.tolist()
-
-    def reduce_scatter_sum(self, shards):
-        total = self.all_reduce_sum(shards)
-        if len(total) % len(shards):
-            raise CollectiveError("InconsistentLengths")
-        w = len(total) // len(shards)
-        return [total[i:i + w] for i in range(0, len(total), w)]
-
-    def all_gather(self, shards):
-        if not shards:
-            raise CollectiveError("EmptyWorld")
-        return [float(x) for s in shards for x in s]
-
-
 # ----------------------------------------------------------------------------- sharding
 def even_shard(total: int, world: int, rank: int) -> tuple[int, int]:
     """[start, stop) of rank's even share of `total` units; total must divide by world."""
@@ -127,6 +52,71 @@ def even_shard(total: int, world: int, rank: int) -> tuple[int, int]:
         raise ValueError(f"{total} units do not split evenly over {world} ranks")
     per = total // world
     return rank * per, (rank + 1) * per
+
+
+def shard_units(units: int, world: int, rank: int) -> tuple[int, int]:
+    """[start, stop) of rank's share of `units` independent units; the first
+    units % world ranks take one unit more, so any count splits."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("bad world/rank")
+    base, extra = divmod(int(units), world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def _view(session, handle, first: int, count: int, unit_elems: int, shape):
+    from .runtime import TensorHandle, _SIZE, contiguous_strides
+    esize = _SIZE[handle.dtype]
+    if tuple(handle.strides) != contiguous_strides(handle.shape):
+        raise ValueError("sharded operands must be contiguous")
+    nbytes = max(count * unit_elems * esize, esize)
+    buf = session.wrap(handle.buffer.device_ptr + first * unit_elems * esize, nbytes)
+    return TensorHandle(session, buf, handle.dtype, tuple(shape), contiguous_strides(shape))
+
+
+def local_request(request, world: int, rank: int):
+    """Rank r's part of an operator request that shards without communication.
+
+    scaled_dot_product_attention shards over batch x heads: Q [B,H,Tq,D] and K, V
+    [B,H,Tk,D] become views [1, n, T, D] of the rank's n = hi - lo (b, h) pairs, and
+    the output spec is [1, n, Tq, D]. conv2d shards over the batch: x (NHWC or NCHW)
+    becomes the rank's images, the weights and bias stay whole, and the output spec
+    covers those images. The views alias the caller's buffers (no copy), so the
+    inputs may be whole on every rank or hold just this rank's units at the same
+    offsets. Returns (request, (lo, hi)); a rank with no units gets hi == lo and
+    should skip the launch."""
+    from .runtime import OpRequest, TensorSpec
+    op = request.operator
+    spec = request.outputs[0]
+    if op == "scaled_dot_product_attention":
+        q, k, v = request.inputs[:3]
+        b, h, tq, d = q.shape
+        tk = k.shape[2]
+        lo, hi = shard_units(b * h, world, rank)
+        n = hi - lo
+        s = q.session
+        ins = [_view(s, q, lo, n, tq * d, (1, n, tq, d)), _view(s, k, lo, n, tk * d, (1, n, tk, d)),
+               _view(s, v, lo, n, tk * d, (1, n, tk, v.shape[3]))]
+        out = TensorSpec(spec.dtype, (1, n, tq, spec.shape[3]))
+    elif op == "conv2d":
+        x = request.inputs[0]
+        lo, hi = shard_units(x.shape[0], world, rank)
+        n = hi - lo
+        per = int(np.prod(x.shape[1:], dtype=np.int64))
+        ins = [_view(x.session, x, lo, n, per, (n,) + tuple(x.shape[1:]))] + list(request.inputs[1:])
+        out = TensorSpec(spec.dtype, (n,) + tuple(spec.shape[1:]))
+    else:
+        raise ValueError(f"{op} does not shard without communication (gemm shards through the collective)")
+    return OpRequest(op, ins, [out], dict(request.attrs)), (lo, hi)
+
+
+def execute_local(runtime, request, world: int, rank: int):
+    """Runs rank r's units of `request` (see local_request) on this rank's Runtime.
+    Returns (ExecutionHandle or None when the rank has no units, (lo, hi))."""
+    local, bounds = local_request(request, world, rank)
+    if bounds[1] == bounds[0]:
+        return None, bounds
+    return runtime.execute(local), bounds
 
 
 def reassemble_column_blocks(gathered: np.ndarray, parts: int) -> np.ndarray:
@@ -240,6 +230,6 @@ class NcclCollective:
             pass
 
 
-__all__ = ["CollectiveError", "checksum", "LocalFrame", "LocalTransport", "Collective", "LocalRing",
-           "ProcessGroupCollective", "even_shard", "reassemble_column_blocks", "new_comm_id", "broadcast_comm_id",
-           "NcclCollective", "HalError"]
+__all__ = ["CollectiveError", "Collective", "ProcessGroupCollective", "even_shard", "shard_units", "local_request",
+           "execute_local", "reassemble_column_blocks", "new_comm_id", "broadcast_comm_id", "NcclCollective",
+           "HalError"]
