@@ -42,7 +42,7 @@ def qkv_bf16(b, h, tq, tk, d, seed):
     return q, k, v
 
 
-TC_CANDIDATES = ["sdpa_fwd_bf16_d128_bn64", "sdpa_fwd_bf16_d128_pair", "sdpa_fwd_bf16_d128"]
+TC_CANDIDATES = ["sdpa_fwd_bf16_d128_bn64", "sdpa_fwd_bf16_d128_pair", "sdpa_fwd_bf16_d128", "sdpa_fwd_bf16_d128_persist"]
 
 
 def run_sdpa(session, rt, q, k, v, causal, dtype=DType.BF16, candidate=None):
@@ -188,3 +188,25 @@ def test_sdpa_bf16_scale_attribute_contract(session, rt):
     for bad in ("0", "-1", "nan", "inf", "abc", "1.0x", 0.0):
         with pytest.raises(tb.ExecutionError, match="scale must be a positive finite number"):
             run_op(rt, "scaled_dot_product_attention", ins, DType.BF16, q.shape, {"scale": bad})
+
+
+@pytest.mark.parametrize("b,h,t,causal", [(4, 16, 2048, True), (3, 5, 1000, True), (2, 40, 512, False)])
+def test_sdpa_persistent_ctas_walk_many_items_like_the_pair_kernel(session, rt, b, h, t, causal):
+    """The persistent kernel (one CTA per SM walking several (head, query-tile pair) items,
+    item boundaries pipelined) computes every item with the pair kernel's arithmetic: the
+    outputs are bit-identical, and sampled rows match the oracle. 512, 300 and 160 items
+    over 148 SMs: several items per CTA, head groups of 16 with a ragged last group, ragged Tq."""
+    d = 128
+    q, k, v = qkv_bf16(b, h, t, t, d, seed=b + h + t)
+    pair = run_sdpa(session, rt, q, k, v, causal, candidate="sdpa_fwd_bf16_d128_pair")
+    want = pair.outputs[0].to_numpy()
+    got_h = run_sdpa(session, rt, q, k, v, causal, candidate="sdpa_fwd_bf16_d128_persist")
+    assert got_h.candidate == "sdpa_fwd_bf16_d128_persist"
+    got = got_h.outputs[0].to_numpy()
+    np.testing.assert_array_equal(got, want)
+    rng = np.random.default_rng(t)
+    ids = np.unique(np.concatenate([rng.integers(0, b * h * t, 512), [0, b * h * t - 1]]))
+    ref = oracle.sdpa_bf16_rows(q, k, v, b, h, t, t, d, causal, ids)
+    got_rows = tb.bf16_bits_to_f32(got).reshape(-1, d)[ids]
+    assert max_rel_err(got_rows, ref) <= BF16_TOL
+

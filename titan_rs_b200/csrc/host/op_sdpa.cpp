@@ -71,6 +71,29 @@ tb_status launch_sdpa_bf16_d128_pair(Session* s, Stream* st, CUdeviceptr q, CUde
                         "sdpa_fwd_bf16_d128_pair");
 }
 
+// The pair pipeline on persistent CTAs (one per SM) walking every (batch*head, pair)
+// item; the kernel's own schedule, so the grid is just the SM count (or fewer items).
+tb_status launch_sdpa_bf16_d128_persist(Session* s, Stream* st, CUdeviceptr q, CUdeviceptr k, CUdeviceptr v,
+                                        CUdeviceptr o, int bh, int tq, int tk, int causal, float scale) {
+  CUtensorMap mq, mk, mv;
+  tb_status rc;
+  if ((rc = tmap_bhtd(&mq, q, bh, tq, TB_SDPA_HD)) || (rc = tmap_bhtd(&mk, k, bh, tk, TB_SDPA_HD)) ||
+      (rc = tmap_bhtd(&mv, v, bh, tk, TB_SDPA_HD)))
+    return rc;
+  CUfunction fn = nullptr;
+  rc = builtin_function(s, "sdpa_bf16_persist", "sdpa_fwd_bf16_d128_persist", &fn);
+  if (rc) return rc;
+  float scale_log2 = (float)(1.4426950408889634 * (double)scale);  // the kernels exponentiate base 2
+  CUdeviceptr status = s->status.device;
+  void* params[] = {&mq, &mk, &mv, &o, &bh, &tq, &tk, &causal, &scale_log2, &status};
+  const unsigned long long items =
+      (unsigned long long)((tq + 2 * TB_SDPA_BM - 1) / (2 * TB_SDPA_BM)) * (unsigned long long)bh;
+  if (items > 0x7fffffffull) return contract("CUDA attention work list exceeds 2^31 items");
+  const unsigned grid = (unsigned)std::min<unsigned long long>(items, (unsigned long long)s->sm_count);
+  return launch_builtin(s, st, fn, grid, 1, 1, TB_SDPA2_THREADS, TB_SDPA2_SMEM_BYTES, params,
+                        "sdpa_fwd_bf16_d128_persist");
+}
+
 tb_status launch_sdpa_bf16_d128_bn64(Session* s, Stream* st, CUdeviceptr q, CUdeviceptr k, CUdeviceptr v,
                                      CUdeviceptr o, int bh, int tq, int tk, int causal, float scale) {
   CUtensorMap mq, mk, mv;
@@ -165,12 +188,15 @@ extern "C" tb_status tb_op_sdpa(tb_session* session, tb_stream* stream, const tb
   float sc = (float)(scale > 0.0 ? scale : 1.0 / std::sqrt((double)D));
   const bool tc_ok = dt == TB_BF16 && D == TB_SDPA_HD && ((pq | pk | pv | po) & 15) == 0;
   if (candidate && strcmp(candidate, "sdpa_fwd_bf16_d128_pair") != 0 && strcmp(candidate, "sdpa_fwd_bf16_d128") != 0 &&
-      strcmp(candidate, "sdpa_fwd_bf16_d128_bn64") != 0 && strcmp(candidate, "sdpa_bf16_generic") != 0)
+      strcmp(candidate, "sdpa_fwd_bf16_d128_bn64") != 0 && strcmp(candidate, "sdpa_fwd_bf16_d128_persist") != 0 &&
+      strcmp(candidate, "sdpa_bf16_generic") != 0)
     return contract(std::string("unknown attention candidate ") + candidate);
   if (candidate && !tc_ok && strcmp(candidate, "sdpa_bf16_generic") != 0)
     return unsupported(std::string("candidate ") + candidate + " does not take this shape or alignment");
   if (tc_ok && (!candidate || strcmp(candidate, "sdpa_fwd_bf16_d128_pair") == 0)) {
     rc = launch_sdpa_bf16_d128_pair(s, st, pq, pk, pv, po, b * h, tq, tk, c, sc);
+  } else if (tc_ok && strcmp(candidate, "sdpa_fwd_bf16_d128_persist") == 0) {
+    rc = launch_sdpa_bf16_d128_persist(s, st, pq, pk, pv, po, b * h, tq, tk, c, sc);
   } else if (tc_ok && strcmp(candidate, "sdpa_fwd_bf16_d128_bn64") == 0) {
     rc = launch_sdpa_bf16_d128_bn64(s, st, pq, pk, pv, po, b * h, tq, tk, c, sc);
   } else if (tc_ok && strcmp(candidate, "sdpa_fwd_bf16_d128") == 0) {

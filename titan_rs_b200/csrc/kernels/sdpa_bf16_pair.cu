@@ -17,8 +17,9 @@
 //                  O_X    += P_X(j) V_j  (TS: P read from TMEM, V MN-major in shared memory)
 //   warps 2..5   softmax group for tile A, warps 6..9 for tile B (each group covers the
 //                four TMEM lane quarters, since warp w reaches lanes 32*(w%4)..): one query row per
-//                thread (its TMEM lane). Per key tile, pass 1 reads the 128 scores
-//                from TMEM in 32-column chunks for the row max; pass 2 exponentiates
+//                thread (its TMEM lane). Per key tile the thread reads its row's 128
+//                scores from TMEM into registers once; pass 1 takes the row max;
+//                pass 2 exponentiates
 //                against the reference max (packed FFMA2 for s*scale - m; a share of
 //                the exponentials on the FMA/ALU pipes, the rest on the MUFU) and
 //                writes P as bf16 pairs over the first 64 columns of the same S
@@ -33,24 +34,13 @@
 //
 // Every wait is bounded; on a timeout the kernel records a code in `status`,
 // drains its copies and MMAs, frees TMEM and exits.
-#include "attn_math.cuh"
 #include "kernel_configs.h"
-#include "sm100.cuh"
+#include "sdpa_pair_common.cuh"
 
 namespace {
 
 using namespace tb;
-
-constexpr int BM = 128, BN = 128, HD = 128;
-constexpr int TILE_BYTES = 128 * HD * 2;  // 32 KB
-constexpr int HALF_BYTES = TILE_BYTES / 2;
-constexpr int THREADS = TB_SDPA2_THREADS;
-constexpr uint32_t IDESC_S = idesc_bf16_f32(BM, BN, false);
-constexpr uint32_t IDESC_O = idesc_bf16_f32(BM, HD, true);  // B = V, MN-major
-// The reference max of a row moves (and O is rescaled) only when a key tile's row
-// max exceeds it by more than 2^8, so P <= 256 and the result is the exact online
-// softmax with the rescale skipped on most tiles.
-constexpr float kLazyRescaleLog2 = 8.0f;
+using namespace tb::sdpa2;
 
 struct Barriers {
   uint64_t q_full;
@@ -75,108 +65,6 @@ static_assert(TB_SDPA2_SMEM_BYTES <= 232448, "exceeds the 227 KB per-CTA shared 
 constexpr uint32_t kFailProducer = 0x50010000u;
 constexpr uint32_t kFailMma = 0x50020000u;
 constexpr uint32_t kFailSoftmax = 0x50030000u;
-
-// Makes later uses of registers filled by tcgen05.ld depend on the preceding
-// tcgen05.wait::ld (the two asm statements share no operands otherwise).
-template <int N>
-__device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
-#pragma unroll
-  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
-}
-
-// Sets columns >= lim of a 32-column S chunk to -inf (its exponential is exactly 0
-// on both exponential paths).
-__device__ __forceinline__ void mask_chunk(uint32_t (&cur)[32], int lim) {
-#pragma unroll
-  for (int i = 0; i < 32; ++i)
-    if (i >= lim) cur[i] = __float_as_uint(-INFINITY);
-}
-
-// Masks the chunk when the tile needs it and folds it into four max accumulators.
-__device__ __forceinline__ void mask_max_chunk(uint32_t (&cur)[32], int lim, bool need_mask, float (&mx)[4]) {
-  if (need_mask) mask_chunk(cur, lim);
-#pragma unroll
-  for (int i = 0; i < 32; i += 8) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) mx[q] = fmax3f(mx[q], __uint_as_float(cur[i + 2 * q]), __uint_as_float(cur[i + 2 * q + 1]));
-  }
-}
-
-// p = 2^(s * scale_log2 - m) for one 32-column S chunk (kPolyPairsOf8 pairs in
-// every 8 on the FMA/ALU pipes, the rest on the MUFU), added to the four packed
-// row-sum accumulators and stored as 16 columns of bf16 pairs at p_tmem.
-template <int kPolyPairsOf8>
-__device__ __forceinline__ void exp_chunk_store(const uint32_t (&cur)[32], float2 scale2, float2 neg_m2, float2 (&rs)[4],
-                                                uint32_t p_tmem) {
-  uint32_t packed[16];
-#pragma unroll
-  for (int i = 0; i < 32; i += 2) {
-    const float2 x = __ffma2_rn(make_float2(__uint_as_float(cur[i]), __uint_as_float(cur[i + 1])), scale2, neg_m2);
-    const float2 p = ((i >> 1) & 7) < kPolyPairsOf8 ? exp2_poly2(x) : make_float2(exp2_mufu(x.x), exp2_mufu(x.y));
-    rs[(i >> 1) & 3] = __fadd2_rn(rs[(i >> 1) & 3], p);
-    packed[i / 2] = pack_bf16x2(p.x, p.y);
-  }
-  tmem_st_x16(p_tmem, packed);
-}
-
-// Rescale of O by alpha for one row: 128 fp32 columns in TMEM.
-__device__ __forceinline__ void rescale_o(uint32_t o_tmem, float alpha) {
-#pragma unroll 1
-  for (int c = 0; c < HD; c += 16) {
-    uint32_t o[16];
-    tmem_ld_x16(o_tmem + c, o);
-    tmem_ld_wait();
-    reg_fence(o);
-#pragma unroll
-    for (int i = 0; i < 16; i += 2) {
-      const float2 v =
-          __fmul2_rn(make_float2(__uint_as_float(o[i]), __uint_as_float(o[i + 1])), make_float2(alpha, alpha));
-      o[i] = __float_as_uint(v.x);
-      o[i + 1] = __float_as_uint(v.y);
-    }
-    tmem_st_x16(o_tmem + c, o);
-  }
-}
-
-__device__ __forceinline__ void load_tile(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int row0, int bh) {
-  tma_load_3d(dst, map, bar, 0, row0, bh);
-  tma_load_3d(dst + HALF_BYTES, map, bar, 64, row0, bh);
-}
-
-__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_addr, int k) {
-  return sdesc_sw128(tile_addr + (k >> 2) * HALF_BYTES + (k & 3) * 32, 16, 1024);
-}
-
-__device__ __forceinline__ uint64_t v_desc(uint32_t tile_addr, int k) {
-  return sdesc_sw128(tile_addr + k * 2048, HALF_BYTES, 1024);
-}
-
-// Moves a shared-memory descriptor's start address by `units` 16-byte units. The
-// start-address field is the descriptor's low 14 bits and every address here is
-// below 256 KB, so a 32-bit add on the low word never carries out of the field.
-__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t units) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(static_cast<uint32_t>(d) + units), "r"(static_cast<uint32_t>(d >> 32)));
-  return r;
-}
-
-// O (+)= P V for keys [64 h, 64 h + 64) of a 128-key tile: P from TMEM (bf16 pairs,
-// 8 columns per 16 keys), V MN-major in shared memory (16 keys = 2 KB per slice).
-__device__ __forceinline__ void issue_pv_half(uint32_t o_tmem, uint32_t p_tmem, uint64_t vd, int h, bool accumulate) {
-#pragma unroll
-  for (int k = 4 * h; k < 4 * h + 4; ++k)
-    umma_bf16_ts(o_tmem, p_tmem + k * 8, desc_add(vd, k * (2048 >> 4)), IDESC_O, (k > 0 || accumulate) ? 1u : 0u);
-}
-
-// S = Q K^T for one 128-key tile: both operands K-major, 16 dims per slice (two
-// 64-dim boxes of HALF_BYTES; 32 bytes per slice inside a box).
-__device__ __forceinline__ void issue_s(uint32_t s_tmem, uint64_t qd, uint64_t kd) {
-#pragma unroll
-  for (int k = 0; k < HD / 16; ++k) {
-    const uint32_t off = (k >> 2) * (HALF_BYTES >> 4) + (k & 3) * 2;
-    umma_bf16_ss(s_tmem, desc_add(qd, off), desc_add(kd, off), IDESC_S, k > 0 ? 1u : 0u);
-  }
-}
 
 }  // namespace
 
@@ -340,7 +228,6 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
     const int qt = qt0 + x;
     const int q_row = qt * BM + r;
     const int n = x ? n_b : n_a;
-    const float2 scale2 = make_float2(scale_log2, scale_log2);
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
@@ -350,65 +237,11 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
         break;
       }
       tc_fence_after_sync();
+      // O_x = sum_{t<j} P_x(t) V_t is complete (S_x(j) was committed after PV_x(j-1)), and
+      // no PV of this tile starts before p_half: the rescale may touch O from j = 1 on.
       const int valid = (causal ? min(Tk, q_row + 1) : Tk) - j * BN;  // visible leading keys of this tile
-      const bool need_mask = valid < BN;
-      // Pass 1: the row max over all 128 columns; chunks 0 and 1 stay in registers.
-      uint32_t ca[32], cb[32], ct[32];
-      tmem_ld_x32(s_tmem, ca);
-      tmem_ld_x32(s_tmem + 32, cb);
-      tmem_ld_x32(s_tmem + 64, ct);
-      tmem_ld_wait();
-      reg_fence(ca);
-      reg_fence(cb);
-      reg_fence(ct);
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      mask_max_chunk(ca, valid, need_mask, mx4);
-      mask_max_chunk(cb, valid - 32, need_mask, mx4);
-      mask_max_chunk(ct, valid - 64, need_mask, mx4);
-      tmem_ld_x32(s_tmem + 96, ct);
-      tmem_ld_wait();
-      reg_fence(ct);
-      mask_max_chunk(ct, valid - 96, need_mask, mx4);
-      const float mx = fmaxf(fmax3f(mx4[0], mx4[1], mx4[2]), mx4[3]) * scale_log2;  // scale_log2 > 0 commutes with max
-      const bool grow = mx > m_used + kLazyRescaleLog2;
-      if (__any_sync(0xffffffffu, grow)) {
-        const float m_new = grow ? mx : m_used;
-        const float alpha = exp2_mufu(m_used - m_new);  // 0 on the first tile
-        l *= alpha;
-        // O_x = sum_{t<j} P_x(t) V_t is complete (S_x(j) was committed after PV_x(j-1)),
-        // and no PV of this tile starts before p_half below.
-        if (j > 0) rescale_o(o_tmem, alpha);
-        m_used = m_new;
-      }
-      // Pass 2: P_x(j) as bf16 pairs over columns [0, 64) of S_x, where the TS-MMA reads
-      // it. Keys [0, 64) first (S chunks 0 and 1, in registers; their P covers columns
-      // [0, 32), which pass 1 has read), then p_half lets the MMA warp start on them
-      // while keys [64, 128) (columns the P never touches) are reloaded and done.
-      const float2 neg_m2 = make_float2(-m_used, -m_used);
-      float2 rs4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      tmem_ld_x32(s_tmem + 64, ct);
-      exp_chunk_store<kPolyPairsOf8>(ca, scale2, neg_m2, rs4, s_tmem);
-      exp_chunk_store<kPolyPairsOf8>(cb, scale2, neg_m2, rs4, s_tmem + 16);
-      tmem_st_wait();
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_half[x]);
-      tmem_ld_x32(s_tmem + 96, ca);
-      tmem_ld_wait();
-      reg_fence(ct);
-      reg_fence(ca);
-      if (need_mask) {
-        mask_chunk(ct, valid - 64);
-        mask_chunk(ca, valid - 96);
-      }
-      exp_chunk_store<kPolyPairsOf8>(ct, scale2, neg_m2, rs4, s_tmem + 32);
-      exp_chunk_store<kPolyPairsOf8>(ca, scale2, neg_m2, rs4, s_tmem + 48);
-      const float2 rsum = __fadd2_rn(__fadd2_rn(rs4[0], rs4[1]), __fadd2_rn(rs4[2], rs4[3]));
-      l += rsum.x + rsum.y;
-      tmem_st_wait();
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[x]);
+      softmax_tile<kPolyPairsOf8>(s_tmem, o_tmem, valid, j > 0, scale_log2, m_used, l, &bars->p_half[x],
+                                  &bars->p_full[x]);
     }
     if (ok) {
       ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_final, 0));
@@ -416,27 +249,7 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
         if (lane == 0) report_status(status, kFailSoftmax | 2);
       } else {
         tc_fence_after_sync();
-        const float inv_l = 1.0f / l;
-        __nv_bfloat16* dst = out + ((long long)bh * Tq + q_row) * HD;
-#pragma unroll 1
-        for (int c = 0; c < HD; c += 32) {
-          uint32_t o[32];
-          tmem_ld_x32(o_tmem + c, o);
-          tmem_ld_wait();
-          reg_fence(o);
-          if (q_row < Tq) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 w;
-              w.x = pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv_l, __uint_as_float(o[8 * q + 1]) * inv_l);
-              w.y = pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv_l, __uint_as_float(o[8 * q + 3]) * inv_l);
-              w.z = pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv_l, __uint_as_float(o[8 * q + 5]) * inv_l);
-              w.w = pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv_l, __uint_as_float(o[8 * q + 7]) * inv_l);
-              d4[q] = w;
-            }
-          }
-        }
+        store_row(o_tmem, l, out + ((long long)bh * Tq + q_row) * HD, q_row < Tq);
       }
     }
   }
@@ -450,8 +263,11 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
   }
 }
 
+// One CTA per SM: 10 warps, three of them on two of the four SM sub-partitions, which
+// caps a thread at 168 registers; each softmax thread keeps its row's 128 scores in
+// registers.
 #define TB_SDPA_PAIR_ENTRY(name, poly)                                                                              \
-  extern "C" __global__ void __launch_bounds__(THREADS, 1)                                                       \
+  extern "C" __global__ void __launch_bounds__(TB_SDPA2_THREADS, 1)                                              \
       name(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,             \
            const __grid_constant__ CUtensorMap tmap_v, __nv_bfloat16* __restrict__ out, int Tq, int Tk, int causal, \
            float scale_log2, uint32_t* status) {                                                                 \
