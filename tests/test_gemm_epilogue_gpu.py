@@ -126,10 +126,13 @@ def test_gemm_bias_act_contract(session, rt):
 
 @pytest.mark.parametrize("tl,tr,m,n,k", [(False, False, 264, 124, 1032),   # B stored [K, N], N % 8 != 0
                                          (False, True, 300, 520, 1001),    # K % 8 != 0
-                                         (True, False, 261, 136, 520)])    # A stored [K, M], M % 8 != 0
+                                         (True, False, 261, 136, 520),     # A stored [K, M], M % 8 != 0
+                                         (False, True, 300, 522, 1024),    # only C's rows misaligned
+                                         (True, True, 264, 1001, 520)])    # layout kernel order, C misaligned
 @pytest.mark.parametrize("act", ["gelu", "silu"])
 def test_gemm_bias_act_staged_for_storage_the_tma_cannot_describe(session, rt, tl, tr, m, n, k, act):
-    """Operands copied K-major with K rounded up to 8, then the tn bias/activation epilogue."""
+    """Operands the TMA cannot read are copied with rows padded to 8 elements, storage order
+    kept, then the bias/activation epilogue of the kernel for that order runs."""
     a, b, bias = _inputs(m, n, k, seed=m + n + k + 1)
     a2, b2 = a.reshape(m, k), b.reshape(n, k)
     a_stored = np.ascontiguousarray(a2.T) if tl else a2

@@ -165,10 +165,15 @@ def test_gemm_bf16_row_major_b_and_transposed_a(session, rt):
     (False, False, 257, 333, 515),   # B row-major [K, N] with N % 8 != 0
     (True, True, 333, 520, 777),     # A stored [K, M] with M % 8 != 0
     (True, False, 129, 130, 1023),   # both stored transposed, all extents ragged
+    (False, False, 264, 130, 1001),  # A [M, K] with K ragged and B [K, N] with N ragged
+    (True, True, 1000, 1001, 999),   # A [K, M] ragged, B [N, K] ragged
+    (False, True, 4096, 1001, 512),  # operands fine, output rows not 16-byte aligned: C through an aligned copy
+    (False, False, 520, 1000, 777),  # A [M, K] ragged; B [K, N] and C fine
 ])
 def test_gemm_bf16_staged_for_storage_the_tma_cannot_describe(session, rt, tl, tr, m, n, k):
-    """Operands are copied K-major with K rounded up to 8 (zero columns), then the
-    tensor-core GEMM runs; the CUDA-core kernel is the cross-check."""
+    """Each operand whose rows the TMA cannot read is copied in its own storage order
+    with its rows padded to a multiple of 8 elements (zeros), then the tensor-core
+    kernel for that order runs; the CUDA-core kernel is the cross-check."""
     a = tb.fill_normal(m * k, seed=m + k, dtype=DType.BF16).reshape((k, m) if tl else (m, k))
     b = tb.fill_normal(n * k, seed=n + k, std=1.0 / math.sqrt(k), dtype=DType.BF16).reshape((n, k) if tr else (k, n))
     ta, tbb = upload(session, rt.stream, a, DType.BF16), upload(session, rt.stream, b, DType.BF16)
@@ -285,3 +290,24 @@ def test_gemm_candidate_attribute(session, rt):
     with pytest.raises(tb.ExecutionError, match="does not take F32") as e:
         run_op(rt, "gemm", [x, x], DType.F32, (8, 8), {"candidate": "gemm_bf16_tn"})
     assert e.value.status == N.TB_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("tl,tr,m,n,k", [(False, False, 4096, 4095, 4096), (True, True, 4095, 4096, 4096),
+                                         (False, True, 4096, 4096, 4095)])
+def test_gemm_bf16_staged_at_full_width(session, rt, tl, tr, m, n, k):
+    """Ragged extents at 4096: the padded copies feed the 2-SM kernels (sampled oracle points,
+    the last row and column included)."""
+    a = tb.fill_normal(m * k, seed=7, dtype=DType.BF16).reshape((k, m) if tl else (m, k))
+    b = tb.fill_normal(n * k, seed=8, std=1.0 / math.sqrt(k), dtype=DType.BF16).reshape((n, k) if tr else (k, n))
+    h = run_op(rt, "gemm", [upload(session, rt.stream, a, DType.BF16), upload(session, rt.stream, b, DType.BF16)],
+               DType.BF16, (m, n), {"transpose_lhs": tl, "transpose_rhs": tr})
+    assert h.candidate == "gemm_bf16_staged"
+    got = h.outputs[0].to_f32()
+    rng = np.random.default_rng(5)
+    rows = np.concatenate([rng.integers(0, m, 2048), [0, m - 1, m - 1, 0]])
+    cols = np.concatenate([rng.integers(0, n, 2048), [0, n - 1, 0, n - 1]])
+    a_mk = np.ascontiguousarray(a.T) if tl else a
+    ref = oracle.gemm_bf16_points(a_mk, b, tr, m, n, k, rows, cols)
+    assert max_rel_err(got[rows, cols], ref) <= BF16_TOL
+    assert np.isfinite(got).all()
+

@@ -62,16 +62,20 @@ tb_status launch_gemm_bf16_tn_2sm(Session* s, Stream* st, CUdeviceptr a, CUdevic
 // operand stored [K, rows] (A with transpose_lhs, B without transpose_rhs) is read
 // through a tensor map over that storage with {64, 64} boxes and fed to the MMA
 // M- or N-contiguous. `name` is gemm_bf16_nn_2sm, gemm_bf16_ta_2sm or gemm_bf16_ta_nn_2sm.
+// lda / ldb: row pitches (elements) of A and B as stored; 0 = the contiguous extent.
 tb_status launch_gemm_bf16_layout_2sm(Session* s, Stream* st, const char* name, bool a_km, bool b_kn, CUdeviceptr a,
                                       CUdeviceptr b, CUdeviceptr c, int M, int N, int K, long long ldc,
-                                      CUdeviceptr bias = 0, int act = TB_ACT_NONE) {
+                                      CUdeviceptr bias = 0, int act = TB_ACT_NONE, uint64_t lda = 0,
+                                      uint64_t ldb = 0) {
   CUtensorMap ta, tbm;
-  tb_status rc = a_km ? tmap_bf16_2d(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)M, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)
-                      : tmap_bf16_2d(&ta, a, (uint64_t)M, (uint64_t)K, (uint64_t)K, 128, TB_GEMM_BK,
+  if (!lda) lda = a_km ? (uint64_t)M : (uint64_t)K;
+  if (!ldb) ldb = b_kn ? (uint64_t)N : (uint64_t)K;
+  tb_status rc = a_km ? tmap_bf16_2d(&ta, a, (uint64_t)K, (uint64_t)M, lda, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)
+                      : tmap_bf16_2d(&ta, a, (uint64_t)M, (uint64_t)K, lda, 128, TB_GEMM_BK,
                                      CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = b_kn ? tmap_bf16_2d(&tbm, b, (uint64_t)K, (uint64_t)N, (uint64_t)N, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)
-            : tmap_bf16_2d(&tbm, b, (uint64_t)N, (uint64_t)K, (uint64_t)K, 128, TB_GEMM_BK, CU_TENSOR_MAP_SWIZZLE_128B);
+  rc = b_kn ? tmap_bf16_2d(&tbm, b, (uint64_t)K, (uint64_t)N, ldb, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)
+            : tmap_bf16_2d(&tbm, b, (uint64_t)N, (uint64_t)K, ldb, 128, TB_GEMM_BK, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   CUfunction fn = nullptr;
   rc = builtin_function(s, "gemm_bf16", name, &fn);
@@ -102,38 +106,33 @@ tb_status launch_gemm_bf16_default(Session* s, Stream* st, CUdeviceptr a, CUdevi
   return launch_gemm_bf16_tn(s, st, a, b, c, M, N, K, ldc);
 }
 
-// K-major [rows, kp] copy of a [rows, k] bf16 operand whose element (r, c) is at
-// src[r * s_r + c * s_c] (one of the strides is 1), zero in columns k..kp-1.
-static tb_status launch_stage_bf16(Session* s, Stream* st, CUdeviceptr src, CUdeviceptr dst, int rows, int k, int kp,
-                                   long long s_r, long long s_c) {
+// Row-padded copy of a bf16 operand stored as `rows` rows of `cols` contiguous elements
+// (pitch ld_src): dst holds the same rows with pitch round_up(cols, 8) and zeros after
+// column `cols` (stage_bf16_pad_rows, one thread per 16-byte chunk of dst).
+static tb_status launch_stage_bf16(Session* s, Stream* st, CUdeviceptr src, CUdeviceptr dst, int rows, int cols,
+                                   long long ld_src) {
   CUfunction fn = nullptr;
-  tb_status rc;
-  if (s_c == 1) {
-    rc = builtin_function(s, "layout", "stage_bf16_k_major_rows", &fn);
-    if (rc) return rc;
-    const unsigned gx = (unsigned)std::min((kp + 255) / 256, 16);
-    const unsigned gy = (unsigned)std::min<long long>({(long long)rows, std::max(1LL, s->sm_count * 16LL / gx), 65535LL});
-    void* params[] = {&src, &dst, &rows, &k, &kp, &s_r};
-    return launch_builtin(s, st, fn, gx, gy, 1, 256, 0, params, "stage_bf16_k_major_rows");
-  }
-  if (s_r != 1) return contract("staged GEMM operand has no unit stride");
-  rc = builtin_function(s, "layout", "stage_bf16_k_major_cols", &fn);
+  tb_status rc = builtin_function(s, "layout", "stage_bf16_pad_rows", &fn);
   if (rc) return rc;
-  const long long tiles = (long long)((kp + 31) / 32) * ((rows + 31) / 32);
-  const unsigned grid = (unsigned)std::min<long long>(tiles, s->sm_count * 8LL);
-  void* params[] = {&src, &dst, &rows, &k, &kp, &s_c};
-  return launch_builtin(s, st, fn, grid, 1, 1, 256, 0, params, "stage_bf16_k_major_cols");
+  int ld_dst = (cols + 7) / 8 * 8;
+  const long long chunks = (long long)rows * (ld_dst / 8);
+  const unsigned grid = (unsigned)std::min<long long>((chunks + 255) / 256, s->sm_count * 8LL);
+  void* params[] = {&src, &dst, &rows, &cols, &ld_src, &ld_dst};
+  return launch_builtin(s, st, fn, grid, 1, 1, 256, 0, params, "stage_bf16_pad_rows");
 }
 
 // op(A) (M x K, strides as0/as1) times op(B) (K x N, strides bs0/bs1) for storage the TMA
-// cannot describe: each operand that is not already K-major with 16-byte aligned rows
-// is staged K-major, K rounded up to 8, in the stream's scratch; the tensor-core GEMM
-// then runs on the copies (an operand that needs no copy is read in place, which
-// happens only when K % 8 == 0, so both agree on the padded K).
+// cannot describe. Each operand keeps its storage order; one whose contiguous extent is
+// not a multiple of 8 (or whose base is not 16-byte aligned) is copied with its rows
+// padded to a multiple of 8 elements into the stream's scratch (no transpose), and the
+// tensor-core kernel for that storage order reads the copy with its padded pitch:
+//   A [M, K] x B [N, K]  gemm_bf16_tn(_2sm) over K rounded up to 8 (both pads are zero)
+//   any other order      gemm_bf16_nn_2sm / _ta_2sm / _ta_nn_2sm, logical extents
 // C = act(A B^T + bias) on the K-major operands A [M, K] and B [N, K] (gemm_bf16_tn_bias_act
 // and its CTA-pair form, chosen as for the plain GEMM unless `candidate` names one).
 static tb_status launch_gemm_bf16_tn_bias_act(Session* s, Stream* st, CUdeviceptr pa, CUdeviceptr pb, CUdeviceptr pc,
-                                              int M, int N, int K, CUdeviceptr pbias, int act, const char* candidate) {
+                                              int M, int N, int K, CUdeviceptr pbias, int act, const char* candidate,
+                                              long long ldc = 0) {
   const long long tiles = (long long)((M + TB_GEMM_BM - 1) / TB_GEMM_BM) * ((N + TB_GEMM_BN - 1) / TB_GEMM_BN);
   const bool pairs = candidate ? strcmp(candidate, "gemm_bf16_tn_bias_act_2sm") == 0
                                : (M >= 256 && tiles >= s->sm_count);
@@ -150,7 +149,7 @@ static tb_status launch_gemm_bf16_tn_bias_act(Session* s, Stream* st, CUdevicept
   rc = builtin_function(s, "gemm_bf16", name, &fn);
   if (rc) return rc;
   CUdeviceptr c = pc, status = s->status.device;
-  long long ldc = N;
+  if (!ldc) ldc = N;
   void* params[] = {&ta, &tbm, &c, &pbias, &act, &M, &N, &K, &ldc, &status};
   if (pairs) {
     const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
@@ -164,21 +163,53 @@ static tb_status launch_gemm_bf16_staged(Session* s, Stream* st, CUdeviceptr a, 
                                          CUdeviceptr b, long long bs0, long long bs1, CUdeviceptr c, int M, int N,
                                          int K, bool epilogue = false, CUdeviceptr bias = 0,
                                          int act = TB_ACT_NONE) {
-  const int kp = (K + 7) / 8 * 8;
-  const bool stage_a = !(as1 == 1 && K % 8 == 0 && (a & 15) == 0);
-  const bool stage_b = !(bs0 == 1 && K % 8 == 0 && (b & 15) == 0);
-  const size_t a_span = stage_a ? ((size_t)M * kp * 2 + 255) & ~(size_t)255 : 0;
-  const size_t b_span = stage_b ? (size_t)N * kp * 2 : 0;
+  // Storage of each operand: A is [K, M] when its M stride is 1 (transpose_lhs), else
+  // [M, K]; B is [K, N] when its N stride is 1, else [N, K] (transpose_rhs).
+  const bool a_km = as0 == 1 && as1 != 1, b_kn = bs1 == 1 && bs0 != 1;
+  const int a_rows = a_km ? K : M, a_cols = a_km ? M : K;
+  const int b_rows = b_kn ? K : N, b_cols = b_kn ? N : K;
+  const long long a_ld = a_km ? as1 : as0, b_ld = b_kn ? bs0 : bs1;
+  const bool stage_a = (a_cols % 8) != 0 || (a & 15) != 0 || a_ld != a_cols;
+  const bool stage_b = (b_cols % 8) != 0 || (b & 15) != 0 || b_ld != b_cols;
+  // An output whose rows do not start 16-byte aligned is computed into an aligned copy
+  // with vector stores, then moved into place (unstage_bf16_rows).
+  const bool stage_c = (N % 8) != 0 || (c & 15) != 0;
+  const uint64_t a_pitch = (uint64_t)(a_cols + 7) / 8 * 8, b_pitch = (uint64_t)(b_cols + 7) / 8 * 8;
+  const int c_pitch = (N + 7) / 8 * 8;
+  const size_t a_span = stage_a ? ((size_t)a_rows * a_pitch * 2 + 255) & ~(size_t)255 : 0;
+  const size_t b_span = stage_b ? ((size_t)b_rows * b_pitch * 2 + 255) & ~(size_t)255 : 0;
+  const size_t c_span = stage_c ? (size_t)M * c_pitch * 2 : 0;
   CUdeviceptr ws = 0;
   tb_status rc = TB_OK;
-  if (a_span + b_span) rc = stream_scratch(s, st, a_span + b_span, &ws);
+  if (a_span + b_span + c_span) rc = stream_scratch(s, st, a_span + b_span + c_span, &ws);
   if (rc) return rc;
-  const CUdeviceptr ka = stage_a ? ws : a, kb = stage_b ? ws + a_span : b;
-  if ((stage_a && (rc = launch_stage_bf16(s, st, a, ka, M, K, kp, as0, as1))) ||
-      (stage_b && (rc = launch_stage_bf16(s, st, b, kb, N, K, kp, bs1, bs0))) ||
-      (rc = epilogue ? launch_gemm_bf16_tn_bias_act(s, st, ka, kb, c, M, N, kp, bias, act, nullptr)
-                     : launch_gemm_bf16_default(s, st, ka, kb, c, M, N, kp, (long long)N)))
+  const CUdeviceptr ka = stage_a ? ws : a, kb = stage_b ? ws + a_span : b, kc = stage_c ? ws + a_span + b_span : c;
+  const long long ldc = stage_c ? c_pitch : N;
+  if ((stage_a && (rc = launch_stage_bf16(s, st, a, ka, a_rows, a_cols, a_ld))) ||
+      (stage_b && (rc = launch_stage_bf16(s, st, b, kb, b_rows, b_cols, b_ld))))
     return rc;
+  if (!a_km && !b_kn) {
+    // Both K-major: the copies (or the operands, when K % 8 == 0) have pitch round_up(K, 8).
+    const int kp = (int)a_pitch;
+    rc = epilogue ? launch_gemm_bf16_tn_bias_act(s, st, ka, kb, kc, M, N, kp, bias, act, nullptr, ldc)
+                  : launch_gemm_bf16_default(s, st, ka, kb, kc, M, N, kp, ldc);
+  } else {
+    const char* name = a_km ? (b_kn ? "gemm_bf16_ta_nn_2sm" : "gemm_bf16_ta_2sm") : "gemm_bf16_nn_2sm";
+    rc = launch_gemm_bf16_layout_2sm(s, st, name, a_km, b_kn, ka, kb, kc, M, N, K, ldc, bias, act,
+                                     stage_a ? a_pitch : (uint64_t)a_ld, stage_b ? b_pitch : (uint64_t)b_ld);
+  }
+  if (rc) return rc;
+  if (stage_c) {
+    CUfunction fn = nullptr;
+    if ((rc = builtin_function(s, "layout", "unstage_bf16_rows", &fn))) return rc;
+    CUdeviceptr src = kc, dst = c;
+    int rows = M, cols = N, ld_src = c_pitch;
+    long long ld_dst = N;
+    const long long units = (long long)rows * (cols / 8 + 2);
+    const unsigned grid = (unsigned)std::min<long long>((units + 255) / 256, s->sm_count * 8LL);
+    void* params[] = {&src, &dst, &rows, &cols, &ld_src, &ld_dst};
+    if ((rc = launch_builtin(s, st, fn, grid, 1, 1, 256, 0, params, "unstage_bf16_rows"))) return rc;
+  }
   note_candidate("gemm_bf16_staged");
   return TB_OK;
 }
@@ -381,18 +412,22 @@ extern "C" tb_status tb_op_gemm(tb_session* session, tb_stream* stream, const tb
                                            strcmp(candidate, "gemm_bf16_ta_nn_2sm") == 0);
     if (want_layout && (!layout_ok || strcmp(candidate, layout_kernel) != 0))
       return unsupported(std::string("candidate ") + candidate + " does not take this layout or alignment");
-    if (layout_ok && (!candidate || want_layout)) {
+    // Output rows that start 16-byte aligned take the epilogue's vector stores; others are
+    // written through an aligned copy by the staged path (the split-K reduction writes
+    // consecutive elements from consecutive threads, so it takes any output).
+    const bool c_vec = (N % 8) == 0 && (pc & 15) == 0;
+    const bool big = (uint64_t)M * N * K >= (1ull << 24);
+    if (layout_ok && (want_layout || (!candidate && (c_vec || !big)))) {
       rc = launch_gemm_bf16_layout_2sm(s, st, layout_kernel, tl, !tr, pa, pb, pc, M, N, K, (long long)N);
       if (rc) return rc;
       return record_event(s, st, nullptr, out);
     }
     const bool tma_ok = !tl && tr && (K % 8) == 0 && ((pa | pb | pc) & 15) == 0;
-    // Any other storage goes through staged K-major copies once the product is large
-    // enough for the tensor cores to repay the two copies (2^24 multiply-adds).
+    const bool split_default = !candidate && tma_ok && plan_split_k(s->sm_count, M, N, K, false).splits >= 2;
+    // Any other storage goes through the staged copies once the product is large enough
+    // for the tensor cores to repay them (2^24 multiply-adds).
     const bool want_staged = candidate && strcmp(candidate, "gemm_bf16_staged") == 0;
-    const bool staged_ok = (pc & 15) == 0;
-    if (want_staged && !staged_ok) return unsupported("candidate gemm_bf16_staged needs a 16-byte aligned output");
-    if (want_staged || (!candidate && !tma_ok && staged_ok && (uint64_t)M * N * K >= (1ull << 24))) {
+    if (want_staged || (!candidate && big && (!tma_ok || (!c_vec && !split_default)))) {
       rc = launch_gemm_bf16_staged(s, st, pa, as0, as1, pb, bs0, bs1, pc, M, N, K);
       if (rc) return rc;
       return record_event(s, st, nullptr, out);
@@ -507,15 +542,16 @@ extern "C" tb_status tb_op_gemm_bias_act(tb_session* session, tb_stream* stream,
   const long long as0 = tl ? 1 : (long long)lhs->shape[1], as1 = tl ? (long long)lhs->shape[1] : 1;
   const long long bs0 = tr ? 1 : (long long)rhs->shape[1], bs1 = tr ? (long long)rhs->shape[1] : 1;
   const bool want_staged = candidate && strcmp(candidate, "gemm_bf16_staged") == 0;
-  const bool staged_ok = (pc & 15) == 0;
+  // Output rows that do not start 16-byte aligned are written through the staged path's
+  // aligned copy of C.
+  const bool c_vec = (N % 8) == 0 && (pc & 15) == 0;
   rc = activate(s);
   if (rc) return rc;
   if (tl || !tr) {
     // Other storage orders: the layout kernels, whose epilogue takes the bias and activation;
     // storage they cannot read goes through the staged copies.
     const char* lk = layout_kernel_for(tl, tr, m, n, k, pa | pb | pc);
-    if (!lk || want_staged) {
-      if (!staged_ok) return unsupported("gemm.bias_act needs a 16-byte aligned output");
+    if (!lk || want_staged || (!candidate && !c_vec)) {
       rc = launch_gemm_bf16_staged(s, st, pa, as0, as1, pb, bs0, bs1, pc, M, N, K, true, pbias, act);
       if (rc) return rc;
       return record_event(s, st, nullptr, out);
@@ -526,8 +562,7 @@ extern "C" tb_status tb_op_gemm_bias_act(tb_session* session, tb_stream* stream,
     if (rc) return rc;
     return record_event(s, st, nullptr, out);
   }
-  if (want_staged || k % 8 != 0 || ((pa | pb | pc) & 15) != 0) {
-    if (!staged_ok) return unsupported("gemm.bias_act needs a 16-byte aligned output");
+  if (want_staged || k % 8 != 0 || ((pa | pb | pc) & 15) != 0 || (!candidate && !c_vec)) {
     rc = launch_gemm_bf16_staged(s, st, pa, as0, as1, pb, bs0, bs1, pc, M, N, K, true, pbias, act);
     if (rc) return rc;
     return record_event(s, st, nullptr, out);
