@@ -62,8 +62,9 @@ CANDIDATES = {
 
 # Candidates that are a sequence of launches rather than one kernel, with their kernels.
 COMPOSED = {
-    "gemm_bf16_staged": ("stage_bf16_k_major_rows", "stage_bf16_k_major_cols", "gemm_bf16_tn_2sm", "gemm_bf16_tn",
-                         "gemm_bf16_tn_bias_act_2sm", "gemm_bf16_tn_bias_act"),
+    "gemm_bf16_staged": ("stage_bf16_pad_rows", "unstage_bf16_rows", "gemm_bf16_tn_2sm", "gemm_bf16_tn",
+                         "gemm_bf16_nn_2sm", "gemm_bf16_ta_2sm", "gemm_bf16_ta_nn_2sm", "gemm_bf16_tn_bias_act_2sm",
+                         "gemm_bf16_tn_bias_act"),
 }
 
 # Correctness bar against the baseline candidate: |got - ref| <= tol * max|ref|.
