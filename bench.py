@@ -1080,7 +1080,20 @@ def main(argv=None) -> int:
 # SHA-256 prefix of the kernel's sources (its .cu file, every shared .cuh and the tile
 # configuration header) at capture time; when the sources differ now, the figure
 # belongs to another build of the kernel and the bench prints null instead.
-TRAFFIC_PER_LAUNCH: dict = {}
+_TRAFFIC_CAPTURE = ("ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum "
+                    "--clock-control none -k regex:{kernel} -s 3 -c 1 python bench.py --op {op} --ops none "
+                    "--steps 5 --warmup 3 --no-cpu-baseline --soak-ms 0")
+TRAFFIC_PER_LAUNCH: dict = {
+    "gemm_bf16_tn_2sm": {"read": 1022161152, "write": 126671872, "source_sha16": "bbd1913bb1a7b079",
+                         "capture": _TRAFFIC_CAPTURE.format(kernel="gemm_bf16_tn_2sm", op="gemm")},
+    "softmax_f32_warp32": {"read": 536933376, "write": 480914432, "source_sha16": "a19088a14dfbed81",
+                           "capture": _TRAFFIC_CAPTURE.format(kernel="softmax_f32_warp32", op="softmax")},
+    "sdpa_fwd_bf16_d128_pair": {"read": 806622976, "write": 265165056, "source_sha16": "c87b3a0c72d2a9b8",
+                                "capture": _TRAFFIC_CAPTURE.format(kernel="sdpa_fwd_bf16_d128_pair", op="sdpa")},
+    "conv2d_fprop_bf16_nhwc_2sm": {"read": 103985152, "write": 55264512, "source_sha16": "ee35a0770bf797fe",
+                                   "capture": _TRAFFIC_CAPTURE.format(kernel="conv2d_fprop_bf16_nhwc_2sm",
+                                                                      op="conv2d")},
+}
 
 KERNEL_SOURCE = {"softmax_f32_warp": "softmax.cu", "gemm_bf16_tn": "gemm_bf16.cu", "gemm_bf16_nn": "gemm_bf16.cu",
                  "gemm_bf16_ta": "gemm_bf16.cu", "sdpa_fwd_bf16_d128_pair": "sdpa_bf16_pair.cu",

@@ -123,7 +123,15 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
       load_tile(smem + OFF_Q + TILE_BYTES, &tmap_q, &bars->q_full, (qt0 + 1) * BM, bh);
       uint32_t k_issued[2] = {0, 0}, v_issued[2] = {0, 0};
       bool ok = true;
+      for (int j = 0; j < kPrefetchAhead && j < n_b; ++j) {
+        prefetch_tile(&tmap_k, j * BN, bh);
+        prefetch_tile(&tmap_v, j * BN, bh);
+      }
       for (int j = 0; j < n_b && ok; ++j) {
+        if (j + kPrefetchAhead < n_b) {
+          prefetch_tile(&tmap_k, (j + kPrefetchAhead) * BN, bh);
+          prefetch_tile(&tmap_v, (j + kPrefetchAhead) * BN, bh);
+        }
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait(&bars->k_empty[st], ph ^ 1)) {
@@ -274,6 +282,8 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
     sdpa_pair_body<poly>(tmap_q, tmap_k, tmap_v, out, Tq, Tk, causal, scale_log2, status);                       \
   }
 
-// Two score pairs in every eight take the FMA/ALU exponential (measured fastest of
-// 1, 2 and 3 on the C4 workload).
-TB_SDPA_PAIR_ENTRY(sdpa_fwd_bf16_d128_pair, 2)
+// Every exponential on the MUFU: measured fastest of 0 to 3 FMA/ALU pairs in 8 on the C4
+// workload once the scores stay in registers (1014 against 1002, 985 and 970 TFLOP/s
+// for an isolated launch); the polynomial's extra instructions take issue slots from the
+// MMA lane, which shares its sub-partition with two softmax warps.
+TB_SDPA_PAIR_ENTRY(sdpa_fwd_bf16_d128_pair, 0)

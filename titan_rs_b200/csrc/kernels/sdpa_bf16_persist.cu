@@ -137,7 +137,15 @@ __device__ __forceinline__ void sdpa_persist_body(const CUtensorMap& tmap_q, con
         load_tile(smem + OFF_Q, &tmap_q, &bars->q_full, qt0 * BM, bh);
         load_tile(smem + OFF_Q + TILE_BYTES, &tmap_q, &bars->q_full, (qt0 + 1) * BM, bh);
         ++q_issued;
+        for (int j = 0; j < kPrefetchAhead && j < n_b; ++j) {
+          prefetch_tile(&tmap_k, j * BN, bh);
+          prefetch_tile(&tmap_v, j * BN, bh);
+        }
         for (int j = 0; j < n_b; ++j, ++kv) {
+          if (j + kPrefetchAhead < n_b) {
+            prefetch_tile(&tmap_k, (j + kPrefetchAhead) * BN, bh);
+            prefetch_tile(&tmap_v, (j + kPrefetchAhead) * BN, bh);
+          }
           const int st = kv & 1;
           const uint32_t ph = (kv >> 1) & 1;
           if (!mbar_wait(&bars->k_empty[st], ph ^ 1)) {
@@ -309,6 +317,6 @@ extern "C" __global__ void __launch_bounds__(TB_SDPA2_THREADS, 1)
     sdpa_fwd_bf16_d128_persist(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                                const __grid_constant__ CUtensorMap tmap_v, __nv_bfloat16* __restrict__ out, int BH,
                                int Tq, int Tk, int causal, float scale_log2, uint32_t* status) {
-  // Two score pairs in every eight take the FMA/ALU exponential, as in the pair kernel.
-  sdpa_persist_body<2>(tmap_q, tmap_k, tmap_v, out, BH, Tq, Tk, causal, scale_log2, status);
+  // Every exponential on the MUFU, as in the pair kernel.
+  sdpa_persist_body<0>(tmap_q, tmap_k, tmap_v, out, BH, Tq, Tk, causal, scale_log2, status);
 }

@@ -87,6 +87,18 @@ __device__ __forceinline__ void load_tile(uint8_t* dst, const CUtensorMap* map, 
   tma_load_3d(dst + HALF_BYTES, map, bar, 64, row0, bh);
 }
 
+// L2 prefetch of the tile load_tile would read (two 64-column boxes).
+__device__ __forceinline__ void prefetch_tile(const CUtensorMap* map, int row0, int bh) {
+  tma_prefetch_l2_3d(map, 0, row0, bh);
+  tma_prefetch_l2_3d(map, 64, row0, bh);
+}
+
+// Key tiles the producer asks L2 for ahead of their loads. The K and V rings hold two
+// tiles each, so a tile's load can start only about one key-tile period before its
+// MMAs; the CTA that leads its head (the heaviest causal pair starts first) would meet
+// DRAM latency there without the prefetch.
+constexpr int kPrefetchAhead = 2;
+
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_addr, int k) {
   return sdesc_sw128(tile_addr + (k >> 2) * HALF_BYTES + (k & 3) * 32, 16, 1024);
 }
