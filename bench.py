@@ -848,6 +848,11 @@ def roofline_of(wl, per_launch_ms, peaks, peak_src, small):
             "frac": achieved / peak, "peak_source": "measured burst figure (MEASURED_PEAKS.json)"
             if peak_src == "measured" else "fallback", "ms_per_launch": per_launch_ms,
             "algorithmic_units_per_launch": wl.units_per_step()}
+    if wl.bound == "tensor":
+        # The bench times its steps after a power soak, between the burst and the
+        # seconds-long sustained regime of the measured cuBLAS figures: both are given.
+        sustained = float(peaks.get("bf16_tflops_sustained", PEAK_FALLBACK["bf16_tflops_sustained"]))
+        line.update({"peak_sustained": sustained, "frac_of_sustained": achieved / sustained})
     line.update(traffic_of(wl.kernel, wl.world == 1 and not small))
     return line
 
