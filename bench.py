@@ -256,7 +256,7 @@ class SoftmaxWorkload(Workload):
 
     def cpu_sample(self, budget_s, threads=0):
         import oracle
-        threads = threads or oracle.num_threads()
+        threads = threads or oracle.cpu_count()
         rows = 256
         t0 = time.perf_counter()
         done = 0
@@ -392,7 +392,7 @@ class GemmWorkload(Workload):
 
     def cpu_sample(self, budget_s, threads=0):
         import oracle
-        threads = threads or oracle.num_threads()
+        threads = threads or oracle.cpu_count()
         rng = np.random.default_rng(0)
         pts = 0
         t0 = time.perf_counter()
@@ -485,7 +485,7 @@ class SdpaWorkload(Workload):
 
     def cpu_sample(self, budget_s, threads=0):
         import oracle
-        threads = threads or oracle.num_threads()
+        threads = threads or oracle.cpu_count()
         S, D = self.S, self.D
         rng = np.random.default_rng(0)
         macs = 0.0
@@ -601,7 +601,7 @@ class ConvWorkload(Workload):
 
     def cpu_sample(self, budget_s, threads=0):
         import oracle
-        threads = threads or oracle.num_threads()
+        threads = threads or oracle.cpu_count()
         rng = np.random.default_rng(0)
         pts = 0
         t0 = time.perf_counter()
@@ -667,7 +667,7 @@ def run_reference_arm(args, world, rank):
     import oracle
     wl_cls = WORKLOADS[args.op]
     sampler = REFERENCE_SAMPLERS[args.op]
-    threads = oracle.num_threads()
+    threads = oracle.cpu_count()  # every core this process may run on (torchrun sets OMP_NUM_THREADS=1)
     inputs = sampler(oracle, None, 0, 0)  # the sample's inputs, made once before the steps
     times = []
     info = None
@@ -1054,7 +1054,7 @@ def main(argv=None) -> int:
         c1 = {"gpu": c1_gpu(tb, N, session, stream, args.steps)}
         if cpu_leg:
             import oracle
-            c1.update(c1_cpu(oracle, oracle.num_threads()))
+            c1.update(c1_cpu(oracle, oracle.cpu_count()))
         ops["C1"] = c1
 
     if rank == 0:

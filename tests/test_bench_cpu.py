@@ -1,6 +1,7 @@
 """bench.py's reference arm on the CPU: it runs the oracle only (the product library is
 never imported), and its line carries the same config dicts as the product arm's."""
 import json
+import os
 import pathlib
 import subprocess
 import sys
@@ -32,12 +33,16 @@ def test_reference_arm_runs_without_the_product_library():
 
 @pytest.mark.parametrize("op", ["softmax", "sdpa", "conv2d"])
 def test_reference_arm_single_op(op):
+    # torchrun starts every rank with OMP_NUM_THREADS=1; the reference arm still uses every
+    # core the process may run on.
+    env = dict(os.environ, OMP_NUM_THREADS="1")
     proc = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--op", op, "--steps", "1",
                            "--warmup", "3", "--ref-step-seconds", "0.05"], capture_output=True, text=True,
-                          timeout=600, cwd=str(ROOT))
+                          timeout=600, cwd=str(ROOT), env=env)
     assert proc.returncode == 0, proc.stderr
     line = json.loads(proc.stdout.strip().splitlines()[-1])
     assert line["config"] == bench.workload_config(op, 1) and "ops" not in line
+    assert line["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))
 
 
 def test_configs_name_the_shard_at_n_gpus():
