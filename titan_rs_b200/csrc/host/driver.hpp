@@ -45,6 +45,7 @@ namespace tb {
   X(cuModuleUnload)                    \
   X(cuModuleGetFunction)               \
   X(cuFuncSetAttribute)                \
+  X(cuFuncGetAttribute)                \
   X(cuLaunchKernel)                    \
   X(cuLaunchKernelEx)                  \
   X(cuOccupancyMaxActiveClusters)      \

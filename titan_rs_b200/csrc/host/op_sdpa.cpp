@@ -62,12 +62,18 @@ tb_status launch_sdpa_bf16_d128_pair(Session* s, Stream* st, CUdeviceptr q, CUde
   CUfunction fn = nullptr;
   rc = builtin_function(s, "sdpa_bf16_pair", "sdpa_fwd_bf16_d128_pair", &fn);
   if (rc) return rc;
+  // The kernel's warpgroups re-divide the registers the CTA was launched with; a launch
+  // with fewer than it assumes would leave the softmax warpgroups waiting for registers.
+  int regs = 0;
+  TB_CU("cuFuncGetAttribute", driver()->cuFuncGetAttribute(&regs, CU_FUNC_ATTRIBUTE_NUM_REGS, fn));
+  if (regs < TB_SDPA2_PAIR_LAUNCH_REGS)
+    return unsupported("sdpa_fwd_bf16_d128_pair was built with fewer registers than its warpgroups share");
   float scale_log2 = (float)(1.4426950408889634 * (double)scale);  // the kernels exponentiate base 2
   CUdeviceptr status = s->status.device;
   void* params[] = {&mq, &mk, &mv, &o, &tq, &tk, &causal, &scale_log2, &status};
   const unsigned long long pairs = (unsigned long long)((tq + 2 * TB_SDPA_BM - 1) / (2 * TB_SDPA_BM));
   if (pairs * (unsigned long long)bh > 0x7fffffffull) return contract("CUDA attention grid exceeds 2^31 CTAs");
-  return launch_builtin(s, st, fn, (unsigned)(pairs * bh), 1, 1, TB_SDPA2_THREADS, TB_SDPA2_SMEM_BYTES, params,
+  return launch_builtin(s, st, fn, (unsigned)(pairs * bh), 1, 1, TB_SDPA2_PAIR_THREADS, TB_SDPA2_SMEM_BYTES, params,
                         "sdpa_fwd_bf16_d128_pair");
 }
 

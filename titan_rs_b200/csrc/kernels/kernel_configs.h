@@ -47,6 +47,14 @@
 #define TB_SDPA2_THREADS 320
 #define TB_SDPA2_BARRIER_BYTES 256
 #define TB_SDPA2_SMEM_BYTES (6 * 32768 + TB_SDPA2_BARRIER_BYTES + 1024)
+// The pair kernel runs three warpgroups (control, softmax A, softmax B) and moves
+// registers from the control warpgroup to the softmax ones: 384 threads launched at
+// TB_SDPA2_PAIR_LAUNCH_REGS registers = 128 x TB_SDPA2_PAIR_CONTROL_REGS + 256 x
+// TB_SDPA2_PAIR_SOFTMAX_REGS.
+#define TB_SDPA2_PAIR_THREADS 384
+#define TB_SDPA2_PAIR_LAUNCH_REGS 168
+#define TB_SDPA2_PAIR_CONTROL_REGS 40
+#define TB_SDPA2_PAIR_SOFTMAX_REGS 232
 
 // 64-key-tile SDPA (sdpa_bf16_bn64.cu), two CTAs per SM: Q 32 KB + K ring 2x16 KB +
 // V ring 2x16 KB + barriers; 256 TMEM columns per CTA.

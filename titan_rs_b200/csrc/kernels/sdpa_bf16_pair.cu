@@ -5,7 +5,8 @@
 // O = softmax(Q K^T / sqrt(D)) V over BHTD, plus a causal mask (query i sees keys j <= i,
 // top-left aligned when Tq != Tk).
 //
-// One CTA per (pair of 128-row query tiles A = 2i, B = 2i+1, batch*head); 320 threads:
+// One CTA per (pair of 128-row query tiles A = 2i, B = 2i+1, batch*head); 384 threads in
+// three warpgroups (control: warps 0-3, softmax A: 4-7, softmax B: 8-11):
 //   warp 0       TMA producer: Q_A and Q_B once, then K_j / V_j (128 keys x 128 dims,
 //                two 64-column 128-byte-swizzled boxes each) through 2-stage rings.
 //   warp 1       owns all 512 TMEM columns: S_A | S_B | O_A | O_B (128 fp32 columns each).
@@ -15,7 +16,9 @@
 //                tile's warpgroup exponentiates.
 //                  S_X(j)  = Q_X K_j^T   (SS: both operands K-major in shared memory)
 //                  O_X    += P_X(j) V_j  (TS: P read from TMEM, V MN-major in shared memory)
-//   warps 2..5   softmax group for tile A, warps 6..9 for tile B (each group covers the
+//   warps 2, 3   idle (they complete the control warpgroup, which gives its registers
+//                to the softmax warpgroups: 40 each against 232).
+//   warps 4..7   softmax group for tile A, warps 8..11 for tile B (each group covers the
 //                four TMEM lane quarters, since warp w reaches lanes 32*(w%4)..): one query row per
 //                thread (its TMEM lane). Per key tile the thread reads its row's 128
 //                scores from TMEM into registers once; pass 1 takes the row max;
@@ -111,123 +114,134 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = bars->tmem_base;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer ----------------
-      tma_prefetch_desc(&tmap_q);
-      tma_prefetch_desc(&tmap_k);
-      tma_prefetch_desc(&tmap_v);
-      mbar_arrive_expect_tx(&bars->q_full, 2 * TILE_BYTES);
-      load_tile(smem + OFF_Q, &tmap_q, &bars->q_full, qt0 * BM, bh);
-      load_tile(smem + OFF_Q + TILE_BYTES, &tmap_q, &bars->q_full, (qt0 + 1) * BM, bh);
-      uint32_t k_issued[2] = {0, 0}, v_issued[2] = {0, 0};
-      bool ok = true;
-      for (int j = 0; j < kPrefetchAhead && j < n_b; ++j) {
-        prefetch_tile(&tmap_k, j * BN, bh);
-        prefetch_tile(&tmap_v, j * BN, bh);
-      }
-      for (int j = 0; j < n_b && ok; ++j) {
-        if (j + kPrefetchAhead < n_b) {
-          prefetch_tile(&tmap_k, (j + kPrefetchAhead) * BN, bh);
-          prefetch_tile(&tmap_v, (j + kPrefetchAhead) * BN, bh);
+  static_assert(TB_SDPA2_PAIR_THREADS == 384, "three warpgroups");
+  static_assert(128 * TB_SDPA2_PAIR_CONTROL_REGS + 256 * TB_SDPA2_PAIR_SOFTMAX_REGS <=
+                    TB_SDPA2_PAIR_THREADS * TB_SDPA2_PAIR_LAUNCH_REGS,
+                "the warpgroups' registers exceed the launch allocation");
+  // Each role runs inside the branch of its register count, so the compiler gives the
+  // softmax code 232 registers and the control code 40.
+  if (warp < 4) {
+    setmaxnreg_dec<TB_SDPA2_PAIR_CONTROL_REGS>();
+    if (warp == 0) {
+      if (lane == 0) {
+        // ---------------- TMA producer ----------------
+        tma_prefetch_desc(&tmap_q);
+        tma_prefetch_desc(&tmap_k);
+        tma_prefetch_desc(&tmap_v);
+        mbar_arrive_expect_tx(&bars->q_full, 2 * TILE_BYTES);
+        load_tile(smem + OFF_Q, &tmap_q, &bars->q_full, qt0 * BM, bh);
+        load_tile(smem + OFF_Q + TILE_BYTES, &tmap_q, &bars->q_full, (qt0 + 1) * BM, bh);
+        uint32_t k_issued[2] = {0, 0}, v_issued[2] = {0, 0};
+        bool ok = true;
+        for (int j = 0; j < kPrefetchAhead && j < n_b; ++j) {
+          prefetch_tile(&tmap_k, j * BN, bh);
+          prefetch_tile(&tmap_v, j * BN, bh);
         }
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&bars->k_empty[st], ph ^ 1)) {
-          report_status(status, kFailProducer | 1);
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&bars->k_full[st], TILE_BYTES);
-        load_tile(smem + OFF_K + st * TILE_BYTES, &tmap_k, &bars->k_full[st], j * BN, bh);
-        ++k_issued[st];
-        if (!mbar_wait(&bars->v_empty[st], ph ^ 1)) {
-          report_status(status, kFailProducer | 2);
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&bars->v_full[st], TILE_BYTES);
-        load_tile(smem + OFF_V + st * TILE_BYTES, &tmap_v, &bars->v_full[st], j * BN, bh);
-        ++v_issued[st];
-      }
-      if (!ok) {
-        if (!mbar_wait(&bars->q_full, 0)) report_status(status, kFailProducer | 3);
-        for (int s = 0; s < 2; ++s) {
-          if (k_issued[s] && !mbar_wait(&bars->k_full[s], (k_issued[s] - 1) & 1)) report_status(status, kFailProducer | 4);
-          if (v_issued[s] && !mbar_wait(&bars->v_full[s], (v_issued[s] - 1) & 1)) report_status(status, kFailProducer | 5);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      // One lane issues every MMA, so its instruction stream is kept short: all
-      // descriptors are formed here once, and each MMA only adds a compile-time
-      // K-slice offset to the low word of one of them.
-      bool ok = mbar_wait(&bars->q_full, 0);
-      if (!ok) report_status(status, kFailMma | 1);
-      const uint64_t qd_a = kmajor_desc(smem_addr(smem + OFF_Q), 0);
-      const uint64_t qd_b = kmajor_desc(smem_addr(smem + OFF_Q + TILE_BYTES), 0);
-      const uint64_t kd0 = kmajor_desc(smem_addr(smem + OFF_K), 0);
-      const uint64_t vd0 = v_desc(smem_addr(smem + OFF_V), 0);
-      // j = key tile whose scores are issued this iteration; PV of tile j-1 goes first.
-      for (int j = 0; j <= n_b && ok; ++j) {
-        const int st = j & 1, pst = (j - 1) & 1;
-        const uint32_t ph = (j >> 1) & 1, pph = ((j - 1) >> 1) & 1;
-        const uint64_t kd = desc_add(kd0, st * (TILE_BYTES >> 4));
-        const uint64_t vd = desc_add(vd0, pst * (TILE_BYTES >> 4));
-        const bool pv_a = j >= 1 && j - 1 < n_a, pv_b = j >= 1 && j - 1 < n_b;  // n_a <= n_b
-        const bool s_a = j < n_a, s_b = j < n_b;
-        if (pv_b && !mbar_wait(&bars->v_full[pst], pph)) {
-          report_status(status, kFailMma | 2);
-          ok = false;
-          break;
-        }
-        // K_j was loaded long before P_A(j-1) is ready: wait for it first, so that
-        // S_A(j) issues right behind PV_A(j-1).
-        const bool k_ready = s_b;
-        if (k_ready && !mbar_wait(&bars->k_full[st], ph)) {
-          report_status(status, kFailMma | 4);
-          ok = false;
-          break;
-        }
-        // Tile A: O_A += P_A(j-1) V_{j-1}, then S_A(j) = Q_A K_j^T; then the same for tile B.
-        for (int x = 0; x < 2; ++x) {
-          if (x ? pv_b : pv_a) {
-            // The first half of P_x(j-1) arrives while its warps still exponentiate the second.
-            if (!mbar_wait(&bars->p_half[x], (j - 1) & 1)) {
-              report_status(status, kFailMma | 3);
-              ok = false;
-              break;
-            }
-            tc_fence_after_sync();
-            issue_pv_half(tmem + (2 + x) * BN, tmem + x * BN, vd, 0, j - 1 > 0);
-            if (!mbar_wait(&bars->p_full[x], (j - 1) & 1)) {
-              report_status(status, kFailMma | 6);
-              ok = false;
-              break;
-            }
-            tc_fence_after_sync();
-            issue_pv_half(tmem + (2 + x) * BN, tmem + x * BN, vd, 1, true);
+        for (int j = 0; j < n_b && ok; ++j) {
+          if (j + kPrefetchAhead < n_b) {
+            prefetch_tile(&tmap_k, (j + kPrefetchAhead) * BN, bh);
+            prefetch_tile(&tmap_v, (j + kPrefetchAhead) * BN, bh);
           }
-          if (x ? s_b : s_a) {
-            tc_fence_after_sync();
-            issue_s(tmem + x * BN, x ? qd_b : qd_a, kd);
-            umma_commit(&bars->s_full[x]);
+          const int st = j & 1;
+          const uint32_t ph = (j >> 1) & 1;
+          if (!mbar_wait(&bars->k_empty[st], ph ^ 1)) {
+            report_status(status, kFailProducer | 1);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bars->k_full[st], TILE_BYTES);
+          load_tile(smem + OFF_K + st * TILE_BYTES, &tmap_k, &bars->k_full[st], j * BN, bh);
+          ++k_issued[st];
+          if (!mbar_wait(&bars->v_empty[st], ph ^ 1)) {
+            report_status(status, kFailProducer | 2);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bars->v_full[st], TILE_BYTES);
+          load_tile(smem + OFF_V + st * TILE_BYTES, &tmap_v, &bars->v_full[st], j * BN, bh);
+          ++v_issued[st];
+        }
+        if (!ok) {
+          if (!mbar_wait(&bars->q_full, 0)) report_status(status, kFailProducer | 3);
+          for (int s = 0; s < 2; ++s) {
+            if (k_issued[s] && !mbar_wait(&bars->k_full[s], (k_issued[s] - 1) & 1))
+              report_status(status, kFailProducer | 4);
+            if (v_issued[s] && !mbar_wait(&bars->v_full[s], (v_issued[s] - 1) & 1))
+              report_status(status, kFailProducer | 5);
           }
         }
-        if (!ok) break;
-        if (pv_b) umma_commit(&bars->v_empty[pst]);
-        if (k_ready) umma_commit(&bars->k_empty[st]);
       }
-      umma_commit(&bars->o_final);
-      umma_commit(&bars->drain);
-      if (!mbar_wait(&bars->drain, 0)) report_status(status, kFailMma | 5);
+    } else if (warp == 1) {
+      if (lane == 0) {
+        // ---------------- MMA issuer ----------------
+        // One lane issues every MMA, so its instruction stream is kept short: all
+        // descriptors are formed here once, and each MMA only adds a compile-time
+        // K-slice offset to the low word of one of them.
+        bool ok = mbar_wait(&bars->q_full, 0);
+        if (!ok) report_status(status, kFailMma | 1);
+        const uint64_t qd_a = kmajor_desc(smem_addr(smem + OFF_Q), 0);
+        const uint64_t qd_b = kmajor_desc(smem_addr(smem + OFF_Q + TILE_BYTES), 0);
+        const uint64_t kd0 = kmajor_desc(smem_addr(smem + OFF_K), 0);
+        const uint64_t vd0 = v_desc(smem_addr(smem + OFF_V), 0);
+        // j = key tile whose scores are issued this iteration; PV of tile j-1 goes first.
+        for (int j = 0; j <= n_b && ok; ++j) {
+          const int st = j & 1, pst = (j - 1) & 1;
+          const uint32_t ph = (j >> 1) & 1, pph = ((j - 1) >> 1) & 1;
+          const uint64_t kd = desc_add(kd0, st * (TILE_BYTES >> 4));
+          const uint64_t vd = desc_add(vd0, pst * (TILE_BYTES >> 4));
+          const bool pv_a = j >= 1 && j - 1 < n_a, pv_b = j >= 1 && j - 1 < n_b;  // n_a <= n_b
+          const bool s_a = j < n_a, s_b = j < n_b;
+          if (pv_b && !mbar_wait(&bars->v_full[pst], pph)) {
+            report_status(status, kFailMma | 2);
+            ok = false;
+            break;
+          }
+          // K_j was loaded long before P_A(j-1) is ready: wait for it first, so that
+          // S_A(j) issues right behind PV_A(j-1).
+          const bool k_ready = s_b;
+          if (k_ready && !mbar_wait(&bars->k_full[st], ph)) {
+            report_status(status, kFailMma | 4);
+            ok = false;
+            break;
+          }
+          // Tile A: O_A += P_A(j-1) V_{j-1}, then S_A(j) = Q_A K_j^T; then the same for tile B.
+          for (int x = 0; x < 2; ++x) {
+            if (x ? pv_b : pv_a) {
+              // The first half of P_x(j-1) arrives while its warps still exponentiate the second.
+              if (!mbar_wait(&bars->p_half[x], (j - 1) & 1)) {
+                report_status(status, kFailMma | 3);
+                ok = false;
+                break;
+              }
+              tc_fence_after_sync();
+              issue_pv_half(tmem + (2 + x) * BN, tmem + x * BN, vd, 0, j - 1 > 0);
+              if (!mbar_wait(&bars->p_full[x], (j - 1) & 1)) {
+                report_status(status, kFailMma | 6);
+                ok = false;
+                break;
+              }
+              tc_fence_after_sync();
+              issue_pv_half(tmem + (2 + x) * BN, tmem + x * BN, vd, 1, true);
+            }
+            if (x ? s_b : s_a) {
+              tc_fence_after_sync();
+              issue_s(tmem + x * BN, x ? qd_b : qd_a, kd);
+              umma_commit(&bars->s_full[x]);
+            }
+          }
+          if (!ok) break;
+          if (pv_b) umma_commit(&bars->v_empty[pst]);
+          if (k_ready) umma_commit(&bars->k_empty[st]);
+        }
+        umma_commit(&bars->o_final);
+        umma_commit(&bars->drain);
+        if (!mbar_wait(&bars->drain, 0)) report_status(status, kFailMma | 5);
+      }
     }
   } else {
+    setmaxnreg_inc<TB_SDPA2_PAIR_SOFTMAX_REGS>();
     // ---------------- softmax warpgroups ----------------
-    const int x = (warp >= 6) ? 1 : 0;  // query tile of this softmax group
+    const int x = (warp >= 8) ? 1 : 0;  // query tile of this softmax group
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
@@ -271,11 +285,11 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
   }
 }
 
-// One CTA per SM: 10 warps, three of them on two of the four SM sub-partitions, which
-// caps a thread at 168 registers; each softmax thread keeps its row's 128 scores in
-// registers.
+// One CTA per SM: 12 warps launched at 168 registers a thread (three on each SM
+// sub-partition); the softmax warps then hold 232, enough for a row's 128 scores in
+// registers beside the exponential's temporaries.
 #define TB_SDPA_PAIR_ENTRY(name, poly)                                                                              \
-  extern "C" __global__ void __launch_bounds__(TB_SDPA2_THREADS, 1)                                              \
+  extern "C" __global__ void __launch_bounds__(TB_SDPA2_PAIR_THREADS, 1)                                         \
       name(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,             \
            const __grid_constant__ CUtensorMap tmap_v, __nv_bfloat16* __restrict__ out, int Tq, int Tk, int causal, \
            float scale_log2, uint32_t* status) {                                                                 \

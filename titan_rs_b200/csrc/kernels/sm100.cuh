@@ -105,6 +105,21 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Register reallocation between warpgroups (all 128 threads of a warpgroup execute
+// it): `dec` returns registers to the CTA's pool, `inc` waits until the pool can
+// cover the new count, so the warpgroups' counts must add up to at most the CTA's
+// launch allocation (threads x registers per thread at launch).
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  static_assert(kRegs % 8 == 0 && kRegs >= 24 && kRegs <= 256, "setmaxnreg takes multiples of 8 in [24, 256]");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  static_assert(kRegs % 8 == 0 && kRegs >= 24 && kRegs <= 256, "setmaxnreg takes multiples of 8 in [24, 256]");
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
 // Brings one tile of a tensor (the box of `map` at the coordinates) into L2 ahead of
 // its load; completes on nothing and writes no shared memory.
 __device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int32_t x, int32_t y, int32_t z) {
