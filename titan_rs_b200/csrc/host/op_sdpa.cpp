@@ -89,14 +89,23 @@ tb_status launch_sdpa_bf16_d128_persist(Session* s, Stream* st, CUdeviceptr q, C
   CUfunction fn = nullptr;
   rc = builtin_function(s, "sdpa_bf16_persist", "sdpa_fwd_bf16_d128_persist", &fn);
   if (rc) return rc;
+  // Same register split as the pair kernel.
+  int regs = 0;
+  TB_CU("cuFuncGetAttribute", driver()->cuFuncGetAttribute(&regs, CU_FUNC_ATTRIBUTE_NUM_REGS, fn));
+  if (regs < TB_SDPA2_PAIR_LAUNCH_REGS)
+    return unsupported("sdpa_fwd_bf16_d128_persist was built with fewer registers than its warpgroups share");
   float scale_log2 = (float)(1.4426950408889634 * (double)scale);  // the kernels exponentiate base 2
   CUdeviceptr status = s->status.device;
-  void* params[] = {&mq, &mk, &mv, &o, &bh, &tq, &tk, &causal, &scale_log2, &status};
   const unsigned long long items =
       (unsigned long long)((tq + 2 * TB_SDPA_BM - 1) / (2 * TB_SDPA_BM)) * (unsigned long long)bh;
   if (items > 0x7fffffffull) return contract("CUDA attention work list exceeds 2^31 items");
   const unsigned grid = (unsigned)std::min<unsigned long long>(items, (unsigned long long)s->sm_count);
-  return launch_builtin(s, st, fn, grid, 1, 1, TB_SDPA2_THREADS, TB_SDPA2_SMEM_BYTES, params,
+  // The work-item counter the CTAs draw from, zeroed in stream order before the launch.
+  CUdeviceptr next_item = 0;
+  if ((rc = stream_scratch(s, st, sizeof(uint32_t), &next_item))) return rc;
+  TB_CU("cuMemsetD32Async", driver()->cuMemsetD32Async(next_item, 0, 1, st->raw));
+  void* params[] = {&mq, &mk, &mv, &o, &bh, &tq, &tk, &causal, &scale_log2, &next_item, &status};
+  return launch_builtin(s, st, fn, grid, 1, 1, TB_SDPA2_PAIR_THREADS, TB_SDPA2_SMEM_BYTES, params,
                         "sdpa_fwd_bf16_d128_persist");
 }
 
