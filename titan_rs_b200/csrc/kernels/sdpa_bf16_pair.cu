@@ -81,10 +81,11 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Barriers* bars = reinterpret_cast<Barriers*>(smem + OFF_BAR);
   const int warp = warp_id(), lane = lane_id();
-  // Flat grid, head-major (a head's K/V stays in L2), heaviest causal pairs first.
+  // Flat grid in the shared work order (groups of heads, heaviest causal pairs first;
+  // the block scheduler hands the next block to the first free SM).
   const int num_pairs = (Tq + 2 * BM - 1) / (2 * BM);
-  const int bh = blockIdx.x / num_pairs;
-  const int pair = num_pairs - 1 - (int)(blockIdx.x % num_pairs);
+  int bh, pair;
+  PairSchedule{(int)(gridDim.x / num_pairs), num_pairs}.item((int)blockIdx.x, bh, pair);
   const int qt0 = 2 * pair;                     // query tile A; tile B = qt0 + 1
   const int kv_tiles_all = (Tk + BN - 1) / BN;
   // Key tiles each query tile needs.

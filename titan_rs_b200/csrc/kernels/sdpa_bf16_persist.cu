@@ -62,22 +62,7 @@ static_assert(OFF_BAR + TB_SDPA2_BARRIER_BYTES + 1024 == TB_SDPA2_SMEM_BYTES, "s
 constexpr uint32_t kFailProducer = 0x50110000u;
 constexpr uint32_t kFailMma = 0x50120000u;
 constexpr uint32_t kFailSoftmax = 0x50130000u;
-constexpr int kHeadGroup = 16;
 constexpr int kItemReaders = 1 + 8;  // MMA lane, softmax warps
-
-// Work item u -> (bh, pair): groups of kHeadGroup heads; inside a group, pair-major
-// from the heaviest causal pair (the last one) down.
-struct Schedule {
-  int bh_count, num_pairs;
-  __device__ void item(int u, int& bh, int& pair) const {
-    const int per_group = kHeadGroup * num_pairs;
-    const int g = u / per_group;
-    const int r = u - g * per_group;
-    const int heads = min(kHeadGroup, bh_count - g * kHeadGroup);
-    pair = num_pairs - 1 - r / heads;
-    bh = g * kHeadGroup + r % heads;
-  }
-};
 
 }  // namespace
 
@@ -92,7 +77,7 @@ __device__ __forceinline__ void sdpa_persist_body(const CUtensorMap& tmap_q, con
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Barriers* bars = reinterpret_cast<Barriers*>(smem + OFF_BAR);
   const int warp = warp_id(), lane = lane_id();
-  const Schedule sched{BH, (Tq + 2 * BM - 1) / (2 * BM)};
+  const PairSchedule sched{BH, (Tq + 2 * BM - 1) / (2 * BM)};
   const int items = BH * sched.num_pairs;
   const int kv_tiles_all = (Tk + BN - 1) / BN;
   // Key tiles query tile qt needs.

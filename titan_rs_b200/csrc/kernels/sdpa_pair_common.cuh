@@ -99,6 +99,23 @@ __device__ __forceinline__ void prefetch_tile(const CUtensorMap* map, int row0, 
 // DRAM latency there without the prefetch.
 constexpr int kPrefetchAhead = 2;
 
+// Work order of the (batch*head, query-tile pair) items: groups of kHeadGroup heads
+// (their K and V, 2 MB a head at T = 4096, stay in L2 while the group runs) and, inside
+// a group, pair-major from the heaviest causal pair (the last one) down, so the long
+// pairs of every head start first and the short ones fill in at the end.
+constexpr int kHeadGroup = 16;
+struct PairSchedule {
+  int bh_count, num_pairs;
+  __device__ __forceinline__ void item(int u, int& bh, int& pair) const {
+    const int per_group = kHeadGroup * num_pairs;
+    const int g = u / per_group;
+    const int r = u - g * per_group;
+    const int heads = min(kHeadGroup, bh_count - g * kHeadGroup);
+    pair = num_pairs - 1 - r / heads;
+    bh = g * kHeadGroup + r % heads;
+  }
+};
+
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_addr, int k) {
   return sdesc_sw128(tile_addr + (k >> 2) * HALF_BYTES + (k & 3) * 32, 16, 1024);
 }
