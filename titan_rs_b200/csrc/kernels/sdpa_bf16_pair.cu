@@ -7,8 +7,9 @@
 //
 // One CTA per (pair of 128-row query tiles A = 2i, B = 2i+1, batch*head); 384 threads in
 // three warpgroups (control: warps 0-3, softmax A: 4-7, softmax B: 8-11):
-//   warp 0       TMA producer: Q_A and Q_B once, then K_j / V_j (128 keys x 128 dims,
-//                two 64-column 128-byte-swizzled boxes each) through 2-stage rings.
+//   warp 0       TMA producer: Q_A and Q_B once, then K_j and V_{j-1} (128 keys x 128
+//                dims, two 64-column 128-byte-swizzled boxes each) into stage j & 1 of a
+//                2-stage ring (one full and one empty barrier per stage).
 //   warp 1       owns all 512 TMEM columns: S_A | S_B | O_A | O_B (128 fp32 columns each).
 //                One lane issues, per key tile j,
 //                  PV_A(j-1) (two halves) then S_A(j), PV_B(j-1) then S_B(j)
@@ -47,8 +48,7 @@ using namespace tb::sdpa2;
 
 struct Barriers {
   uint64_t q_full;
-  uint64_t k_full[2], k_empty[2];
-  uint64_t v_full[2], v_empty[2];
+  uint64_t kv_full[2], kv_empty[2];  // stage j & 1 holds K_j and V_{j-1}
   uint64_t s_full[2];  // per query tile (A, B)
   uint64_t p_half[2];  // per query tile: P of keys [0, 64) is in TMEM
   uint64_t p_full[2];  // per query tile: P of keys [64, 128) is in TMEM
@@ -95,10 +95,8 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars->k_full[i], 1);
-      mbar_init(&bars->k_empty[i], 1);
-      mbar_init(&bars->v_full[i], 1);
-      mbar_init(&bars->v_empty[i], 1);
+      mbar_init(&bars->kv_full[i], 1);
+      mbar_init(&bars->kv_empty[i], 1);
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->p_half[i], 4);
       mbar_init(&bars->p_full[i], 4);
@@ -132,44 +130,37 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
         mbar_arrive_expect_tx(&bars->q_full, 2 * TILE_BYTES);
         load_tile(smem + OFF_Q, &tmap_q, &bars->q_full, qt0 * BM, bh);
         load_tile(smem + OFF_Q + TILE_BYTES, &tmap_q, &bars->q_full, (qt0 + 1) * BM, bh);
-        uint32_t k_issued[2] = {0, 0}, v_issued[2] = {0, 0};
+        // Stage j & 1 of the ring holds K_j and V_{j-1}: the two tiles the MMA lane's
+        // iteration j reads, so it waits once and releases once per iteration.
+        uint32_t issued[2] = {0, 0};
         bool ok = true;
         for (int j = 0; j < kPrefetchAhead && j < n_b; ++j) {
           prefetch_tile(&tmap_k, j * BN, bh);
           prefetch_tile(&tmap_v, j * BN, bh);
         }
-        for (int j = 0; j < n_b && ok; ++j) {
+        for (int j = 0; j <= n_b && ok; ++j) {
           if (j + kPrefetchAhead < n_b) {
             prefetch_tile(&tmap_k, (j + kPrefetchAhead) * BN, bh);
             prefetch_tile(&tmap_v, (j + kPrefetchAhead) * BN, bh);
           }
           const int st = j & 1;
           const uint32_t ph = (j >> 1) & 1;
-          if (!mbar_wait(&bars->k_empty[st], ph ^ 1)) {
+          if (!mbar_wait(&bars->kv_empty[st], ph ^ 1)) {
             report_status(status, kFailProducer | 1);
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&bars->k_full[st], TILE_BYTES);
-          load_tile(smem + OFF_K + st * TILE_BYTES, &tmap_k, &bars->k_full[st], j * BN, bh);
-          ++k_issued[st];
-          if (!mbar_wait(&bars->v_empty[st], ph ^ 1)) {
-            report_status(status, kFailProducer | 2);
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&bars->v_full[st], TILE_BYTES);
-          load_tile(smem + OFF_V + st * TILE_BYTES, &tmap_v, &bars->v_full[st], j * BN, bh);
-          ++v_issued[st];
+          const bool has_k = j < n_b, has_v = j >= 1;
+          mbar_arrive_expect_tx(&bars->kv_full[st], (has_k ? TILE_BYTES : 0) + (has_v ? TILE_BYTES : 0));
+          if (has_k) load_tile(smem + OFF_K + st * TILE_BYTES, &tmap_k, &bars->kv_full[st], j * BN, bh);
+          if (has_v) load_tile(smem + OFF_V + st * TILE_BYTES, &tmap_v, &bars->kv_full[st], (j - 1) * BN, bh);
+          ++issued[st];
         }
         if (!ok) {
           if (!mbar_wait(&bars->q_full, 0)) report_status(status, kFailProducer | 3);
-          for (int s = 0; s < 2; ++s) {
-            if (k_issued[s] && !mbar_wait(&bars->k_full[s], (k_issued[s] - 1) & 1))
+          for (int s = 0; s < 2; ++s)
+            if (issued[s] && !mbar_wait(&bars->kv_full[s], (issued[s] - 1) & 1))
               report_status(status, kFailProducer | 4);
-            if (v_issued[s] && !mbar_wait(&bars->v_full[s], (v_issued[s] - 1) & 1))
-              report_status(status, kFailProducer | 5);
-          }
         }
       }
     } else if (warp == 1) {
@@ -186,26 +177,19 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
         const uint64_t vd0 = v_desc(smem_addr(smem + OFF_V), 0);
         // j = key tile whose scores are issued this iteration; PV of tile j-1 goes first.
         for (int j = 0; j <= n_b && ok; ++j) {
-          const int st = j & 1, pst = (j - 1) & 1;
-          const uint32_t ph = (j >> 1) & 1, pph = ((j - 1) >> 1) & 1;
+          const int st = j & 1;
           const uint64_t kd = desc_add(kd0, st * (TILE_BYTES >> 4));
-          const uint64_t vd = desc_add(vd0, pst * (TILE_BYTES >> 4));
-          const bool pv_a = j >= 1 && j - 1 < n_a, pv_b = j >= 1 && j - 1 < n_b;  // n_a <= n_b
+          const uint64_t vd = desc_add(vd0, st * (TILE_BYTES >> 4));
+          const bool pv_a = j >= 1 && j - 1 < n_a, pv_b = j >= 1;  // n_a <= n_b; j <= n_b
           const bool s_a = j < n_a, s_b = j < n_b;
-          if (pv_b && !mbar_wait(&bars->v_full[pst], pph)) {
+          if (!mbar_wait(&bars->kv_full[st], (j >> 1) & 1)) {
             report_status(status, kFailMma | 2);
             ok = false;
             break;
           }
-          // K_j was loaded long before P_A(j-1) is ready: wait for it first, so that
-          // S_A(j) issues right behind PV_A(j-1).
-          const bool k_ready = s_b;
-          if (k_ready && !mbar_wait(&bars->k_full[st], ph)) {
-            report_status(status, kFailMma | 4);
-            ok = false;
-            break;
-          }
           // Tile A: O_A += P_A(j-1) V_{j-1}, then S_A(j) = Q_A K_j^T; then the same for tile B.
+          // S_x(j) overwrites P_x(j-1) after the PV that reads it (the tensor core runs
+          // them in order), and its softmax warps read S_x(j-1) before announcing p_full.
           for (int x = 0; x < 2; ++x) {
             if (x ? pv_b : pv_a) {
               // The first half of P_x(j-1) arrives while its warps still exponentiate the second.
@@ -225,14 +209,12 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
               issue_pv_half(tmem + (2 + x) * BN, tmem + x * BN, vd, 1, true);
             }
             if (x ? s_b : s_a) {
-              tc_fence_after_sync();
               issue_s(tmem + x * BN, x ? qd_b : qd_a, kd);
               umma_commit(&bars->s_full[x]);
             }
           }
           if (!ok) break;
-          if (pv_b) umma_commit(&bars->v_empty[pst]);
-          if (k_ready) umma_commit(&bars->k_empty[st]);
+          umma_commit(&bars->kv_empty[st]);  // after this iteration's MMAs have read K_j and V_{j-1}
         }
         umma_commit(&bars->o_final);
         umma_commit(&bars->drain);
