@@ -53,8 +53,8 @@
 // TB_SDPA2_PAIR_SOFTMAX_REGS.
 #define TB_SDPA2_PAIR_THREADS 384
 #define TB_SDPA2_PAIR_LAUNCH_REGS 168
-#define TB_SDPA2_PAIR_CONTROL_REGS 40
-#define TB_SDPA2_PAIR_SOFTMAX_REGS 232
+#define TB_SDPA2_PAIR_CONTROL_REGS 56
+#define TB_SDPA2_PAIR_SOFTMAX_REGS 216
 
 // 64-key-tile SDPA (sdpa_bf16_bn64.cu), two CTAs per SM: Q 32 KB + K ring 2x16 KB +
 // V ring 2x16 KB + barriers; 256 TMEM columns per CTA.

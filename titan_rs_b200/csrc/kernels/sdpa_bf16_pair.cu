@@ -18,7 +18,7 @@
 //                  S_X(j)  = Q_X K_j^T   (SS: both operands K-major in shared memory)
 //                  O_X    += P_X(j) V_j  (TS: P read from TMEM, V MN-major in shared memory)
 //   warps 2, 3   idle (they complete the control warpgroup, which gives its registers
-//                to the softmax warpgroups: 40 each against 232).
+//                to the softmax warpgroups: 56 each against 216).
 //   warps 4..7   softmax group for tile A, warps 8..11 for tile B (each group covers the
 //                four TMEM lane quarters, since warp w reaches lanes 32*(w%4)..): one query row per
 //                thread (its TMEM lane). Per key tile the thread reads its row's 128
@@ -118,7 +118,7 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
                     TB_SDPA2_PAIR_THREADS * TB_SDPA2_PAIR_LAUNCH_REGS,
                 "the warpgroups' registers exceed the launch allocation");
   // Each role runs inside the branch of its register count, so the compiler gives the
-  // softmax code 232 registers and the control code 40.
+  // softmax code 216 registers and the control code 56.
   if (warp < 4) {
     setmaxnreg_dec<TB_SDPA2_PAIR_CONTROL_REGS>();
     if (warp == 0) {
@@ -269,7 +269,7 @@ __device__ __forceinline__ void sdpa_pair_body(const CUtensorMap& tmap_q, const 
 }
 
 // One CTA per SM: 12 warps launched at 168 registers a thread (three on each SM
-// sub-partition); the softmax warps then hold 232, enough for a row's 128 scores in
+// sub-partition); the softmax warps then hold 216, enough for a row's 128 scores in
 // registers beside the exponential's temporaries.
 #define TB_SDPA_PAIR_ENTRY(name, poly)                                                                              \
   extern "C" __global__ void __launch_bounds__(TB_SDPA2_PAIR_THREADS, 1)                                         \

@@ -13,8 +13,8 @@
 // a group, every head's heaviest causal pair first. The producer thread draws the item
 // numbers and passes them to the other roles through a two-slot ring in shared memory
 // (item_full / item_empty). The roles are those of the pair kernel (three warpgroups:
-// control = TMA producer warp, MMA warp and two idle warps at 40 registers; softmax A and
-// softmax B at 232; TMEM = S_A | S_B | O_A | O_B), and the item boundary is pipelined
+// control = TMA producer warp, MMA warp and two idle warps at 56 registers; softmax A and
+// softmax B at 216; TMEM = S_A | S_B | O_A | O_B), and the item boundary is pipelined
 // instead of paid by a new CTA:
 //   - the producer loads the next item's Q as soon as the last S MMA of the current item
 //     has read Q (q_empty), and its K/V stream on through the same rings;
@@ -350,7 +350,7 @@ __device__ __forceinline__ void sdpa_persist_body(const CUtensorMap& tmap_q, con
 }
 
 // One CTA per SM, 12 warps launched at 168 registers a thread; the softmax warps then
-// hold 232 (the pair kernel's split). `next_item` is a zeroed 32-bit counter.
+// hold 216 (the pair kernel's split). `next_item` is a zeroed 32-bit counter.
 extern "C" __global__ void __launch_bounds__(TB_SDPA2_PAIR_THREADS, 1)
     sdpa_fwd_bf16_d128_persist(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                                const __grid_constant__ CUtensorMap tmap_v, __nv_bfloat16* __restrict__ out, int BH,
