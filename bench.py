@@ -1089,13 +1089,13 @@ _TRAFFIC_CAPTURE = ("ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gp
                     "--clock-control none -k regex:{kernel} -s 3 -c 1 python bench.py --op {op} --ops none "
                     "--steps 5 --warmup 3 --no-cpu-baseline --soak-ms 0")
 TRAFFIC_PER_LAUNCH: dict = {
-    "gemm_bf16_tn_2sm": {"read": 1022161152, "write": 126671872, "source_sha16": "bbd1913bb1a7b079",
+    "gemm_bf16_tn_2sm": {"read": 1081105408, "write": 127481344, "source_sha16": "54dc0bd85b841016",
                          "capture": _TRAFFIC_CAPTURE.format(kernel="gemm_bf16_tn_2sm", op="gemm")},
-    "softmax_f32_warp32": {"read": 536933376, "write": 480914432, "source_sha16": "a19088a14dfbed81",
+    "softmax_f32_warp32": {"read": 536910848, "write": 481062656, "source_sha16": "ce3281e4870b4353",
                            "capture": _TRAFFIC_CAPTURE.format(kernel="softmax_f32_warp32", op="softmax")},
-    "sdpa_fwd_bf16_d128_pair": {"read": 806622976, "write": 265165056, "source_sha16": "c87b3a0c72d2a9b8",
+    "sdpa_fwd_bf16_d128_pair": {"read": 817396736, "write": 248575744, "source_sha16": "5103eb121de93dd7",
                                 "capture": _TRAFFIC_CAPTURE.format(kernel="sdpa_fwd_bf16_d128_pair", op="sdpa")},
-    "conv2d_fprop_bf16_nhwc_2sm": {"read": 103985152, "write": 55264512, "source_sha16": "ee35a0770bf797fe",
+    "conv2d_fprop_bf16_nhwc_2sm": {"read": 103993088, "write": 55552256, "source_sha16": "7d20457bf8c14ec6",
                                    "capture": _TRAFFIC_CAPTURE.format(kernel="conv2d_fprop_bf16_nhwc_2sm",
                                                                       op="conv2d")},
 }
