@@ -72,12 +72,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait that may suspend the thread for up to `hint_ns` while the phase is open (it
+// returns as soon as the phase completes), so a waiting warp takes no issue slots.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
+// Suspend hint of the bounded waits: far below the 1 s limit, far above a pipeline step.
+constexpr uint32_t kWaitSuspendNs = 20000;
+
 // Waits for the phase with the given parity to complete; false after ~1 s.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_addr(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t start = global_timer_ns();
-  while (!mbar_try_wait(a, parity)) {
+  while (!mbar_try_wait_suspend(a, parity, kWaitSuspendNs)) {
     if (global_timer_ns() - start > kWaitLimitNs) return false;
   }
   return true;
