@@ -180,6 +180,11 @@ class Workload:
     def e2e_download(self, stream):
         raise NotImplementedError
 
+    # A workload whose public API streams host operands through the GPU (upload,
+    # compute and download overlapped inside a step) sets this to a callable
+    # (stream, after_event_or_None) -> None that enqueues one such step.
+    e2e_streamed = None
+
     def h2d_bytes(self) -> int:
         raise NotImplementedError
 
@@ -380,6 +385,22 @@ class GemmWorkload(Workload):
 
     def e2e_download(self, stream):
         self.s.download_pinned(stream, self.dc, self.host_c)
+
+    def _streamed_step(self, stream, after):
+        if self._streamer is None:
+            from titan_rs_b200.streaming import StreamedGemm
+            self._streamer = StreamedGemm(self.s, self.M, self.N, self.K)
+        self._streamer.run(stream, self.host_a, self.host_b, self.host_c, after=after)
+
+    @property
+    def e2e_streamed(self):
+        # One GPU: the host-operand GEMM of titan_rs_b200.streaming (B, then A in row
+        # blocks, each block's GEMM and download overlapping the later blocks' uploads).
+        if self.world != 1 or os.environ.get("TITAN_B200_E2E", "streamed") != "streamed":
+            return None
+        return self._streamed_step
+
+    _streamer = None
 
     def h2d_bytes(self):
         return self.a_bytes + self.b_bytes
@@ -925,7 +946,15 @@ def measure(wl, args, session, stream, dist, peaks, peak_src, tb, N) -> dict:
     if not args.small:
         out_stream = session.create_stream()
 
-        def e2e_run(steps):
+        streamed = wl.e2e_streamed
+
+        def e2e_run(steps, start=None):
+            if streamed is not None:
+                # Every step's uploads, operator and downloads are enqueued by the
+                # public call; the first step's uploads wait for the start event.
+                for i in range(steps):
+                    streamed(stream, start if i == 0 else None)
+                return
             prev_download = None
             for _ in range(steps):
                 wl.e2e_upload(stream)
@@ -943,13 +972,19 @@ def measure(wl, args, session, stream, dist, peaks, peak_src, tb, N) -> dict:
         session.synchronize(stream)
         e0 = session.record(stream)
         e2e_steps = max(3, min(args.steps, 10))
-        e2e_run(e2e_steps)
-        e1 = session.record(out_stream)
+        e2e_run(e2e_steps, e0)
+        if streamed is None:
+            e1 = session.record(out_stream)
+        else:
+            e1 = session.record(stream)  # the call's stream waits for its last download
         session.synchronize(out_stream)
         session.synchronize(stream)
         e2e_ms = reduce_max(dist, session.elapsed_ms(e0, e1)) / e2e_steps
         e2e = {"value": units_step / (e2e_ms / 1e3) / scale, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d_bytes(),
-               "d2h_bytes_per_step": wl.d2h_bytes(), "ms_per_step": e2e_ms}
+               "d2h_bytes_per_step": wl.d2h_bytes(), "ms_per_step": e2e_ms,
+               "path": ("titan_rs_b200.streaming.StreamedGemm.run (row blocks: upload, GEMM and download "
+                        "overlapped)" if streamed is not None else
+                        "tb_upload_pinned + operator + tb_download_pinned, steps pipelined over two streams")}
     out = {"metric": wl.metric, "value": value, "unit": wl.unit, "ms_per_step": ms_step, "scaling": wl.scaling,
            "dtype": wl.dtype, "config": wl.config(), "op": wl.name, "roofline": roofline, "e2e": e2e,
            "gpu_launches": launches, "clocks": clock_info}

@@ -1,0 +1,106 @@
+"""GEMM on host-resident operands, streamed through the GPU.
+
+The reference runs `gemm` on CPU tensors with its scalar loop (titan-runtime/src/lib.rs:
+955-989), and its CUDA path uploads every input, runs the kernel and downloads the
+result one after the other (Tensor::from_slice / to_vec, titan-tensor/src/lib.rs:
+215-260). For operands that live in host memory this module overlaps the three: B is
+uploaded first (every row block of C needs all of it), then A in row blocks, each
+block's GEMM starting as soon as its rows have landed and each block of C going back
+to the host while later blocks compute. One call is one `C = A · Bᵀ` (bf16, B stored
+[N, K], fp32 accumulation, the `transpose_rhs` GEMM of `tb_op_gemm`); consecutive
+calls pipeline as well: the next call's uploads start while this call's last blocks
+compute and download (B alternates between two device buffers).
+
+Each row block runs the same operator (`tb_op_gemm`) on views of one device A and one
+device C, so a block's rows are computed exactly as the whole GEMM computes them when
+the operator picks the same kernel for the block. Host buffers must be page-locked
+(`Session.host_alloc`): the copies are asynchronous and the caller keeps them alive
+until the call's work on `stream` is done.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import List, Optional
+
+from . import _native as native
+from .hal import Event, PinnedHost, Session, Stream, _check
+from .kernel_abi import DType
+from .runtime import c_tensor, contiguous_strides
+
+
+class StreamedGemm:
+    """C[M, N] = A[M, K] · B[N, K]ᵀ from and to page-locked host buffers.
+
+    `row_blocks` splits M into at most that many blocks (multiples of 256 rows where M
+    allows, so each block still fills the GPU with 256-row CTA-pair tiles)."""
+
+    def __init__(self, session: Session, M: int, N: int, K: int, row_blocks: int = 4):
+        if min(M, N, K) <= 0:
+            raise ValueError("StreamedGemm needs positive M, N and K")
+        self.s, self.M, self.N, self.K = session, M, N, K
+        unit = 256 if M >= 256 * row_blocks else 1
+        base = -(-M // row_blocks)
+        rows = -(-base // unit) * unit
+        self.blocks = [(r0, min(rows, M - r0)) for r0 in range(0, M, rows)]
+        self.da = session.allocate(M * K * 2)
+        self.db = [session.allocate(N * K * 2), session.allocate(N * K * 2)]
+        self.dc = session.allocate(M * N * 2)
+        self._views = []  # the wrapped buffers must outlive their tensors
+        self.ta, self.tc = [], []
+        for r0, n in self.blocks:
+            va = session.wrap(self.da.device_ptr + r0 * K * 2, n * K * 2)
+            vc = session.wrap(self.dc.device_ptr + r0 * N * 2, n * N * 2)
+            self._views += [va, vc]
+            self.ta.append(c_tensor(va, DType.BF16, (n, K), contiguous_strides((n, K))))
+            self.tc.append(c_tensor(vc, DType.BF16, (n, N), contiguous_strides((n, N))))
+        self.tb = [c_tensor(b, DType.BF16, (N, K), contiguous_strides((N, K))) for b in self.db]
+        self.up = session.create_stream()    # host -> device copies, in the order they are needed
+        self.down = session.create_stream()  # device -> host copies of finished row blocks
+        self._key = b"transpose_rhs"
+        self.attrs = (native.Attr * 1)()
+        self.attrs[0].key = self._key
+        self.attrs[0].value = 1
+        nb = len(self.blocks)
+        self._gemm_done: List[Optional[Event]] = [None] * nb  # block i's A and C views are in use until then
+        self._down_done: List[Optional[Event]] = [None] * nb
+        self._b_free: List[Optional[Event]] = [None, None]
+        self.calls = 0
+
+    def run(self, stream: Stream, a: PinnedHost, b: PinnedHost, c: PinnedHost, after: Optional[Event] = None) -> None:
+        """Enqueues one call on `stream`: when `stream` reaches the end of it, C is in `c`.
+        `after`: an event the uploads wait for (e.g. the start of a timed region)."""
+        s, M, Nn, K = self.s, self.M, self.N, self.K
+        if a.nbytes < M * K * 2 or b.nbytes < Nn * K * 2 or c.nbytes < M * Nn * 2:
+            raise ValueError("host buffers smaller than the GEMM's operands")
+        slot = self.calls & 1
+        if after is not None:
+            s.wait_event(self.up, after)
+        if self._b_free[slot] is not None:
+            s.wait_event(self.up, self._b_free[slot])  # the GEMMs of two calls ago read this B
+        s.upload_pinned(self.up, self.db[slot], b, nbytes=Nn * K * 2)
+        s.wait_event(stream, s.record(self.up))
+        lib = native.lib()
+        for i, (r0, n) in enumerate(self.blocks):
+            if self._gemm_done[i] is not None:
+                s.wait_event(self.up, self._gemm_done[i])  # the previous call's block i has read its A rows
+            s.upload_pinned(self.up, self.da, a, nbytes=n * K * 2, dst_offset=r0 * K * 2, src_offset=r0 * K * 2)
+            s.wait_event(stream, s.record(self.up))
+            if self._down_done[i] is not None:
+                s.wait_event(stream, self._down_done[i])  # the previous call's block i of C is on the host
+            _check(lib.tb_op_gemm(s.ptr, stream.ptr, ctypes.byref(self.ta[i]), ctypes.byref(self.tb[slot]),
+                                  ctypes.byref(self.tc[i]), self.attrs, 1, None))
+            done = s.record(stream)
+            self._gemm_done[i] = done
+            s.wait_event(self.down, done)
+            s.download_pinned(self.down, self.dc, c, nbytes=n * Nn * 2, src_offset=r0 * Nn * 2,
+                              dst_offset=r0 * Nn * 2)
+            self._down_done[i] = s.record(self.down)
+        self._b_free[slot] = s.record(stream)
+        s.wait_event(stream, self._down_done[-1])  # the call ends on `stream` once C is back on the host
+        self.calls += 1
+
+    def h2d_bytes(self) -> int:
+        return (self.M + self.N) * self.K * 2
+
+    def d2h_bytes(self) -> int:
+        return self.M * self.N * 2
