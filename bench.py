@@ -492,6 +492,26 @@ class SdpaWorkload(Workload):
         for h, d in zip(self.hosts, self.dev):
             self.s.upload_pinned(stream, d, h)
 
+    _streamer = None
+
+    def _streamed_step(self, stream, after):
+        if self._streamer is None:
+            from titan_rs_b200.kernel_abi import DType
+            from titan_rs_b200.streaming import StreamedBatchOp
+            # [B*H, 1, S, D]: the same (batch, head) problems, blocked over the leading dimension.
+            spec = (DType.BF16, (self.bh_local, 1, self.S, self.D), True)
+            self._streamer = StreamedBatchOp(self.s, "scaled_dot_product_attention", [spec, spec, spec],
+                                             (DType.BF16, (self.bh_local, 1, self.S, self.D)),
+                                             {"causal": 1, "candidate": self._cval.decode()})
+        self._streamer.run(stream, self.hosts, self.host_o, after=after)
+
+    @property
+    def e2e_streamed(self):
+        # One GPU: titan_rs_b200.streaming.StreamedBatchOp over (batch, head) blocks.
+        if self.world != 1 or os.environ.get("TITAN_B200_E2E", "streamed") != "streamed":
+            return None
+        return self._streamed_step
+
     def e2e_download(self, stream):
         self.s.download_pinned(stream, self.do, self.host_o)
 
@@ -580,6 +600,7 @@ class ConvWorkload(Workload):
             vals.append(cand.encode())
         self._keys = [n.encode() for n in names]
         self._strs = [v for v in vals if isinstance(v, bytes)]  # kept alive for the C strings
+        self.attr_dict = {n: (v.decode() if isinstance(v, bytes) else v) for n, v in zip(names, vals)}
         self.attrs = (N.Attr * len(names))()
         for i, (key, v) in enumerate(zip(self._keys, vals)):
             self.attrs[i].key = key
@@ -607,6 +628,29 @@ class ConvWorkload(Workload):
         self.s.upload_pinned(stream, self.dx[0], self.host_x)
         self.s.upload_pinned(stream, self.dw, self.host_w)
         self.i = 0  # the next step() uses input/output pair 0
+
+    _streamer = None
+
+    def _streamed_step(self, stream, after):
+        if self._streamer is None:
+            from titan_rs_b200.kernel_abi import DType
+            from titan_rs_b200.streaming import StreamedBatchOp
+            attrs = self.attr_dict
+            H, W, C, K = self.H, self.W, self.C, self.K
+            self._streamer = StreamedBatchOp(
+                self.s, "conv2d", [(DType.BF16, (self.n_local, H, W, C), True),
+                                   (DType.BF16, (K, self.R, self.S, C), False)],
+                (DType.BF16, (self.n_local, H, W, K)), attrs)
+        self._streamer.run(stream, [self.host_x, self.host_w], self.host_y, after=after)
+
+    @property
+    def e2e_streamed(self):
+        # titan_rs_b200.streaming.StreamedBatchOp over image blocks (weights once per call) on
+        # request only: the conv's uploads (99 MB) dwarf its 0.16 ms of compute, and the
+        # blocks measured no faster (97.5 against 98.6 TFLOP/s end to end).
+        if self.world != 1 or os.environ.get("TITAN_B200_E2E", "") != "streamed":
+            return None
+        return self._streamed_step
 
     def e2e_download(self, stream):
         self.s.download_pinned(stream, self.dy[0], self.host_y)
@@ -982,8 +1026,8 @@ def measure(wl, args, session, stream, dist, peaks, peak_src, tb, N) -> dict:
         e2e_ms = reduce_max(dist, session.elapsed_ms(e0, e1)) / e2e_steps
         e2e = {"value": units_step / (e2e_ms / 1e3) / scale, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d_bytes(),
                "d2h_bytes_per_step": wl.d2h_bytes(), "ms_per_step": e2e_ms,
-               "path": ("titan_rs_b200.streaming.StreamedGemm.run (row blocks: upload, GEMM and download "
-                        "overlapped)" if streamed is not None else
+               "path": (f"titan_rs_b200.streaming.{type(wl._streamer).__name__}.run (blocks: upload, operator and "
+                        "download overlapped)" if streamed is not None else
                         "tb_upload_pinned + operator + tb_download_pinned, steps pipelined over two streams")}
     out = {"metric": wl.metric, "value": value, "unit": wl.unit, "ms_per_step": ms_step, "scaling": wl.scaling,
            "dtype": wl.dtype, "config": wl.config(), "op": wl.name, "roofline": roofline, "e2e": e2e,

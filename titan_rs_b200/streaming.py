@@ -1,4 +1,4 @@
-"""GEMM on host-resident operands, streamed through the GPU.
+"""Operators on host-resident operands, streamed through the GPU.
 
 The reference runs `gemm` on CPU tensors with its scalar loop (titan-runtime/src/lib.rs:
 955-989), and its CUDA path uploads every input, runs the kernel and downloads the
@@ -16,16 +16,25 @@ device C, so a block's rows are computed exactly as the whole GEMM computes them
 the operator picks the same kernel for the block. Host buffers must be page-locked
 (`Session.host_alloc`): the copies are asynchronous and the caller keeps them alive
 until the call's work on `stream` is done.
+
+`StreamedBatchOp` does the same for an operator whose output rows are independent over
+a leading batch dimension (attention over [B, H, T, D], conv2d over NHWC images): the
+batched inputs go up in batch blocks, each block runs through the native router
+(`tb_execute`, the Runtime::execute of titan-runtime/src/lib.rs:1171-1256) on views of
+the device tensors, and each block of the output comes back while later blocks run;
+inputs without a batch dimension (the conv weights) go up once per call.
 """
 from __future__ import annotations
 
 import ctypes
 from typing import List, Optional
 
+import numpy as np
+
 from . import _native as native
 from .hal import Event, PinnedHost, Session, Stream, _check
-from .kernel_abi import DType
-from .runtime import c_tensor, contiguous_strides
+from .kernel_abi import DType, scalar_width
+from .runtime import _attrs, c_tensor, contiguous_strides
 
 
 class StreamedGemm:
@@ -104,3 +113,107 @@ class StreamedGemm:
 
     def d2h_bytes(self) -> int:
         return self.M * self.N * 2
+
+
+class StreamedBatchOp:
+    """One operator over a leading batch dimension, inputs and output in page-locked host
+    memory. `inputs`: (dtype, shape, batched) per operator input, in the operator's order;
+    `output`: (dtype, shape), batch leading. The batch splits into at most `blocks` blocks."""
+
+    def __init__(self, session: Session, operator: str, inputs, output, attrs: Optional[dict] = None,
+                 blocks: int = 4):
+        self.s, self.op = session, operator
+        out_dtype, out_shape = output
+        batch = int(out_shape[0])
+        if batch <= 0:
+            raise ValueError("StreamedBatchOp needs a positive batch")
+        step = -(-batch // blocks)
+        self.blocks = [(b0, min(step, batch - b0)) for b0 in range(0, batch, step)]
+        self._keep = []  # wrapped views must outlive their tensors
+        self.inputs = []  # per input: (batched, item_bytes or total bytes, device buffers, per-block tensors)
+        for dtype, shape, batched in inputs:
+            shape = tuple(int(x) for x in shape)
+            nbytes = int(np.prod(shape)) * scalar_width(dtype)
+            if batched:
+                if shape[0] != batch:
+                    raise ValueError("a batched input's leading dimension must equal the output's")
+                item = nbytes // batch
+                dev = session.allocate(nbytes)
+                per_block = [self._view(dev, b0 * item, n * item, dtype, (n,) + shape[1:]) for b0, n in self.blocks]
+                self.inputs.append((True, item, [dev], per_block))
+            else:
+                devs = [session.allocate(nbytes), session.allocate(nbytes)]  # alternate between calls
+                whole = [c_tensor(d, dtype, shape, contiguous_strides(shape)) for d in devs]
+                self.inputs.append((False, nbytes, devs, whole))
+        out_shape = tuple(int(x) for x in out_shape)
+        self.out_item = int(np.prod(out_shape)) * scalar_width(out_dtype) // batch
+        self.dout = session.allocate(self.out_item * batch)
+        self.outs = [self._view(self.dout, b0 * self.out_item, n * self.out_item, out_dtype, (n,) + out_shape[1:])
+                     for b0, n in self.blocks]
+        self.attrs, self.n_attrs, self._attr_keep = _attrs(dict(attrs or {}))
+        self.up = session.create_stream()
+        self.down = session.create_stream()
+        nb = len(self.blocks)
+        self._op_done: List[Optional[Event]] = [None] * nb
+        self._down_done: List[Optional[Event]] = [None] * nb
+        self._shared_free: List[Optional[Event]] = [None, None]
+        self.calls = 0
+
+    def _view(self, dev, offset, nbytes, dtype, shape):
+        v = self.s.wrap(dev.device_ptr + offset, nbytes)
+        self._keep.append(v)
+        return c_tensor(v, dtype, shape, contiguous_strides(shape))
+
+    def run(self, stream: Stream, hosts, out: PinnedHost, after: Optional[Event] = None) -> None:
+        """Enqueues one call on `stream` (inputs: one PinnedHost per operator input, in
+        order); when `stream` reaches its end, the output is in `out`."""
+        s = self.s
+        if len(hosts) != len(self.inputs):
+            raise ValueError("one host buffer per operator input")
+        for (batched, size, _, _), h in zip(self.inputs, hosts):
+            if h.nbytes < (size * self.blocks[-1][0] + size * self.blocks[-1][1] if batched else size):
+                raise ValueError("host buffer smaller than its operand")
+        if out.nbytes < self.out_item * (self.blocks[-1][0] + self.blocks[-1][1]):
+            raise ValueError("host output buffer smaller than the output")
+        slot = self.calls & 1
+        if after is not None:
+            s.wait_event(self.up, after)
+        if self._shared_free[slot] is not None:
+            s.wait_event(self.up, self._shared_free[slot])  # the operators of two calls ago read these
+        for (batched, size, devs, _), h in zip(self.inputs, hosts):
+            if not batched:
+                s.upload_pinned(self.up, devs[slot], h, nbytes=size)
+        s.wait_event(stream, s.record(self.up))
+        lib = native.lib()
+        for i, (b0, n) in enumerate(self.blocks):
+            if self._op_done[i] is not None:
+                s.wait_event(self.up, self._op_done[i])  # the previous call's block i has read its inputs
+            for (batched, item, devs, _), h in zip(self.inputs, hosts):
+                if batched:
+                    s.upload_pinned(self.up, devs[0], h, nbytes=n * item, dst_offset=b0 * item, src_offset=b0 * item)
+            s.wait_event(stream, s.record(self.up))
+            if self._down_done[i] is not None:
+                s.wait_event(stream, self._down_done[i])  # the previous call's output block is on the host
+            ins = (native.Tensor * len(self.inputs))(*[t[i] if batched else t[slot]
+                                                       for batched, _, _, t in self.inputs])
+            ev = ctypes.c_void_p(0)
+            _check(lib.tb_execute(s.ptr, stream.ptr, self.op.encode(), ins, len(self.inputs),
+                                  ctypes.byref(self.outs[i]), self.attrs, self.n_attrs, ctypes.byref(ev)))
+            if ev.value:
+                Event(s, ev.value)  # released when this wrapper goes away
+            done = s.record(stream)
+            self._op_done[i] = done
+            s.wait_event(self.down, done)
+            s.download_pinned(self.down, self.dout, out, nbytes=n * self.out_item, src_offset=b0 * self.out_item,
+                              dst_offset=b0 * self.out_item)
+            self._down_done[i] = s.record(self.down)
+        self._shared_free[slot] = s.record(stream)
+        s.wait_event(stream, self._down_done[-1])
+        self.calls += 1
+
+    def h2d_bytes(self) -> int:
+        batch = self.blocks[-1][0] + self.blocks[-1][1]
+        return sum(size * batch if batched else size for batched, size, _, _ in self.inputs)
+
+    def d2h_bytes(self) -> int:
+        return self.out_item * (self.blocks[-1][0] + self.blocks[-1][1])
