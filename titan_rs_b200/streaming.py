@@ -15,7 +15,8 @@ Each row block runs the same operator (`tb_op_gemm`) on views of one device A an
 device C, so a block's rows are computed exactly as the whole GEMM computes them when
 the operator picks the same kernel for the block. Host buffers must be page-locked
 (`Session.host_alloc`): the copies are asynchronous and the caller keeps them alive
-until the call's work on `stream` is done.
+until the call's work on `stream` is done. An instance keeps the events of its previous
+call to order the next one, so one host thread drives it at a time.
 
 `StreamedBatchOp` does the same for an operator whose output rows are independent over
 a leading batch dimension (attention over [B, H, T, D], conv2d over NHWC images): the
