@@ -94,7 +94,7 @@ class ClockSampler:
             self.proc.kill()
         if self.thread:
             self.thread.join(timeout=2)
-        sm, smax, reasons = [], [], set()
+        sm, smax, power, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
@@ -105,13 +105,17 @@ class ClockSampler:
                 smax.append(float(parts[2]))
             except ValueError:
                 continue
+            try:
+                power.append(float(parts[3]))
+            except ValueError:
+                pass
             for name, flag in zip(names, parts[5:9]):
                 if flag.lower() == "active":
                     reasons.add(name)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "power_w": statistics.median(power) if power else None}
 
 
 # ----------------------------------------------------------------------------- workloads
