@@ -38,6 +38,17 @@ from .kernel_abi import DType, scalar_width
 from .runtime import _attrs, c_tensor, contiguous_strides
 
 
+def split_rows(rows: int, blocks: int, unit: int = 256):
+    """Splits `rows` into at most `blocks` consecutive (first row, rows) blocks, each a
+    multiple of `unit` rows (but the last) when rows >= unit * blocks."""
+    if rows <= 0 or blocks <= 0:
+        raise ValueError("split_rows needs positive rows and blocks")
+    u = unit if rows >= unit * blocks else 1
+    base = -(-rows // blocks)
+    step = -(-base // u) * u
+    return [(r0, min(step, rows - r0)) for r0 in range(0, rows, step)]
+
+
 class StreamedGemm:
     """C[M, N] = A[M, K] · B[N, K]ᵀ from and to page-locked host buffers.
 
@@ -48,10 +59,7 @@ class StreamedGemm:
         if min(M, N, K) <= 0:
             raise ValueError("StreamedGemm needs positive M, N and K")
         self.s, self.M, self.N, self.K = session, M, N, K
-        unit = 256 if M >= 256 * row_blocks else 1
-        base = -(-M // row_blocks)
-        rows = -(-base // unit) * unit
-        self.blocks = [(r0, min(rows, M - r0)) for r0 in range(0, M, rows)]
+        self.blocks = split_rows(M, row_blocks)
         self.da = session.allocate(M * K * 2)
         self.db = [session.allocate(N * K * 2), session.allocate(N * K * 2)]
         self.dc = session.allocate(M * N * 2)
@@ -128,8 +136,7 @@ class StreamedBatchOp:
         batch = int(out_shape[0])
         if batch <= 0:
             raise ValueError("StreamedBatchOp needs a positive batch")
-        step = -(-batch // blocks)
-        self.blocks = [(b0, min(step, batch - b0)) for b0 in range(0, batch, step)]
+        self.blocks = split_rows(batch, blocks, unit=1)
         self._keep = []  # wrapped views must outlive their tensors
         self.inputs = []  # per input: (batched, item_bytes or total bytes, device buffers, per-block tensors)
         for dtype, shape, batched in inputs:
