@@ -42,15 +42,14 @@
 #define TB_SDPA_BARRIER_BYTES 256
 #define TB_SDPA_SMEM_BYTES (7 * 32768 + TB_SDPA_BARRIER_BYTES + 1024)
 
-// Two-query-tile SDPA (sdpa_bf16_pair.cu): Q 2x32 KB + K ring 2x32 KB + V ring 2x32 KB + barriers;
-// P lives in tensor memory. 10 warps: producer, MMA, two softmax groups of four.
-#define TB_SDPA2_THREADS 320
+// Two-query-tile SDPA (sdpa_bf16_pair.cu, sdpa_bf16_persist.cu): Q 2x32 KB + a 2-stage
+// ring of K and V tiles (2 x 64 KB) + barriers; P lives in tensor memory. Three
+// warpgroups (control: producer, MMA and two idle warps; softmax A; softmax B), with
+// registers moved from the control warpgroup to the softmax ones: 384 threads launched
+// at TB_SDPA2_PAIR_LAUNCH_REGS registers = 128 x TB_SDPA2_PAIR_CONTROL_REGS + 256 x
+// TB_SDPA2_PAIR_SOFTMAX_REGS.
 #define TB_SDPA2_BARRIER_BYTES 256
 #define TB_SDPA2_SMEM_BYTES (6 * 32768 + TB_SDPA2_BARRIER_BYTES + 1024)
-// The pair kernel runs three warpgroups (control, softmax A, softmax B) and moves
-// registers from the control warpgroup to the softmax ones: 384 threads launched at
-// TB_SDPA2_PAIR_LAUNCH_REGS registers = 128 x TB_SDPA2_PAIR_CONTROL_REGS + 256 x
-// TB_SDPA2_PAIR_SOFTMAX_REGS.
 #define TB_SDPA2_PAIR_THREADS 384
 #define TB_SDPA2_PAIR_LAUNCH_REGS 168
 #define TB_SDPA2_PAIR_CONTROL_REGS 56
