@@ -70,6 +70,7 @@ typedef struct tb_stream tb_stream;
 typedef struct tb_event tb_event;
 typedef struct tb_kernel tb_kernel;
 typedef struct tb_comm tb_comm;
+typedef struct tb_graph_exec tb_graph_exec;
 
 /* DeviceFingerprint (titan-types/src/lib.rs:28-38); capability_revision is
  * "sm_<major><minor>" as in CudaDiscovery (titan-backend-cuda/src/lib.rs:221-226). */
@@ -201,6 +202,19 @@ tb_status tb_event_elapsed_ms(tb_session* session, tb_event* start, tb_event* en
 tb_status tb_stream_synchronize(tb_session* session, tb_stream* stream);
 /* Raw CUstream of a session stream (for interop with other CUDA users). */
 uint64_t tb_stream_handle(const tb_stream* stream);
+
+/* CUDA graphs (no counterpart in the reference, which launches every kernel from the
+ * host, titan-backend-cuda/src/lib.rs:1413-1507). The device work enqueued on `stream`
+ * by this thread between tb_capture_begin and tb_capture_end (operators, device
+ * copies, event records) becomes a graph that tb_graph_exec_launch replays on any
+ * stream of the session with one launch, on the same device buffers. Host-staged
+ * uploads/downloads, host waits and an operator's first use of per-stream scratch
+ * (split-K, the persistent attention candidate: run it once first) cannot be
+ * captured: tb_capture_end then returns the driver's error and no graph. */
+tb_status tb_capture_begin(tb_session* session, tb_stream* stream);
+tb_status tb_capture_end(tb_session* session, tb_stream* stream, tb_graph_exec** out);
+tb_status tb_graph_exec_launch(tb_session* session, tb_graph_exec* graph, tb_stream* stream);
+void tb_graph_exec_release(tb_graph_exec* graph);
 
 /* Page-locked host memory and copies that use it directly (no staging): the
  * caller keeps `src`/`dst` alive until the returned event completes. */

@@ -116,6 +116,10 @@ _SIGNATURES = {
     "tb_event_elapsed_ms": (_S, [_P, _P, _P, ctypes.POINTER(ctypes.c_float)]),
     "tb_stream_synchronize": (_S, [_P, _P]),
     "tb_stream_handle": (_U64, [_P]),
+    "tb_capture_begin": (_S, [_P, _P]),
+    "tb_capture_end": (_S, [_P, _P, _PP]),
+    "tb_graph_exec_launch": (_S, [_P, _P, _P]),
+    "tb_graph_exec_release": (None, [_P]),
     "tb_host_alloc": (_S, [_P, _SZ, _PP]),
     "tb_host_free": (_S, [_P, _P]),
     "tb_upload_pinned": (_S, [_P, _P, _P, _SZ, _P, _SZ, _PP]),

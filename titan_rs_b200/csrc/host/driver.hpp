@@ -35,6 +35,13 @@ namespace tb {
   X(cuStreamDestroy_v2)                \
   X(cuStreamSynchronize)               \
   X(cuStreamWaitEvent)                 \
+  X(cuStreamBeginCapture_v2)           \
+  X(cuStreamIsCapturing)               \
+  X(cuStreamEndCapture)                \
+  X(cuGraphInstantiateWithFlags)       \
+  X(cuGraphLaunch)                     \
+  X(cuGraphExecDestroy)                \
+  X(cuGraphDestroy)                    \
   X(cuEventCreate)                     \
   X(cuEventDestroy_v2)                 \
   X(cuEventRecord)                     \

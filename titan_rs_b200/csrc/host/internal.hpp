@@ -114,6 +114,11 @@ tb_status check_event(Session* s, tb_event* e, Event** out);
 // At least `bytes` of the stream's scratch memory (allocating or growing it).
 tb_status stream_scratch(Session* s, Stream* st, size_t bytes, CUdeviceptr* out);
 
+// Whether `st` is being captured into a CUDA graph (tb_capture_begin): host-staged
+// copies and allocations are refused then, since a replay would run them on memory
+// the call no longer owns.
+bool stream_capturing(Stream* st);
+
 // Records an event on `stream` and hands it to the caller (or drops it if out is null).
 tb_status record_event(Session* s, Stream* stream, std::shared_ptr<std::vector<uint8_t>> staging, tb_event** out);
 

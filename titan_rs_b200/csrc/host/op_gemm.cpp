@@ -467,11 +467,15 @@ extern "C" tb_status tb_op_gemm(tb_session* session, tb_stream* stream, const tb
   } else {
     if (candidate && strcmp(candidate, "gemm_f32_tiled") != 0)
       return unsupported(std::string("candidate ") + candidate + " does not take F32");
-    rc = builtin_function(s, "compat", "gemm_f32_tiled", &fn);
+    // 64 x 64 tiles unless that leaves most SMs idle, then 16 x 16 (same per-output
+    // summation order, so the same bits).
+    const long long blocks64 = (long long)((N + 63) / 64) * ((M + 63) / 64);
+    const int tile = blocks64 < 2LL * s->sm_count ? 16 : 64;
+    rc = builtin_function(s, "compat", tile == 16 ? "gemm_f32_tiled16" : "gemm_f32_tiled", &fn);
     if (rc) return rc;
     void* params[] = {&pa, &pb, &pc, &M, &N, &K, &as0, &as1, &bs0, &bs1};
-    rc = launch_builtin(s, st, fn, (unsigned)((N + 63) / 64), (unsigned)((M + 63) / 64), 1, 256, 0, params,
-                        "gemm_f32_tiled");
+    rc = launch_builtin(s, st, fn, (unsigned)((N + tile - 1) / tile), (unsigned)((M + tile - 1) / tile), 1, 256, 0,
+                        params, "gemm_f32_tiled");
   }
   if (rc) return rc;
   return record_event(s, st, nullptr, out);

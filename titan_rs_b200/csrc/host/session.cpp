@@ -261,11 +261,19 @@ tb_status record_event(Session* s, Stream* stream, std::shared_ptr<std::vector<u
   return TB_OK;
 }
 
+bool stream_capturing(Stream* st) {
+  CUstreamCaptureStatus status = CU_STREAM_CAPTURE_STATUS_NONE;
+  return driver()->cuStreamIsCapturing(st->raw, &status) == CUDA_SUCCESS && status != CU_STREAM_CAPTURE_STATUS_NONE;
+}
+
 tb_status stream_scratch(Session* s, Stream* st, size_t bytes, CUdeviceptr* out) {
   if (st->scratch_bytes >= bytes) {
     *out = st->scratch;
     return TB_OK;
   }
+  if (stream_capturing(st))
+    return set_error(TB_ERR_INVALID, "capture",
+                     "first use of the stream's scratch memory inside a graph capture: run the operator once before");
   const DriverApi* d = driver();
   if (st->scratch) {
     // Earlier kernels on this stream may still read the old scratch.
@@ -607,10 +615,12 @@ tb_status tb_upload(tb_session* session, tb_stream* stream, tb_buffer* dst, cons
   if (rc) return rc;
   if (len > b->bytes) return set_error(TB_ERR_INVALID, "upload", "source exceeds allocation");
   if (len && !src) return set_error(TB_ERR_INVALID, "upload", "null source");
-  auto staging = std::make_shared<std::vector<uint8_t>>(static_cast<const uint8_t*>(src),
-                                                        static_cast<const uint8_t*>(src) + len);
   rc = activate(s);
   if (rc) return rc;
+  if (stream_capturing(st))
+    return set_error(TB_ERR_INVALID, "upload", "staged upload inside a graph capture (use tb_upload_pinned)");
+  auto staging = std::make_shared<std::vector<uint8_t>>(static_cast<const uint8_t*>(src),
+                                                        static_cast<const uint8_t*>(src) + len);
   if (len) TB_CU("cuMemcpyHtoDAsync", driver()->cuMemcpyHtoDAsync_v2(b->ptr, staging->data(), len, st->raw));
   return record_event(s, st, staging, out);
 }
@@ -629,6 +639,8 @@ tb_status tb_download(tb_session* session, tb_stream* stream, tb_buffer* src, vo
   if (len && !dst) return set_error(TB_ERR_INVALID, "download", "null destination");
   rc = activate(s);
   if (rc) return rc;
+  if (stream_capturing(st))
+    return set_error(TB_ERR_INVALID, "download", "download inside a graph capture (use tb_download_pinned)");
   const DriverApi* d = driver();
   if (len) TB_CU("cuMemcpyDtoHAsync", d->cuMemcpyDtoHAsync_v2(dst, b->ptr, len, st->raw));
   // The borrowed host destination cannot outlive this call (lib.rs:1300-1304).

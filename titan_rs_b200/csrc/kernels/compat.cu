@@ -52,40 +52,64 @@ extern "C" __global__ void gemm_f32(const float* __restrict__ a, const float* __
 }
 
 // C[M,N] = op(A) op(B); A element (m,k) at a[m*as0 + k*as1], B element (k,n) at b[k*bs0 + n*bs1].
-extern "C" __global__ void __launch_bounds__(256) gemm_f32_tiled(const float* __restrict__ a,
-                                                                 const float* __restrict__ b, float* __restrict__ c,
-                                                                 int M, int N, int K, long long as0, long long as1,
-                                                                 long long bs0, long long bs1) {
-  __shared__ float As[16][64 + 1];
-  __shared__ float Bs[16][64 + 1];
-  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
-  float acc[4][4] = {};
-  for (int k0 = 0; k0 < K; k0 += 16) {
-    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
-      const int kk = i / 64, mm = i % 64;
+// A block computes a TM x TM tile with 256 threads, each an RM x RM patch, stepping K by
+// KS through shared memory; every output still adds its products in ascending k, each
+// rounded before the add (the reference's loop), whatever the tile size.
+template <int TM, int RM, int KS>
+__device__ __forceinline__ void gemm_f32_tile(const float* __restrict__ a, const float* __restrict__ b,
+                                              float* __restrict__ c, int M, int N, int K, long long as0,
+                                              long long as1, long long bs0, long long bs1) {
+  static_assert((TM / RM) * (TM / RM) == 256, "256 threads per block");
+  __shared__ float As[KS][TM + 1];
+  __shared__ float Bs[KS][TM + 1];
+  constexpr int TPR = TM / RM;  // threads per tile row
+  const int tx = threadIdx.x % TPR, ty = threadIdx.x / TPR;
+  const int m0 = blockIdx.y * TM, n0 = blockIdx.x * TM;
+  float acc[RM][RM] = {};
+  for (int k0 = 0; k0 < K; k0 += KS) {
+    for (int i = threadIdx.x; i < KS * TM; i += 256) {
+      const int kk = i / TM, mm = i % TM;
       const int m = m0 + mm, k = k0 + kk;
       As[kk][mm] = (m < M && k < K) ? a[(long long)m * as0 + (long long)k * as1] : 0.f;
       const int n = n0 + mm;
       Bs[kk][mm] = (n < N && k < K) ? b[(long long)k * bs0 + (long long)n * bs1] : 0.f;
     }
     __syncthreads();
-    const int kmax = min(16, K - k0);
+    const int kmax = min(KS, K - k0);
     for (int kk = 0; kk < kmax; ++kk) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < RM; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = mul_add_unfused(acc[i][j], As[kk][ty * 4 + i], Bs[kk][tx * 4 + j]);
+        for (int j = 0; j < RM; ++j)
+          acc[i][j] = mul_add_unfused(acc[i][j], As[kk][ty * RM + i], Bs[kk][tx * RM + j]);
     }
     __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < RM; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
+    for (int j = 0; j < RM; ++j) {
+      const int m = m0 + ty * RM + i, n = n0 + tx * RM + j;
       if (m < M && n < N) c[(long long)m * N + n] = acc[i][j];
     }
+}
+
+// 64 x 64 tiles: outputs large enough to give every SM blocks.
+extern "C" __global__ void __launch_bounds__(256) gemm_f32_tiled(const float* __restrict__ a,
+                                                                 const float* __restrict__ b, float* __restrict__ c,
+                                                                 int M, int N, int K, long long as0, long long as1,
+                                                                 long long bs0, long long bs1) {
+  gemm_f32_tile<64, 4, 16>(a, b, c, M, N, K, as0, as1, bs0, bs1);
+}
+
+// 16 x 16 tiles, one output per thread, K in steps of 64 (fewer load-and-barrier
+// rounds for a thread's single chain of products): small outputs (C1's 256 x 256 is 256
+// blocks instead of 16).
+extern "C" __global__ void __launch_bounds__(256) gemm_f32_tiled16(const float* __restrict__ a,
+                                                                   const float* __restrict__ b, float* __restrict__ c,
+                                                                   int M, int N, int K, long long as0, long long as1,
+                                                                   long long bs0, long long bs1) {
+  gemm_f32_tile<16, 1, 64>(a, b, c, M, N, K, as0, as1, bs0, bs1);
 }
 
 extern "C" __global__ void gemm_bf16_generic(const __nv_bfloat16* __restrict__ a, const __nv_bfloat16* __restrict__ b,

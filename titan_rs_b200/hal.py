@@ -125,6 +125,15 @@ class Event(_Handle):
     _release = "tb_event_release"
 
 
+class GraphExec(_Handle):
+    """A captured CUDA graph of a session's device work (tb_capture_begin / tb_capture_end);
+    launch() replays it on a stream with one launch."""
+    _release = "tb_graph_exec_release"
+
+    def launch(self, stream: "Stream") -> None:
+        _check(N.lib().tb_graph_exec_launch(self.session.ptr, self.ptr, stream.ptr))
+
+
 class LoadedKernel(_Handle):
     _release = "tb_kernel_release"
 
@@ -281,6 +290,16 @@ class Session:
 
     def synchronize(self, stream: Stream) -> None:
         _check(N.lib().tb_stream_synchronize(self.ptr, stream.ptr))
+
+    def capture_begin(self, stream: Stream) -> None:
+        """Starts capturing this thread's device work on `stream` into a CUDA graph."""
+        _check(N.lib().tb_capture_begin(self.ptr, stream.ptr))
+
+    def capture_end(self, stream: Stream) -> GraphExec:
+        """Ends the capture; the graph replays the captured work on the same buffers."""
+        h = _out()
+        _check(N.lib().tb_capture_end(self.ptr, stream.ptr, ctypes.byref(h)))
+        return GraphExec(self, h.value)
 
     def host_alloc(self, nbytes: int) -> "PinnedHost":
         p = _out()
