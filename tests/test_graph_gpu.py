@@ -88,3 +88,43 @@ def test_attention_chain_fuses_into_one_flash_attention_launch():
     assert max_rel_err(fused.to_f32(), ref) <= 1e-2
     assert max_rel_err(unfused.to_f32(), ref) <= 3e-2
     s.close()
+
+
+def test_compiled_plan_captured_as_a_cuda_graph_replays_on_new_inputs():
+    """ExecutionPlan.capture: the MLP's two fused nodes as one CUDA graph. Each replay,
+    after new contents are uploaded into the bound input, must equal an eager run of
+    the plan on the same input, bit for bit (same kernels, same buffers)."""
+    s = tb.Session(0)
+    rt = tb.Runtime(s)
+    m, d_in, d_hid, d_out = 256, 512, 768, 384
+    w1 = tb.fill_normal(d_hid * d_in, seed=402, std=1 / math.sqrt(d_in), dtype=DType.BF16).reshape(d_hid, d_in)
+    b1 = tb.fill_normal(d_hid, seed=403, std=0.5)
+    w2 = tb.fill_normal(d_out * d_hid, seed=404, std=1 / math.sqrt(d_hid), dtype=DType.BF16).reshape(d_out, d_hid)
+    b2 = tb.fill_normal(d_out, seed=405, std=0.5)
+    values = {0: TensorSpec(DType.BF16, (m, d_in)), 1: TensorSpec(DType.BF16, (d_hid, d_in)),
+              2: TensorSpec(DType.F32, (d_hid,)), 3: TensorSpec(DType.BF16, (m, d_hid)),
+              4: TensorSpec(DType.BF16, (m, d_hid)), 5: TensorSpec(DType.BF16, (m, d_hid)),
+              6: TensorSpec(DType.BF16, (d_out, d_hid)), 7: TensorSpec(DType.F32, (d_out,)),
+              8: TensorSpec(DType.BF16, (m, d_out)), 9: TensorSpec(DType.BF16, (m, d_out))}
+    nodes = [G.GraphNode(10, "gemm", [0, 1], [3], {"transpose_rhs": True}),
+             G.GraphNode(11, "broadcast.add", [3, 2], [4]),
+             G.GraphNode(12, "gelu", [4], [5]),
+             G.GraphNode(13, "gemm", [5, 6], [8], {"transpose_rhs": True}),
+             G.GraphNode(14, "broadcast.add", [8, 7], [9])]
+    plan = G.compile(G.Graph([0, 1, 2, 6, 7], [9], values, nodes))
+    x0 = tb.fill_normal(m * d_in, seed=400, dtype=DType.BF16).reshape(m, d_in)
+    x_t = tb.TensorHandle.from_numpy(s, x0, DType.BF16)
+    bind = {0: x_t, 1: tb.TensorHandle.from_numpy(s, w1, DType.BF16), 2: tb.TensorHandle.from_numpy(s, b1),
+            6: tb.TensorHandle.from_numpy(s, w2, DType.BF16), 7: tb.TensorHandle.from_numpy(s, b2)}
+    captured = plan.capture(rt, bind)
+    for seed in (410, 420):
+        x = tb.fill_normal(m * d_in, seed=seed, dtype=DType.BF16).reshape(m, d_in)
+        s.wait(s.upload(rt.stream, x_t.buffer, x))
+        captured.launch()
+        s.synchronize(rt.stream)
+        got = captured.outputs[0].to_numpy(rt.stream)
+        want = plan.execute(rt, bind).wait().outputs[0].to_numpy(rt.stream)
+        np.testing.assert_array_equal(got, want)
+        assert np.isfinite(tb.bf16_bits_to_f32(got)).all()
+    captured.graph.release()
+    s.close()

@@ -148,7 +148,7 @@ class ExecutionPlan:
     def node_count(self) -> int:
         return len(self.graph.nodes)
 
-    def execute(self, runtime: Runtime, bindings: dict) -> ExecutionHandle:
+    def execute(self, runtime: Runtime, bindings: dict, _outputs: Optional[dict] = None) -> ExecutionHandle:
         env = dict(bindings)
         for v in self.graph.inputs:
             if v not in env:
@@ -166,7 +166,9 @@ class ExecutionPlan:
                     raise ExecutionError(node.operator, "bind", f"missing TensorSpec for value {v}")
                 specs.append(self.graph.values[v])
             # Fused nodes ("gemm.bias_act", "attention.fused") are operators of the router too.
-            handle = runtime.execute(OpRequest(node.operator, inputs, specs, dict(node.attrs)))
+            request = OpRequest(node.operator, inputs, specs, dict(node.attrs))
+            out = _outputs.get(node.outputs[0]) if _outputs else None
+            handle = runtime.execute(request) if out is None else runtime.execute(request, output=out)
             if len(handle.outputs) != len(node.outputs):
                 raise ExecutionError(node.operator, "execute", f"node {node.id} produced {len(handle.outputs)} "
                                                                f"outputs, expected {len(node.outputs)}")
@@ -181,7 +183,36 @@ class ExecutionPlan:
         if not outs and last is not None:
             outs = last.outputs
         # Every node ran on the runtime's stream: the last node's event covers them all.
-        return ExecutionHandle(outs, "b200/graph", "graph.plan", last.event if last else None)
+        handle = ExecutionHandle(outs, "b200/graph", "graph.plan", last.event if last else None)
+        handle.values = env
+        return handle
+
+    def capture(self, runtime: Runtime, bindings: dict) -> "CapturedPlan":
+        """The plan as a CUDA graph: one eager run allocates every node's output (and any
+        per-stream scratch its operators use), then the same nodes, writing into those
+        outputs, are captured on the runtime's stream. CapturedPlan.launch() replays them
+        with one launch, on the bound input tensors (upload new contents to replay on new
+        data) and into the same output tensors."""
+        eager = self.execute(runtime, bindings)
+        eager.wait()
+        produced = {v: t for v, t in eager.values.items() if v not in bindings}
+        runtime.session.capture_begin(runtime.stream)
+        try:
+            self.execute(runtime, bindings, _outputs=produced)
+        finally:
+            graph = runtime.session.capture_end(runtime.stream)
+        return CapturedPlan(runtime, graph, eager.outputs)
+
+
+class CapturedPlan:
+    """A compiled plan captured as a CUDA graph (ExecutionPlan.capture)."""
+
+    def __init__(self, runtime: Runtime, graph, outputs: list):
+        self.runtime, self.graph, self.outputs = runtime, graph, outputs
+
+    def launch(self) -> None:
+        """Enqueues one replay on the runtime's stream."""
+        self.graph.launch(self.runtime.stream)
 
 
 def compile(graph: Graph) -> ExecutionPlan:
@@ -191,5 +222,6 @@ def compile(graph: Graph) -> ExecutionPlan:
     return ExecutionPlan(g, reports)
 
 
-__all__ = ["GraphNode", "Graph", "PassReport", "ExecutionPlan", "compile", "validate", "dead_code_eliminate",
+__all__ = ["GraphNode", "Graph", "PassReport", "ExecutionPlan", "CapturedPlan", "compile", "validate",
+           "dead_code_eliminate",
            "fuse_gemm_epilogues", "fuse_attention"]
