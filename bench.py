@@ -1189,13 +1189,13 @@ _TRAFFIC_CAPTURE = ("ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gp
                     "--clock-control none -k regex:{kernel} -s 3 -c 1 python bench.py --op {op} --ops none "
                     "--steps 5 --warmup 3 --no-cpu-baseline --soak-ms 0")
 TRAFFIC_PER_LAUNCH: dict = {
-    "gemm_bf16_tn_2sm": {"read": 1040327936, "write": 129578240, "source_sha16": "83c708fbd8ce4403",
+    "gemm_bf16_tn_2sm": {"read": 1078643200, "write": 126348544, "source_sha16": "6722c8ca86ecdafa",
                          "capture": _TRAFFIC_CAPTURE.format(kernel="gemm_bf16_tn_2sm", op="gemm")},
-    "softmax_f32_warp32": {"read": 536910592, "write": 481103104, "source_sha16": "75f1d1615b0b0d59",
+    "softmax_f32_warp32": {"read": 536956160, "write": 480842240, "source_sha16": "442ecc3d80f9c965",
                            "capture": _TRAFFIC_CAPTURE.format(kernel="softmax_f32_warp32", op="softmax")},
-    "sdpa_fwd_bf16_d128_pair": {"read": 818295808, "write": 247968000, "source_sha16": "2c8b21b4a8905a1d",
+    "sdpa_fwd_bf16_d128_pair": {"read": 816640512, "write": 247690240, "source_sha16": "8c8feb03576d07b9",
                                 "capture": _TRAFFIC_CAPTURE.format(kernel="sdpa_fwd_bf16_d128_pair", op="sdpa")},
-    "conv2d_fprop_bf16_nhwc_2sm": {"read": 103990784, "write": 55257344, "source_sha16": "2739d42714d42ab2",
+    "conv2d_fprop_bf16_nhwc_2sm": {"read": 103998720, "write": 55672576, "source_sha16": "55daf445a17e1a22",
                                    "capture": _TRAFFIC_CAPTURE.format(kernel="conv2d_fprop_bf16_nhwc_2sm",
                                                                       op="conv2d")},
 }
