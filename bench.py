@@ -11,9 +11,12 @@ Prints ONE JSON line (rank 0). Workloads are the BASELINE.json configurations:
 Inputs are seeded synthetic data (no dataset exists for this path).
 
 `value` is the device-timed whole-job throughput with inputs resident in HBM;
-`e2e` is the same metric through the C ABI with pinned-host inputs copied in and
-the result copied out inside every timed step (steps pipelined over two streams, so one
-step's upload overlaps the previous step's download). `--impl reference` times the CPU
+`e2e` is the same metric through the public API with pinned-host inputs copied in and
+the result copied out inside every timed step: at N=1 the GEMM and attention through
+titan_rs_b200.streaming (blocks uploaded, computed and downloaded overlapped), otherwise
+whole-tensor copies around the operator with steps pipelined over two streams (one
+step's upload overlaps the previous step's download); `e2e.path` names which.
+`--impl reference` times the CPU
 restatement of the reference's scalar operator (oracle/) on the host cores; it never
 loads the product library (its inputs come from the oracle's copy of the generator).
 
@@ -21,7 +24,8 @@ The headline line is `--op` (default gemm, C3). With `--ops` (default: the other
 configs when `--op` is gemm) the same run measures C2, C4 and C5 the same way and
 reports them under "ops", each with value, ms_per_step, roofline, e2e and, at N=1,
 cpu_baseline; "ops" also holds C1, the reference's own CPU configuration (f32 256^3),
-timed on the host at one thread and at all threads beside the f32 kernel on the GPU.
+timed on the host at one thread and at all threads beside the f32 kernel on the GPU
+(launched from the host, and replayed from a CUDA graph).
 """
 from __future__ import annotations
 
