@@ -1193,13 +1193,13 @@ _TRAFFIC_CAPTURE = ("ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gp
                     "--clock-control none -k regex:{kernel} -s 3 -c 1 python bench.py --op {op} --ops none "
                     "--steps 5 --warmup 3 --no-cpu-baseline --soak-ms 0")
 TRAFFIC_PER_LAUNCH: dict = {
-    "gemm_bf16_tn_2sm": {"read": 1078643200, "write": 126348544, "source_sha16": "6722c8ca86ecdafa",
+    "gemm_bf16_tn_2sm": {"read": 1044584704, "write": 126917888, "source_sha16": "a1c6ceac6de8b7b5",
                          "capture": _TRAFFIC_CAPTURE.format(kernel="gemm_bf16_tn_2sm", op="gemm")},
-    "softmax_f32_warp32": {"read": 536956160, "write": 480842240, "source_sha16": "442ecc3d80f9c965",
+    "softmax_f32_warp32": {"read": 536921856, "write": 481277184, "source_sha16": "d9c1e674e4ee55f3",
                            "capture": _TRAFFIC_CAPTURE.format(kernel="softmax_f32_warp32", op="softmax")},
-    "sdpa_fwd_bf16_d128_pair": {"read": 816640512, "write": 247690240, "source_sha16": "8c8feb03576d07b9",
+    "sdpa_fwd_bf16_d128_pair": {"read": 817332224, "write": 250097664, "source_sha16": "634d5518b8f1f1b4",
                                 "capture": _TRAFFIC_CAPTURE.format(kernel="sdpa_fwd_bf16_d128_pair", op="sdpa")},
-    "conv2d_fprop_bf16_nhwc_2sm": {"read": 103998720, "write": 55672576, "source_sha16": "55daf445a17e1a22",
+    "conv2d_fprop_bf16_nhwc_2sm": {"read": 103998464, "write": 55198720, "source_sha16": "b42c3a7b52ea5292",
                                    "capture": _TRAFFIC_CAPTURE.format(kernel="conv2d_fprop_bf16_nhwc_2sm",
                                                                       op="conv2d")},
 }

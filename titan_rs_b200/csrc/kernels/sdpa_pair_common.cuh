@@ -93,11 +93,12 @@ __device__ __forceinline__ void prefetch_tile(const CUtensorMap* map, int row0, 
   tma_prefetch_l2_3d(map, 64, row0, bh);
 }
 
-// Key tiles the producer asks L2 for ahead of their loads. The K and V rings hold two
-// tiles each, so a tile's load can start only about one key-tile period before its
-// MMAs; the CTA that leads its head (the heaviest causal pair starts first) would meet
-// DRAM latency there without the prefetch.
-constexpr int kPrefetchAhead = 2;
+// Key tiles the producer asks L2 for ahead of their loads. The ring holds two stages,
+// so a tile's load can start only about one key-tile period before its MMAs; the CTA
+// that leads its head group would meet DRAM latency there without the prefetch. One
+// tile ahead measured best (1064-1066 TFLOP/s at C4 against 1058-1061 for two and
+// 1041-1050 for four).
+constexpr int kPrefetchAhead = 1;
 
 // Work order of the (batch*head, query-tile pair) items: groups of kHeadGroup heads
 // (their K and V, 2 MB a head at T = 4096, stay in L2 while the group runs) and, inside
